@@ -1,0 +1,442 @@
+#!/usr/bin/env python3
+"""Benchmark of the Q4_0 x Q8_0 projection hot path.
+
+Workload: the Qwen2.5-1.5B projection set -- fused
+QKV 2048x1536 (+bias), o 1536x1536, gate+up 2x8960x1536 (+SiLU*mul, Q8 epilogue),
+down 1536x8960 -- each behind its Q8_0 activation quantiser.  One step = one pass
+of the whole set over M tokens of synthetic activations.
+
+* value  = prefill tokens/s at M = 2048 (whole job, all ranks), device-timed with
+           CUDA events on the library's stream, inputs resident in HBM;
+* e2e    = the same through the C ABI with pinned host buffers: host->device copy
+           of the step's two fp32 inputs and device->host copy of its three fp32
+           outputs inside the timed region;
+* decode = the same set at M = 1 (microseconds per token) in `decode`;
+* roofline: the dominant kernel's algorithmic throughput against MEASURED_PEAKS.json;
+* cpu_baseline: the reference's own matvec_q4q8/quantize_q8 (oracle/_ref when built
+  here, else the oracle restatement) on the host cores, on a bounded token sample.
+
+Weights are seeded synthetic Q4_0 (N(0, 0.02)); ten weight copies (263 MB, over
+twice the 126 MB L2) are rotated across steps so every step streams from HBM.
+`--impl reference` times the reference's CPU implementation on this workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "simple-inference_b200"))
+
+H, I = 1536, 8960
+QKV_N = 2048
+PREFILL_M = 2048
+METRIC = "Qwen layer prefill tok/s + decode µs/token; % of HBM / int8-TC roofline"
+INT8_SPEC_TOPS = 4500.0  # B200 dense int8 tensor-core spec; not in MEASURED_PEAKS.json
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True,
+                                         text=True, timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([s.strip() for s in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 3 + i and s[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+class ProjectionSet:
+    """Device weights (several copies) and activation buffers for one M."""
+
+    def __init__(self, ctx, torch, copies: int, seed: int = 1):
+        self.ctx, self.torch = ctx, torch
+        self.sets = []
+        for c in range(copies):
+            s = seed * 1000 + 10 * c
+            self.sets.append(dict(
+                qkv=ctx.matrix_synth(QKV_N, H, s + 1), o=ctx.matrix_synth(H, H, s + 2),
+                gate=ctx.matrix_synth(I, H, s + 3), up=ctx.matrix_synth(I, H, s + 4),
+                down=ctx.matrix_synth(H, I, s + 5)))
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.bias = (torch.randn(QKV_N, device="cuda", generator=g) * 0.02).contiguous()
+        ctx.sync()
+
+    def buffers(self, M):
+        t = self.torch
+        dev = "cuda"
+        return dict(
+            x=t.randn(M, H, device=dev), oin=t.randn(M, H, device=dev),
+            xq=t.empty(M * H, dtype=t.int8, device=dev), xd=t.empty(M * H // 32, dtype=t.int16, device=dev),
+            oq=t.empty(M * H, dtype=t.int8, device=dev), od=t.empty(M * H // 32, dtype=t.int16, device=dev),
+            aq=t.empty(M * I, dtype=t.int8, device=dev), ad=t.empty(M * I // 32, dtype=t.int16, device=dev),
+            qkv=t.empty(M, QKV_N, device=dev), yo=t.empty(M, H, device=dev), yd=t.empty(M, H, device=dev))
+
+    def step(self, b, M, i, timers=None):
+        """One pass of the projection set; returns the number of kernels launched."""
+        ctx, w = self.ctx, self.sets[i % len(self.sets)]
+        ev = timers
+        if ev: ev[0].record()
+        ctx.q8_quantize(b["x"], M, H, b["xq"], b["xd"])
+        if ev: ev[1].record()
+        ctx.matmul(w["qkv"], b["xq"], b["xd"], M, self.bias, b["qkv"])
+        if ev: ev[2].record()
+        ctx.q8_quantize(b["oin"], M, H, b["oq"], b["od"])
+        if ev: ev[3].record()
+        ctx.matmul(w["o"], b["oq"], b["od"], M, None, b["yo"])
+        if ev: ev[4].record()
+        ctx.gateup_q8(w["gate"], w["up"], b["xq"], b["xd"], M, b["aq"], b["ad"])
+        if ev: ev[5].record()
+        ctx.matmul(w["down"], b["aq"], b["ad"], M, None, b["yd"])
+        if ev: ev[6].record()
+        return 6
+
+
+def weight_bytes(M):
+    """Algorithmic HBM bytes of each projection kernel (weights 18 B/32, Q8 input
+    34 B/32 per token, fp32 outputs)."""
+    def mm(N, K, out_elem=4):
+        return N * K * 18 // 32 + M * K * 34 // 32 + M * N * out_elem
+    return {"qkv": mm(QKV_N, H) + QKV_N * 4, "o": mm(H, H),
+            "gateup": 2 * I * H * 18 // 32 + M * H * 34 // 32 + M * I * 34 // 32,
+            "down": mm(H, I)}
+
+
+def flops(M):
+    return {"qkv": 2 * M * QKV_N * H, "o": 2 * M * H * H, "gateup": 2 * M * 2 * I * H,
+            "down": 2 * M * H * I}
+
+
+def time_region(torch, stream, fn, steps):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record()
+        for i in range(steps):
+            fn(i)
+        end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import sib200
+    torch.cuda.set_device(local_rank)
+    ctx = sib200.Context(local_rank, max_positions=4096, rope_theta=1e6, head_dim=128)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    copies = 10
+    ps = ProjectionSet(ctx, torch, copies)
+    dist = world > 1
+    if dist:
+        import torch.distributed as tdist
+
+    def barrier_sync():
+        torch.cuda.synchronize()
+        ctx.sync()
+        if dist:
+            tdist.barrier()
+
+    def max_over_ranks(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        return float(t.item())
+
+    M = PREFILL_M
+    b = ps.buffers(M)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            ps.step(b, M, i)
+    barrier_sync()
+    with Clocks(local_rank) as clk:
+        t = time_region(torch, stream, lambda i: ps.step(b, M, i + args.warmup), args.steps)
+    barrier_sync()
+    t = max_over_ranks(t)
+    value = world * M * args.steps / t
+    ms_per_step = t / args.steps * 1e3
+
+    # Per-kernel device times (CUDA events on the library's stream).
+    names = ["q8_x", "qkv", "q8_o", "o", "gateup", "down"]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    acc = {n: 0.0 for n in names}
+    reps = max(3, args.steps)
+    with torch.cuda.stream(stream):
+        for i in range(reps):
+            ps.step(b, M, i, ev)
+            ev[6].synchronize()
+            for k, n in enumerate(names):
+                acc[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
+    kt = {n: acc[n] / reps for n in names}
+
+    # Decode: the same set at M = 1.
+    bd = ps.buffers(1)
+    barrier_sync()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            ps.step(bd, 1, i)
+    barrier_sync()
+    dsteps = max(args.steps, 50)
+    td = time_region(torch, stream, lambda i: ps.step(bd, 1, i), dsteps)
+    td = max_over_ranks(td)
+    acc_d = {n: 0.0 for n in names}
+    with torch.cuda.stream(stream):
+        for i in range(dsteps):
+            ps.step(bd, 1, i, ev)
+            ev[6].synchronize()
+            for k, n in enumerate(names):
+                acc_d[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
+    kd = {n: acc_d[n] / dsteps for n in names}
+
+    # End to end through the C ABI with pinned host buffers.
+    hx = torch.randn(M, H).pin_memory()
+    ho = torch.randn(M, H).pin_memory()
+    out_q = torch.empty(M, QKV_N).pin_memory()
+    out_o = torch.empty(M, H).pin_memory()
+    out_d = torch.empty(M, H).pin_memory()
+
+    def e2e_step(i):
+        b["x"].copy_(hx, non_blocking=True)
+        b["oin"].copy_(ho, non_blocking=True)
+        ps.step(b, M, i)
+        out_q.copy_(b["qkv"], non_blocking=True)
+        out_o.copy_(b["yo"], non_blocking=True)
+        out_d.copy_(b["yd"], non_blocking=True)
+    barrier_sync()
+    te = time_region(torch, stream, e2e_step, args.steps)
+    te = max_over_ranks(te)
+    h2d = 2 * M * H * 4
+    d2h = M * (QKV_N + 2 * H) * 4
+
+    pk = peaks()
+    wb = weight_bytes(1)
+    dom_d = max(kd, key=lambda n: kd[n] if n in wb else -1)
+    fl = flops(M)
+    dom_p = max((n for n in fl), key=lambda n: kt[n])
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8",
+        "data": "synthetic (seeded Q4_0 N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": "BASELINE config 1: Qwen2.5-1.5B projection set (QKV 2048x1536"
+                               " +bias, o 1536^2, gate+up 2x8960x1536 +SiLU*mul+Q8, down "
+                               "1536x8960), Q4_0 x Q8_0",
+                   "prefill_tokens_per_step": M, "parallelism": f"replicas x{world}",
+                   "l2": "10 weight copies (263 MB > 2x L2) rotated per step"},
+        "decode": {"us_per_token": round(td / dsteps * 1e6, 3),
+                   "kernel_us": {n: round(kd[n] * 1e6, 3) for n in names},
+                   "roofline": {"bound": "hbm", "kernel": dom_d,
+                                "achieved": round(wb[dom_d] / kd[dom_d] / 1e9, 1),
+                                "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                "frac": round(wb[dom_d] / kd[dom_d] / 1e9 / pk["hbm_gbs"], 4),
+                                "peak_src": pk["src"]}},
+        "prefill_kernel_ms": {n: round(kt[n] * 1e3, 4) for n in names},
+        "roofline": {"bound": "tensor", "kernel": dom_p,
+                     "achieved": round(fl[dom_p] / kt[dom_p] / 1e12, 2),
+                     "peak": INT8_SPEC_TOPS, "unit": "TOP/s",
+                     "frac": round(fl[dom_p] / kt[dom_p] / 1e12 / INT8_SPEC_TOPS, 4),
+                     "peak_src": "spec (dense int8; MEASURED_PEAKS.json has no int8 figure)",
+                     "traffic": None},
+        "e2e": {"value": round(world * M * args.steps / te, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    ctx.close()
+    return result
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own functions on the host cores
+# ---------------------------------------------------------------------------
+def cpu_impl():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    if os.path.exists(oracle.LIB_REF):
+        r = oracle.Reference()
+        return "reference", r.lib.ref_matvec_q4q8, r.lib.ref_quantize_q8
+    o = oracle.Oracle()
+    return "port", o.lib.oc_matvec_q4q8, o.lib.oc_quantize_q8
+
+
+def cpu_projection_tokens(seconds: float, threads: int):
+    """Tokens/s of the projection set on the host: each token runs quantize_q8 +
+    matvec_q4q8 for QKV/o/gate/up/down (+SiLU*mul), rows split over threads."""
+    import ctypes as C
+    from concurrent.futures import ThreadPoolExecutor
+    from sib200 import synth
+    kind, matvec, quant = cpu_impl()
+    rng = np.random.default_rng(1)
+    W = {"qkv": synth.random_q4(rng, QKV_N, H), "o": synth.random_q4(rng, H, H),
+         "gate": synth.random_q4(rng, I, H), "up": synth.random_q4(rng, I, H),
+         "down": synth.random_q4(rng, H, I)}
+    bias = rng.normal(0, 0.02, QKV_N).astype(np.float32)
+    pool = ThreadPoolExecutor(threads)
+
+    def mv(w, q8, K, N, b, out):
+        rows = -(-N // threads)
+
+        def part(t):  # row slices: the same arithmetic per row, so results are unchanged
+            r0, r1 = t * rows, min(N, (t + 1) * rows)
+            if r0 < r1:
+                matvec(w[r0:r1], q8, K, r1 - r0,
+                       None if b is None else b[r0:r1].ctypes.data_as(C.c_void_p), out[r0:r1])
+        list(pool.map(part, range(threads)))
+
+    def token(x, o_in):
+        q8 = np.zeros(H // 32 * 34, np.uint8)
+        quant(x, q8, H)
+        qkv = np.zeros(QKV_N, np.float32)
+        mv(W["qkv"], q8, H, QKV_N, bias, qkv)
+        oq = np.zeros(H // 32 * 34, np.uint8)
+        quant(o_in, oq, H)
+        yo = np.zeros(H, np.float32)
+        mv(W["o"], oq, H, H, None, yo)
+        g = np.zeros(I, np.float32)
+        u = np.zeros(I, np.float32)
+        mv(W["gate"], q8, H, I, None, g)
+        mv(W["up"], q8, H, I, None, u)
+        a = ((g / (np.float32(1) + np.exp(-g))) * u).astype(np.float32)
+        aq = np.zeros(I // 32 * 34, np.uint8)
+        quant(a, aq, I)
+        yd = np.zeros(H, np.float32)
+        mv(W["down"], aq, I, H, None, yd)
+
+    x = rng.standard_normal((64, H)).astype(np.float32)
+    token(x[0], x[1])  # warm
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        token(x[n % 64], x[(n + 1) % 64])
+        n += 1
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return kind, n, dt
+
+
+def cpu_baseline(seconds):
+    threads = len(os.sched_getaffinity(0))
+    kind, n, dt = cpu_projection_tokens(seconds, threads)
+    return {"value": round(n / dt, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": f"{n} tokens of the config-1 projection set (quantize_q8 + matvec_q4q8 "
+                      f"x5 + SiLU*mul), rows split over {threads} threads, {dt:.1f} s"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    per_step = []
+    threads = len(os.sched_getaffinity(0))
+    kind = None
+    for i in range(args.warmup + args.steps):
+        kind, n, dt = cpu_projection_tokens(args.cpu_seconds / max(1, args.steps), threads)
+        if i >= args.warmup:
+            per_step.append((n, dt))
+    toks = sum(n for n, _ in per_step)
+    secs = sum(dt for _, dt in per_step)
+    v = toks / secs
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1 projection set, per-token (the reference "
+                                   "has no batched prefill on CPU)", "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": threads,
+                             "kind": kind, "sample": f"{toks} tokens over {args.steps} steps"},
+            "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+        tdist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

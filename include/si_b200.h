@@ -1,0 +1,307 @@
+/*
+ * si_b200.h -- C ABI of libsi_b200.so, the B200 (sm_100a) implementation of the
+ * keyvan-dadash/simple-inference Qwen decoder-layer hot path.
+ *
+ * Two layers of entry points:
+ *
+ *  1. The handle API (si_*): a context owns one CUDA device and stream; weights
+ *     are uploaded once as device matrices in the SoA Q4_0 layout; KV caches live
+ *     on the device.  Everything the benchmarks and the reference-shaped calls do
+ *     goes through these functions.  Plain pointers and sizes only.
+ *
+ *  2. Reference-shaped entry points with the reference's names and argument
+ *     lists (quantize_q8, matvec_q4q8, rmsnorm, rope, attention_compute,
+ *     run_layer, fused_column_matvec, run_layer_fused, pf_run_batch, ...), so a
+ *     translation unit written against the reference's headers builds against
+ *     this header instead.  They take HOST pointers, run on the GPU of an
+ *     implicit per-process context, and copy results back.  The functions whose
+ *     reference versions read compile-time dims (HIDDEN, QHEADS, ...) are static
+ *     inline wrappers over dims-parametrised si_ref_* symbols; the dims macros
+ *     default to the reference's defines.h values and can be overridden.
+ *
+ * Errors: every si_* function returns si_status.  The reference-shaped wrappers
+ * keep the reference's contract (qwen_one_layer.c:26-28): on error they print
+ * "error: <message>" to stderr and exit(1).  There is no CPU fallback: without
+ * an sm_100 device every entry point fails with SI_ERR_NO_DEVICE.
+ */
+#ifndef SI_B200_H
+#define SI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define SI_API
+#else
+#define SI_API __attribute__((visibility("default")))
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Reference compile-time configuration (defines.h:16-25); overridable.      */
+/* ------------------------------------------------------------------------ */
+#ifndef HIDDEN
+#define HIDDEN 1536
+#endif
+#ifndef QHEADS
+#define QHEADS 12
+#endif
+#ifndef KVHEADS
+#define KVHEADS 2
+#endif
+#ifndef HDIM
+#define HDIM 128
+#endif
+#ifndef KVDIM
+#define KVDIM (KVHEADS * HDIM)
+#endif
+#ifndef QK
+#define QK 32
+#endif
+#ifndef Q4_BYTES
+#define Q4_BYTES 18
+#endif
+#ifndef Q8_BYTES
+#define Q8_BYTES 34
+#endif
+#ifndef ROPE_BASE
+#define ROPE_BASE 1000000.0f
+#endif
+#ifndef RMS_EPS
+#define RMS_EPS 1e-6f
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status                                                                    */
+/* ------------------------------------------------------------------------ */
+typedef enum {
+    SI_OK = 0,
+    SI_ERR_INVALID = 1,    /* bad argument, shape or handle */
+    SI_ERR_CUDA = 2,       /* CUDA runtime error */
+    SI_ERR_OOM = 3,        /* device allocation failed */
+    SI_ERR_NO_DEVICE = 4,  /* no sm_100 device / CUDA unavailable */
+    SI_ERR_DEVICE = 5,     /* a kernel set the device error word */
+    SI_ERR_TIMEOUT = 6,    /* a bounded device wait expired */
+    SI_ERR_IO = 7,         /* file missing or of the wrong size */
+    SI_ERR_UNSUPPORTED = 8 /* configuration not implemented */
+} si_status;
+
+SI_API const char *si_status_str(si_status s);
+
+/* ------------------------------------------------------------------------ */
+/* Reference types, byte-identical (defines.h:27-37, attention_kernels.h:24). */
+/* ------------------------------------------------------------------------ */
+#ifndef SI_NO_REFERENCE_TYPES
+typedef struct { uint16_t d; int8_t qs[32]; } block_q8_0;      /* defines.h:27-28 */
+typedef struct {                                                /* defines.h:30-33 */
+    uint8_t *wq, *wk, *wv, *wo;
+    float *norm, *bq, *bk, *bv;
+} layer_t;
+typedef struct {                                                /* defines.h:35-37 */
+    float rms, q8_input, q_proj, k_proj, v_proj, rope_cache, attention, q8_output, out_proj;
+} phase_t;
+typedef enum { ATTENTION_STANDARD = 0, ATTENTION_FLASH = 1 } attention_method_t;
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Handle API                                                                */
+/* ------------------------------------------------------------------------ */
+typedef struct si_ctx si_ctx;
+typedef struct si_matrix si_matrix;
+typedef struct si_layer si_layer;
+typedef struct si_kv si_kv;
+
+typedef struct {
+    int hidden, n_q_heads, n_kv_heads, head_dim, intermediate; /* intermediate 0 = no MLP */
+    float rope_theta, rms_eps;
+} si_dims;
+
+/* Host-side layer description.  Q4_0 matrices are GGUF row-major blocks
+ * ([rows][cols/32] x 18 B: fp16 d + 16 nibble bytes); optional vectors may be
+ * NULL (identity norm, zero bias) as in qwen_one_layer.c:216-219. */
+typedef struct {
+    const uint8_t *wq, *wk, *wv, *wo;       /* [Hq*D][H], [Hkv*D][H] x2, [H][Hq*D] */
+    const uint8_t *w_gate, *w_up, *w_down;  /* [I][H], [I][H], [H][I]; NULL if intermediate==0 */
+    const float *norm, *bq, *bk, *bv, *norm2;
+} si_layer_host;
+
+/* Layer run modes. */
+#define SI_LAYER_ATTN 0  /* run_layer semantics: y = W_O(attn(rmsnorm(x))), no residual */
+#define SI_LAYER_FULL 1  /* decoder layer: h = x + attn; y = h + down(silu(gate)*up) */
+
+/* Context: one device, one stream, RoPE cos/sin tables for positions
+ * [0, max_positions) computed on the host with the reference's expressions. */
+SI_API si_status si_ctx_create(int device, int max_positions, float rope_theta, int head_dim,
+                               si_ctx **out);
+SI_API void si_ctx_destroy(si_ctx *ctx);
+SI_API si_status si_ctx_synchronize(si_ctx *ctx);
+/* Synchronises, then returns and clears the device error word. */
+SI_API si_status si_ctx_status(si_ctx *ctx);
+SI_API void *si_ctx_stream(si_ctx *ctx); /* the cudaStream_t all work is queued on */
+SI_API const char *si_last_error(void);  /* message of the last failing call on this thread */
+
+/* Weight matrices.  Upload GGUF Q4_0 rows and repack on the device into the
+ * row-tile SoA layout (see si_matrix_layout). rows % 32 == 0, cols % 32 == 0. */
+SI_API si_status si_matrix_upload(si_ctx *ctx, const uint8_t *gguf_host, int rows, int cols,
+                                  si_matrix **out);
+SI_API si_status si_matrix_upload_dev(si_ctx *ctx, const uint8_t *gguf_dev, int rows, int cols,
+                                      si_matrix **out);
+SI_API void si_matrix_free(si_matrix *m);
+SI_API int si_matrix_rows(const si_matrix *m);
+SI_API int si_matrix_cols(const si_matrix *m);
+/* Device pointers of the layout: nibbles [rows/32][cols/32][32][16] bytes
+ * (GGUF nibble order, each byte XOR 0x88) and scales [rows/32][cols/32][32] fp16. */
+SI_API si_status si_matrix_layout(const si_matrix *m, void **nib_dev, void **scale_dev);
+/* Fill a matrix with seeded synthetic Q4_0 weights on the device: element
+ * values ~N(0, std) from a counter hash of (seed, row, col), quantised with the
+ * GGUF rule.  Used for large benchmark configurations. */
+SI_API si_status si_matrix_synth(si_ctx *ctx, int rows, int cols, uint64_t seed, float std,
+                                 si_matrix **out);
+/* Copy a matrix back as GGUF row-major Q4_0 bytes (host). */
+SI_API si_status si_matrix_download(si_ctx *ctx, const si_matrix *m, uint8_t *gguf_host);
+
+/* Activations on the device: Q8 tensors are two arrays, qs int8 [M][K] and
+ * d fp16 [M][K/32] (block_q8_0 split for coalescing); the reference's 34-byte
+ * blocks are produced by si_q8_to_blocks. */
+SI_API si_status si_q8_quantize_dev(si_ctx *ctx, const float *x_dev, int M, int K,
+                                    int8_t *qs_dev, uint16_t *d_dev);
+SI_API si_status si_q8_to_blocks_dev(si_ctx *ctx, const int8_t *qs_dev, const uint16_t *d_dev,
+                                     int M, int K, block_q8_0 *blocks_dev);
+SI_API si_status si_q8_from_blocks_dev(si_ctx *ctx, const block_q8_0 *blocks_dev, int M, int K,
+                                       int8_t *qs_dev, uint16_t *d_dev);
+/* out[m][n] = bias[n] + sum_b ((float)isum * dw) * dx, blocks in order
+ * (qwen_one_layer.c:148-162); picks the GEMV or the tensor-core GEMM by M. */
+SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
+                               const uint16_t *d_dev, int M, const float *bias_dev,
+                               float *out_dev);
+/* Force a kernel: 0 = CUDA-core GEMV, 1 = tcgen05 GEMM. */
+SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
+                                      const uint16_t *d_dev, int M, const float *bias_dev,
+                                      float *out_dev, int kernel);
+/* Per-(row, block) int32 partial sums [M][rows][cols/32] (parity checks). */
+SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
+                                    int M, int32_t *isum_dev);
+/* SwiGLU pair: act = silu(gate@x) * (up@x), quantised to Q8 in the epilogue. */
+SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate, const si_matrix *up,
+                                  const int8_t *qs_dev, const uint16_t *d_dev, int M,
+                                  int8_t *act_qs_dev, uint16_t *act_d_dev, float *act_f32_dev);
+/* RMSNorm over rows of x [M][n] (qwen_one_layer.c:164-169) with optional fp32
+ * output and fused Q8 output. */
+SI_API si_status si_rmsnorm_q8_dev(si_ctx *ctx, const float *x_dev, const float *w_dev, int M,
+                                   int n, float eps, float *out_dev, int8_t *qs_dev,
+                                   uint16_t *d_dev);
+
+/* Layers and KV caches. */
+SI_API si_status si_layer_upload(si_ctx *ctx, const si_dims *dims, const si_layer_host *host,
+                                 si_layer **out);
+/* Synthetic layer generated on the device (seeded); norms 1+N(0,0.02), biases N(0,0.02). */
+SI_API si_status si_layer_synth(si_ctx *ctx, const si_dims *dims, uint64_t seed, si_layer **out);
+SI_API void si_layer_free(si_layer *l);
+SI_API si_status si_layer_matrix(si_layer *l, int which, si_matrix **out); /* 0 qkv,1 o,2 gate,3 up,4 down */
+
+/* KV cache [batch][max_ctx][Hkv][D], fp16 (kv_f32=0, the reference's format,
+ * attention_kernels.h:43-44) or fp32. */
+SI_API si_status si_kv_create(si_ctx *ctx, const si_dims *dims, int batch, int max_ctx,
+                              int kv_f32, si_kv **out);
+SI_API void si_kv_free(si_kv *kv);
+SI_API si_status si_kv_write(si_ctx *ctx, si_kv *kv, int seq, int pos0, int npos,
+                             const void *k_host, const void *v_host);
+SI_API si_status si_kv_read(si_ctx *ctx, si_kv *kv, int seq, int pos0, int npos, void *k_host,
+                            void *v_host);
+SI_API si_status si_kv_fill_synth(si_ctx *ctx, si_kv *kv, uint64_t seed, float std, int npos);
+SI_API void *si_kv_device_ptr(si_kv *kv, int which); /* 0 = K, 1 = V */
+
+/* Optional intermediate captures of a decode step (device or host pointers as
+ * the calling function states; NULL = off). */
+typedef struct {
+    float *attn;        /* [B][Hq*D] attention output before W_O */
+    block_q8_0 *attn_q8;/* [B][Hq*D/32] quantised attention output */
+    float *qkv;         /* [B][Hq*D + 2*Hkv*D] projections before RoPE */
+} si_captures;
+
+/* One decode step for a batch: sequence b appends its token at slot
+ * ctx_lens[b]-1 and attends over [0, ctx_lens[b]).  x and y are [B][H].
+ * _dev variants take device pointers (ctx_lens stays a host array). */
+SI_API si_status si_decode_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x_host,
+                                int batch, const int *ctx_lens, float *y_host, int mode,
+                                const si_captures *cap_host);
+SI_API si_status si_decode_step_dev(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x_dev,
+                                    int batch, const int *ctx_lens, float *y_dev, int mode,
+                                    const si_captures *cap_dev);
+/* Causal prefill of ntok tokens of sequence seq at positions [prefix,
+ * prefix+ntok): token t attends over [0, prefix+t+1) (prefill_weight_stationary.h:173-186). */
+SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const float *x_host,
+                            int ntok, int prefix, float *y_host, int mode);
+SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const float *x_dev,
+                                int ntok, int prefix, float *y_dev, int mode);
+
+/* Decode attention alone (parity): q [B][Hq][D] after RoPE. */
+SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *dims,
+                                         const float *q_dev, int batch, const int *ctx_lens,
+                                         float *out_dev);
+
+/* ------------------------------------------------------------------------ */
+/* Reference-shaped entry points (host pointers, implicit context).          */
+/* ------------------------------------------------------------------------ */
+
+/* qwen_one_layer.c:98 quantize_q8 */
+SI_API void quantize_q8(const float *src, block_q8_0 *dst, int count);
+/* qwen_one_layer.c:148 matvec_q4q8.  Device copies of `weights` are cached by
+ * host address and size; call si_forget_host_weights() after changing them. */
+SI_API void matvec_q4q8(const uint8_t *weights, const block_q8_0 *input, int inputs, int outputs,
+                        const float *bias, float *out);
+SI_API void si_forget_host_weights(const void *host_ptr);
+
+/* Dims-parametrised symbols behind the inline wrappers below. */
+SI_API void si_ref_rmsnorm(const float *input, const float *weight, float *out, int n, float eps);
+SI_API void si_ref_rope(float *heads, int nheads, int position, int head_dim, float theta);
+SI_API void si_ref_attention(int method, const float *q, const uint16_t *kc, const uint16_t *vc,
+                             int context, float *out, float *scores, int n_q_heads,
+                             int n_kv_heads, int head_dim);
+SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uint16_t *kc, uint16_t *vc,
+                                int context, float *output, int method, float *scores,
+                                float *attn_copy, block_q8_0 *q8_copy, int hidden, int n_q_heads,
+                                int n_kv_heads, int head_dim, float theta, float eps);
+SI_API layer_t si_ref_load_layer(const char *dir, int hidden, int kvdim);
+SI_API void si_ref_free_layer(layer_t *l);
+
+/* qwen_one_layer.c:164 rmsnorm */
+static inline void rmsnorm(const float *input, const float *weight, float *out) {
+    si_ref_rmsnorm(input, weight, out, HIDDEN, RMS_EPS);
+}
+/* qwen_one_layer.c:172 rope */
+static inline void rope(float *heads, int nheads, int position) {
+    si_ref_rope(heads, nheads, position, HDIM, ROPE_BASE);
+}
+/* attention_kernels.h:166 attention_compute (flash: :80, standard: :33) */
+static inline void attention_compute(attention_method_t method, const float *q,
+                                     const uint16_t *kc, const uint16_t *vc, int context,
+                                     float *out, float *score_workspace) {
+    si_ref_attention((int)method, q, kc, vc, context, out, score_workspace, QHEADS, KVHEADS, HDIM);
+}
+static inline void attention_flash(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                   int context, float *out) {
+    si_ref_attention(1, q, kc, vc, context, out, NULL, QHEADS, KVHEADS, HDIM);
+}
+static inline void attention_standard(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                      int context, float *out, float *scores) {
+    si_ref_attention(0, q, kc, vc, context, out, scores, QHEADS, KVHEADS, HDIM);
+}
+/* qwen_one_layer.c:237 run_layer (phase_t filled from CUDA events) */
+static inline phase_t run_layer(const layer_t *l, const float *x, uint16_t *kc, uint16_t *vc,
+                                int context, float *output, attention_method_t method,
+                                float *scores, float *attn_copy, block_q8_0 *q8_copy) {
+    return si_ref_run_layer(l, x, kc, vc, context, output, (int)method, scores, attn_copy,
+                            q8_copy, HIDDEN, QHEADS, KVHEADS, HDIM, ROPE_BASE, RMS_EPS);
+}
+/* qwen_one_layer.c:210 load_layer / :223 free_layer */
+static inline layer_t load_layer(const char *dir) { return si_ref_load_layer(dir, HIDDEN, KVDIM); }
+static inline void free_layer(layer_t *l) { si_ref_free_layer(l); }
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SI_B200_H */

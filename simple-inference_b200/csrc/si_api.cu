@@ -1,0 +1,1284 @@
+// si_api.cu -- the C ABI of libsi_b200.so (declared in include/si_b200.h).
+//
+// Host orchestration only: argument checks, device memory, stream ordering and
+// the layer schedules.  Every computation is a kernel from the other .cu files;
+// there is no CPU compute path.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/si_b200.h"
+#include "si_kernels.cuh"
+
+// ----------------------------------------------------------------------------
+// errors
+// ----------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+static si_status fail(si_status s, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+#define SI_CUDA(call)                                                                        \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return fail(e_ == cudaErrorMemoryAllocation ? SI_ERR_OOM : SI_ERR_CUDA, "%s: %s (%s:%d)", \
+                  #call, cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+  } while (0)
+
+#define SI_CHECK(cond, ...)                                  \
+  do {                                                       \
+    if (!(cond)) return fail(SI_ERR_INVALID, __VA_ARGS__);   \
+  } while (0)
+
+#define SI_TRY(expr)                  \
+  do {                                \
+    si_status s_ = (expr);            \
+    if (s_ != SI_OK) return s_;       \
+  } while (0)
+
+extern "C" SI_API const char *si_status_str(si_status s) {
+  switch (s) {
+    case SI_OK: return "ok";
+    case SI_ERR_INVALID: return "invalid argument";
+    case SI_ERR_CUDA: return "CUDA error";
+    case SI_ERR_OOM: return "out of device memory";
+    case SI_ERR_NO_DEVICE: return "no sm_100 CUDA device";
+    case SI_ERR_DEVICE: return "device-side error";
+    case SI_ERR_TIMEOUT: return "device wait timed out";
+    case SI_ERR_IO: return "file error";
+    case SI_ERR_UNSUPPORTED: return "unsupported configuration";
+  }
+  return "unknown status";
+}
+
+extern "C" SI_API const char *si_last_error(void) { return g_last_error.c_str(); }
+
+// ----------------------------------------------------------------------------
+// handles
+// ----------------------------------------------------------------------------
+struct DevBuf {
+  void *p = nullptr;
+  size_t bytes = 0;
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  si_status reserve(size_t n) {
+    if (n <= bytes) return SI_OK;
+    release();
+    cudaError_t e = cudaMalloc(&p, n);
+    if (e != cudaSuccess) {
+      p = nullptr;
+      return fail(SI_ERR_OOM, "cudaMalloc(%zu): %s", n, cudaGetErrorString(e));
+    }
+    bytes = n;
+    return SI_OK;
+  }
+};
+
+struct si_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int max_positions = 0;
+  int head_dim = 0;
+  float rope_theta = 0.f;
+  float *cos_tab = nullptr, *sin_tab = nullptr;
+  int *err = nullptr;           // device error word
+  DevBuf work;                  // layer-schedule arena
+  DevBuf idx;                   // per-token index arrays
+  int *pinned_idx = nullptr;    // host staging for idx
+  size_t pinned_idx_n = 0;
+  cudaEvent_t ev[12] = {};
+};
+
+struct si_matrix {
+  si_ctx *ctx = nullptr;
+  int rows = 0, cols = 0;
+  uint8_t *nib = nullptr;
+  uint16_t *scl = nullptr;
+};
+
+struct si_layer {
+  si_ctx *ctx = nullptr;
+  si_dims d{};
+  si_matrix *qkv = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+  float *bias_qkv = nullptr, *norm = nullptr, *norm2 = nullptr;
+};
+
+struct si_kv {
+  si_ctx *ctx = nullptr;
+  si_dims d{};
+  int batch = 0, max_ctx = 0, kv_f32 = 0;
+  void *k = nullptr, *v = nullptr;
+  size_t elem() const { return kv_f32 ? 4 : 2; }
+  size_t row_elems() const { return (size_t)d.n_kv_heads * d.head_dim; }
+  size_t seq_elems() const { return (size_t)max_ctx * row_elems(); }
+};
+
+static si_status set_device(si_ctx *ctx) {
+  SI_CHECK(ctx, "null context");
+  SI_CUDA(cudaSetDevice(ctx->device));
+  return SI_OK;
+}
+
+// ----------------------------------------------------------------------------
+// context
+// ----------------------------------------------------------------------------
+extern "C" SI_API si_status si_ctx_create(int device, int max_positions, float rope_theta,
+                                          int head_dim, si_ctx **out) {
+  SI_CHECK(out, "null output handle");
+  SI_CHECK(max_positions > 0 && max_positions <= (1 << 20), "max_positions out of range");
+  SI_CHECK(head_dim > 0 && head_dim % 2 == 0 && head_dim <= 256, "bad head_dim");
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(SI_ERR_NO_DEVICE, "no CUDA device visible");
+  }
+  SI_CHECK(device >= 0 && device < count, "device %d out of range (%d devices)", device, count);
+  cudaDeviceProp prop;
+  SI_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(SI_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                device, prop.major, prop.minor);
+  SI_CUDA(cudaSetDevice(device));
+  si_ctx *c = new si_ctx();
+  c->device = device;
+  c->max_positions = max_positions;
+  c->head_dim = head_dim;
+  c->rope_theta = rope_theta;
+  si_status st = SI_OK;
+  do {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      st = fail(SI_ERR_CUDA, "cudaStreamCreate failed");
+      break;
+    }
+    // RoPE tables with the reference's expressions (qwen_one_layer.c:176-177),
+    // evaluated by the host libm exactly as the reference evaluates them.
+    const int half = head_dim / 2;
+    std::vector<float> ct((size_t)max_positions * half), stab((size_t)max_positions * half);
+    std::vector<float> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = powf(rope_theta, (float)(2 * i) / head_dim);
+    for (int p = 0; p < max_positions; ++p)
+      for (int i = 0; i < half; ++i) {
+        float a = (float)p / inv[i];
+        ct[(size_t)p * half + i] = cosf(a);
+        stab[(size_t)p * half + i] = sinf(a);
+      }
+    size_t tb = ct.size() * sizeof(float);
+    if (cudaMalloc(&c->cos_tab, tb) != cudaSuccess || cudaMalloc(&c->sin_tab, tb) != cudaSuccess ||
+        cudaMalloc(&c->err, sizeof(int)) != cudaSuccess) {
+      st = fail(SI_ERR_OOM, "context allocation failed");
+      break;
+    }
+    if (cudaMemcpy(c->cos_tab, ct.data(), tb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->sin_tab, stab.data(), tb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess) {
+      st = fail(SI_ERR_CUDA, "context upload failed");
+      break;
+    }
+    for (auto &e : c->ev)
+      if (cudaEventCreate(&e) != cudaSuccess) st = fail(SI_ERR_CUDA, "event create failed");
+  } while (0);
+  if (st != SI_OK) {
+    si_ctx_destroy(c);
+    return st;
+  }
+  *out = c;
+  return SI_OK;
+}
+
+extern "C" SI_API void si_ctx_destroy(si_ctx *c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  cudaFree(c->cos_tab);
+  cudaFree(c->sin_tab);
+  cudaFree(c->err);
+  c->work.release();
+  c->idx.release();
+  if (c->pinned_idx) cudaFreeHost(c->pinned_idx);
+  for (auto &e : c->ev)
+    if (e) cudaEventDestroy(e);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+extern "C" SI_API si_status si_ctx_synchronize(si_ctx *ctx) {
+  SI_TRY(set_device(ctx));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_ctx_status(si_ctx *ctx) {
+  SI_TRY(si_ctx_synchronize(ctx));
+  int code = 0;
+  SI_CUDA(cudaMemcpy(&code, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
+  SI_CUDA(cudaMemset(ctx->err, 0, sizeof(int)));
+  if (code) return fail((si_status)code, "device error word = %d", code);
+  return SI_OK;
+}
+
+extern "C" SI_API void *si_ctx_stream(si_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+// ----------------------------------------------------------------------------
+// matrices
+// ----------------------------------------------------------------------------
+static si_status matrix_alloc(si_ctx *ctx, int rows, int cols, si_matrix **out) {
+  SI_CHECK(out, "null output handle");
+  SI_CHECK(rows > 0 && cols > 0 && rows % 32 == 0 && cols % 32 == 0,
+           "matrix %dx%d: rows and cols must be positive multiples of 32", rows, cols);
+  si_matrix *m = new si_matrix();
+  m->ctx = ctx;
+  m->rows = rows;
+  m->cols = cols;
+  size_t nb = (size_t)rows * (cols / 32);
+  if (cudaMalloc(&m->nib, nb * 16) != cudaSuccess || cudaMalloc(&m->scl, nb * 2) != cudaSuccess) {
+    si_matrix_free(m);
+    return fail(SI_ERR_OOM, "matrix allocation %dx%d failed", rows, cols);
+  }
+  *out = m;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_matrix_upload_dev(si_ctx *ctx, const uint8_t *gguf_dev, int rows,
+                                                 int cols, si_matrix **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(gguf_dev, "null weights");
+  SI_TRY(matrix_alloc(ctx, rows, cols, out));
+  SI_CUDA(si::launch_repack_gguf(gguf_dev, rows, cols / 32, (*out)->nib, (*out)->scl,
+                                 ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_matrix_upload(si_ctx *ctx, const uint8_t *gguf_host, int rows,
+                                             int cols, si_matrix **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(gguf_host && out, "null argument");
+  SI_CHECK(rows > 0 && cols > 0 && rows % 32 == 0 && cols % 32 == 0, "bad matrix shape %dx%d",
+           rows, cols);
+  size_t bytes = (size_t)rows * (cols / 32) * 18;
+  uint8_t *tmp = nullptr;
+  SI_CUDA(cudaMalloc(&tmp, bytes));
+  si_status st = SI_OK;
+  if (cudaMemcpyAsync(tmp, gguf_host, bytes, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+    st = fail(SI_ERR_CUDA, "weight upload failed");
+  if (st == SI_OK) st = si_matrix_upload_dev(ctx, tmp, rows, cols, out);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(tmp);
+  return st;
+}
+
+extern "C" SI_API si_status si_matrix_synth(si_ctx *ctx, int rows, int cols, uint64_t seed,
+                                            float stdv, si_matrix **out) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(matrix_alloc(ctx, rows, cols, out));
+  SI_CUDA(si::launch_synth_q4(rows, cols / 32, seed, stdv, (*out)->nib, (*out)->scl,
+                              ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API void si_matrix_free(si_matrix *m) {
+  if (!m) return;
+  if (m->ctx) cudaSetDevice(m->ctx->device);
+  cudaFree(m->nib);
+  cudaFree(m->scl);
+  delete m;
+}
+
+extern "C" SI_API int si_matrix_rows(const si_matrix *m) { return m ? m->rows : 0; }
+extern "C" SI_API int si_matrix_cols(const si_matrix *m) { return m ? m->cols : 0; }
+
+extern "C" SI_API si_status si_matrix_layout(const si_matrix *m, void **nib_dev, void **scale_dev) {
+  SI_CHECK(m, "null matrix");
+  if (nib_dev) *nib_dev = m->nib;
+  if (scale_dev) *scale_dev = m->scl;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_matrix_download(si_ctx *ctx, const si_matrix *m,
+                                               uint8_t *gguf_host) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(m && gguf_host, "null argument");
+  size_t bytes = (size_t)m->rows * (m->cols / 32) * 18;
+  uint8_t *tmp = nullptr;
+  SI_CUDA(cudaMalloc(&tmp, bytes));
+  cudaError_t e = si::launch_unpack_to_gguf(m->nib, m->scl, m->rows, m->cols / 32, tmp,
+                                            ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(gguf_host, tmp, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(tmp);
+  SI_CUDA(e);
+  return SI_OK;
+}
+
+// ----------------------------------------------------------------------------
+// activations and products on device pointers
+// ----------------------------------------------------------------------------
+extern "C" SI_API si_status si_q8_quantize_dev(si_ctx *ctx, const float *x, int M, int K,
+                                               int8_t *qs, uint16_t *d) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(M >= 0 && K > 0 && K % 32 == 0, "Q8 quantization length must be multiple of 32");
+  SI_CHECK(x && qs && d, "null pointer");
+  SI_CUDA(si::launch_q8_quantize(x, M, K, qs, d, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_q8_to_blocks_dev(si_ctx *ctx, const int8_t *qs, const uint16_t *d,
+                                                int M, int K, block_q8_0 *blocks) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(K % 32 == 0 && qs && d && blocks, "bad argument");
+  SI_CUDA(si::launch_q8_to_blocks(qs, d, M, K, reinterpret_cast<uint8_t *>(blocks),
+                                  ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_q8_from_blocks_dev(si_ctx *ctx, const block_q8_0 *blocks, int M,
+                                                  int K, int8_t *qs, uint16_t *d) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(K % 32 == 0 && qs && d && blocks, "bad argument");
+  SI_CUDA(si::launch_q8_from_blocks(reinterpret_cast<const uint8_t *>(blocks), M, K, qs, d,
+                                    ctx->stream));
+  return SI_OK;
+}
+
+static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16_t *d, int M) {
+  si::GemvArgs a{};
+  a.nib = w->nib;
+  a.scl = w->scl;
+  a.N = w->rows;
+  a.K = w->cols;
+  a.xq = qs;
+  a.xd = d;
+  a.M = M;
+  return a;
+}
+
+static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
+                        int M, const float *bias, const float *resid, float *out, int kernel) {
+  SI_CHECK(w && qs && d && out, "null pointer");
+  SI_CHECK(M >= 0, "negative token count");
+  si::GemvArgs a = gemv_args(w, qs, d, M);
+  a.bias = bias;
+  a.resid = resid;
+  a.out = out;
+  if (kernel < 0) kernel = (M > 8 && si::gemm_tc_supported(w->rows, w->cols, M)) ? 1 : 0;
+  if (kernel == 1) {
+    if (!si::gemm_tc_supported(w->rows, w->cols, M))
+      return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
+                  w->cols, M);
+    SI_CUDA(si::launch_gemm_tc(a, false, ctx->stream));
+  } else {
+    SI_CUDA(si::launch_gemv(a, false, ctx->stream));
+  }
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs,
+                                          const uint16_t *d, int M, const float *bias,
+                                          float *out) {
+  SI_TRY(set_device(ctx));
+  return matmul(ctx, w, qs, d, M, bias, nullptr, out, -1);
+}
+
+extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w,
+                                                 const int8_t *qs, const uint16_t *d, int M,
+                                                 const float *bias, float *out, int kernel) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(kernel == 0 || kernel == 1, "kernel must be 0 (GEMV) or 1 (tcgen05 GEMM)");
+  return matmul(ctx, w, qs, d, M, bias, nullptr, out, kernel);
+}
+
+extern "C" SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs,
+                                               int M, int32_t *isum) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(w && qs && isum, "null pointer");
+  // The GEMV writes the exact per-block sums as a side output; its float output
+  // and scales are irrelevant here, so point them at scratch.
+  size_t need = (size_t)M * w->rows * sizeof(float) + (size_t)M * (w->cols / 32) * 2;
+  SI_TRY(ctx->work.reserve(need));
+  float *out = static_cast<float *>(ctx->work.p);
+  uint16_t *d = reinterpret_cast<uint16_t *>(out + (size_t)M * w->rows);
+  SI_CUDA(cudaMemsetAsync(d, 0, (size_t)M * (w->cols / 32) * 2, ctx->stream));
+  si::GemvArgs a = gemv_args(w, qs, d, M);
+  a.out = out;
+  a.isum_out = isum;
+  SI_CUDA(si::launch_gemv(a, false, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate,
+                                             const si_matrix *up, const int8_t *qs,
+                                             const uint16_t *d, int M, int8_t *act_qs,
+                                             uint16_t *act_d, float *act_f32) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(gate && up && qs && d && act_qs && act_d, "null pointer");
+  SI_CHECK(gate->rows == up->rows && gate->cols == up->cols, "gate/up shape mismatch");
+  si::GemvArgs a = gemv_args(gate, qs, d, M);
+  a.nib2 = up->nib;
+  a.scl2 = up->scl;
+  a.out = act_f32;
+  a.act_qs = act_qs;
+  a.act_d = act_d;
+  if (M > 8 && si::gemm_tc_supported(gate->rows, gate->cols, M)) {
+    SI_CUDA(si::launch_gemm_tc(a, true, ctx->stream));
+  } else {
+    SI_CUDA(si::launch_gemv(a, true, ctx->stream));
+  }
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_rmsnorm_q8_dev(si_ctx *ctx, const float *x, const float *w, int M,
+                                              int n, float eps, float *out, int8_t *qs,
+                                              uint16_t *d) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(x && n > 0 && n % 32 == 0 && M >= 0, "bad rmsnorm arguments");
+  SI_CHECK((qs == nullptr) == (d == nullptr), "qs and d must be given together");
+  SI_CUDA(si::launch_rmsnorm_q8(x, w, M, n, eps, out, qs, d, ctx->stream));
+  return SI_OK;
+}
+
+// ----------------------------------------------------------------------------
+// layers and KV caches
+// ----------------------------------------------------------------------------
+static si_status check_dims(const si_dims *d) {
+  SI_CHECK(d, "null dims");
+  SI_CHECK(d->hidden > 0 && d->hidden % 32 == 0, "hidden must be a multiple of 32");
+  SI_CHECK(d->n_kv_heads > 0 && d->n_q_heads % d->n_kv_heads == 0, "bad head counts");
+  SI_CHECK(d->n_q_heads / d->n_kv_heads <= 8, "GQA group size above 8 is not supported");
+  SI_CHECK(d->head_dim == 64 || d->head_dim == 128, "head_dim must be 64 or 128");
+  SI_CHECK(d->intermediate >= 0 && d->intermediate % 32 == 0, "bad intermediate size");
+  SI_CHECK(((size_t)d->n_kv_heads * d->head_dim) % 32 == 0, "KV width must be a multiple of 32");
+  return SI_OK;
+}
+
+static si_status upload_f32(si_ctx *ctx, const float *host, size_t n, float **out) {
+  *out = nullptr;
+  if (!host) return SI_OK;
+  SI_CUDA(cudaMalloc(out, n * sizeof(float)));
+  SI_CUDA(cudaMemcpyAsync(*out, host, n * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API void si_layer_free(si_layer *l) {
+  if (!l) return;
+  if (l->ctx) cudaSetDevice(l->ctx->device);
+  si_matrix_free(l->qkv);
+  si_matrix_free(l->o);
+  si_matrix_free(l->gate);
+  si_matrix_free(l->up);
+  si_matrix_free(l->down);
+  cudaFree(l->bias_qkv);
+  cudaFree(l->norm);
+  cudaFree(l->norm2);
+  delete l;
+}
+
+extern "C" SI_API si_status si_layer_upload(si_ctx *ctx, const si_dims *d, const si_layer_host *h,
+                                            si_layer **out) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(check_dims(d));
+  SI_CHECK(h && out && h->wq && h->wk && h->wv && h->wo, "missing attention weights");
+  if (d->intermediate > 0) SI_CHECK(h->w_gate && h->w_up && h->w_down, "missing MLP weights");
+  const int H = d->hidden, QD = d->n_q_heads * d->head_dim, KVD = d->n_kv_heads * d->head_dim;
+  si_layer *l = new si_layer();
+  l->ctx = ctx;
+  l->d = *d;
+  si_status st = SI_OK;
+  do {
+    // Fused QKV: rows [Q | K | V] so one launch streams all three.
+    size_t qb = (size_t)QD * (H / 32) * 18, kb = (size_t)KVD * (H / 32) * 18;
+    std::vector<uint8_t> cat(qb + 2 * kb);
+    memcpy(cat.data(), h->wq, qb);
+    memcpy(cat.data() + qb, h->wk, kb);
+    memcpy(cat.data() + qb + kb, h->wv, kb);
+    if ((st = si_matrix_upload(ctx, cat.data(), QD + 2 * KVD, H, &l->qkv)) != SI_OK) break;
+    if ((st = si_matrix_upload(ctx, h->wo, H, QD, &l->o)) != SI_OK) break;
+    if (h->bq || h->bk || h->bv) {
+      std::vector<float> b((size_t)QD + 2 * KVD, 0.0f);
+      if (h->bq) memcpy(b.data(), h->bq, (size_t)QD * 4);
+      if (h->bk) memcpy(b.data() + QD, h->bk, (size_t)KVD * 4);
+      if (h->bv) memcpy(b.data() + QD + KVD, h->bv, (size_t)KVD * 4);
+      if ((st = upload_f32(ctx, b.data(), b.size(), &l->bias_qkv)) != SI_OK) break;
+      if ((st = si_ctx_synchronize(ctx)) != SI_OK) break;
+    }
+    if ((st = upload_f32(ctx, h->norm, H, &l->norm)) != SI_OK) break;
+    if (d->intermediate > 0) {
+      const int I = d->intermediate;
+      if ((st = si_matrix_upload(ctx, h->w_gate, I, H, &l->gate)) != SI_OK) break;
+      if ((st = si_matrix_upload(ctx, h->w_up, I, H, &l->up)) != SI_OK) break;
+      if ((st = si_matrix_upload(ctx, h->w_down, H, I, &l->down)) != SI_OK) break;
+      if ((st = upload_f32(ctx, h->norm2, H, &l->norm2)) != SI_OK) break;
+    }
+    st = si_ctx_synchronize(ctx);
+  } while (0);
+  if (st != SI_OK) {
+    si_layer_free(l);
+    return st;
+  }
+  *out = l;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_layer_synth(si_ctx *ctx, const si_dims *d, uint64_t seed,
+                                           si_layer **out) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(check_dims(d));
+  SI_CHECK(out, "null output handle");
+  const int H = d->hidden, QD = d->n_q_heads * d->head_dim, KVD = d->n_kv_heads * d->head_dim;
+  si_layer *l = new si_layer();
+  l->ctx = ctx;
+  l->d = *d;
+  si_status st = SI_OK;
+  const float wstd = 0.02f;
+  do {
+    if ((st = si_matrix_synth(ctx, QD + 2 * KVD, H, seed * 16 + 1, wstd, &l->qkv)) != SI_OK) break;
+    if ((st = si_matrix_synth(ctx, H, QD, seed * 16 + 2, wstd, &l->o)) != SI_OK) break;
+    size_t nb = (size_t)QD + 2 * KVD;
+    if (cudaMalloc(&l->bias_qkv, nb * 4) != cudaSuccess || cudaMalloc(&l->norm, (size_t)H * 4)) {
+      st = fail(SI_ERR_OOM, "layer vectors");
+      break;
+    }
+    if (si::launch_synth_f32(l->bias_qkv, nb, seed * 16 + 3, 0.0f, 0.02f, ctx->stream) ||
+        si::launch_synth_f32(l->norm, H, seed * 16 + 4, 1.0f, 0.02f, ctx->stream)) {
+      st = fail(SI_ERR_CUDA, "synth launch");
+      break;
+    }
+    if (d->intermediate > 0) {
+      const int I = d->intermediate;
+      if ((st = si_matrix_synth(ctx, I, H, seed * 16 + 5, wstd, &l->gate)) != SI_OK) break;
+      if ((st = si_matrix_synth(ctx, I, H, seed * 16 + 6, wstd, &l->up)) != SI_OK) break;
+      if ((st = si_matrix_synth(ctx, H, I, seed * 16 + 7, wstd, &l->down)) != SI_OK) break;
+      if (cudaMalloc(&l->norm2, (size_t)H * 4) != cudaSuccess ||
+          si::launch_synth_f32(l->norm2, H, seed * 16 + 8, 1.0f, 0.02f, ctx->stream)) {
+        st = fail(SI_ERR_CUDA, "norm2");
+        break;
+      }
+    }
+    st = si_ctx_synchronize(ctx);
+  } while (0);
+  if (st != SI_OK) {
+    si_layer_free(l);
+    return st;
+  }
+  *out = l;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_layer_matrix(si_layer *l, int which, si_matrix **out) {
+  SI_CHECK(l && out, "null argument");
+  si_matrix *m[5] = {l->qkv, l->o, l->gate, l->up, l->down};
+  SI_CHECK(which >= 0 && which < 5, "matrix index out of range");
+  *out = m[which];
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_kv_create(si_ctx *ctx, const si_dims *d, int batch, int max_ctx,
+                                         int kv_f32, si_kv **out) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(check_dims(d));
+  SI_CHECK(out && batch > 0 && max_ctx > 0, "bad KV cache arguments");
+  si_kv *kv = new si_kv();
+  kv->ctx = ctx;
+  kv->d = *d;
+  kv->batch = batch;
+  kv->max_ctx = max_ctx;
+  kv->kv_f32 = kv_f32 ? 1 : 0;
+  size_t bytes = (size_t)batch * kv->seq_elems() * kv->elem();
+  if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
+    si_kv_free(kv);
+    return fail(SI_ERR_OOM, "KV cache of %zu bytes x2", bytes);
+  }
+  if (cudaMemsetAsync(kv->k, 0, bytes, ctx->stream) != cudaSuccess ||
+      cudaMemsetAsync(kv->v, 0, bytes, ctx->stream) != cudaSuccess) {
+    si_kv_free(kv);
+    return fail(SI_ERR_CUDA, "KV memset");
+  }
+  *out = kv;
+  return SI_OK;
+}
+
+extern "C" SI_API void si_kv_free(si_kv *kv) {
+  if (!kv) return;
+  if (kv->ctx) cudaSetDevice(kv->ctx->device);
+  cudaFree(kv->k);
+  cudaFree(kv->v);
+  delete kv;
+}
+
+static si_status kv_range(si_kv *kv, int seq, int pos0, int npos) {
+  SI_CHECK(kv, "null KV cache");
+  SI_CHECK(seq >= 0 && seq < kv->batch, "sequence %d out of range", seq);
+  SI_CHECK(pos0 >= 0 && npos >= 0 && pos0 + npos <= kv->max_ctx, "KV range out of bounds");
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_kv_write(si_ctx *ctx, si_kv *kv, int seq, int pos0, int npos,
+                                        const void *k_host, const void *v_host) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(kv_range(kv, seq, pos0, npos));
+  size_t off = ((size_t)seq * kv->seq_elems() + (size_t)pos0 * kv->row_elems()) * kv->elem();
+  size_t bytes = (size_t)npos * kv->row_elems() * kv->elem();
+  if (k_host)
+    SI_CUDA(cudaMemcpyAsync((char *)kv->k + off, k_host, bytes, cudaMemcpyHostToDevice,
+                            ctx->stream));
+  if (v_host)
+    SI_CUDA(cudaMemcpyAsync((char *)kv->v + off, v_host, bytes, cudaMemcpyHostToDevice,
+                            ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_kv_read(si_ctx *ctx, si_kv *kv, int seq, int pos0, int npos,
+                                       void *k_host, void *v_host) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(kv_range(kv, seq, pos0, npos));
+  size_t off = ((size_t)seq * kv->seq_elems() + (size_t)pos0 * kv->row_elems()) * kv->elem();
+  size_t bytes = (size_t)npos * kv->row_elems() * kv->elem();
+  if (k_host)
+    SI_CUDA(cudaMemcpyAsync(k_host, (char *)kv->k + off, bytes, cudaMemcpyDeviceToHost,
+                            ctx->stream));
+  if (v_host)
+    SI_CUDA(cudaMemcpyAsync(v_host, (char *)kv->v + off, bytes, cudaMemcpyDeviceToHost,
+                            ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_kv_fill_synth(si_ctx *ctx, si_kv *kv, uint64_t seed, float stdv,
+                                             int npos) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(kv && npos >= 0 && npos <= kv->max_ctx, "bad KV fill");
+  for (int b = 0; b < kv->batch; ++b) {
+    size_t off = (size_t)b * kv->seq_elems() * kv->elem();
+    size_t n = (size_t)npos * kv->row_elems();
+    SI_CUDA(si::launch_synth_kv((char *)kv->k + off, n, kv->kv_f32, seed * 1000003 + 2 * b,
+                                stdv, ctx->stream));
+    SI_CUDA(si::launch_synth_kv((char *)kv->v + off, n, kv->kv_f32, seed * 1000003 + 2 * b + 1,
+                                stdv, ctx->stream));
+  }
+  return SI_OK;
+}
+
+extern "C" SI_API void *si_kv_device_ptr(si_kv *kv, int which) {
+  if (!kv) return nullptr;
+  return which == 0 ? kv->k : kv->v;
+}
+
+// ----------------------------------------------------------------------------
+// layer schedules
+// ----------------------------------------------------------------------------
+namespace {
+// Carves the context arena into the per-token intermediates of one step.
+struct Arena {
+  char *base = nullptr;
+  size_t off = 0;
+  template <class T>
+  T *take(size_t n) {
+    off = (off + 255) & ~(size_t)255;
+    T *p = reinterpret_cast<T *>(base + off);
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+struct StepBuffers {
+  int8_t *xq; uint16_t *xd;
+  float *qkv, *qrot, *attn;
+  int8_t *aq; uint16_t *ad;
+  float *h;
+  int8_t *hq; uint16_t *hd;
+  int8_t *actq; uint16_t *actd;
+  float *part;
+  int *tok_seq, *tok_pos, *tok_ctx;
+};
+
+size_t step_bytes(const si_dims &d, int T, int nsplit, bool with_idx) {
+  Arena a;  // dry run on a null base just to measure
+  const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
+  const int I = d.intermediate > 0 ? d.intermediate : 32;
+  a.take<int8_t>((size_t)T * H); a.take<uint16_t>((size_t)T * H / 32);
+  a.take<float>((size_t)T * (QD + 2 * KVD)); a.take<float>((size_t)T * QD);
+  a.take<float>((size_t)T * QD);
+  a.take<int8_t>((size_t)T * QD); a.take<uint16_t>((size_t)T * QD / 32);
+  a.take<float>((size_t)T * H);
+  a.take<int8_t>((size_t)T * H); a.take<uint16_t>((size_t)T * H / 32);
+  a.take<int8_t>((size_t)T * I); a.take<uint16_t>((size_t)T * I / 32);
+  a.take<float>(si::attn_part_floats(T, d.n_q_heads, d.head_dim, nsplit) + 1);
+  (void)with_idx;
+  return a.off + 1024;
+}
+
+StepBuffers carve(void *base, const si_dims &d, int T, int nsplit) {
+  Arena a;
+  a.base = static_cast<char *>(base);
+  const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
+  const int I = d.intermediate > 0 ? d.intermediate : 32;
+  StepBuffers b{};
+  b.xq = a.take<int8_t>((size_t)T * H); b.xd = a.take<uint16_t>((size_t)T * H / 32);
+  b.qkv = a.take<float>((size_t)T * (QD + 2 * KVD)); b.qrot = a.take<float>((size_t)T * QD);
+  b.attn = a.take<float>((size_t)T * QD);
+  b.aq = a.take<int8_t>((size_t)T * QD); b.ad = a.take<uint16_t>((size_t)T * QD / 32);
+  b.h = a.take<float>((size_t)T * H);
+  b.hq = a.take<int8_t>((size_t)T * H); b.hd = a.take<uint16_t>((size_t)T * H / 32);
+  b.actq = a.take<int8_t>((size_t)T * I); b.actd = a.take<uint16_t>((size_t)T * I / 32);
+  b.part = a.take<float>(si::attn_part_floats(T, d.n_q_heads, d.head_dim, nsplit) + 1);
+  return b;
+}
+}  // namespace
+
+// Events bracketing the phases of one step, for the reference's phase_t.
+enum { EV_START, EV_RMS, EV_QKV, EV_ROPE, EV_ATTN, EV_Q8O, EV_OPROJ, EV_MLP, EV_COUNT };
+
+static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, int T,
+                          const int *seq_host, const int *ctx_host, int seq0, int prefix,
+                          float *y, int mode, const si_captures *cap, bool timing) {
+  const si_dims &d = l->d;
+  const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
+  SI_CHECK(mode == SI_LAYER_ATTN || mode == SI_LAYER_FULL, "bad layer mode");
+  SI_CHECK(mode == SI_LAYER_ATTN || (d.intermediate > 0 && l->gate),
+           "full-layer mode needs MLP weights");
+  SI_CHECK(kv->d.n_kv_heads == d.n_kv_heads && kv->d.head_dim == d.head_dim,
+           "KV cache dims do not match the layer");
+  SI_CHECK(ctx->head_dim == d.head_dim, "context RoPE table built for head_dim %d",
+           ctx->head_dim);
+  SI_CHECK(T > 0 && x && y, "bad step arguments");
+  int max_len = 0;
+  if (ctx_host) {
+    for (int t = 0; t < T; ++t) {
+      SI_CHECK(ctx_host[t] >= 1 && ctx_host[t] <= kv->max_ctx && ctx_host[t] <= ctx->max_positions,
+               "context length %d out of range [1, %d]", ctx_host[t], kv->max_ctx);
+      SI_CHECK(seq_host[t] >= 0 && seq_host[t] < kv->batch, "sequence out of range");
+      max_len = ctx_host[t] > max_len ? ctx_host[t] : max_len;
+    }
+  } else {
+    SI_CHECK(seq0 >= 0 && seq0 < kv->batch, "sequence %d out of range", seq0);
+    SI_CHECK(prefix >= 0 && prefix + T <= kv->max_ctx && prefix + T <= ctx->max_positions,
+             "prefill range [%d, %d) exceeds the cache", prefix, prefix + T);
+    max_len = prefix + T;
+  }
+  const int nsplit = si::attn_pick_splits(T, d.n_kv_heads, max_len);
+  SI_TRY(ctx->work.reserve(step_bytes(d, T, nsplit, true)));
+  StepBuffers b = carve(ctx->work.p, d, T, nsplit);
+  cudaStream_t s = ctx->stream;
+
+  // Per-token sequence / position / context arrays for the decode form.
+  if (ctx_host) {
+    size_t n = (size_t)3 * T;
+    if (ctx->pinned_idx_n < n) {
+      if (ctx->pinned_idx) cudaFreeHost(ctx->pinned_idx);
+      ctx->pinned_idx = nullptr;
+      ctx->pinned_idx_n = 0;
+      SI_CUDA(cudaMallocHost(&ctx->pinned_idx, n * sizeof(int)));
+      ctx->pinned_idx_n = n;
+    }
+    SI_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still be in flight
+    for (int t = 0; t < T; ++t) {
+      ctx->pinned_idx[t] = seq_host[t];
+      ctx->pinned_idx[T + t] = ctx_host[t] - 1;
+      ctx->pinned_idx[2 * T + t] = ctx_host[t];
+    }
+    SI_TRY(ctx->idx.reserve(n * sizeof(int)));
+    SI_CUDA(cudaMemcpyAsync(ctx->idx.p, ctx->pinned_idx, n * sizeof(int), cudaMemcpyHostToDevice, s));
+    b.tok_seq = static_cast<int *>(ctx->idx.p);
+    b.tok_pos = b.tok_seq + T;
+    b.tok_ctx = b.tok_seq + 2 * T;
+  }
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_START], s));
+  // 1. RMSNorm + Q8 of the input (qwen_one_layer.c:247-250).
+  SI_CUDA(si::launch_rmsnorm_q8(x, l->norm, T, H, d.rms_eps, nullptr, b.xq, b.xd, s));
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_RMS], s));
+  // 2. Fused Q|K|V projection + bias (qwen_one_layer.c:253-258).
+  SI_TRY(matmul(ctx, l->qkv, b.xq, b.xd, T, l->bias_qkv, nullptr, b.qkv, -1));
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_QKV], s));
+  if (cap && cap->qkv)
+    SI_CUDA(cudaMemcpyAsync(cap->qkv, b.qkv, (size_t)T * (QD + 2 * KVD) * 4,
+                            cudaMemcpyDeviceToDevice, s));
+  // 3. RoPE on q and k, KV append (qwen_one_layer.c:260-266).
+  si::RopeKvArgs ra{};
+  ra.qkv = b.qkv; ra.q_out = b.qrot; ra.kc = kv->k; ra.vc = kv->v; ra.kv_f32 = kv->kv_f32;
+  ra.T = T; ra.n_q_heads = d.n_q_heads; ra.n_kv_heads = d.n_kv_heads; ra.head_dim = d.head_dim;
+  ra.max_ctx = kv->max_ctx; ra.tok_pos = b.tok_pos; ra.tok_seq = b.tok_seq;
+  ra.seq0 = seq0; ra.pos0 = prefix; ra.cos_tab = ctx->cos_tab; ra.sin_tab = ctx->sin_tab;
+  ra.max_positions = ctx->max_positions;
+  SI_CUDA(si::launch_rope_kv(ra, s));
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_ROPE], s));
+  // 4. GQA attention (qwen_one_layer.c:269; causal for prefill).
+  si::AttnArgs aa{};
+  aa.q = b.qrot; aa.kc = kv->k; aa.vc = kv->v; aa.kv_f32 = kv->kv_f32; aa.T = T;
+  aa.n_q_heads = d.n_q_heads; aa.n_kv_heads = d.n_kv_heads; aa.head_dim = d.head_dim;
+  aa.max_ctx = kv->max_ctx; aa.tok_seq = b.tok_seq; aa.tok_ctx = b.tok_ctx; aa.seq0 = seq0;
+  aa.ctx0 = prefix + 1; aa.out = b.attn; aa.part = b.part; aa.nsplit = nsplit;
+  SI_CUDA(si::launch_attention(aa, s));
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_ATTN], s));
+  // 5. Q8 of the attention output (qwen_one_layer.c:272).
+  SI_CUDA(si::launch_q8_quantize(b.attn, T, QD, b.aq, b.ad, s));
+  if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_Q8O], s));
+  if (cap && cap->attn)
+    SI_CUDA(cudaMemcpyAsync(cap->attn, b.attn, (size_t)T * QD * 4, cudaMemcpyDeviceToDevice, s));
+  if (cap && cap->attn_q8)
+    SI_CUDA(si::launch_q8_to_blocks(b.aq, b.ad, T, QD, reinterpret_cast<uint8_t *>(cap->attn_q8), s));
+  // 6. Output projection (qwen_one_layer.c:275); the decoder layer adds the residual.
+  if (mode == SI_LAYER_ATTN) {
+    SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, y, -1));
+    if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
+    if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
+  } else {
+    SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, x, b.h, -1));
+    if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
+    // 7. MLP: rmsnorm2 + Q8 -> gate/up + SiLU*mul + Q8 -> down + residual.
+    SI_CUDA(si::launch_rmsnorm_q8(b.h, l->norm2, T, H, d.rms_eps, nullptr, b.hq, b.hd, s));
+    SI_TRY(si_gateup_q8_dev(ctx, l->gate, l->up, b.hq, b.hd, T, b.actq, b.actd, nullptr));
+    SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, b.h, y, -1));
+    if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
+  }
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_decode_step_dev(si_ctx *ctx, si_layer *l, si_kv *kv,
+                                               const float *x, int batch, const int *ctx_lens,
+                                               float *y, int mode, const si_captures *cap) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l && kv && ctx_lens, "null argument");
+  SI_CHECK(batch > 0 && batch <= kv->batch, "batch %d exceeds the KV cache's %d", batch, kv->batch);
+  std::vector<int> seqs(batch);
+  for (int i = 0; i < batch; ++i) seqs[i] = i;
+  return run_step(ctx, l, kv, x, batch, seqs.data(), ctx_lens, 0, 0, y, mode, cap, false);
+}
+
+extern "C" SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq,
+                                           const float *x, int ntok, int prefix, float *y,
+                                           int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l && kv, "null argument");
+  return run_step(ctx, l, kv, x, ntok, nullptr, nullptr, seq, prefix, y, mode, nullptr, false);
+}
+
+// Host-pointer forms: stage x/y through a device buffer.
+struct HostStage {
+  float *x = nullptr, *y = nullptr;
+  ~HostStage() {
+    cudaFree(x);
+    cudaFree(y);
+  }
+};
+
+extern "C" SI_API si_status si_decode_step(si_ctx *ctx, si_layer *l, si_kv *kv,
+                                           const float *x_host, int batch, const int *ctx_lens,
+                                           float *y_host, int mode, const si_captures *cap_host) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l && x_host && y_host && batch > 0, "null argument");
+  const int H = l->d.hidden, QD = l->d.n_q_heads * l->d.head_dim;
+  const int KVD = l->d.n_kv_heads * l->d.head_dim;
+  HostStage hs;
+  size_t n = (size_t)batch * H;
+  SI_CUDA(cudaMalloc(&hs.x, n * 4));
+  SI_CUDA(cudaMalloc(&hs.y, n * 4));
+  si_captures dcap{};
+  std::vector<void *> owned;
+  if (cap_host) {
+    if (cap_host->attn) { SI_CUDA(cudaMalloc(&dcap.attn, (size_t)batch * QD * 4)); owned.push_back(dcap.attn); }
+    if (cap_host->attn_q8) { SI_CUDA(cudaMalloc(&dcap.attn_q8, (size_t)batch * QD / 32 * 34)); owned.push_back(dcap.attn_q8); }
+    if (cap_host->qkv) { SI_CUDA(cudaMalloc(&dcap.qkv, (size_t)batch * (QD + 2 * KVD) * 4)); owned.push_back(dcap.qkv); }
+  }
+  SI_CUDA(cudaMemcpyAsync(hs.x, x_host, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  si_status st = si_decode_step_dev(ctx, l, kv, hs.x, batch, ctx_lens, hs.y, mode,
+                                    cap_host ? &dcap : nullptr);
+  if (st == SI_OK) {
+    cudaError_t e = cudaMemcpyAsync(y_host, hs.y, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess && cap_host && cap_host->attn)
+      e = cudaMemcpyAsync(cap_host->attn, dcap.attn, (size_t)batch * QD * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess && cap_host && cap_host->attn_q8)
+      e = cudaMemcpyAsync(cap_host->attn_q8, dcap.attn_q8, (size_t)batch * QD / 32 * 34, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess && cap_host && cap_host->qkv)
+      e = cudaMemcpyAsync(cap_host->qkv, dcap.qkv, (size_t)batch * (QD + 2 * KVD) * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) st = fail(SI_ERR_CUDA, "decode step: %s", cudaGetErrorString(e));
+  }
+  cudaStreamSynchronize(ctx->stream);
+  for (void *p : owned) cudaFree(p);
+  if (st == SI_OK) st = si_ctx_status(ctx);
+  return st;
+}
+
+extern "C" SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int seq,
+                                       const float *x_host, int ntok, int prefix, float *y_host,
+                                       int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l && x_host && y_host && ntok > 0, "null argument");
+  HostStage hs;
+  size_t n = (size_t)ntok * l->d.hidden;
+  SI_CUDA(cudaMalloc(&hs.x, n * 4));
+  SI_CUDA(cudaMalloc(&hs.y, n * 4));
+  SI_CUDA(cudaMemcpyAsync(hs.x, x_host, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  SI_TRY(si_prefill_dev(ctx, l, kv, seq, hs.x, ntok, prefix, hs.y, mode));
+  SI_CUDA(cudaMemcpyAsync(y_host, hs.y, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return si_ctx_status(ctx);
+}
+
+extern "C" SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *d,
+                                                    const float *q, int batch,
+                                                    const int *ctx_lens, float *out) {
+  SI_TRY(set_device(ctx));
+  SI_TRY(check_dims(d));
+  SI_CHECK(kv && q && out && ctx_lens && batch > 0 && batch <= kv->batch, "bad arguments");
+  int max_len = 0;
+  for (int i = 0; i < batch; ++i) {
+    SI_CHECK(ctx_lens[i] >= 0 && ctx_lens[i] <= kv->max_ctx, "context out of range");
+    max_len = ctx_lens[i] > max_len ? ctx_lens[i] : max_len;
+  }
+  const int nsplit = si::attn_pick_splits(batch, d->n_kv_heads, max_len);
+  size_t part = si::attn_part_floats(batch, d->n_q_heads, d->head_dim, nsplit);
+  size_t n = (size_t)2 * batch;
+  SI_TRY(ctx->work.reserve(part * 4 + 1024));
+  SI_TRY(ctx->idx.reserve(n * sizeof(int)));
+  std::vector<int> h(n);
+  for (int i = 0; i < batch; ++i) { h[i] = i; h[batch + i] = ctx_lens[i]; }
+  SI_CUDA(cudaMemcpyAsync(ctx->idx.p, h.data(), n * sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+  si::AttnArgs aa{};
+  aa.q = q; aa.kc = kv->k; aa.vc = kv->v; aa.kv_f32 = kv->kv_f32; aa.T = batch;
+  aa.n_q_heads = d->n_q_heads; aa.n_kv_heads = d->n_kv_heads; aa.head_dim = d->head_dim;
+  aa.max_ctx = kv->max_ctx; aa.tok_seq = static_cast<int *>(ctx->idx.p);
+  aa.tok_ctx = aa.tok_seq + batch; aa.out = out; aa.part = static_cast<float *>(ctx->work.p);
+  aa.nsplit = nsplit;
+  SI_CUDA(si::launch_attention(aa, ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));  // h is a pageable host array
+  return SI_OK;
+}
+
+// ----------------------------------------------------------------------------
+// reference-shaped entry points (host pointers, implicit context)
+// ----------------------------------------------------------------------------
+static std::mutex g_ref_mu;
+static si_ctx *g_ref_ctx = nullptr;
+struct WeightKey {
+  const void *p;
+  int rows, cols;
+  bool operator<(const WeightKey &o) const {
+    return p != o.p ? p < o.p : (rows != o.rows ? rows < o.rows : cols < o.cols);
+  }
+};
+static std::map<WeightKey, si_matrix *> g_weights;
+static std::map<const void *, si_layer *> g_layers;
+static si_kv *g_ref_kv = nullptr;
+
+static void ref_die(const char *what) {
+  fprintf(stderr, "error: %s: %s\n", what, g_last_error.c_str());
+  exit(1);
+}
+
+static si_ctx *ref_ctx(int head_dim, float theta) {
+  if (g_ref_ctx && (g_ref_ctx->head_dim != head_dim || g_ref_ctx->rope_theta != theta)) {
+    for (auto &kvp : g_layers) si_layer_free(kvp.second);
+    g_layers.clear();
+    si_kv_free(g_ref_kv);
+    g_ref_kv = nullptr;
+    for (auto &w : g_weights) si_matrix_free(w.second);
+    g_weights.clear();
+    si_ctx_destroy(g_ref_ctx);
+    g_ref_ctx = nullptr;
+  }
+  if (!g_ref_ctx) {
+    const char *dev = getenv("SI_DEVICE");
+    if (si_ctx_create(dev ? atoi(dev) : 0, 32768, theta, head_dim, &g_ref_ctx) != SI_OK)
+      ref_die("cannot create the CUDA context");
+  }
+  return g_ref_ctx;
+}
+
+// Device scratch for the host-pointer wrappers.
+static DevBuf g_ref_scratch;
+static char *ref_scratch(size_t n) {
+  if (g_ref_scratch.reserve(n) != SI_OK) ref_die("scratch allocation");
+  return static_cast<char *>(g_ref_scratch.p);
+}
+
+static void ref_ck(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    g_last_error = cudaGetErrorString(e);
+    ref_die(what);
+  }
+}
+
+extern "C" SI_API void quantize_q8(const float *src, block_q8_0 *dst, int count) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  if (count % 32) {
+    fprintf(stderr, "error: Q8 quantization length must be multiple of 32\n");
+    exit(1);
+  }
+  si_ctx *c = ref_ctx(HDIM, ROPE_BASE);
+  size_t nb = (size_t)count / 32;
+  char *s = ref_scratch((size_t)count * 4 + nb * 34 + (size_t)count + nb * 2 + 1024);
+  float *x = reinterpret_cast<float *>(s);
+  uint8_t *blk = reinterpret_cast<uint8_t *>(s + (size_t)count * 4);
+  int8_t *qs = reinterpret_cast<int8_t *>(blk + ((nb * 34 + 255) & ~(size_t)255));
+  uint16_t *d = reinterpret_cast<uint16_t *>(qs + (((size_t)count + 255) & ~(size_t)255));
+  ref_ck(cudaMemcpyAsync(x, src, (size_t)count * 4, cudaMemcpyHostToDevice, c->stream), "quantize_q8");
+  ref_ck(si::launch_q8_quantize(x, 1, count, qs, d, c->stream), "quantize_q8");
+  ref_ck(si::launch_q8_to_blocks(qs, d, 1, count, blk, c->stream), "quantize_q8");
+  ref_ck(cudaMemcpyAsync(dst, blk, nb * 34, cudaMemcpyDeviceToHost, c->stream), "quantize_q8");
+  ref_ck(cudaStreamSynchronize(c->stream), "quantize_q8");
+}
+
+static si_matrix *ref_weights(si_ctx *c, const uint8_t *w, int rows, int cols) {
+  WeightKey k{w, rows, cols};
+  auto it = g_weights.find(k);
+  if (it != g_weights.end()) return it->second;
+  si_matrix *m = nullptr;
+  if (si_matrix_upload(c, w, rows, cols, &m) != SI_OK) ref_die("weight upload");
+  g_weights[k] = m;
+  return m;
+}
+
+extern "C" SI_API void si_forget_host_weights(const void *host_ptr) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  for (auto it = g_weights.begin(); it != g_weights.end();) {
+    if (it->first.p == host_ptr) {
+      si_matrix_free(it->second);
+      it = g_weights.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  auto l = g_layers.find(host_ptr);
+  if (l != g_layers.end()) {
+    si_layer_free(l->second);
+    g_layers.erase(l);
+  }
+}
+
+extern "C" SI_API void matvec_q4q8(const uint8_t *weights, const block_q8_0 *input, int inputs,
+                                   int outputs, const float *bias, float *out) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  si_ctx *c = ref_ctx(HDIM, ROPE_BASE);
+  si_matrix *m = ref_weights(c, weights, outputs, inputs);
+  size_t nb = (size_t)inputs / 32;
+  char *s = ref_scratch(nb * 34 + (size_t)inputs + nb * 2 + (size_t)outputs * 8 + 4096);
+  uint8_t *blk = reinterpret_cast<uint8_t *>(s);
+  int8_t *qs = reinterpret_cast<int8_t *>(s + ((nb * 34 + 255) & ~(size_t)255));
+  uint16_t *d = reinterpret_cast<uint16_t *>(reinterpret_cast<char *>(qs) + (((size_t)inputs + 255) & ~(size_t)255));
+  float *b = reinterpret_cast<float *>(reinterpret_cast<char *>(d) + ((nb * 2 + 255) & ~(size_t)255));
+  float *o = b + (((size_t)outputs + 63) & ~(size_t)63);
+  ref_ck(cudaMemcpyAsync(blk, input, nb * 34, cudaMemcpyHostToDevice, c->stream), "matvec_q4q8");
+  if (bias) ref_ck(cudaMemcpyAsync(b, bias, (size_t)outputs * 4, cudaMemcpyHostToDevice, c->stream), "matvec_q4q8");
+  ref_ck(si::launch_q8_from_blocks(blk, 1, inputs, qs, d, c->stream), "matvec_q4q8");
+  if (matmul(c, m, qs, d, 1, bias ? b : nullptr, nullptr, o, 0) != SI_OK) ref_die("matvec_q4q8");
+  ref_ck(cudaMemcpyAsync(out, o, (size_t)outputs * 4, cudaMemcpyDeviceToHost, c->stream), "matvec_q4q8");
+  ref_ck(cudaStreamSynchronize(c->stream), "matvec_q4q8");
+}
+
+extern "C" SI_API void si_ref_rmsnorm(const float *input, const float *weight, float *out, int n,
+                                      float eps) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  si_ctx *c = ref_ctx(HDIM, ROPE_BASE);
+  char *s = ref_scratch((size_t)n * 12 + 1024);
+  float *x = reinterpret_cast<float *>(s), *w = x + n, *o = w + n;
+  ref_ck(cudaMemcpyAsync(x, input, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "rmsnorm");
+  if (weight) ref_ck(cudaMemcpyAsync(w, weight, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "rmsnorm");
+  ref_ck(si::launch_rmsnorm_q8(x, weight ? w : nullptr, 1, n, eps, o, nullptr, nullptr, c->stream), "rmsnorm");
+  ref_ck(cudaMemcpyAsync(out, o, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream), "rmsnorm");
+  ref_ck(cudaStreamSynchronize(c->stream), "rmsnorm");
+}
+
+extern "C" SI_API void si_ref_rope(float *heads, int nheads, int position, int head_dim,
+                                   float theta) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  si_ctx *c = ref_ctx(head_dim, theta);
+  if (position < 0 || position >= c->max_positions) {
+    fprintf(stderr, "error: RoPE position %d outside [0, %d)\n", position, c->max_positions);
+    exit(1);
+  }
+  // Route through the RoPE kernel with a row that has only q heads.
+  size_t n = (size_t)nheads * head_dim;
+  char *s = ref_scratch(n * 8 + 1024);
+  float *in = reinterpret_cast<float *>(s), *o = in + n;
+  ref_ck(cudaMemcpyAsync(in, heads, n * 4, cudaMemcpyHostToDevice, c->stream), "rope");
+  si::RopeKvArgs ra{};
+  ra.qkv = in; ra.q_out = o; ra.kc = nullptr; ra.vc = nullptr; ra.T = 1;
+  ra.n_q_heads = nheads; ra.n_kv_heads = 0; ra.head_dim = head_dim; ra.max_ctx = 0;
+  ra.pos0 = position; ra.cos_tab = c->cos_tab; ra.sin_tab = c->sin_tab;
+  ra.max_positions = c->max_positions;
+  // max_ctx = 0 makes the kernel skip the cache append but still rotate.
+  ref_ck(si::launch_rope_kv(ra, c->stream), "rope");
+  ref_ck(cudaMemcpyAsync(heads, o, n * 4, cudaMemcpyDeviceToHost, c->stream), "rope");
+  ref_ck(cudaStreamSynchronize(c->stream), "rope");
+}
+
+extern "C" SI_API void si_ref_attention(int method, const float *q, const uint16_t *kc,
+                                        const uint16_t *vc, int context, float *out,
+                                        float *scores, int n_q_heads, int n_kv_heads,
+                                        int head_dim) {
+  (void)method;   // standard and flash compute the same function on the GPU
+  (void)scores;   // the reference's score workspace is not materialised here
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  si_ctx *c = ref_ctx(head_dim, ROPE_BASE);
+  si_dims d{n_q_heads * head_dim, n_q_heads, n_kv_heads, head_dim, 0, ROPE_BASE, RMS_EPS};
+  if (check_dims(&d) != SI_OK) ref_die("attention dims");
+  const int ctxlen = context > 0 ? context : 0;
+  const size_t row = (size_t)n_kv_heads * head_dim;
+  if (g_ref_kv && (g_ref_kv->max_ctx < ctxlen || g_ref_kv->kv_f32 || g_ref_kv->row_elems() != row)) {
+    si_kv_free(g_ref_kv);
+    g_ref_kv = nullptr;
+  }
+  if (!g_ref_kv && si_kv_create(c, &d, 1, ctxlen > 4096 ? ctxlen : 4096, 0, &g_ref_kv) != SI_OK)
+    ref_die("attention cache");
+  size_t qn = (size_t)n_q_heads * head_dim;
+  char *s = ref_scratch(qn * 8 + 1024);
+  float *qd = reinterpret_cast<float *>(s), *od = qd + qn;
+  if (ctxlen) {
+    ref_ck(cudaMemcpyAsync(g_ref_kv->k, kc, ctxlen * row * 2, cudaMemcpyHostToDevice, c->stream), "attention");
+    ref_ck(cudaMemcpyAsync(g_ref_kv->v, vc, ctxlen * row * 2, cudaMemcpyHostToDevice, c->stream), "attention");
+  }
+  ref_ck(cudaMemcpyAsync(qd, q, qn * 4, cudaMemcpyHostToDevice, c->stream), "attention");
+  int lens[1] = {ctxlen};
+  if (si_attention_decode_dev(c, g_ref_kv, &d, qd, 1, lens, od) != SI_OK) ref_die("attention");
+  ref_ck(cudaMemcpyAsync(out, od, qn * 4, cudaMemcpyDeviceToHost, c->stream), "attention");
+  ref_ck(cudaStreamSynchronize(c->stream), "attention");
+}
+
+extern "C" SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uint16_t *kc,
+                                           uint16_t *vc, int context, float *output, int method,
+                                           float *scores, float *attn_copy, block_q8_0 *q8_copy,
+                                           int hidden, int n_q_heads, int n_kv_heads,
+                                           int head_dim, float theta, float eps) {
+  (void)method;
+  (void)scores;
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  phase_t ph;
+  memset(&ph, 0, sizeof(ph));
+  si_ctx *c = ref_ctx(head_dim, theta);
+  si_dims d{hidden, n_q_heads, n_kv_heads, head_dim, 0, theta, eps};
+  if (check_dims(&d) != SI_OK) ref_die("run_layer dims");
+  if (context < 1 || context > 32768) {
+    fprintf(stderr, "error: Context must be 1..32768\n");
+    exit(1);
+  }
+  si_layer *L = nullptr;
+  auto it = g_layers.find(l->wq);
+  if (it != g_layers.end() && it->second->d.hidden == hidden) {
+    L = it->second;
+  } else {
+    si_layer_host h{};
+    h.wq = l->wq; h.wk = l->wk; h.wv = l->wv; h.wo = l->wo;
+    h.norm = l->norm; h.bq = l->bq; h.bk = l->bk; h.bv = l->bv;
+    if (si_layer_upload(c, &d, &h, &L) != SI_OK) ref_die("layer upload");
+    g_layers[l->wq] = L;
+  }
+  const size_t row = (size_t)n_kv_heads * head_dim;
+  if (g_ref_kv && (g_ref_kv->max_ctx < context || g_ref_kv->kv_f32 || g_ref_kv->row_elems() != row)) {
+    si_kv_free(g_ref_kv);
+    g_ref_kv = nullptr;
+  }
+  if (!g_ref_kv && si_kv_create(c, &d, 1, context > 4096 ? context : 4096, 0, &g_ref_kv) != SI_OK)
+    ref_die("KV cache");
+  // The caller owns the fp16 cache on the host (qwen_one_layer.c:625-626); mirror
+  // its history, run the step, and write the new slot back.
+  if (context > 1) {
+    ref_ck(cudaMemcpyAsync(g_ref_kv->k, kc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), "run_layer");
+    ref_ck(cudaMemcpyAsync(g_ref_kv->v, vc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), "run_layer");
+  }
+  const size_t QD = (size_t)n_q_heads * head_dim;
+  char *s = ref_scratch((size_t)hidden * 8 + QD * 4 + QD / 32 * 34 + 4096);
+  float *xd = reinterpret_cast<float *>(s), *yd = xd + hidden;
+  float *ad = yd + hidden;
+  block_q8_0 *qd = reinterpret_cast<block_q8_0 *>(ad + QD);
+  ref_ck(cudaMemcpyAsync(xd, x, (size_t)hidden * 4, cudaMemcpyHostToDevice, c->stream), "run_layer");
+  si_captures cap{};
+  cap.attn = attn_copy ? ad : nullptr;
+  cap.attn_q8 = q8_copy ? qd : nullptr;
+  int lens[1] = {context}, seqs[1] = {0};
+  if (run_step(c, L, g_ref_kv, xd, 1, seqs, lens, 0, 0, yd, SI_LAYER_ATTN, &cap, true) != SI_OK)
+    ref_die("run_layer");
+  ref_ck(cudaMemcpyAsync(output, yd, (size_t)hidden * 4, cudaMemcpyDeviceToHost, c->stream), "run_layer");
+  size_t slot = (size_t)(context - 1) * row;
+  ref_ck(cudaMemcpyAsync(kc + slot, (uint16_t *)g_ref_kv->k + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), "run_layer");
+  ref_ck(cudaMemcpyAsync(vc + slot, (uint16_t *)g_ref_kv->v + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), "run_layer");
+  if (attn_copy) ref_ck(cudaMemcpyAsync(attn_copy, ad, QD * 4, cudaMemcpyDeviceToHost, c->stream), "run_layer");
+  if (q8_copy) ref_ck(cudaMemcpyAsync(q8_copy, qd, QD / 32 * 34, cudaMemcpyDeviceToHost, c->stream), "run_layer");
+  ref_ck(cudaStreamSynchronize(c->stream), "run_layer");
+  if (si_ctx_status(c) != SI_OK) ref_die("run_layer");
+  // Phase times from CUDA events: RMSNorm and the input Q8 are one kernel, and
+  // Q/K/V are one fused launch, so those are reported on the first field.
+  float ms[EV_COUNT] = {};
+  for (int i = 1; i <= EV_OPROJ; ++i) cudaEventElapsedTime(&ms[i], c->ev[i - 1], c->ev[i]);
+  ph.rms = ms[EV_RMS] * 1e-3f;
+  ph.q_proj = ms[EV_QKV] * 1e-3f;
+  ph.rope_cache = ms[EV_ROPE] * 1e-3f;
+  ph.attention = ms[EV_ATTN] * 1e-3f;
+  ph.q8_output = ms[EV_Q8O] * 1e-3f;
+  ph.out_proj = ms[EV_OPROJ] * 1e-3f;
+  return ph;
+}
+
+static void *ref_load_file(const char *dir, const char *name, size_t expected, int optional) {
+  char path[1024];
+  int n = snprintf(path, sizeof(path), "%s/%s", dir, name);
+  if (n < 0 || (size_t)n >= sizeof(path)) {
+    fprintf(stderr, "error: Weights directory path too long\n");
+    exit(1);
+  }
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    if (optional) return nullptr;
+    perror(path);
+    exit(1);
+  }
+  if (fseek(f, 0, SEEK_END) != 0 || ftell(f) != (long)expected || fseek(f, 0, SEEK_SET) != 0) {
+    fprintf(stderr, "Wrong size for %s (expected %zu bytes)\n", path, expected);
+    exit(1);
+  }
+  void *buf = malloc(expected);
+  if (!buf || fread(buf, 1, expected, f) != expected) {
+    fprintf(stderr, "error: Failed to read weight file\n");
+    exit(1);
+  }
+  fclose(f);
+  return buf;
+}
+
+// qwen_one_layer.c:210-221: same files, sizes and optional vectors.
+extern "C" SI_API layer_t si_ref_load_layer(const char *dir, int hidden, int kvdim) {
+  layer_t l;
+  memset(&l, 0, sizeof(l));
+  size_t hb = (size_t)hidden * hidden / 32 * 18, kb = (size_t)kvdim * hidden / 32 * 18;
+  l.wq = (uint8_t *)ref_load_file(dir, "q.q4_0", hb, 0);
+  l.wk = (uint8_t *)ref_load_file(dir, "k.q4_0", kb, 0);
+  l.wv = (uint8_t *)ref_load_file(dir, "v.q4_0", kb, 0);
+  l.wo = (uint8_t *)ref_load_file(dir, "o.q4_0", hb, 0);
+  l.norm = (float *)ref_load_file(dir, "norm.f32", (size_t)hidden * 4, 1);
+  l.bq = (float *)ref_load_file(dir, "q_bias.f32", (size_t)hidden * 4, 1);
+  l.bk = (float *)ref_load_file(dir, "k_bias.f32", (size_t)kvdim * 4, 1);
+  l.bv = (float *)ref_load_file(dir, "v_bias.f32", (size_t)kvdim * 4, 1);
+  return l;
+}
+
+extern "C" SI_API void si_ref_free_layer(layer_t *l) {
+  if (!l) return;
+  si_forget_host_weights(l->wq);
+  si_forget_host_weights(l->wk);
+  si_forget_host_weights(l->wv);
+  si_forget_host_weights(l->wo);
+  free(l->wq); free(l->wk); free(l->wv); free(l->wo);
+  free(l->norm); free(l->bq); free(l->bk); free(l->bv);
+  memset(l, 0, sizeof(*l));
+}

@@ -1,0 +1,75 @@
+// si_common.cuh -- shared device helpers for the sm_100a kernels.
+//
+// Numerics follow the reference's portable C path, which is built with
+// -ffp-contract=off (reference Makefile:7): every product and sum below is an
+// explicitly rounded __f*_rn intrinsic so nvcc cannot contract it into an FMA.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define SI_QK 32
+#define SI_RT 32  // rows per row-tile of the SoA weight layout
+
+namespace si {
+
+// Kernels that detect bad input or a bounded wait that ran out record a
+// si_status code in the context's device error word (first error wins); the
+// host reads and clears it in si_ctx_status().
+__device__ __forceinline__ void raise_error(int *err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// Exact fp16 -> fp32 of the reference (qwen_one_layer.c:42-59); the hardware
+// conversion is exact for every half including subnormals.
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+// Round-to-nearest-even fp32 -> fp16 with subnormals and overflow to inf, the
+// rounding of qwen_one_layer.c:61-86 for every finite input.
+__device__ __forceinline__ uint16_t f32_to_f16(float x) {
+  return __half_as_ushort(__float2half_rn(x));
+}
+
+// One Q8_0 block from 32 values held one per lane of a full warp
+// (qwen_one_layer.c:98-116): amax -> d = amax/127 (fp32) -> store fp16(d) ->
+// inv = d==0 ? 0 : 1/d -> q = rint(x*inv) clamped to +-127.
+__device__ __forceinline__ int8_t q8_lane(float x, uint16_t &d16) {
+  float a = fabsf(x);
+  unsigned amax_bits = __reduce_max_sync(0xffffffffu, __float_as_uint(a));
+  float amax = __uint_as_float(amax_bits);
+  float d = __fdiv_rn(amax, 127.0f);
+  d16 = f32_to_f16(d);
+  float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  int q = __float2int_rn(__fmul_rn(x, inv));
+  q = q > 127 ? 127 : (q < -127 ? -127 : q);
+  return (int8_t)q;
+}
+
+// Q4 nibble words stored with every byte XOR 0x88, so each nibble is the
+// 4-bit two's complement of (q - 8).  Placing a nibble in the high half of a
+// byte gives the signed byte 16*(q-8); the dp4a sums are therefore 16*isum.
+__device__ __forceinline__ int lo_nib_s8x16(uint32_t w) { return (int)((w << 4) & 0xF0F0F0F0u); }
+__device__ __forceinline__ int hi_nib_s8x16(uint32_t w) { return (int)(w & 0xF0F0F0F0u); }
+
+// 16 bytes of one Q4_0 block (elements j | j+16 per byte) against 32 int8
+// activations: returns the exact int32 block sum of qwen_one_layer.c:137-144.
+__device__ __forceinline__ int block_isum(const uint4 w, const int4 a0, const int4 a1) {
+  int acc = 0;
+  acc = __dp4a(lo_nib_s8x16(w.x), a0.x, acc);
+  acc = __dp4a(lo_nib_s8x16(w.y), a0.y, acc);
+  acc = __dp4a(lo_nib_s8x16(w.z), a0.z, acc);
+  acc = __dp4a(lo_nib_s8x16(w.w), a0.w, acc);
+  acc = __dp4a(hi_nib_s8x16(w.x), a1.x, acc);
+  acc = __dp4a(hi_nib_s8x16(w.y), a1.y, acc);
+  acc = __dp4a(hi_nib_s8x16(w.z), a1.z, acc);
+  acc = __dp4a(hi_nib_s8x16(w.w), a1.w, acc);
+  return acc >> 4;
+}
+
+// ((float)isum * dw) * dx with the reference's two roundings (qwen_one_layer.c:158).
+__device__ __forceinline__ float block_term(int isum, float dw, float dx) {
+  return __fmul_rn(__fmul_rn((float)isum, dw), dx);
+}
+
+}  // namespace si

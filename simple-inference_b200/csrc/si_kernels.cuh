@@ -1,0 +1,90 @@
+// si_kernels.cuh -- internal launch interface between the C ABI (si_api.cu)
+// and the kernel translation units.  Not installed; plain pointers only.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace si {
+
+// ---- layout.cu -------------------------------------------------------------
+// GGUF Q4_0 rows [rows][KB] x 18 B  ->  row-tile SoA: nib [rows/32][KB][32][16]
+// (each byte XOR 0x88) and scl [rows/32][KB][32] fp16.
+cudaError_t launch_repack_gguf(const uint8_t *gguf, int rows, int KB, uint8_t *nib,
+                               uint16_t *scl, cudaStream_t s);
+cudaError_t launch_unpack_to_gguf(const uint8_t *nib, const uint16_t *scl, int rows, int KB,
+                                  uint8_t *gguf, cudaStream_t s);
+cudaError_t launch_synth_q4(int rows, int KB, uint64_t seed, float std, uint8_t *nib,
+                            uint16_t *scl, cudaStream_t s);
+cudaError_t launch_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float std,
+                             cudaStream_t s);
+cudaError_t launch_synth_kv(void *dst, size_t n, int f32, uint64_t seed, float std,
+                            cudaStream_t s);
+cudaError_t launch_q8_to_blocks(const int8_t *qs, const uint16_t *d, int M, int K,
+                                uint8_t *blocks, cudaStream_t s);
+cudaError_t launch_q8_from_blocks(const uint8_t *blocks, int M, int K, int8_t *qs, uint16_t *d,
+                                  cudaStream_t s);
+
+// ---- norm_q8.cu -------------------------------------------------------------
+cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_t *d,
+                               cudaStream_t s);
+cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, float eps,
+                              float *out, int8_t *qs, uint16_t *d, cudaStream_t s);
+// y = a + b elementwise (residual), fp32, round-to-nearest.
+cudaError_t launch_add(const float *a, const float *b, float *y, size_t n, cudaStream_t s);
+
+// ---- gemv.cu ----------------------------------------------------------------
+struct GemvArgs {
+  const uint8_t *nib;      // row-tile nibbles of the (first) matrix
+  const uint16_t *scl;     // row-tile scales
+  const uint8_t *nib2;     // second matrix (SwiGLU "up"), same shape
+  const uint16_t *scl2;
+  int N, K;                // rows, inputs
+  const int8_t *xq;        // activations [M][K]
+  const uint16_t *xd;      // [M][K/32] fp16 scales
+  int M;
+  const float *bias;       // [N] or null
+  const float *resid;      // [M][N] added after the block sum, or null
+  float *out;              // [M][N] fp32 (non-SwiGLU), or SwiGLU fp32 act (optional)
+  int8_t *act_qs;          // SwiGLU: Q8 of silu(gate)*up, [M][N]
+  uint16_t *act_d;         // [M][N/32]
+  int32_t *isum_out;       // [M][N][K/32] block partial sums (parity), or null
+};
+cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
+
+// ---- gemm_tc.cu (tcgen05) ------------------------------------------------------
+cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s);
+bool gemm_tc_supported(int N, int K, int M);
+
+// ---- rope_kv.cu -------------------------------------------------------------
+struct RopeKvArgs {
+  const float *qkv;      // [T][QD + 2*KVD] projections (bias included)
+  float *q_out;          // [T][QD] rotated queries
+  void *kc, *vc;         // caches [B][max_ctx][Hkv][D]
+  int kv_f32;
+  int T, n_q_heads, n_kv_heads, head_dim, max_ctx;
+  const int *tok_pos;    // [T] device positions (decode) or null
+  const int *tok_seq;    // [T] device sequence ids (decode) or null
+  int seq0, pos0;        // prefill: seq = seq0, pos = pos0 + t
+  const float *cos_tab, *sin_tab;  // [max_positions][D/2]
+  int max_positions;
+};
+cudaError_t launch_rope_kv(const RopeKvArgs &a, cudaStream_t s);
+
+// ---- attention.cu -----------------------------------------------------------
+struct AttnArgs {
+  const float *q;        // [T][Hq][D] (after RoPE)
+  const void *kc, *vc;   // [B][max_ctx][Hkv][D]
+  int kv_f32;
+  int T, n_q_heads, n_kv_heads, head_dim, max_ctx;
+  const int *tok_seq;    // [T] device, or null (then seq0)
+  const int *tok_ctx;    // [T] device context lengths, or null (then ctx0 + t)
+  int seq0, ctx0;
+  float *out;            // [T][Hq][D]
+  float *part;           // split-K scratch, >= attn_part_floats() floats
+  int nsplit;
+};
+size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
+int attn_pick_splits(int T, int n_kv_heads, int max_len);
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
+
+}  // namespace si
