@@ -39,6 +39,7 @@ sys.path.insert(0, os.path.join(ROOT, "simple-inference_b200"))
 H, I = 1536, 8960
 QKV_N = 2048
 PREFILL_M = 2048
+COPIES = 10
 METRIC = "Qwen layer prefill tok/s + decode µs/token; % of HBM / int8-TC roofline"
 INT8_SPEC_TOPS = 4500.0  # B200 dense int8 tensor-core spec; not in MEASURED_PEAKS.json
 
@@ -145,6 +146,28 @@ class ProjectionSet:
         if ev: ev[6].record()
         return 6
 
+    def kernel(self, b, M, i, name):
+        """Launch one kernel of the step (for per-kernel timing)."""
+        ctx, w = self.ctx, self.sets[i % len(self.sets)]
+        if name == "q8_x":
+            ctx.q8_quantize(b["x"], M, H, b["xq"], b["xd"])
+        elif name == "qkv":
+            ctx.matmul(w["qkv"], b["xq"], b["xd"], M, self.bias, b["qkv"])
+        elif name == "q8_o":
+            ctx.q8_quantize(b["oin"], M, H, b["oq"], b["od"])
+        elif name == "o":
+            ctx.matmul(w["o"], b["oq"], b["od"], M, None, b["yo"])
+        elif name == "gateup":
+            ctx.gateup_q8(w["gate"], w["up"], b["xq"], b["xd"], M, b["aq"], b["ad"])
+        else:
+            ctx.matmul(w["down"], b["aq"], b["ad"], M, None, b["yd"])
+
+    def free(self):
+        for s in self.sets:
+            for m in s.values():
+                m.free()
+        self.sets = []
+
 
 def weight_bytes(M):
     """Algorithmic HBM bytes of each projection kernel (weights 18 B/32, Q8 input
@@ -174,13 +197,13 @@ def time_region(torch, stream, fn, steps):
 
 
 def run_ours(args, rank, world, local_rank):
+    import gc
     import torch
     import sib200
     torch.cuda.set_device(local_rank)
     ctx = sib200.Context(local_rank, max_positions=4096, rope_theta=1e6, head_dim=128)
     stream = torch.cuda.ExternalStream(ctx.stream)
-    copies = 10
-    ps = ProjectionSet(ctx, torch, copies)
+    ps = ProjectionSet(ctx, torch, COPIES)
     dist = world > 1
     if dist:
         import torch.distributed as tdist
@@ -198,53 +221,57 @@ def run_ours(args, rank, world, local_rank):
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         return float(t.item())
 
+    names = ["q8_x", "qkv", "q8_o", "o", "gateup", "down"]
+
+    def graphs_for(M, b):
+        """One CUDA graph per weight copy (one step each), and per kernel one graph
+        launching that kernel on every copy, so per-kernel device time is measured
+        without host launch gaps."""
+        steps = [ctx.capture(lambda c=c: ps.step(b, M, c)) for c in range(COPIES)]
+        per_kernel = {n: ctx.capture(lambda n=n: [ps.kernel(b, M, c, n) for c in range(COPIES)])
+                      for n in names}
+        return steps, per_kernel
+
+    def kernel_times(per_kernel, reps):
+        out = {}
+        for n, g in per_kernel.items():
+            g.launch()
+            t = time_region(torch, stream, lambda i: g.launch(), reps)
+            out[n] = t / (reps * COPIES)
+        return out
+
+    # ---- prefill, M = 2048 -------------------------------------------------
     M = PREFILL_M
     b = ps.buffers(M)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            ps.step(b, M, i)
+    steps, per_kernel = graphs_for(M, b)
+    log("graphs captured")
+    for i in range(args.warmup):
+        steps[i % COPIES].launch()
     barrier_sync()
     with Clocks(local_rank) as clk:
-        t = time_region(torch, stream, lambda i: ps.step(b, M, i + args.warmup), args.steps)
+        t = time_region(torch, stream, lambda i: steps[(i + args.warmup) % COPIES].launch(),
+                        args.steps)
     barrier_sync()
     t = max_over_ranks(t)
+    log(f"prefill timed {t:.4f}s")
     value = world * M * args.steps / t
     ms_per_step = t / args.steps * 1e3
+    kt = kernel_times(per_kernel, 3)
+    log(f"prefill kernels {kt}")
 
-    # Per-kernel device times (CUDA events on the library's stream).
-    names = ["q8_x", "qkv", "q8_o", "o", "gateup", "down"]
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-    acc = {n: 0.0 for n in names}
-    reps = max(3, args.steps)
-    with torch.cuda.stream(stream):
-        for i in range(reps):
-            ps.step(b, M, i, ev)
-            ev[6].synchronize()
-            for k, n in enumerate(names):
-                acc[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
-    kt = {n: acc[n] / reps for n in names}
-
-    # Decode: the same set at M = 1.
+    # ---- decode, M = 1 -----------------------------------------------------
     bd = ps.buffers(1)
+    dsteps_g, dper_kernel = graphs_for(1, bd)
+    for i in range(max(args.warmup, COPIES)):
+        dsteps_g[i % COPIES].launch()
     barrier_sync()
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            ps.step(bd, 1, i)
-    barrier_sync()
-    dsteps = max(args.steps, 50)
-    td = time_region(torch, stream, lambda i: ps.step(bd, 1, i), dsteps)
+    dsteps = max(args.steps, 100)
+    td = time_region(torch, stream, lambda i: dsteps_g[i % COPIES].launch(), dsteps)
     td = max_over_ranks(td)
-    acc_d = {n: 0.0 for n in names}
-    with torch.cuda.stream(stream):
-        for i in range(dsteps):
-            ps.step(bd, 1, i, ev)
-            ev[6].synchronize()
-            for k, n in enumerate(names):
-                acc_d[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
-    kd = {n: acc_d[n] / dsteps for n in names}
+    kd = kernel_times(dper_kernel, 20)
+    log(f"decode kernels {kd}")
 
-    # End to end through the C ABI with pinned host buffers.
+    # ---- end to end through the C ABI with pinned host buffers ---------------
     hx = torch.randn(M, H).pin_memory()
     ho = torch.randn(M, H).pin_memory()
     out_q = torch.empty(M, QKV_N).pin_memory()
@@ -254,21 +281,24 @@ def run_ours(args, rank, world, local_rank):
     def e2e_step(i):
         b["x"].copy_(hx, non_blocking=True)
         b["oin"].copy_(ho, non_blocking=True)
-        ps.step(b, M, i)
+        steps[i % COPIES].launch()
         out_q.copy_(b["qkv"], non_blocking=True)
         out_o.copy_(b["yo"], non_blocking=True)
         out_d.copy_(b["yd"], non_blocking=True)
+    with torch.cuda.stream(stream):
+        e2e_step(0)
     barrier_sync()
     te = time_region(torch, stream, e2e_step, args.steps)
     te = max_over_ranks(te)
+    log(f"e2e {te:.4f}s")
     h2d = 2 * M * H * 4
     d2h = M * (QKV_N + 2 * H) * 4
 
     pk = peaks()
     wb = weight_bytes(1)
-    dom_d = max(kd, key=lambda n: kd[n] if n in wb else -1)
+    dom_d = max(wb, key=lambda n: kd[n])
     fl = flops(M)
-    dom_p = max((n for n in fl), key=lambda n: kt[n])
+    dom_p = max(fl, key=lambda n: kt[n])
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -278,20 +308,23 @@ def run_ours(args, rank, world, local_rank):
                                " +bias, o 1536^2, gate+up 2x8960x1536 +SiLU*mul+Q8, down "
                                "1536x8960), Q4_0 x Q8_0",
                    "prefill_tokens_per_step": M, "parallelism": f"replicas x{world}",
-                   "l2": "10 weight copies (263 MB > 2x L2) rotated per step"},
+                   "l2": f"{COPIES} weight copies ({COPIES * 26.3:.0f} MB > 2x L2) rotated per step",
+                   "timing": "CUDA graph replays, CUDA events on the library stream"},
         "decode": {"us_per_token": round(td / dsteps * 1e6, 3),
                    "kernel_us": {n: round(kd[n] * 1e6, 3) for n in names},
                    "roofline": {"bound": "hbm", "kernel": dom_d,
                                 "achieved": round(wb[dom_d] / kd[dom_d] / 1e9, 1),
                                 "peak": pk["hbm_gbs"], "unit": "GB/s",
                                 "frac": round(wb[dom_d] / kd[dom_d] / 1e9 / pk["hbm_gbs"], 4),
-                                "peak_src": pk["src"]}},
+                                "peak_src": pk["src"],
+                                "all": {n: round(wb[n] / kd[n] / 1e9, 1) for n in wb}}},
         "prefill_kernel_ms": {n: round(kt[n] * 1e3, 4) for n in names},
         "roofline": {"bound": "tensor", "kernel": dom_p,
                      "achieved": round(fl[dom_p] / kt[dom_p] / 1e12, 2),
                      "peak": INT8_SPEC_TOPS, "unit": "TOP/s",
                      "frac": round(fl[dom_p] / kt[dom_p] / 1e12 / INT8_SPEC_TOPS, 4),
                      "peak_src": "spec (dense int8; MEASURED_PEAKS.json has no int8 figure)",
+                     "all": {n: round(fl[n] / kt[n] / 1e12, 2) for n in fl},
                      "traffic": None},
         "e2e": {"value": round(world * M * args.steps / te, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -299,8 +332,17 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:
+        log("cpu baseline")
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
-    ctx.close()
+    # torch's allocators keep events recorded on the library's stream (pinned
+    # copies ran on it), so the stream is left to process exit rather than
+    # destroyed under them; graphs and weights are released explicitly.
+    torch.cuda.synchronize()
+    ctx.sync()
+    del steps, per_kernel, dsteps_g, dper_kernel
+    gc.collect()
+    ps.free()
+    ctx.h = None
     return result
 
 
@@ -404,7 +446,14 @@ def run_reference(args, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def log(msg):
+    if os.environ.get("SI_BENCH_VERBOSE"):
+        print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
+    import faulthandler
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

@@ -238,6 +238,15 @@ SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const 
 SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const float *x_dev,
                                 int ntok, int prefix, float *y_dev, int mode);
 
+/* CUDA-graph capture of a sequence of calls on the context's stream (no host
+ * synchronisation may happen between begin and end: the *_dev matrix/Q8 calls
+ * qualify).  Replays run the captured kernels with no launch gaps. */
+typedef struct si_graph si_graph;
+SI_API si_status si_graph_begin(si_ctx *ctx);
+SI_API si_status si_graph_end(si_ctx *ctx, si_graph **out);
+SI_API si_status si_graph_launch(si_ctx *ctx, si_graph *g);
+SI_API void si_graph_free(si_graph *g);
+
 /* Decode attention alone (parity): q [B][Hq][D] after RoPE. */
 SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *dims,
                                          const float *q_dev, int batch, const int *ctx_lens,

@@ -136,6 +136,9 @@ struct si_kv {
 static si_status set_device(si_ctx *ctx) {
   SI_CHECK(ctx, "null context");
   SI_CUDA(cudaSetDevice(ctx->device));
+  // Drop a non-sticky error left by an earlier, already reported call so the
+  // launch checks below only see errors of this call.
+  (void)cudaGetLastError();
   return SI_OK;
 }
 
@@ -240,6 +243,48 @@ extern "C" SI_API si_status si_ctx_status(si_ctx *ctx) {
 extern "C" SI_API void *si_ctx_stream(si_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
 
 // ----------------------------------------------------------------------------
+// CUDA graphs
+// ----------------------------------------------------------------------------
+struct si_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" SI_API si_status si_graph_begin(si_ctx *ctx) {
+  SI_TRY(set_device(ctx));
+  SI_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_graph_end(si_ctx *ctx, si_graph **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(out, "null output handle");
+  si_graph *g = new si_graph();
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &g->graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&g->exec, g->graph, 0);
+  if (e != cudaSuccess) {
+    si_graph_free(g);
+    return fail(SI_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+  }
+  *out = g;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_graph_launch(si_ctx *ctx, si_graph *g) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(g && g->exec, "null graph");
+  SI_CUDA(cudaGraphLaunch(g->exec, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API void si_graph_free(si_graph *g) {
+  if (!g) return;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
+}
+
+// ----------------------------------------------------------------------------
 // matrices
 // ----------------------------------------------------------------------------
 static si_status matrix_alloc(si_ctx *ctx, int rows, int cols, si_matrix **out) {
@@ -298,7 +343,6 @@ extern "C" SI_API si_status si_matrix_synth(si_ctx *ctx, int rows, int cols, uin
 
 extern "C" SI_API void si_matrix_free(si_matrix *m) {
   if (!m) return;
-  if (m->ctx) cudaSetDevice(m->ctx->device);
   cudaFree(m->nib);
   cudaFree(m->scl);
   delete m;
@@ -481,7 +525,6 @@ static si_status upload_f32(si_ctx *ctx, const float *host, size_t n, float **ou
 
 extern "C" SI_API void si_layer_free(si_layer *l) {
   if (!l) return;
-  if (l->ctx) cudaSetDevice(l->ctx->device);
   si_matrix_free(l->qkv);
   si_matrix_free(l->o);
   si_matrix_free(l->gate);
@@ -619,7 +662,6 @@ extern "C" SI_API si_status si_kv_create(si_ctx *ctx, const si_dims *d, int batc
 
 extern "C" SI_API void si_kv_free(si_kv *kv) {
   if (!kv) return;
-  if (kv->ctx) cudaSetDevice(kv->ctx->device);
   cudaFree(kv->k);
   cudaFree(kv->v);
   delete kv;

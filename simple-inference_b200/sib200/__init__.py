@@ -106,6 +106,10 @@ def lib() -> C.CDLL:
         "si_prefill": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_prefill_dev": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_attention_decode_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, vp, vp]),
+        "si_graph_begin": (i32, [vp]),
+        "si_graph_end": (i32, [vp, pp]),
+        "si_graph_launch": (i32, [vp, vp]),
+        "si_graph_free": (None, [vp]),
         "quantize_q8": (None, [vp, vp, i32]),
         "matvec_q4q8": (None, [vp, vp, i32, i32, vp, vp]),
         "si_forget_host_weights": (None, [vp]),
@@ -168,6 +172,17 @@ class Context:
 
     def status(self):
         check(self.L.si_ctx_status(self.h), "si_ctx_status")
+
+    def capture(self, fn) -> "Graph":
+        """Capture the library calls made by fn() into a replayable CUDA graph."""
+        check(self.L.si_graph_begin(self.h), "si_graph_begin")
+        try:
+            fn()
+        finally:
+            g = C.c_void_p()
+            st = self.L.si_graph_end(self.h, C.byref(g))
+        check(st, "si_graph_end")
+        return Graph(self, g)
 
     # -- matrices -----------------------------------------------------------
     def matrix(self, gguf, rows: int, cols: int) -> "Matrix":
@@ -239,6 +254,25 @@ class Context:
         lens = (C.c_int * batch)(*ctx_lens)
         check(self.L.si_attention_decode_dev(self.h, kv.h, C.byref(dm), _p(q), batch, lens,
                                              _p(out)), "si_attention_decode_dev")
+
+
+class Graph:
+    def __init__(self, ctx: Context, h):
+        self.ctx, self.h = ctx, h
+
+    def launch(self):
+        check(self.ctx.L.si_graph_launch(self.ctx.h, self.h), "si_graph_launch")
+
+    def free(self):
+        if self.h:
+            self.ctx.L.si_graph_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 class Matrix:

@@ -77,6 +77,20 @@ def xs_kv_history(oc: Oracle, seed: int, context: int, kvdim: int, kscale=0.25, 
     return kc, vc
 
 
+def assert_layer_close(ref, got, rel=1e-3, what=""):
+    """Layer-output bar (1e-3 relative): ||got-ref|| <= rel*||ref|| and every
+    element within rel * max|ref|.  Near-zero elements are judged against the
+    vector's scale, since a flipped Q8 rounding of one activation moves every
+    output by roughly dx*dw regardless of that output's own size."""
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    assert np.all(np.isfinite(got)), f"{what}: non-finite output"
+    d = got - ref
+    n = np.linalg.norm(d) / max(np.linalg.norm(ref), 1e-30)
+    m = np.max(np.abs(d)) / max(np.max(np.abs(ref)), 1e-30)
+    assert n <= rel and m <= rel, f"{what}: rel-L2 {n:.3g}, max/scale {m:.3g} (bar {rel})"
+
+
 def assert_close(ref, got, atol, rtol, what=""):
     ref = np.asarray(ref, np.float64)
     got = np.asarray(got, np.float64)
