@@ -414,6 +414,7 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
   a.xq = qs;
   a.xd = d;
   a.M = M;
+  a.err = w->ctx ? w->ctx->err : nullptr;
   return a;
 }
 

@@ -48,6 +48,7 @@ struct GemvArgs {
   int8_t *act_qs;          // SwiGLU: Q8 of silu(gate)*up, [M][N]
   uint16_t *act_d;         // [M][N/32]
   int32_t *isum_out;       // [M][N][K/32] block partial sums (parity), or null
+  int *err;                // context device error word (bounded waits), or null
 };
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
 
