@@ -227,6 +227,8 @@ def run_ours(args, rank, world, local_rank):
         """One CUDA graph per weight copy (one step each), and per kernel one graph
         launching that kernel on every copy, so per-kernel device time is measured
         without host launch gaps."""
+        ps.step(b, M, 0)  # one eager pass sizes the library's scratch before capture
+        ctx.sync()
         steps = [ctx.capture(lambda c=c: ps.step(b, M, c)) for c in range(COPIES)]
         per_kernel = {n: ctx.capture(lambda n=n: [ps.kernel(b, M, c, n) for c in range(COPIES)])
                       for n in names}

@@ -11,18 +11,28 @@
 // warps rescale it in fp32 and add it to register accumulators in block order,
 // so results are bit-identical to the reference's serial loop.  Four TMEM
 // accumulators (512 columns) let the MMA run up to four blocks ahead of the
-// rescale.
+// rescale.  The accumulators are pre-set to the integer 0x4B400000 and the MMA
+// accumulates onto it, so each read-back is already the float C + 16*isum; one
+// exact FMA per element folds that into round(isum*dw), then a scalar
+// round-to-nearest multiply by dx and add keep the reference's rounding.
+//
+// The kernel is persistent (one CTA per SM, tiles visited token-tile fastest)
+// so the TMA / unpack / MMA / epilogue pipeline never drains between tiles.
 //
 // Warp roles (384 threads):
-//   warp 0      TMA producer (packed Q4 nibbles, int8 activations) and the
-//               loader of the activation scales for each stage
-//   warp 1      TMEM allocation; lane 0 issues the MMAs and commits
+//   warp 0      TMA producer: packed Q4 nibbles, int8 activations (128-byte
+//               swizzle) and the stage's fp32 activation scales
+//   warp 1      TMEM allocation; lane 0 issues the MMAs, one commit per stage
 //   warps 2-3   nibble unpack: Q4 -> signed int8 in the 128B-swizzled K-major
 //               layout the MMA reads (byte = 16*(q-8), so sums are 16*isum)
-//   warps 4-11  epilogue: TMEM -> registers, rescale, accumulate, store
-// Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  Every
-// wait is bounded (about 2 s); on expiry the kernel records SI_ERR_TIMEOUT in
-// the context's error word, stops all roles, frees its TMEM and returns.
+//   warps 4-11  epilogue (2 per TMEM lane quarter, 64 columns each, read in
+//               double-buffered 16-column chunks): TMEM -> registers, rescale,
+//               accumulate, re-arm, store
+// Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  The
+// epilogue hands each accumulator back to the MMA issuer through a shared-
+// memory release counter instead of an mbarrier round trip.  Every wait is
+// bounded (about 2 s); on expiry the kernel records SI_ERR_TIMEOUT in the
+// context's error word, stops all roles, frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,8 +48,10 @@ constexpr int KBS = 4;                    // blocks per stage
 constexpr int STAGES = 4;
 constexpr int NACC = 4;                   // TMEM accumulators (= blocks per stage)
 constexpr uint32_t TMEM_COLS = NACC * BN; // 512
-constexpr int THREADS = 384;
 constexpr int EPI_WARP0 = 4, EPI_WARPS = 8;
+constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+constexpr uint32_t kMagic = 0x4B400000u;  // bits of 12582912.0f = 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
 
 constexpr int A_INT8_BYTES = BM * 128;       // 16 KB, SW128 K-major
 constexpr int B_BYTES = BN * 128;            // 16 KB, SW128 K-major (TMA swizzled)
@@ -50,8 +62,10 @@ constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_INT8_BYTES;
 constexpr int OFF_PACK = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_DX = OFF_PACK + STAGES * A_PACK_BYTES;
-constexpr int OFF_BAR = OFF_DX + STAGES * DX_BYTES;
-constexpr int NBAR = 5 * STAGES + 2 * NACC;
+constexpr int XCHG_BYTES = 64 * BN * 4;      // SwiGLU up-row hand-off, 32 KB
+constexpr int OFF_XCHG = OFF_DX + STAGES * DX_BYTES;
+constexpr int OFF_BAR = OFF_XCHG + XCHG_BYTES;
+constexpr int NBAR = 4 * STAGES + 2 * NACC;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
 
@@ -60,7 +74,7 @@ static_assert(KBS == NACC, "one accumulator per block of a stage");
 struct Params {
   int N, K, M;              // rows (or gate rows for SwiGLU), inputs, tokens
   const uint16_t *scl, *scl2;
-  const uint16_t *xd;       // [M][K/32] fp16
+  int mtiles, ntiles;       // token tiles, total tiles (persistent schedule)
   const float *bias, *resid;
   float *out;
   int8_t *act_qs;
@@ -100,28 +114,66 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (or the hint, 0.5 ms, runs out) instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(500000u)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: false if the 2 s deadline passes or another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
+  while (!mbar_try_sleep(bar, parity)) {
+    if (*abort) return false;
+    if (globaltimer() - t0 > 2000000000ull) return false;
+  }
+  return true;
+}
+// The same for a whole warp: every lane polls (each observes the phase itself),
+// and all lanes leave together.  A dependent mbarrier wait costs a few hundred
+// cycles on B200 even when the phase is already complete, so the kernel keeps
+// them to one or two per 4-block stage and issues independent ones together.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+__device__ __forceinline__ bool mbar_wait2_warp(uint32_t b1, uint32_t p1, uint32_t b2, uint32_t p2,
+                                                volatile int *abort) {
+  const bool t1 = mbar_try(b1, p1), t2 = mbar_try(b2, p2);  // both in flight at once
+  bool ok = true;
+  if (!t1) ok = mbar_wait(b1, p1, abort);
+  if (ok && !t2) ok = mbar_wait(b2, p2, abort);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+// Release / acquire on a shared-memory counter: the cheap path for the
+// epilogue -> MMA "accumulator free" signal (a plain load to spin on).
+__device__ __forceinline__ void smem_add_release(int *p, int v) {
+  asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
+               : "memory");
+}
+__device__ __forceinline__ int smem_ld_acquire(const int *p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool counter_wait(const int *p, int target, volatile int *abort) {
+  if (smem_ld_acquire(p) >= target) return true;
+  const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 0) {
+    if (smem_ld_acquire(p) >= target) return true;
+    if ((i & 1023) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > 2000000000ull) return false;
     }
   }
-}
-// The same for a whole warp: lane 0 waits, the outcome is broadcast, so all
-// lanes leave together (no divergence at later warp-synchronous steps).
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  // Each lane observes the completed phase itself (its own acquire); the phase
-  // cannot advance again before this warp proceeds, so this returns at once.
-  if (ok) ok = mbar_wait(bar, parity, abort);
-  return __all_sync(0xffffffffu, ok) != 0;
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
                                             uint32_t bar) {
@@ -187,6 +239,71 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// 32 columns of this warp's 32 lanes all set to one value (one source register).
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Packed f32x2 arithmetic as explicit .rn PTX: each lane is one IEEE operation
+// with its own rounding, and explicit instructions are never contracted, so
+// a product followed by a sum keeps the reference's two roundings.
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
@@ -195,37 +312,64 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// Columns per epilogue warp: the 4 TMEM lane quarters x (EPI_WARPS / 4) slices.
+constexpr int NC = BN * 4 / EPI_WARPS;
+constexpr int NCH = NC / 16;  // 16-column chunks per block
+static_assert(NCH >= 2 && NCH % 2 == 0, "chunk double-buffering needs an even chunk count");
+
+// One 16-column chunk h of the rescale: acc[h*16 + c] += ((C+D)*dw16 - C*dw16) * dx.
+// The fold is a packed FMA (exact, see above); product and sum stay scalar so
+// both keep the reference's separate roundings.
+__device__ __forceinline__ void rescale16(float (&acc)[NC], int h, const uint32_t (&d)[16],
+                                          const float4 *dx4, float2 dw2, float2 nc2) {
+#pragma unroll
+  for (int c4 = 0; c4 < 4; ++c4) {
+    const float4 x = dx4[h * 4 + c4];
+    const float2 f0 = make_float2(__uint_as_float(d[4 * c4]), __uint_as_float(d[4 * c4 + 1]));
+    const float2 f1 = make_float2(__uint_as_float(d[4 * c4 + 2]), __uint_as_float(d[4 * c4 + 3]));
+    const float2 p0 = fma2_rn(f0, dw2, nc2), p1 = fma2_rn(f1, dw2, nc2);
+    const int a = h * 16 + 4 * c4;
+    acc[a] = __fadd_rn(acc[a], __fmul_rn(p0.x, x.x));
+    acc[a + 1] = __fadd_rn(acc[a + 1], __fmul_rn(p0.y, x.y));
+    acc[a + 2] = __fadd_rn(acc[a + 2], __fmul_rn(p1.x, x.z));
+    acc[a + 3] = __fadd_rn(acc[a + 3], __fmul_rn(p1.y, x.w));
+  }
+}
+
 template <bool SWIGLU>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_q4q8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-                const __grid_constant__ CUtensorMap tmB, const Params p) {
+                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
+                const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = p.K / 32;
-  const int G = KB / KBS;  // stages over K
-  const int t0 = blockIdx.y * BN;
+  const int G = KB / KBS;  // stages per tile
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  // barrier indices
-  const int B_TMA = 0, B_AREADY = STAGES, B_SEMPTY = 2 * STAGES, B_DXFULL = 3 * STAGES,
-            B_DXEMPTY = 4 * STAGES, B_ACCFULL = 5 * STAGES, B_ACCEMPTY = 5 * STAGES + NACC;
+  // tma_full: packed A + B + activation scales landed; a_ready: A unpacked;
+  // stage_empty: the MMAs of the stage finished; dx_empty: the epilogue used
+  // the stage's scales; acc_full: all four accumulators of a stage written
+  // (one commit per stage).  The epilogue frees each accumulator through a
+  // shared counter (acc_cnt[j] = EPI_WARPS x uses released), which the MMA
+  // thread spins on with plain loads.
+  const int B_TMA = 0, B_AREADY = STAGES, B_SEMPTY = 2 * STAGES, B_DXEMPTY = 3 * STAGES,
+            B_ACCFULL = 4 * STAGES;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC + 16);
+  int *acc_cnt = reinterpret_cast<int *>(smem + OFF_MISC + 32);  // [NACC]
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar(B_TMA + s), 1);
       mbar_init(bar(B_AREADY + s), 64);
       mbar_init(bar(B_SEMPTY + s), 1);
-      mbar_init(bar(B_DXFULL + s), 1);
       mbar_init(bar(B_DXEMPTY + s), EPI_WARPS);
     }
-    for (int j = 0; j < NACC; ++j) {
-      mbar_init(bar(B_ACCFULL + j), 1);
-      mbar_init(bar(B_ACCEMPTY + j), EPI_WARPS);
-    }
+    mbar_init(bar(B_ACCFULL), 1);
+    for (int j = 0; j < NACC; ++j) acc_cnt[j] = 0;
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -244,192 +388,236 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (p.err) atomicCAS(p.err, 0, 6 /* SI_ERR_TIMEOUT */);
     *abort_flag = 1;
   };
+  // Persistent schedule: tiles are visited token-tile fastest, so the CTAs in
+  // flight share each weight tile through L2 while it streams from HBM once.
+  const int tiles_per_row = SWIGLU ? 2 : 4;  // 32-row tiles of each weight matrix per CTA tile
 
   if (warp == 0) {
-    // ---------------- producer: TMA + activation scales ----------------
-    for (int g = 0; g < G; ++g) {
-      const int s = g % STAGES;
-      const uint32_t ph = ((g / STAGES) & 1) ^ 1;
-      if (!mbar_wait_warp(bar(B_SEMPTY + s), ph, abort_flag) ||
-          !mbar_wait_warp(bar(B_DXEMPTY + s), ph, abort_flag)) {
-        if (lane == 0) fail();
-        break;
-      }
-      if (lane == 0) {
-        mbar_expect_tx(bar(B_TMA + s), A_PACK_BYTES + B_BYTES);
-        uint32_t pack = smem_u32(smem + OFF_PACK + s * A_PACK_BYTES);
-        if (SWIGLU) {
-          tma_load_4d(pack, &tmA, 0, 0, g * KBS, blockIdx.x * 2, bar(B_TMA + s));
-          tma_load_4d(pack + A_PACK_BYTES / 2, &tmA2, 0, 0, g * KBS, blockIdx.x * 2,
-                      bar(B_TMA + s));
-        } else {
-          tma_load_4d(pack, &tmA, 0, 0, g * KBS, blockIdx.x * 4, bar(B_TMA + s));
+    // ---------------- producer ----------------
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+      const int nt = tile / p.mtiles, t0 = (tile % p.mtiles) * BN;
+      for (int g = 0; g < G; ++g, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = ((it / STAGES) & 1) ^ 1;
+        if (!mbar_wait2_warp(bar(B_SEMPTY + s), ph, bar(B_DXEMPTY + s), ph, abort_flag)) {
+          if (lane == 0) fail();
+          ok = false;
+          break;
         }
-        tma_load_2d(smem_u32(smem + OFF_B + s * B_BYTES), &tmB, g * 128, t0, bar(B_TMA + s));
+        if (lane == 0) {
+          const uint32_t full = bar(B_TMA + s);
+          mbar_expect_tx(full, A_PACK_BYTES + B_BYTES + DX_BYTES);
+          const uint32_t pack = smem_u32(smem + OFF_PACK + s * A_PACK_BYTES);
+          tma_load_2d(pack, &tmA, g * 256, nt * tiles_per_row, full);
+          if (SWIGLU) tma_load_2d(pack + A_PACK_BYTES / 2, &tmA2, g * 256, nt * 2, full);
+          tma_load_2d(smem_u32(smem + OFF_B + s * B_BYTES), &tmB, g * 128, t0, full);
+          tma_load_2d(smem_u32(smem + OFF_DX + s * DX_BYTES), &tmD, t0, g * KBS, full);
+        }
+        __syncwarp();
       }
-      float *dx = reinterpret_cast<float *>(smem + OFF_DX + s * DX_BYTES);
-#pragma unroll
-      for (int i = 0; i < BN / 32; ++i) {
-        const int tl = lane + 32 * i, t = t0 + tl;
-        uint2 v = make_uint2(0, 0);
-        if (t < p.M) v = __ldg(reinterpret_cast<const uint2 *>(p.xd + (size_t)t * KB + g * KBS));
-        dx[0 * BN + tl] = f16_to_f32((uint16_t)v.x);
-        dx[1 * BN + tl] = f16_to_f32((uint16_t)(v.x >> 16));
-        dx[2 * BN + tl] = f16_to_f32((uint16_t)v.y);
-        dx[3 * BN + tl] = f16_to_f32((uint16_t)(v.y >> 16));
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_DXFULL + s));
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_i8(BM, BN);
-      for (int g = 0; g < G; ++g) {
-        const int s = g % STAGES;
-        if (!mbar_wait(bar(B_AREADY + s), (g / STAGES) & 1, abort_flag)) {
-          fail();
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + OFF_A + s * A_INT8_BYTES);
-        const uint32_t b0 = smem_u32(smem + OFF_B + s * B_BYTES);
-        bool ok = true;
-        for (int j = 0; j < KBS; ++j) {
-          if (!mbar_wait(bar(B_ACCEMPTY + j), (g & 1) ^ 1, abort_flag)) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+        for (int g = 0; g < G; ++g, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(bar(B_AREADY + s), (it / STAGES) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          mma_i8(tmem_base + j * BN, smem_desc(a0 + 32 * j), smem_desc(b0 + 32 * j), idesc, 0);
-          mma_commit(bar(B_ACCFULL + j));
+          const uint32_t a0 = smem_u32(smem + OFF_A + s * A_INT8_BYTES);
+          const uint32_t b0 = smem_u32(smem + OFF_B + s * B_BYTES);
+          for (int j = 0; j < KBS && ok; ++j) {
+            // Use number `it` of accumulator j needs the epilogue to have
+            // (re)armed it with the magic constant it+1 times (each of its warps).
+            if (!counter_wait(&acc_cnt[j], EPI_WARPS * (it + 1), abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            mma_i8(tmem_base + j * BN, smem_desc(a0 + 32 * j), smem_desc(b0 + 32 * j), idesc, 1);
+          }
+          if (!ok) break;
+          mma_commit(bar(B_ACCFULL));  // phase `it`: the stage's four block sums are in TMEM
+          mma_commit(bar(B_SEMPTY + s));
         }
-        if (!ok) {
-          fail();
-          break;
-        }
-        mma_commit(bar(B_SEMPTY + s));
       }
+      if (!ok) fail();
     }
   } else if (warp < EPI_WARP0) {
     // ---------------- nibble unpack ----------------
     const int u = threadIdx.x - 64;  // 0..63
-    for (int g = 0; g < G; ++g) {
-      const int s = g % STAGES;
-      if (!mbar_wait_warp(bar(B_TMA + s), (g / STAGES) & 1, abort_flag)) {
-        fail();
-        break;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+      for (int g = 0; g < G; ++g, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait_warp(bar(B_TMA + s), (it / STAGES) & 1, abort_flag)) {
+          if (lane == 0) fail();
+          ok = false;
+          break;
+        }
+        const uint4 *pack = reinterpret_cast<const uint4 *>(smem + OFF_PACK + s * A_PACK_BYTES);
+        uint8_t *a = smem + OFF_A + s * A_INT8_BYTES;
+#pragma unroll 4
+        for (int i = 0; i < (BM * KBS) / 64; ++i) {
+          const int idx = i * 64 + u;  // [tile(4)][block(4)][row(32)] x 16 bytes
+          const int r32 = idx & 31, blk = (idx >> 5) & 3, tl = idx >> 7;
+          const int r = tl * 32 + r32;
+          const uint4 w = pack[idx];
+          const uint4 lo = make_uint4((w.x << 4) & 0xF0F0F0F0u, (w.y << 4) & 0xF0F0F0F0u,
+                                      (w.z << 4) & 0xF0F0F0F0u, (w.w << 4) & 0xF0F0F0F0u);
+          const uint4 hi = make_uint4(w.x & 0xF0F0F0F0u, w.y & 0xF0F0F0F0u, w.z & 0xF0F0F0F0u,
+                                      w.w & 0xF0F0F0F0u);
+          uint8_t *row = a + (r >> 3) * 1024 + (r & 7) * 128;
+          *reinterpret_cast<uint4 *>(row + (((2 * blk) ^ (r & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4 *>(row + (((2 * blk + 1) ^ (r & 7)) << 4)) = hi;
+        }
+        fence_proxy_async();
+        mbar_arrive(bar(B_AREADY + s));
       }
-      const uint4 *pack = reinterpret_cast<const uint4 *>(smem + OFF_PACK + s * A_PACK_BYTES);
-      uint8_t *a = smem + OFF_A + s * A_INT8_BYTES;
-#pragma unroll
-      for (int i = 0; i < (BM * KBS) / 64; ++i) {
-        const int idx = i * 64 + u;  // [tile(4)][block(4)][row(32)]
-        const int r32 = idx & 31, blk = (idx >> 5) & 3, tile = idx >> 7;
-        const int r = tile * 32 + r32;
-        const uint4 w = pack[idx];
-        const uint4 lo = make_uint4((w.x << 4) & 0xF0F0F0F0u, (w.y << 4) & 0xF0F0F0F0u,
-                                    (w.z << 4) & 0xF0F0F0F0u, (w.w << 4) & 0xF0F0F0F0u);
-        const uint4 hi = make_uint4(w.x & 0xF0F0F0F0u, w.y & 0xF0F0F0F0u, w.z & 0xF0F0F0F0u,
-                                    w.w & 0xF0F0F0F0u);
-        uint8_t *row = a + (r >> 3) * 1024 + (r & 7) * 128;
-        *reinterpret_cast<uint4 *>(row + (((2 * blk) ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4 *>(row + (((2 * blk + 1) ^ (r & 7)) << 4)) = hi;
-      }
-      fence_proxy_async();
-      mbar_arrive(bar(B_AREADY + s));
     }
   } else {
     // ---------------- epilogue ----------------
+    // Warp e: lane quarter q = warp % 4, column slice hc = e / 4 (NC columns).
+    // Each warp walks its columns of every block in 16-column chunks,
+    // software-pipelined: the TMEM load of chunk k+1 is in flight while chunk k
+    // is rescaled, and the accumulator's re-arm store overlaps the last chunk.
     const int e = warp - EPI_WARP0;
-    const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int hc = e >> 2;            // column half
-    const int r = q * 32 + lane;      // tile row
-    // Weight row and scale pointer of this thread.
-    int n;
-    const uint16_t *sc;
-    if (SWIGLU) {
-      n = blockIdx.x * 64 + (r & 63);
-      sc = (r < 64 ? p.scl : p.scl2);
-    } else {
-      n = blockIdx.x * BM + r;
-      sc = p.scl;
-    }
-    const uint16_t *scrow = sc + (size_t)(n >> 5) * KB * 32 + (n & 31);
-    float acc[64];
-    const float init = (!SWIGLU && p.bias) ? p.bias[n] : 0.0f;
-#pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = init;
+    const int q = warp & 3;       // TMEM lane quarter this warp may access
+    const int hc = e >> 2;        // column slice of the tile
+    const int r = q * 32 + lane;  // tile row
+    const uint32_t tcol = tmem_base + ((uint32_t)(q * 32) << 16) + hc * NC;
+    // Accumulators hold C + 16*isum as float bits: the MMA accumulates onto the
+    // integer 0x4B400000 (C = 1.5*2^23 as a float), so C + D is an exactly
+    // representable float in [2^23, 2^24) and no int->float conversion is needed.
+    for (int j = 0; j < NACC; ++j)
+      for (int f = 0; f < NC / 32; ++f) tmem_fill32(tcol + j * BN + 32 * f, kMagic);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int j = 0; j < NACC; ++j) smem_add_release(&acc_cnt[j], 1);
+    float *xchg = reinterpret_cast<float *>(smem + OFF_XCHG);  // [64 rows][BN]
+    int it = 0;
     bool ok = true;
-    uint16_t dw_next = __ldg(scrow);
-    for (int b = 0; b < KB && ok; ++b) {
-      const int g = b / KBS, j = b % KBS, s = g % STAGES;
-      const float dw16 = __fmul_rn(f16_to_f32(dw_next), 0.0625f);  // sums are 16*isum
-      if (b + 1 < KB) dw_next = __ldg(scrow + (size_t)(b + 1) * 32);
-      if (j == 0 && !mbar_wait_warp(bar(B_DXFULL + s), (g / STAGES) & 1, abort_flag)) {
-        ok = false;
-        break;
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+      const int nt = tile / p.mtiles, t0 = (tile % p.mtiles) * BN;
+      int n;
+      const uint16_t *sc;
+      if (SWIGLU) {
+        n = nt * 64 + (r & 63);
+        sc = (r < 64 ? p.scl : p.scl2);
+      } else {
+        n = nt * BM + r;
+        sc = p.scl;
       }
-      if (!mbar_wait_warp(bar(B_ACCFULL + j), g & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t d0[32], d1[32];
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + j * BN + hc * 64;
-      tmem_ld32(taddr, d0);
-      tmem_ld32(taddr + 32, d1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_ACCEMPTY + j));
-      const float4 *dx4 =
-          reinterpret_cast<const float4 *>(smem + OFF_DX + s * DX_BYTES) + (j * BN + hc * 64) / 4;
+      const uint16_t *scrow = sc + (size_t)(n >> 5) * KB * 32 + (n & 31);
+      float acc[NC];
+      const float init = (!SWIGLU && p.bias) ? p.bias[n] : 0.0f;
 #pragma unroll
-      for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 x = dx4[c4];
-        const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int c = c4 * 4 + k;
-          const int iv = (int)(c < 32 ? d0[c] : d1[c - 32]);
-          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn((float)iv, dw16), xs[k]));
-        }
-      }
-      if (j == KBS - 1) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_DXEMPTY + s));
-      }
-    }
-    if (!ok && lane == 0) fail();
-    if (!SWIGLU) {
+      for (int c = 0; c < NC; ++c) acc[c] = init;
+      const int it0 = it;  // stage counter at the tile's first block
+      uint32_t dbuf[2][16];
+      // Prime: block 0 of the tile, chunk 0.
+      if (!mbar_wait2_warp(bar(B_TMA + it0 % STAGES), (it0 / STAGES) & 1, bar(B_ACCFULL),
+                           it0 & 1, abort_flag))
+        ok = false;
       if (ok) {
+        tc_fence_after();
+        tmem_ld16(tcol, dbuf[0]);
+        tmem_wait_ld();
+      }
+      uint16_t dw_cur = __ldg(scrow);
+      for (int b = 0; ok && b < KB; ++b) {
+        const int j = b % KBS, itb = it0 + b / KBS, s = itb % STAGES;
+        const uint16_t dw_nx = (b + 1 < KB) ? __ldg(scrow + (size_t)(b + 1) * 32) : (uint16_t)0;
+        // (C + D) * dw/16 - C * dw/16 = isum * dw in one rounding: C*dw/16 is exact
+        // (dw has 11 significant bits, C/16 = 3*2^18), so this equals the
+        // reference's (float)isum * dw.
+        const float dw16 = __fmul_rn(f16_to_f32(dw_cur), 0.0625f);
+        const float ncdw = -__fmul_rn(kMagicF, dw16);
+        const float2 dw2 = make_float2(dw16, dw16), nc2 = make_float2(ncdw, ncdw);
+        const float4 *dx4 = reinterpret_cast<const float4 *>(smem + OFF_DX + s * DX_BYTES) +
+                            (j * BN + hc * NC) / 4;
+        const uint32_t ta = tcol + j * BN;
+        bool more = b + 1 < KB;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int t = t0 + hc * 64 + c;
+        for (int h = 0; h < NCH; ++h) {  // dbuf[h & 1] holds chunk h on entry
+          if (h + 1 < NCH) {
+            tmem_ld16(ta + (h + 1) * 16, dbuf[(h + 1) & 1]);
+          } else {
+            // Every chunk of block b is in registers: re-arm the accumulator and
+            // start block b+1 (next accumulator, maybe next stage) into dbuf[0].
+#pragma unroll
+            for (int f = 0; f < NC / 32; ++f) tmem_fill32(ta + 32 * f, kMagic);
+            // The next block of the same stage is already in TMEM (one commit per
+            // stage): start it now.  A new stage is waited for only after this
+            // accumulator is released below -- its MMAs need that release.
+            if (more && j != KBS - 1) {
+              tc_fence_after();
+              tmem_ld16(tcol + (j + 1) * BN, dbuf[0]);
+            }
+          }
+          rescale16(acc, h, dbuf[h & 1], dx4, dw2, nc2);
+          if (h + 1 < NCH) tmem_wait_ld();
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) smem_add_release(&acc_cnt[j], 1);
+        if (j == KBS - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_DXEMPTY + s));
+          if (more) {
+            // A new stage: its scales and all four of its block sums.
+            const int it1 = itb + 1;
+            if (!mbar_wait2_warp(bar(B_TMA + it1 % STAGES), (it1 / STAGES) & 1, bar(B_ACCFULL),
+                                 it1 & 1, abort_flag)) {
+              ok = false;
+              more = false;
+            } else {
+              tc_fence_after();
+              tmem_ld16(tcol, dbuf[0]);
+            }
+          }
+        }
+        if (more) tmem_wait_ld();
+        dw_cur = dw_nx;
+      }
+      it = it0 + G;
+      if (!ok && lane == 0) fail();
+      if (!SWIGLU) {
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const int t = t0 + hc * NC + c;
           if (t < p.M) {
             const size_t o = (size_t)t * p.N + n;
             p.out[o] = p.resid ? __fadd_rn(p.resid[o], acc[c]) : acc[c];
           }
         }
-      }
-    } else {
-      {
-        // Up rows (lanes 64..127) hand their sums to the gate rows through smem
-        // (the A ring is idle once every accumulator has been consumed).  Every
-        // epilogue warp reaches the named barrier, aborted or not.
-        float *xchg = reinterpret_cast<float *>(smem + OFF_A);  // [64 rows][BN]
+      } else {
+        // Up rows (lanes 64..127) hand their sums to the gate rows.  Every
+        // epilogue warp reaches both named barriers, aborted or not.
         if (ok && q >= 2) {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) xchg[(size_t)(r - 64) * BN + hc * 64 + c] = acc[c];
+          for (int c = 0; c < NC; ++c) xchg[(size_t)(r - 64) * BN + hc * NC + c] = acc[c];
         }
         asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32));
         if (ok && !*abort_flag && q < 2) {
           const int I = p.N;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const int t = t0 + hc * 64 + c;
-            const float act = silu_mul(acc[c], xchg[(size_t)r * BN + hc * 64 + c]);
+          for (int c = 0; c < NC; ++c) {
+            const int t = t0 + hc * NC + c;
+            const float act = silu_mul(acc[c], xchg[(size_t)r * BN + hc * NC + c]);
             uint16_t d16;
             const int8_t qv = q8_lane(act, d16);
             if (t < p.M) {
@@ -440,6 +628,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+        asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32));  // xchg free for the next tile
+        if (!ok || *abort_flag) break;
       }
     }
   }
@@ -451,6 +641,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(TMEM_COLS));
   }
+}
+
+// Activation scales fp16 [M][KB] -> fp32 [KB][Mp] (Mp = M rounded up to 4, zero
+// padded): the layout the GEMM's TMA loads per stage.
+__global__ void k_scales_t(const uint16_t *__restrict__ xd, int M, int KB, int Mp,
+                           float *__restrict__ dT) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+  if (t < Mp) dT[(size_t)b * Mp + t] = t < M ? f16_to_f32(xd[(size_t)t * KB + b]) : 0.0f;
 }
 
 // ---------------------------------------------------------------------------
@@ -469,27 +667,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-tile SoA nibbles as a 4-D tensor: (16 bytes, 32 rows, KB blocks, N/32 tiles).
-bool map_nibbles(CUtensorMap *m, const uint8_t *nib, int N, int KB, int tiles_per_box) {
-  cuuint64_t dims[4] = {16, 32, (cuuint64_t)KB, (cuuint64_t)(N / 32)};
-  cuuint64_t strides[3] = {16, 512, (cuuint64_t)KB * 512};
-  cuuint32_t box[4] = {16, 32, (cuuint32_t)KBS, (cuuint32_t)tiles_per_box};
+static bool encode(CUtensorMap *m, CUtensorMapDataType dt, int rank, const void *base,
+                   const cuuint64_t *dims, const cuuint64_t *strides, const cuuint32_t *box,
+                   CUtensorMapSwizzle swz) {
   cuuint32_t es[4] = {1, 1, 1, 1};
-  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(nib), dims,
-                     strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// int8 activations [M][K] as 128-byte swizzled K-major boxes of (128 bytes, BN rows).
-bool map_acts(CUtensorMap *m, const int8_t *xq, int M, int K) {
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  cuuint64_t strides[1] = {(cuuint64_t)K};
-  cuuint32_t box[2] = {128, (cuuint32_t)BN};
-  cuuint32_t es[2] = {1, 1};
-  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(xq), dims, strides,
-                     box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return encode_fn()(m, dt, rank, const_cast<void *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -499,32 +682,69 @@ bool gemm_tc_supported(int N, int K, int M) {
   return M >= 1 && K % 128 == 0 && N % 128 == 0 && tc::encode_fn() != nullptr;
 }
 
+size_t gemm_tc_scratch_bytes(int K, int M) {
+  return (size_t)(K / 32) * ((M + 3) & ~3) * sizeof(float);
+}
+
 cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   using namespace tc;
   if (a.M <= 0) return cudaSuccess;
-  if (!gemm_tc_supported(swiglu ? 2 * a.N : a.N, a.K, a.M) || (swiglu && a.N % 64))
+  if (!gemm_tc_supported(swiglu ? 2 * a.N : a.N, a.K, a.M) || (swiglu && a.N % 64) || !a.scratch)
     return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.xq) & 15) || (reinterpret_cast<uintptr_t>(a.nib) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.xd) & 7))
+      (reinterpret_cast<uintptr_t>(a.scratch) & 15) ||
+      (swiglu && (reinterpret_cast<uintptr_t>(a.nib2) & 15)))
     return cudaErrorInvalidValue;
-  CUtensorMap tmA, tmA2, tmB;
-  const int KB = a.K / 32;
-  if (!map_nibbles(&tmA, a.nib, a.N, KB, swiglu ? 2 : 4)) return cudaErrorInvalidValue;
+  const int KB = a.K / 32, Mp = (a.M + 3) & ~3;
+  float *dT = a.scratch;
+  k_scales_t<<<dim3((Mp + 127) / 128, KB), 128, 0, s>>>(a.xd, a.M, KB, Mp, dT);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  CUtensorMap tmA, tmA2, tmB, tmD;
+  // Nibbles of a 32-row tile are contiguous over K ([KB][32][16] bytes): a 2-D view
+  // of 8-byte elements, (KB*64, rows/32), box = 4 blocks x (4 or 2) row-tiles.
+  const int rt = a.N / 32, per = swiglu ? 2 : 4;
+  cuuint64_t dA[2] = {(cuuint64_t)KB * 64, (cuuint64_t)rt};
+  cuuint64_t sA[1] = {(cuuint64_t)KB * 512};
+  cuuint32_t bA[2] = {256, (cuuint32_t)per};
+  if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dA, sA, bA,
+              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
   if (swiglu) {
-    if (!map_nibbles(&tmA2, a.nib2, a.N, KB, 2)) return cudaErrorInvalidValue;
+    if (!encode(&tmA2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dA, sA, bA,
+                CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
   } else {
     tmA2 = tmA;
   }
-  if (!map_acts(&tmB, a.xq, a.M, a.K)) return cudaErrorInvalidValue;
+  cuuint64_t dB[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+  cuuint64_t sB[1] = {(cuuint64_t)a.K};
+  cuuint32_t bB[2] = {128, (cuuint32_t)BN};
+  if (!encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.xq, dB, sB, bB,
+              CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  cuuint64_t dD[2] = {(cuuint64_t)Mp, (cuuint64_t)KB};
+  cuuint64_t sD[1] = {(cuuint64_t)Mp * 4};
+  cuuint32_t bD[2] = {(cuuint32_t)BN, (cuuint32_t)KBS};
+  if (!encode(&tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dT, dD, sD, bD,
+              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+
+  static int sms = 0;
+  if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess)
+    sms = 148;
   Params p{};
   p.N = a.N; p.K = a.K; p.M = a.M;
-  p.scl = a.scl; p.scl2 = a.scl2; p.xd = a.xd; p.bias = a.bias; p.resid = a.resid;
+  p.scl = a.scl; p.scl2 = a.scl2; p.bias = a.bias; p.resid = a.resid;
   p.out = a.out; p.act_qs = a.act_qs; p.act_d = a.act_d; p.err = a.err;
-  dim3 grid(swiglu ? a.N / 64 : a.N / BM, (a.M + BN - 1) / BN);
+  p.mtiles = (a.M + BN - 1) / BN;
+  p.ntiles = (swiglu ? a.N / 64 : a.N / BM) * p.mtiles;
+  const int grid = p.ntiles < sms ? p.ntiles : sms;
   auto kern = swiglu ? k_gemm_q4q8<true> : k_gemm_q4q8<false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  kern<<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmA2, tmB, p);
+  kern<<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmA2, tmB, tmD, p);
   return cudaGetLastError();
 }
 

@@ -104,6 +104,7 @@ struct si_ctx {
   int *err = nullptr;           // device error word
   DevBuf work;                  // layer-schedule arena
   DevBuf idx;                   // per-token index arrays
+  DevBuf gemm;                  // tcgen05 GEMM scratch (transposed activation scales)
   int *pinned_idx = nullptr;    // host staging for idx
   size_t pinned_idx_n = 0;
   cudaEvent_t ev[12] = {};
@@ -218,6 +219,7 @@ extern "C" SI_API void si_ctx_destroy(si_ctx *c) {
   cudaFree(c->err);
   c->work.release();
   c->idx.release();
+  c->gemm.release();
   if (c->pinned_idx) cudaFreeHost(c->pinned_idx);
   for (auto &e : c->ev)
     if (e) cudaEventDestroy(e);
@@ -431,6 +433,8 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
     if (!si::gemm_tc_supported(w->rows, w->cols, M))
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
                   w->cols, M);
+    SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(w->cols, M)));
+    a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, false, ctx->stream));
   } else {
     SI_CUDA(si::launch_gemv(a, false, ctx->stream));
@@ -485,6 +489,8 @@ extern "C" SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate,
   a.act_qs = act_qs;
   a.act_d = act_d;
   if (M > 8 && si::gemm_tc_supported(gate->rows, gate->cols, M)) {
+    SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(gate->cols, M)));
+    a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, true, ctx->stream));
   } else {
     SI_CUDA(si::launch_gemv(a, true, ctx->stream));

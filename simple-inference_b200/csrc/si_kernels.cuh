@@ -49,12 +49,15 @@ struct GemvArgs {
   uint16_t *act_d;         // [M][N/32]
   int32_t *isum_out;       // [M][N][K/32] block partial sums (parity), or null
   int *err;                // context device error word (bounded waits), or null
+  float *scratch;          // tcgen05 GEMM: gemm_tc_scratch_bytes() of device memory
 };
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
 
 // ---- gemm_tc.cu (tcgen05) ------------------------------------------------------
 cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s);
 bool gemm_tc_supported(int N, int K, int M);
+// Scratch the GEMM needs for its transposed fp32 activation scales.
+size_t gemm_tc_scratch_bytes(int K, int M);
 
 // ---- rope_kv.cu -------------------------------------------------------------
 struct RopeKvArgs {
