@@ -104,6 +104,13 @@ typedef struct {                                                /* defines.h:35-
     float rms, q8_input, q_proj, k_proj, v_proj, rope_cache, attention, q8_output, out_proj;
 } phase_t;
 typedef enum { ATTENTION_STANDARD = 0, ATTENTION_FLASH = 1 } attention_method_t;
+#ifdef __cplusplus
+static_assert(sizeof(block_q8_0) == 34, "block_q8_0 must be the reference's 34 bytes");
+static_assert(sizeof(phase_t) == 9 * sizeof(float), "phase_t must be 9 floats");
+#else
+_Static_assert(sizeof(block_q8_0) == 34, "block_q8_0 must be the reference's 34 bytes");
+_Static_assert(sizeof(phase_t) == 9 * sizeof(float), "phase_t must be 9 floats");
+#endif
 #endif
 
 /* ------------------------------------------------------------------------ */
