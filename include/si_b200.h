@@ -188,6 +188,23 @@ SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs
 SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                       const uint16_t *d_dev, int M, const float *bias_dev,
                                       float *out_dev, int kernel);
+/* The tcgen05 GEMM of si_matmul_dev_kernel(..., 1) with the same results, but
+ * allocating nothing: its scratch (the transposed fp32 activation scales,
+ * (cols/32) * round_up(M, 4) * 4 bytes) is a fixed array of
+ * SI_STATIC_GEMM_SCRATCH_BYTES inside the library, which every GPU that loads
+ * the library holds until the process exits.  For callers that must not
+ * allocate device memory while they run (an allocator that already owns the
+ * free memory, or a loop that cannot take cudaMalloc's synchronisation).
+ * Larger shapes fail with SI_ERR_INVALID.  The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress) and should come before
+ * any stream capture.  All calls on a device share the one array: calls that
+ * overlap on the GPU (other streams, other contexts of the same device) race
+ * and must be serialised by the caller.  This entry point has no counterpart
+ * in the reference. */
+#define SI_STATIC_GEMM_SCRATCH_BYTES (4 * 1024 * 1024)
+SI_API si_status si_matmul_tc_static_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
+                                         const uint16_t *d_dev, int M, const float *bias_dev,
+                                         float *out_dev);
 /* Per-(row, block) int32 partial sums [M][rows][cols/32] (parity checks). */
 SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                     int M, int32_t *isum_dev);

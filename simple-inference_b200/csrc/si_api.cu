@@ -457,6 +457,68 @@ extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w
   return matmul(ctx, w, qs, d, M, bias, nullptr, out, kernel);
 }
 
+// ----------------------------------------------------------------------------
+// tcgen05 GEMM on library-owned scratch: allocates nothing per call
+// ----------------------------------------------------------------------------
+// si_matmul_dev grows a per-context device buffer on demand for the GEMM's
+// transposed fp32 activation scales, which means cudaMalloc (and the device
+// synchronisation it implies) on the first call at a new size.  Callers that
+// may not allocate at that point -- a serving loop whose allocator has already
+// claimed the device's free memory, or a latency-bound loop that cannot afford
+// the implicit synchronisation -- use si_matmul_tc_static_dev instead.  Its
+// scratch is this fixed array, part of the library's device image: every GPU
+// that loads the library holds these SI_STATIC_GEMM_SCRATCH_BYTES until the
+// process exits.
+static __device__ __align__(256) float
+    g_static_gemm_scratch[SI_STATIC_GEMM_SCRATCH_BYTES / sizeof(float)];
+
+// In host code g_static_gemm_scratch is only a stand-in that names the
+// symbol; the device address comes from cudaGetSymbolAddress, resolved once
+// per device with that device current and cached here.
+static std::mutex g_static_scratch_mu;
+static float *g_static_scratch_addr[64] = {};
+
+static si_status static_gemm_scratch(int device, float **out) {
+  SI_CHECK(device >= 0 && device < 64, "device %d beyond the static scratch table", device);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_addr[device]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_gemm_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(SI_ERR_CUDA, "cudaGetSymbolAddress(static GEMM scratch) on device %d: %s",
+                  device, cudaGetErrorString(e));
+    g_static_scratch_addr[device] = static_cast<float *>(p);
+  }
+  *out = g_static_scratch_addr[device];
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_matmul_tc_static_dev(si_ctx *ctx, const si_matrix *w,
+                                                    const int8_t *qs, const uint16_t *d, int M,
+                                                    const float *bias, float *out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(w && qs && d && out, "null pointer");
+  SI_CHECK(M >= 0, "negative token count");
+  if (!si::gemm_tc_supported(w->rows, w->cols, M > 0 ? M : 1))
+    return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
+                w->cols, M);
+  const size_t need = si::gemm_tc_scratch_bytes(w->cols, M);
+  SI_CHECK(need <= SI_STATIC_GEMM_SCRATCH_BYTES,
+           "static GEMM scratch too small: K=%d, M=%d needs %zu bytes, the maximum is %d "
+           "((K/32) * round_up(M, 4) * 4 bytes)",
+           w->cols, M, need, SI_STATIC_GEMM_SCRATCH_BYTES);
+  float *scratch = nullptr;
+  SI_TRY(static_gemm_scratch(ctx->device, &scratch));
+  // The GEMM rewrites every scratch word it reads (scales and zero padding)
+  // earlier in the same stream, so the array's previous contents never matter.
+  si::GemvArgs a = gemv_args(w, qs, d, M);
+  a.bias = bias;
+  a.out = out;
+  a.scratch = scratch;
+  SI_CUDA(si::launch_gemm_tc(a, false, ctx->stream));
+  return SI_OK;
+}
+
 extern "C" SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs,
                                                int M, int32_t *isum) {
   SI_TRY(set_device(ctx));

@@ -88,6 +88,7 @@ def lib() -> C.CDLL:
         "si_q8_from_blocks_dev": (i32, [vp, vp, i32, i32, vp, vp]),
         "si_matmul_dev": (i32, [vp, vp, vp, vp, i32, vp, vp]),
         "si_matmul_dev_kernel": (i32, [vp, vp, vp, vp, i32, vp, vp, i32]),
+        "si_matmul_tc_static_dev": (i32, [vp, vp, vp, vp, i32, vp, vp]),
         "si_block_isums_dev": (i32, [vp, vp, vp, i32, vp]),
         "si_gateup_q8_dev": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, vp]),
         "si_rmsnorm_q8_dev": (i32, [vp, vp, vp, i32, i32, f32, vp, vp, vp]),
