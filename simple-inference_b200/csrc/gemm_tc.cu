@@ -20,13 +20,14 @@
 // so the TMA / unpack / MMA / epilogue pipeline never drains between tiles.
 //
 // Warp roles (384 threads):
-//   warp 0      TMA producer: packed Q4 nibbles, int8 activations (128-byte
-//               swizzle) and the stage's fp32 activation scales
+//   warp 0      TMA producer: packed Q4 nibbles and their fp16 scales, int8
+//               activations (128-byte swizzle) and the stage's fp32
+//               activation scales
 //   warp 1      TMEM allocation; lane 0 issues the MMAs, one commit per stage
 //   warps 2-3   nibble unpack: Q4 -> signed int8 in the 128B-swizzled K-major
 //               layout the MMA reads (byte = 16*(q-8), so sums are 16*isum)
 //   warps 4-11  epilogue (2 per TMEM lane quarter, 64 columns each, read in
-//               double-buffered 16-column chunks): TMEM -> registers, rescale,
+//               double-buffered 32-column chunks): TMEM -> registers, rescale,
 //               accumulate, re-arm, store
 // Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  The
 // epilogue hands each accumulator back to the MMA issuer through a shared-
@@ -57,13 +58,15 @@ constexpr int A_INT8_BYTES = BM * 128;       // 16 KB, SW128 K-major
 constexpr int B_BYTES = BN * 128;            // 16 KB, SW128 K-major (TMA swizzled)
 constexpr int A_PACK_BYTES = BM * KBS * 16;  // 8 KB
 constexpr int DX_BYTES = KBS * BN * 4;       // 2 KB
+constexpr int SW_BYTES = BM * KBS * 2;       // 1 KB: weight scales [4 row tiles][4 blocks][32]
 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_INT8_BYTES;
 constexpr int OFF_PACK = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_DX = OFF_PACK + STAGES * A_PACK_BYTES;
 constexpr int XCHG_BYTES = 64 * BN * 4;      // SwiGLU up-row hand-off, 32 KB
-constexpr int OFF_XCHG = OFF_DX + STAGES * DX_BYTES;
+constexpr int OFF_SW = OFF_DX + STAGES * DX_BYTES;
+constexpr int OFF_XCHG = OFF_SW + STAGES * SW_BYTES;
 constexpr int OFF_BAR = OFF_XCHG + XCHG_BYTES;
 constexpr int NBAR = 4 * STAGES + 2 * NACC;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
@@ -168,6 +171,9 @@ __device__ __forceinline__ bool counter_wait(const int *p, int target, volatile 
   if (smem_ld_acquire(p) >= target) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
+    // Back off between polls: the poller shares its SM sub-partition with two
+    // epilogue warps, and a hot spin would take a third of their issue slots.
+    __nanosleep(32);
     if (smem_ld_acquire(p) >= target) return true;
     if ((i & 1023) == 0) {
       if (*abort) return false;
@@ -261,14 +267,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
-// 32 columns of this warp's 32 lanes all set to one value (one source register).
+template <int CW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CW]) {
+  if constexpr (CW == 16) tmem_ld16(taddr, r);
+  else tmem_ld32(taddr, r);
+}
+// 32 columns of this warp's 32 lanes all set to one value, as four 8-column
+// stores so the value occupies 8 registers rather than 32.
 __device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
+            taddr + 8 * k),
+        "r"(v)
+        : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -314,21 +327,22 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // ---------------------------------------------------------------------------
 // Columns per epilogue warp: the 4 TMEM lane quarters x (EPI_WARPS / 4) slices.
 constexpr int NC = BN * 4 / EPI_WARPS;
-constexpr int NCH = NC / 16;  // 16-column chunks per block
+constexpr int CW = 16;        // columns per TMEM load chunk
+constexpr int NCH = NC / CW;  // chunks per block
 static_assert(NCH >= 2 && NCH % 2 == 0, "chunk double-buffering needs an even chunk count");
 
-// One 16-column chunk h of the rescale: acc[h*16 + c] += ((C+D)*dw16 - C*dw16) * dx.
+// One CW-column chunk h of the rescale: acc[h*CW + c] += ((C+D)*dw16 - C*dw16) * dx.
 // The fold is a packed FMA (exact, see above); product and sum stay scalar so
 // both keep the reference's separate roundings.
-__device__ __forceinline__ void rescale16(float (&acc)[NC], int h, const uint32_t (&d)[16],
-                                          const float4 *dx4, float2 dw2, float2 nc2) {
+__device__ __forceinline__ void rescale(float (&acc)[NC], int h, const uint32_t (&d)[CW],
+                                        const float4 *dx4, float2 dw2, float2 nc2) {
 #pragma unroll
-  for (int c4 = 0; c4 < 4; ++c4) {
-    const float4 x = dx4[h * 4 + c4];
+  for (int c4 = 0; c4 < CW / 4; ++c4) {
+    const float4 x = dx4[h * (CW / 4) + c4];
     const float2 f0 = make_float2(__uint_as_float(d[4 * c4]), __uint_as_float(d[4 * c4 + 1]));
     const float2 f1 = make_float2(__uint_as_float(d[4 * c4 + 2]), __uint_as_float(d[4 * c4 + 3]));
     const float2 p0 = fma2_rn(f0, dw2, nc2), p1 = fma2_rn(f1, dw2, nc2);
-    const int a = h * 16 + 4 * c4;
+    const int a = h * CW + 4 * c4;
     acc[a] = __fadd_rn(acc[a], __fmul_rn(p0.x, x.x));
     acc[a + 1] = __fadd_rn(acc[a + 1], __fmul_rn(p0.y, x.y));
     acc[a + 2] = __fadd_rn(acc[a + 2], __fmul_rn(p1.x, x.z));
@@ -340,6 +354,7 @@ template <bool SWIGLU>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_q4q8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                 const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
+                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
                 const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -351,8 +366,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   // tma_full: packed A + B + activation scales landed; a_ready: A unpacked;
   // stage_empty: the MMAs of the stage finished; dx_empty: the epilogue used
-  // the stage's scales; acc_full: all four accumulators of a stage written
-  // (one commit per stage).  The epilogue frees each accumulator through a
+  // the stage's scales; acc_full[h]: accumulators 2h and 2h+1 of a stage
+  // written (two commits per stage, so the epilogue starting a stage never
+  // waits on the MMA that the release of its last accumulator unblocks).  The epilogue frees each accumulator through a
   // shared counter (acc_cnt[j] = EPI_WARPS x uses released), which the MMA
   // thread spins on with plain loads.
   const int B_TMA = 0, B_AREADY = STAGES, B_SEMPTY = 2 * STAGES, B_DXEMPTY = 3 * STAGES,
@@ -369,6 +385,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar(B_DXEMPTY + s), EPI_WARPS);
     }
     mbar_init(bar(B_ACCFULL), 1);
+    mbar_init(bar(B_ACCFULL + 1), 1);
     for (int j = 0; j < NACC; ++j) acc_cnt[j] = 0;
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -408,12 +425,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (lane == 0) {
           const uint32_t full = bar(B_TMA + s);
-          mbar_expect_tx(full, A_PACK_BYTES + B_BYTES + DX_BYTES);
+          mbar_expect_tx(full, A_PACK_BYTES + B_BYTES + DX_BYTES + SW_BYTES);
           const uint32_t pack = smem_u32(smem + OFF_PACK + s * A_PACK_BYTES);
           tma_load_2d(pack, &tmA, g * 256, nt * tiles_per_row, full);
           if (SWIGLU) tma_load_2d(pack + A_PACK_BYTES / 2, &tmA2, g * 256, nt * 2, full);
           tma_load_2d(smem_u32(smem + OFF_B + s * B_BYTES), &tmB, g * 128, t0, full);
           tma_load_2d(smem_u32(smem + OFF_DX + s * DX_BYTES), &tmD, t0, g * KBS, full);
+          const uint32_t sw = smem_u32(smem + OFF_SW + s * SW_BYTES);
+          tma_load_2d(sw, &tmS, g * 128, nt * tiles_per_row, full);
+          if (SWIGLU) tma_load_2d(sw + SW_BYTES / 2, &tmS2, g * 128, nt * 2, full);
         }
         __syncwarp();
       }
@@ -443,9 +463,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             tc_fence_after();
             mma_i8(tmem_base + j * BN, smem_desc(a0 + 32 * j), smem_desc(b0 + 32 * j), idesc, 1);
+            // Phase `it` of acc_full[h]: block sums 2h and 2h+1 of the stage are in TMEM.
+            if (j % 2 == 1) mma_commit(bar(B_ACCFULL + j / 2));
           }
           if (!ok) break;
-          mma_commit(bar(B_ACCFULL));  // phase `it`: the stage's four block sums are in TMEM
           mma_commit(bar(B_SEMPTY + s));
         }
       }
@@ -487,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- epilogue ----------------
     // Warp e: lane quarter q = warp % 4, column slice hc = e / 4 (NC columns).
-    // Each warp walks its columns of every block in 16-column chunks,
+    // Each warp walks its columns of every block in CW-column chunks,
     // software-pipelined: the TMEM load of chunk k+1 is in flight while chunk k
     // is rescaled, and the accumulator's re-arm store overlaps the last chunk.
     const int e = warp - EPI_WARP0;
@@ -506,39 +527,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0)
       for (int j = 0; j < NACC; ++j) smem_add_release(&acc_cnt[j], 1);
     float *xchg = reinterpret_cast<float *>(smem + OFF_XCHG);  // [64 rows][BN]
+    int pending = -1;  // accumulator re-armed but not yet handed back to the MMA
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
       const int nt = tile / p.mtiles, t0 = (tile % p.mtiles) * BN;
-      int n;
-      const uint16_t *sc;
-      if (SWIGLU) {
-        n = nt * 64 + (r & 63);
-        sc = (r < 64 ? p.scl : p.scl2);
-      } else {
-        n = nt * BM + r;
-        sc = p.scl;
-      }
-      const uint16_t *scrow = sc + (size_t)(n >> 5) * KB * 32 + (n & 31);
+      const int n = SWIGLU ? nt * 64 + (r & 63) : nt * BM + r;
       float acc[NC];
       const float init = (!SWIGLU && p.bias) ? p.bias[n] : 0.0f;
 #pragma unroll
       for (int c = 0; c < NC; ++c) acc[c] = init;
       const int it0 = it;  // stage counter at the tile's first block
-      uint32_t dbuf[2][16];
+      uint32_t dbuf[2][CW];
       // Prime: block 0 of the tile, chunk 0.
       if (!mbar_wait2_warp(bar(B_TMA + it0 % STAGES), (it0 / STAGES) & 1, bar(B_ACCFULL),
                            it0 & 1, abort_flag))
         ok = false;
       if (ok) {
         tc_fence_after();
-        tmem_ld16(tcol, dbuf[0]);
+        tmem_ld<CW>(tcol, dbuf[0]);
         tmem_wait_ld();
       }
-      uint16_t dw_cur = __ldg(scrow);
       for (int b = 0; ok && b < KB; ++b) {
         const int j = b % KBS, itb = it0 + b / KBS, s = itb % STAGES;
-        const uint16_t dw_nx = (b + 1 < KB) ? __ldg(scrow + (size_t)(b + 1) * 32) : (uint16_t)0;
+        // This row's scale of block b, staged by TMA with the stage's tiles
+        // ([row tile][block][32 rows] fp16; SwiGLU: gate tiles 0-1, up tiles 2-3).
+        const uint16_t dw_cur = reinterpret_cast<const uint16_t *>(
+            smem + OFF_SW + s * SW_BYTES)[((r >> 5) * KBS + j) * 32 + lane];
         // (C + D) * dw/16 - C * dw/16 = isum * dw in one rounding: C*dw/16 is exact
         // (dw has 11 significant bits, C/16 = 3*2^18), so this equals the
         // reference's (float)isum * dw.
@@ -552,32 +567,42 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int h = 0; h < NCH; ++h) {  // dbuf[h & 1] holds chunk h on entry
           if (h + 1 < NCH) {
-            tmem_ld16(ta + (h + 1) * 16, dbuf[(h + 1) & 1]);
+            tmem_ld<CW>(ta + (h + 1) * CW, dbuf[(h + 1) & 1]);
           } else {
-            // Every chunk of block b is in registers: re-arm the accumulator and
-            // start block b+1 (next accumulator, maybe next stage) into dbuf[0].
+            // Every chunk of block b is in registers.  Hand back the accumulator
+            // re-armed one block ago (its store has long completed, so this wait
+            // is short), then re-arm this one and start block b+1 (next
+            // accumulator, maybe next stage) into dbuf[0].
+            if (pending >= 0) {
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) smem_add_release(&acc_cnt[pending], 1);
+            }
 #pragma unroll
             for (int f = 0; f < NC / 32; ++f) tmem_fill32(ta + 32 * f, kMagic);
-            // The next block of the same stage is already in TMEM (one commit per
-            // stage): start it now.  A new stage is waited for only after this
-            // accumulator is released below -- its MMAs need that release.
+            pending = j;
+            // Blocks 2-3 of a stage are committed together; the MMAs behind that
+            // commit needed only releases made before this point.
+            if (more && j == KBS / 2 - 1 &&
+                !mbar_wait_warp(bar(B_ACCFULL + 1), itb & 1, abort_flag)) {
+              ok = false;
+              more = false;
+            }
             if (more && j != KBS - 1) {
               tc_fence_after();
-              tmem_ld16(tcol + (j + 1) * BN, dbuf[0]);
+              tmem_ld<CW>(tcol + (j + 1) * BN, dbuf[0]);
             }
           }
-          rescale16(acc, h, dbuf[h & 1], dx4, dw2, nc2);
+          rescale(acc, h, dbuf[h & 1], dx4, dw2, nc2);
           if (h + 1 < NCH) tmem_wait_ld();
         }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) smem_add_release(&acc_cnt[j], 1);
         if (j == KBS - 1) {
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(B_DXEMPTY + s));
           if (more) {
-            // A new stage: its scales and all four of its block sums.
+            // A new stage: its scales and its first two block sums (their
+            // accumulators were released during blocks 1 and 2 of this stage).
             const int it1 = itb + 1;
             if (!mbar_wait2_warp(bar(B_TMA + it1 % STAGES), (it1 / STAGES) & 1, bar(B_ACCFULL),
                                  it1 & 1, abort_flag)) {
@@ -585,12 +610,11 @@ __global__ void __launch_bounds__(THREADS, 1)
               more = false;
             } else {
               tc_fence_after();
-              tmem_ld16(tcol, dbuf[0]);
+              tmem_ld<CW>(tcol, dbuf[0]);
             }
           }
         }
         if (more) tmem_wait_ld();
-        dw_cur = dw_nx;
       }
       it = it0 + G;
       if (!ok && lane == 0) fail();
@@ -632,6 +656,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok || *abort_flag) break;
       }
     }
+    tmem_wait_st();  // the last re-arm completes before TMEM is freed
   }
 
   tc_fence_before();
@@ -692,8 +717,9 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   if (!gemm_tc_supported(swiglu ? 2 * a.N : a.N, a.K, a.M) || (swiglu && a.N % 64) || !a.scratch)
     return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(a.xq) & 15) || (reinterpret_cast<uintptr_t>(a.nib) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.scratch) & 15) ||
-      (swiglu && (reinterpret_cast<uintptr_t>(a.nib2) & 15)))
+      (reinterpret_cast<uintptr_t>(a.scratch) & 15) || (reinterpret_cast<uintptr_t>(a.scl) & 15) ||
+      (swiglu && ((reinterpret_cast<uintptr_t>(a.nib2) & 15) ||
+                  (reinterpret_cast<uintptr_t>(a.scl2) & 15))))
     return cudaErrorInvalidValue;
   const int KB = a.K / 32, Mp = (a.M + 3) & ~3;
   float *dT = a.scratch;
@@ -701,7 +727,7 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap tmA, tmA2, tmB, tmD;
+  CUtensorMap tmA, tmA2, tmB, tmD, tmS, tmS2;
   // Nibbles of a 32-row tile are contiguous over K ([KB][32][16] bytes): a 2-D view
   // of 8-byte elements, (KB*64, rows/32), box = 4 blocks x (4 or 2) row-tiles.
   const int rt = a.N / 32, per = swiglu ? 2 : 4;
@@ -730,6 +756,21 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   if (!encode(&tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dT, dD, sD, bD,
               CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
+  // Weight scales [rows/32][KB][32] fp16 as a 2-D view (KB*32, rows/32); box =
+  // 4 blocks x (4 or 2) row tiles, matching the nibble box.
+  cuuint64_t dS[2] = {(cuuint64_t)KB * 32, (cuuint64_t)rt};
+  cuuint64_t sS[1] = {(cuuint64_t)KB * 64};
+  cuuint32_t bS[2] = {128, (cuuint32_t)per};
+  if (!encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
+              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (swiglu) {
+    if (!encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
+                CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    tmS2 = tmS;
+  }
 
   static int sms = 0;
   if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess)
@@ -744,7 +785,7 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   auto kern = swiglu ? k_gemm_q4q8<true> : k_gemm_q4q8<false>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  kern<<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmA2, tmB, tmD, p);
+  kern<<<grid, THREADS, SMEM_BYTES, s>>>(tmA, tmA2, tmB, tmD, tmS, tmS2, p);
   return cudaGetLastError();
 }
 
