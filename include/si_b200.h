@@ -172,7 +172,8 @@ SI_API si_status si_matrix_download(si_ctx *ctx, const si_matrix *m, uint8_t *gg
 
 /* Activations on the device: Q8 tensors are two arrays, qs int8 [M][K] and
  * d fp16 [M][K/32] (block_q8_0 split for coalescing); the reference's 34-byte
- * blocks are produced by si_q8_to_blocks. */
+ * blocks are produced by si_q8_to_blocks.  si_q8_quantize_dev needs x 16-byte
+ * aligned and qs 4-byte aligned (SI_ERR_CUDA otherwise). */
 SI_API si_status si_q8_quantize_dev(si_ctx *ctx, const float *x_dev, int M, int K,
                                     int8_t *qs_dev, uint16_t *d_dev);
 SI_API si_status si_q8_to_blocks_dev(si_ctx *ctx, const int8_t *qs_dev, const uint16_t *d_dev,

@@ -58,6 +58,8 @@ struct KvRow<D, false> {
 
 template <int D, bool KVF32>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attn_split(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int N = D / 32;
   const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -140,6 +142,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn_split(const AttnArgs a
 }
 
 __global__ void k_attn_combine(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
   const int D = a.head_dim, S = a.nsplit;
   const float *p = a.part + ((size_t)t * a.n_q_heads + h) * S * (D + 2);
@@ -159,11 +163,9 @@ __global__ void k_attn_combine(const AttnArgs a) {
 template <int D, bool F32>
 cudaError_t run(const AttnArgs &a, cudaStream_t s) {
   dim3 grid(a.nsplit, a.n_kv_heads, a.T);
-  k_attn_split<D, F32><<<grid, kAttnWarps * 32, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(k_attn_split<D, F32>, grid, dim3(kAttnWarps * 32), 0, s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
-  k_attn_combine<<<dim3(a.n_q_heads, a.T), D, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D), 0, s, a);
 }
 }  // namespace
 

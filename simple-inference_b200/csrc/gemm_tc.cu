@@ -672,6 +672,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // padded): the layout the GEMM's TMA loads per stage.
 __global__ void k_scales_t(const uint16_t *__restrict__ xd, int M, int KB, int Mp,
                            float *__restrict__ dT) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
   if (t < Mp) dT[(size_t)b * Mp + t] = t < M ? f16_to_f32(xd[(size_t)t * KB + b]) : 0.0f;
 }
@@ -723,8 +725,8 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
     return cudaErrorInvalidValue;
   const int KB = a.K / 32, Mp = (a.M + 3) & ~3;
   float *dT = a.scratch;
-  k_scales_t<<<dim3((Mp + 127) / 128, KB), 128, 0, s>>>(a.xd, a.M, KB, Mp, dT);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(k_scales_t, dim3((Mp + 127) / 128, KB), dim3(128), 0, s,
+                             (const uint16_t *)a.xd, a.M, KB, Mp, dT);
   if (e != cudaSuccess) return e;
 
   CUtensorMap tmA, tmA2, tmB, tmD, tmS, tmS2;

@@ -10,16 +10,37 @@
 
 namespace si {
 
-// grid: one warp per block; x [M][K] contiguous, so block index is global.
+// Eight lanes per Q8 block, four elements per lane (one 16-byte load and one
+// 4-byte store each); the block's amax is reduced over the eight lanes.  Same
+// per-element arithmetic as q8_lane.  Warp-strided over x [M][K] contiguous
+// (so the block index is global); every lane of a warp runs every iteration.
 __global__ void k_q8_quantize(const float *__restrict__ x, size_t nblocks,
                               int8_t *__restrict__ qs, uint16_t *__restrict__ d) {
-  size_t blk = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  int lane = threadIdx.x & 31;
-  if (blk >= nblocks) return;  // whole warp exits together
-  uint16_t d16;
-  int8_t q = q8_lane(x[blk * 32 + lane], d16);
-  qs[blk * 32 + lane] = q;
-  if (lane == 0) d[blk] = d16;
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const size_t nwarp = (nblocks + 3) / 4;
+  const size_t stride = (size_t)gridDim.x * (blockDim.x >> 5);
+  for (size_t w = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < nwarp; w += stride) {
+    const size_t i = w * 32 + lane;  // float4 index
+    const bool ok = i < nblocks * 8;
+    const float4 v = ok ? reinterpret_cast<const float4 *>(x)[i] : make_float4(0, 0, 0, 0);
+    unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                     max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    if (!ok) continue;
+    const float dd = __fdiv_rn(__uint_as_float(m), 127.0f);
+    const float inv = dd == 0.0f ? 0.0f : __fdiv_rn(1.0f, dd);
+    auto q = [&](float e) {
+      int t = __float2int_rn(__fmul_rn(e, inv));
+      t = t > 127 ? 127 : (t < -127 ? -127 : t);
+      return (uint32_t)(t & 0xFF);
+    };
+    reinterpret_cast<uint32_t *>(qs)[i] = q(v.x) | q(v.y) << 8 | q(v.z) << 16 | q(v.w) << 24;
+    if ((lane & 7) == 0) d[i >> 3] = f32_to_f16(dd);
+  }
 }
 
 // One CTA per row.  out (fp32) and the Q8 pair are each optional.
@@ -28,6 +49,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float *__restrict__ x,
                                                     float *__restrict__ out,
                                                     int8_t *__restrict__ qs,
                                                     uint16_t *__restrict__ d) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const float *xr = x + (size_t)row * n;
   double ss = 0.0;
@@ -67,6 +90,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float *__restrict__ x,
 
 __global__ void k_add(const float *__restrict__ a, const float *__restrict__ b,
                       float *__restrict__ y, size_t n) {
+  pdl_trigger();
+  pdl_wait();
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = __fadd_rn(a[i], b[i]);
 }
@@ -75,22 +100,24 @@ cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_
                                cudaStream_t s) {
   size_t nblocks = (size_t)M * (K / 32);
   if (nblocks == 0) return cudaSuccess;
-  size_t threads = nblocks * 32;
-  k_q8_quantize<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, nblocks, qs, d);
-  return cudaGetLastError();
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(qs) & 3) ||
+      (reinterpret_cast<uintptr_t>(d) & 1))
+    return cudaErrorMisalignedAddress;
+  // 4 blocks per warp, 8 warps per CTA; at most 8 CTAs per SM's worth of grid.
+  const size_t ctas = (nblocks + 31) / 32;
+  const unsigned grid = (unsigned)(ctas < 148 * 8 ? ctas : 148 * 8);
+  return launch_pdl(k_q8_quantize, dim3(grid), dim3(256), 0, s, x, nblocks, qs, d);
 }
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, float eps,
                               float *out, int8_t *qs, uint16_t *d, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
-  k_rmsnorm_q8<<<M, 256, 0, s>>>(x, w, n, eps, out, qs, d);
-  return cudaGetLastError();
+  return launch_pdl(k_rmsnorm_q8, dim3(M), dim3(256), 0, s, x, w, n, eps, out, qs, d);
 }
 
 cudaError_t launch_add(const float *a, const float *b, float *y, size_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  k_add<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, b, y, n);
-  return cudaGetLastError();
+  return launch_pdl(k_add, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a, b, y, n);
 }
 
 }  // namespace si

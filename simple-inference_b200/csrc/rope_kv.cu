@@ -14,6 +14,8 @@
 namespace si {
 
 __global__ void k_rope_kv(const RopeKvArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int D = a.head_dim, half = D / 2;
   const int Hq = a.n_q_heads, Hkv = a.n_kv_heads;
@@ -60,8 +62,7 @@ __global__ void k_rope_kv(const RopeKvArgs a) {
 
 cudaError_t launch_rope_kv(const RopeKvArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  k_rope_kv<<<a.T, 256, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(k_rope_kv, dim3(a.T), dim3(256), 0, s, a);
 }
 
 }  // namespace si

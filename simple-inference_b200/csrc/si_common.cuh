@@ -11,7 +11,44 @@
 #define SI_QK 32
 #define SI_RT 32  // rows per row-tile of the SoA weight layout
 
+#include <utility>
+
 namespace si {
+
+// Programmatic dependent launch.  A decode step is a chain of small kernels,
+// each shorter than its own launch latency plus the latency of its first
+// loads.  Kernels launched with launch_pdl() may start while the previous
+// kernel of the stream is still running: they call pdl_trigger() first (so
+// their own successor may be scheduled early too), may then read data no
+// earlier kernel writes (weights), and call pdl_wait() -- which returns once
+// every grid they depend on has completed and its writes are visible --
+// before they read or write anything else.  Both are no-ops in a launch
+// without the attribute.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Grids larger than this many CTAs gain nothing from an early start (most of
+// their CTAs cannot be resident before the previous grid ends) and are
+// launched without the attribute.
+constexpr unsigned kPdlMaxCtas = 4096;
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (unsigned long long)grid.x * grid.y * grid.z <= kPdlMaxCtas ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Kernels that detect bad input or a bounded wait that ran out record a
 // si_status code in the context's device error word (first error wins); the
