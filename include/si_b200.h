@@ -104,6 +104,38 @@ typedef struct {                                                /* defines.h:35-
     float rms, q8_input, q_proj, k_proj, v_proj, rope_cache, attention, q8_output, out_proj;
 } phase_t;
 typedef enum { ATTENTION_STANDARD = 0, ATTENTION_FLASH = 1 } attention_method_t;
+/* Column-SoA tile geometry of repack_weights.py (fused_layer.h:33-36): one
+ * 5120-byte group per Q4_0 block (32 columns x 128 bytes of nibble pairs for
+ * 256 outputs, then 256 fp32 scales); a tile is 256 outputs over HIDDEN. */
+#ifndef FUSED_COL_BYTES
+#define FUSED_COL_BYTES 128u
+#define FUSED_GROUP_BYTES 5120u
+#define FUSED_TILE_BYTES ((unsigned)(HIDDEN / QK) * FUSED_GROUP_BYTES)
+#define FUSED_WO_SUBTILE (8u * FUSED_GROUP_BYTES)
+#endif
+typedef struct {                                                /* fused_layer.h:59-66 */
+    uint8_t *q, *kv, *o;
+    int tcm_fd;
+    uint8_t *tcm_map;
+    uint8_t *tcm_tile;
+    size_t tcm_map_bytes;
+    int tcm_block;
+} fused_weights_t;
+typedef struct {                                                /* fused_layer.h:68-71 */
+    phase_t phase;
+    double tcm_stage;
+} fused_stats_t;
+typedef struct {                            /* prefill_weight_stationary.h:149-155 */
+    block_q8_0 *xin;
+    block_q8_0 *oq;
+    float *acc;
+    float *cv, *sv;
+    int capacity;
+} pf_workspace_t;
+/* The reference's AI-DMA pipeline handle (ai_dma_pipeline.h:79-97).  Weight
+ * staging happens inside the GPU kernels (TMA / cp.async), so here it is an
+ * opaque type that pf_run_batch accepts and ignores; NULL is fine. */
+typedef struct si_ai_pipeline rt_ai_pipeline_t;
 #ifdef __cplusplus
 static_assert(sizeof(block_q8_0) == 34, "block_q8_0 must be the reference's 34 bytes");
 static_assert(sizeof(phase_t) == 9 * sizeof(float), "phase_t must be 9 floats");
@@ -284,7 +316,9 @@ SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *
 /* qwen_one_layer.c:98 quantize_q8 */
 SI_API void quantize_q8(const float *src, block_q8_0 *dst, int count);
 /* qwen_one_layer.c:148 matvec_q4q8.  Device copies of `weights` are cached by
- * host address and size; call si_forget_host_weights() after changing them. */
+ * host address and size; call si_forget_host_weights() after changing them
+ * (also for a layer's wq, and for column-SoA tiles or blobs of
+ * fused_weights_load). */
 SI_API void matvec_q4q8(const uint8_t *weights, const block_q8_0 *input, int inputs, int outputs,
                         const float *bias, float *out);
 SI_API void si_forget_host_weights(const void *host_ptr);
@@ -301,6 +335,44 @@ SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uint16_t *kc, 
                                 int n_kv_heads, int head_dim, float theta, float eps);
 SI_API layer_t si_ref_load_layer(const char *dir, int hidden, int kvdim);
 SI_API void si_ref_free_layer(layer_t *l);
+
+/* fused_layer.h:169 fused_column_matvec: output[0..255] = (add ? output :
+ * bias) + sum over nblocks groups of one column-SoA tile, in block order.
+ * The tile's device copy is cached by host address and size. */
+SI_API void fused_column_matvec(const uint8_t *tile, const block_q8_0 *x, int nblocks,
+                                const float *bias_lo, const float *bias_hi, float *output,
+                                int add);
+/* fused_layer.h:131 fused_weights_load / :141 fused_weights_free: the
+ * q/kv/o.colsoa tiles.  use_tcm and block select the RISC-V TCM staging of the
+ * reference; they are accepted and ignored (tcm_fd = -1, no TCM mapping). */
+SI_API fused_weights_t si_ref_fused_weights_load(const char *dir, int use_tcm, int block,
+                                                 int hidden, int n_q_heads, int n_kv_heads);
+SI_API void fused_weights_free(fused_weights_t *fw);
+/* register_fusion.h:344 run_layer_fused, fused_layer.h:397
+ * run_layer_legacy_fused, soa_staged.h:18 run_layer_soa_staged: one decode
+ * step whose Q/K/V/O weights come from the column-SoA tiles and norm/biases
+ * from l.  The three schedules compute the same function (the reference's
+ * portable build runs the legacy schedule for all three); here they share one
+ * GPU schedule.  tcm_stage is 0. */
+SI_API fused_stats_t si_ref_run_layer_fused(const layer_t *l, const fused_weights_t *fw,
+                                            const float *x, uint16_t *kc, uint16_t *vc,
+                                            int context, float *output, float *attn_capture,
+                                            block_q8_0 *q8_capture, int hidden, int n_q_heads,
+                                            int n_kv_heads, int head_dim, float theta,
+                                            float eps);
+/* prefill_weight_stationary.h:157-168 pf_workspace_open / close (host
+ * buffers of the reference's layout; the GPU prefill keeps its own). */
+SI_API void si_ref_pf_workspace_open(pf_workspace_t *p, int ntok, int hidden);
+SI_API void pf_workspace_close(pf_workspace_t *p);
+/* prefill_weight_stationary.h:183 pf_run_batch: causal prefill of ntok tokens
+ * at positions [prefix, prefix+ntok) -- token t attends over prefix+t+1
+ * positions -- appending their K/V to the caller's fp16 cache and writing
+ * output[ntok][hidden]; equal to ntok sequential run_layer steps. */
+SI_API void si_ref_pf_run_batch(const layer_t *l, const fused_weights_t *fw,
+                                rt_ai_pipeline_t *a, pf_workspace_t *p, const float *x,
+                                int ntok, int prefix, uint16_t *kc, uint16_t *vc,
+                                float *output, int hidden, int n_q_heads, int n_kv_heads,
+                                int head_dim, float theta, float eps);
 
 /* qwen_one_layer.c:164 rmsnorm */
 static inline void rmsnorm(const float *input, const float *weight, float *out) {
@@ -330,6 +402,48 @@ static inline phase_t run_layer(const layer_t *l, const float *x, uint16_t *kc, 
                                 float *scores, float *attn_copy, block_q8_0 *q8_copy) {
     return si_ref_run_layer(l, x, kc, vc, context, output, (int)method, scores, attn_copy,
                             q8_copy, HIDDEN, QHEADS, KVHEADS, HDIM, ROPE_BASE, RMS_EPS);
+}
+/* attention_kernels.h:29 attention_name */
+static inline const char *attention_name(attention_method_t method) {
+    return method == ATTENTION_FLASH ? "flash" : "standard";
+}
+static inline fused_weights_t fused_weights_load(const char *dir, int use_tcm, int block) {
+    return si_ref_fused_weights_load(dir, use_tcm, block, HIDDEN, QHEADS, KVHEADS);
+}
+static inline fused_stats_t run_layer_fused(const layer_t *l, const fused_weights_t *fw,
+                                            const float *x, uint16_t *kc, uint16_t *vc,
+                                            int context, float *output, float *attn_capture,
+                                            block_q8_0 *q8_capture) {
+    return si_ref_run_layer_fused(l, fw, x, kc, vc, context, output, attn_capture, q8_capture,
+                                  HIDDEN, QHEADS, KVHEADS, HDIM, ROPE_BASE, RMS_EPS);
+}
+static inline fused_stats_t run_layer_legacy_fused(const layer_t *l, const fused_weights_t *fw,
+                                                   const float *x, uint16_t *kc, uint16_t *vc,
+                                                   int context, float *output,
+                                                   float *attn_capture, block_q8_0 *q8_capture) {
+    return run_layer_fused(l, fw, x, kc, vc, context, output, attn_capture, q8_capture);
+}
+static inline fused_stats_t run_layer_soa_staged(const layer_t *l, const fused_weights_t *fw,
+                                                 const float *x, uint16_t *kc, uint16_t *vc,
+                                                 int context, float *out, float *attn_copy,
+                                                 block_q8_0 *q8_copy) {
+    return run_layer_fused(l, fw, x, kc, vc, context, out, attn_copy, q8_copy);
+}
+/* fused_layer.h:457 fused_total: all phase times plus TCM staging. */
+static inline double fused_total(const fused_stats_t *p) {
+    const phase_t *t = &p->phase;
+    return (double)t->rms + t->q8_input + t->q_proj + t->k_proj + t->v_proj + t->rope_cache +
+           t->attention + t->q8_output + t->out_proj + p->tcm_stage;
+}
+static inline void pf_workspace_open(pf_workspace_t *p, int ntok) {
+    si_ref_pf_workspace_open(p, ntok, HIDDEN);
+}
+static inline void pf_run_batch(const layer_t *l, const fused_weights_t *fw,
+                                rt_ai_pipeline_t *a, pf_workspace_t *p, const float *x,
+                                int ntok, int prefix, uint16_t *kc, uint16_t *vc,
+                                float *output) {
+    si_ref_pf_run_batch(l, fw, a, p, x, ntok, prefix, kc, vc, output, HIDDEN, QHEADS, KVHEADS,
+                        HDIM, ROPE_BASE, RMS_EPS);
 }
 /* qwen_one_layer.c:210 load_layer / :223 free_layer */
 static inline layer_t load_layer(const char *dir) { return si_ref_load_layer(dir, HIDDEN, KVDIM); }

@@ -176,4 +176,100 @@ cudaError_t launch_q8_from_blocks(const uint8_t *blocks, int M, int K, int8_t *q
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Column-SoA tiles (the reference's repack_weights.py output, read by
+// fused_column_matvec, fused_layer.h:169-245).  A tile is one 32-input group
+// per Q4_0 block: 32 columns of 128 bytes (byte j of column k holds output j in
+// its low nibble and output j+128 in its high nibble, input k of the block),
+// then 256 fp32 scales -- 5120 bytes per group.
+// ---------------------------------------------------------------------------
+constexpr int kGroupBytes = 5120;
+
+__device__ __forceinline__ uint32_t colsoa_nib(const uint8_t *g, int k, int j, int half) {
+  return (g[k * 128 + j] >> (4 * half)) & 15u;
+}
+
+// Destination row r (of the rows this launch fills) and block b -> the group
+// that holds them, the byte column j and the nibble half.
+//   kind 0 (Q):   tile p covers rows [256p, 256p+256) over all KB blocks.
+//   kind 1 (K|V): tile g holds K rows [128g, 128g+128) low and V rows high;
+//                 the destination has all K rows, then all V rows (kv_rows each).
+//   kind 2 (O):   pair p, output subtile yt (8 groups each, p-major) covers
+//                 rows [256yt, 256yt+256) for input blocks [8p, 8p+8).
+__global__ void k_colsoa_to_rt(const uint8_t *__restrict__ tiles, int kind, int nrows, int row0,
+                               int KB, int hidden, size_t tile_bytes, int kv_rows,
+                               uint8_t *__restrict__ nib, uint16_t *__restrict__ scl) {
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (size_t)nrows * KB) return;
+  const int r = (int)(idx / KB), b = (int)(idx % KB);
+  int j, half;
+  size_t off;
+  if (kind == 0) {
+    half = (r % 256) / 128;
+    j = r % 128;
+    off = (size_t)(r / 256) * tile_bytes + (size_t)b * kGroupBytes;
+  } else if (kind == 1) {
+    half = r >= kv_rows;
+    const int rr = half ? r - kv_rows : r;
+    j = rr % 128;
+    off = (size_t)(rr / 128) * tile_bytes + (size_t)b * kGroupBytes;
+  } else {
+    half = (r % 256) / 128;
+    j = r % 128;
+    off = ((size_t)(b / 8) * (hidden / 256) + r / 256) * 8 * kGroupBytes +
+          (size_t)(b % 8) * kGroupBytes;
+  }
+  const uint8_t *g = tiles + off;
+  const int n = row0 + r;
+  uint8_t *dst = nib + (((size_t)(n / SI_RT) * KB + b) * SI_RT + n % SI_RT) * 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    dst[i] = (uint8_t)((colsoa_nib(g, i, j, half) | colsoa_nib(g, i + 16, j, half) << 4) ^ 0x88u);
+  const float sc = *reinterpret_cast<const float *>(g + 4096 + 4 * (j + 128 * half));
+  scl[((size_t)(n / SI_RT) * KB + b) * SI_RT + n % SI_RT] = f32_to_f16(sc);
+}
+
+// fused_column_matvec (fused_layer.h:169-245) on one tile: thread j owns output
+// j (low nibbles for j < 128, high for j >= 128); blocks in order with the
+// reference's roundings, ((float)isum * scale) * dx.
+__global__ void __launch_bounds__(256) k_colsoa_matvec(const uint8_t *__restrict__ tile,
+                                                      const uint8_t *__restrict__ xb, int nblocks,
+                                                      const float *__restrict__ bias_lo,
+                                                      const float *__restrict__ bias_hi,
+                                                      float *__restrict__ out, int add) {
+  const int jo = threadIdx.x, half = jo / 128, j = jo % 128;
+  float acc;
+  if (add) acc = out[jo];
+  else if (half) acc = bias_hi ? bias_hi[j] : 0.0f;
+  else acc = bias_lo ? bias_lo[j] : 0.0f;
+  for (int b = 0; b < nblocks; ++b) {
+    const uint8_t *g = tile + (size_t)b * kGroupBytes;
+    const uint8_t *x = xb + (size_t)b * 34;
+    int isum = 0;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) isum += ((int)colsoa_nib(g, k, j, half) - 8) * (int8_t)x[2 + k];
+    const float sc = *reinterpret_cast<const float *>(g + 4096 + 4 * jo);
+    const float dx = f16_to_f32((uint16_t)(x[0] | x[1] << 8));
+    acc = __fadd_rn(acc, __fmul_rn(__fmul_rn((float)isum, sc), dx));
+  }
+  out[jo] = acc;
+}
+
+cudaError_t launch_colsoa_to_rt(const uint8_t *tiles, int kind, int nrows, int row0, int KB,
+                                int hidden, size_t tile_bytes, int kv_rows, uint8_t *nib,
+                                uint16_t *scl, cudaStream_t s) {
+  size_t n = (size_t)nrows * KB;
+  if (n == 0) return cudaSuccess;
+  k_colsoa_to_rt<<<nblk(n, 256), 256, 0, s>>>(tiles, kind, nrows, row0, KB, hidden, tile_bytes,
+                                             kv_rows, nib, scl);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_colsoa_matvec(const uint8_t *tile, const uint8_t *x_blocks, int nblocks,
+                                 const float *bias_lo, const float *bias_hi, float *out, int add,
+                                 cudaStream_t s) {
+  k_colsoa_matvec<<<1, 256, 0, s>>>(tile, x_blocks, nblocks, bias_lo, bias_hi, out, add);
+  return cudaGetLastError();
+}
+
 }  // namespace si

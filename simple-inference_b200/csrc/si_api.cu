@@ -1161,8 +1161,11 @@ static si_matrix *ref_weights(si_ctx *c, const uint8_t *w, int rows, int cols) {
   return m;
 }
 
+static void ref_forget_fused(const void *host_ptr);
+
 extern "C" SI_API void si_forget_host_weights(const void *host_ptr) {
   std::lock_guard<std::mutex> lk(g_ref_mu);
+  ref_forget_fused(host_ptr);
   for (auto it = g_weights.begin(); it != g_weights.end();) {
     if (it->first.p == host_ptr) {
       si_matrix_free(it->second);
@@ -1267,6 +1270,66 @@ extern "C" SI_API void si_ref_attention(int method, const float *q, const uint16
   ref_ck(cudaStreamSynchronize(c->stream), "attention");
 }
 
+// The reference-shaped decode step on device layer L: mirror the caller's fp16
+// KV history (qwen_one_layer.c:625-626 -- the cache is a host array the caller
+// owns), run the step, and copy the output, the new KV slot and the captures
+// back.  Phase times come from CUDA events; RMSNorm and the input Q8 are one
+// kernel, and Q/K/V one fused launch, so those are reported on the first field.
+static si_kv *ref_kv(si_ctx *c, const si_dims &d, int context) {
+  const size_t row = (size_t)d.n_kv_heads * d.head_dim;
+  if (g_ref_kv && (g_ref_kv->max_ctx < context || g_ref_kv->kv_f32 || g_ref_kv->row_elems() != row)) {
+    si_kv_free(g_ref_kv);
+    g_ref_kv = nullptr;
+  }
+  if (!g_ref_kv && si_kv_create(c, &d, 1, context > 4096 ? context : 4096, 0, &g_ref_kv) != SI_OK)
+    ref_die("KV cache");
+  return g_ref_kv;
+}
+
+static phase_t ref_step(si_ctx *c, si_layer *L, const float *x, uint16_t *kc, uint16_t *vc,
+                        int context, float *output, float *attn_copy, block_q8_0 *q8_copy,
+                        const char *what) {
+  phase_t ph;
+  memset(&ph, 0, sizeof(ph));
+  const si_dims &d = L->d;
+  const int hidden = d.hidden;
+  si_kv *kv = ref_kv(c, d, context);
+  const size_t row = (size_t)d.n_kv_heads * d.head_dim;
+  if (context > 1) {
+    ref_ck(cudaMemcpyAsync(kv->k, kc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), what);
+    ref_ck(cudaMemcpyAsync(kv->v, vc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), what);
+  }
+  const size_t QD = (size_t)d.n_q_heads * d.head_dim;
+  char *s = ref_scratch((size_t)hidden * 8 + QD * 4 + QD / 32 * 34 + 4096);
+  float *xd = reinterpret_cast<float *>(s), *yd = xd + hidden;
+  float *ad = yd + hidden;
+  block_q8_0 *qd = reinterpret_cast<block_q8_0 *>(ad + QD);
+  ref_ck(cudaMemcpyAsync(xd, x, (size_t)hidden * 4, cudaMemcpyHostToDevice, c->stream), what);
+  si_captures cap{};
+  cap.attn = attn_copy ? ad : nullptr;
+  cap.attn_q8 = q8_copy ? qd : nullptr;
+  int lens[1] = {context}, seqs[1] = {0};
+  if (run_step(c, L, kv, xd, 1, seqs, lens, 0, 0, yd, SI_LAYER_ATTN, &cap, true) != SI_OK)
+    ref_die(what);
+  ref_ck(cudaMemcpyAsync(output, yd, (size_t)hidden * 4, cudaMemcpyDeviceToHost, c->stream), what);
+  size_t slot = (size_t)(context - 1) * row;
+  ref_ck(cudaMemcpyAsync(kc + slot, (uint16_t *)kv->k + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), what);
+  ref_ck(cudaMemcpyAsync(vc + slot, (uint16_t *)kv->v + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), what);
+  if (attn_copy) ref_ck(cudaMemcpyAsync(attn_copy, ad, QD * 4, cudaMemcpyDeviceToHost, c->stream), what);
+  if (q8_copy) ref_ck(cudaMemcpyAsync(q8_copy, qd, QD / 32 * 34, cudaMemcpyDeviceToHost, c->stream), what);
+  ref_ck(cudaStreamSynchronize(c->stream), what);
+  if (si_ctx_status(c) != SI_OK) ref_die(what);
+  float ms[EV_COUNT] = {};
+  for (int i = 1; i <= EV_OPROJ; ++i) cudaEventElapsedTime(&ms[i], c->ev[i - 1], c->ev[i]);
+  ph.rms = ms[EV_RMS] * 1e-3f;
+  ph.q_proj = ms[EV_QKV] * 1e-3f;
+  ph.rope_cache = ms[EV_ROPE] * 1e-3f;
+  ph.attention = ms[EV_ATTN] * 1e-3f;
+  ph.q8_output = ms[EV_Q8O] * 1e-3f;
+  ph.out_proj = ms[EV_OPROJ] * 1e-3f;
+  return ph;
+}
+
 extern "C" SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uint16_t *kc,
                                            uint16_t *vc, int context, float *output, int method,
                                            float *scores, float *attn_copy, block_q8_0 *q8_copy,
@@ -1275,8 +1338,6 @@ extern "C" SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uin
   (void)method;
   (void)scores;
   std::lock_guard<std::mutex> lk(g_ref_mu);
-  phase_t ph;
-  memset(&ph, 0, sizeof(ph));
   si_ctx *c = ref_ctx(head_dim, theta);
   si_dims d{hidden, n_q_heads, n_kv_heads, head_dim, 0, theta, eps};
   if (check_dims(&d) != SI_OK) ref_die("run_layer dims");
@@ -1295,50 +1356,7 @@ extern "C" SI_API phase_t si_ref_run_layer(const layer_t *l, const float *x, uin
     if (si_layer_upload(c, &d, &h, &L) != SI_OK) ref_die("layer upload");
     g_layers[l->wq] = L;
   }
-  const size_t row = (size_t)n_kv_heads * head_dim;
-  if (g_ref_kv && (g_ref_kv->max_ctx < context || g_ref_kv->kv_f32 || g_ref_kv->row_elems() != row)) {
-    si_kv_free(g_ref_kv);
-    g_ref_kv = nullptr;
-  }
-  if (!g_ref_kv && si_kv_create(c, &d, 1, context > 4096 ? context : 4096, 0, &g_ref_kv) != SI_OK)
-    ref_die("KV cache");
-  // The caller owns the fp16 cache on the host (qwen_one_layer.c:625-626); mirror
-  // its history, run the step, and write the new slot back.
-  if (context > 1) {
-    ref_ck(cudaMemcpyAsync(g_ref_kv->k, kc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), "run_layer");
-    ref_ck(cudaMemcpyAsync(g_ref_kv->v, vc, (size_t)(context - 1) * row * 2, cudaMemcpyHostToDevice, c->stream), "run_layer");
-  }
-  const size_t QD = (size_t)n_q_heads * head_dim;
-  char *s = ref_scratch((size_t)hidden * 8 + QD * 4 + QD / 32 * 34 + 4096);
-  float *xd = reinterpret_cast<float *>(s), *yd = xd + hidden;
-  float *ad = yd + hidden;
-  block_q8_0 *qd = reinterpret_cast<block_q8_0 *>(ad + QD);
-  ref_ck(cudaMemcpyAsync(xd, x, (size_t)hidden * 4, cudaMemcpyHostToDevice, c->stream), "run_layer");
-  si_captures cap{};
-  cap.attn = attn_copy ? ad : nullptr;
-  cap.attn_q8 = q8_copy ? qd : nullptr;
-  int lens[1] = {context}, seqs[1] = {0};
-  if (run_step(c, L, g_ref_kv, xd, 1, seqs, lens, 0, 0, yd, SI_LAYER_ATTN, &cap, true) != SI_OK)
-    ref_die("run_layer");
-  ref_ck(cudaMemcpyAsync(output, yd, (size_t)hidden * 4, cudaMemcpyDeviceToHost, c->stream), "run_layer");
-  size_t slot = (size_t)(context - 1) * row;
-  ref_ck(cudaMemcpyAsync(kc + slot, (uint16_t *)g_ref_kv->k + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), "run_layer");
-  ref_ck(cudaMemcpyAsync(vc + slot, (uint16_t *)g_ref_kv->v + slot, row * 2, cudaMemcpyDeviceToHost, c->stream), "run_layer");
-  if (attn_copy) ref_ck(cudaMemcpyAsync(attn_copy, ad, QD * 4, cudaMemcpyDeviceToHost, c->stream), "run_layer");
-  if (q8_copy) ref_ck(cudaMemcpyAsync(q8_copy, qd, QD / 32 * 34, cudaMemcpyDeviceToHost, c->stream), "run_layer");
-  ref_ck(cudaStreamSynchronize(c->stream), "run_layer");
-  if (si_ctx_status(c) != SI_OK) ref_die("run_layer");
-  // Phase times from CUDA events: RMSNorm and the input Q8 are one kernel, and
-  // Q/K/V are one fused launch, so those are reported on the first field.
-  float ms[EV_COUNT] = {};
-  for (int i = 1; i <= EV_OPROJ; ++i) cudaEventElapsedTime(&ms[i], c->ev[i - 1], c->ev[i]);
-  ph.rms = ms[EV_RMS] * 1e-3f;
-  ph.q_proj = ms[EV_QKV] * 1e-3f;
-  ph.rope_cache = ms[EV_ROPE] * 1e-3f;
-  ph.attention = ms[EV_ATTN] * 1e-3f;
-  ph.q8_output = ms[EV_Q8O] * 1e-3f;
-  ph.out_proj = ms[EV_OPROJ] * 1e-3f;
-  return ph;
+  return ref_step(c, L, x, kc, vc, context, output, attn_copy, q8_copy, "run_layer");
 }
 
 static void *ref_load_file(const char *dir, const char *name, size_t expected, int optional) {
@@ -1392,4 +1410,298 @@ extern "C" SI_API void si_ref_free_layer(layer_t *l) {
   free(l->wq); free(l->wk); free(l->wv); free(l->wo);
   free(l->norm); free(l->bq); free(l->bk); free(l->bv);
   memset(l, 0, sizeof(*l));
+}
+
+// ----------------------------------------------------------------------------
+// column-SoA (fused) entry points and the batched prefill
+// ----------------------------------------------------------------------------
+// Device copies of column-SoA tiles, by host address and size.
+static std::map<std::pair<const void *, size_t>, void *> g_tiles;
+static std::map<const void *, si_layer *> g_fused_layers;  // by fw->q
+static std::map<const void *, size_t> g_blob_bytes;        // blobs of fused_weights_load
+
+static const uint8_t *ref_tile(si_ctx *c, const uint8_t *host, size_t bytes, const char *what) {
+  auto key = std::make_pair((const void *)host, bytes);
+  auto it = g_tiles.find(key);
+  if (it != g_tiles.end()) return static_cast<const uint8_t *>(it->second);
+  void *dev = nullptr;
+  ref_ck(cudaMalloc(&dev, bytes), what);
+  ref_ck(cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, c->stream), what);
+  g_tiles[key] = dev;
+  return static_cast<const uint8_t *>(dev);
+}
+
+static void ref_forget_tiles(const void *lo, const void *hi) {
+  for (auto it = g_tiles.begin(); it != g_tiles.end();) {
+    const char *p = static_cast<const char *>(it->first.first);
+    if (p >= static_cast<const char *>(lo) && p < static_cast<const char *>(hi)) {
+      cudaFree(it->second);
+      it = g_tiles.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
+// Drops device copies made from host_ptr: the fused layer keyed by it, and the
+// tiles inside its blob (or, for a pointer that is no known blob, the tiles
+// starting at it).  Caller holds g_ref_mu.
+static void ref_forget_fused(const void *host_ptr) {
+  auto fl = g_fused_layers.find(host_ptr);
+  if (fl != g_fused_layers.end()) {
+    si_layer_free(fl->second);
+    g_fused_layers.erase(fl);
+  }
+  auto bb = g_blob_bytes.find(host_ptr);
+  const size_t span = bb != g_blob_bytes.end() ? bb->second : 1;
+  ref_forget_tiles(host_ptr, static_cast<const char *>(host_ptr) + span);
+}
+
+extern "C" SI_API void fused_column_matvec(const uint8_t *tile, const block_q8_0 *x, int nblocks,
+                                           const float *bias_lo, const float *bias_hi,
+                                           float *output, int add) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  if (!tile || !x || !output || nblocks < 1) {
+    fprintf(stderr, "error: fused_column_matvec: bad arguments\n");
+    exit(1);
+  }
+  si_ctx *c = ref_ctx(HDIM, ROPE_BASE);
+  const uint8_t *t = ref_tile(c, tile, (size_t)nblocks * 5120, "fused_column_matvec");
+  char *s = ref_scratch((size_t)nblocks * 34 + 4 * 256 + 4 * 256 + 1024);
+  float *out = reinterpret_cast<float *>(s);
+  float *blo = out + 256, *bhi = blo + 128;
+  uint8_t *xb = reinterpret_cast<uint8_t *>(bhi + 128);
+  const char *w = "fused_column_matvec";
+  ref_ck(cudaMemcpyAsync(xb, x, (size_t)nblocks * 34, cudaMemcpyHostToDevice, c->stream), w);
+  if (add) ref_ck(cudaMemcpyAsync(out, output, 256 * 4, cudaMemcpyHostToDevice, c->stream), w);
+  if (!add && bias_lo) ref_ck(cudaMemcpyAsync(blo, bias_lo, 128 * 4, cudaMemcpyHostToDevice, c->stream), w);
+  if (!add && bias_hi) ref_ck(cudaMemcpyAsync(bhi, bias_hi, 128 * 4, cudaMemcpyHostToDevice, c->stream), w);
+  ref_ck(si::launch_colsoa_matvec(t, xb, nblocks, bias_lo ? blo : nullptr, bias_hi ? bhi : nullptr,
+                                  out, add, c->stream), w);
+  ref_ck(cudaMemcpyAsync(output, out, 256 * 4, cudaMemcpyDeviceToHost, c->stream), w);
+  ref_ck(cudaStreamSynchronize(c->stream), w);
+}
+
+static void *ref_load_blob(const char *dir, const char *name, size_t expected) {
+  char path[1024];
+  int n = snprintf(path, sizeof(path), "%s/%s", dir, name);
+  if (n < 0 || (size_t)n >= sizeof(path)) {
+    fprintf(stderr, "error: column-SoA weight path too long\n");
+    exit(1);
+  }
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    fprintf(stderr, "%s is missing: build the column-SoA tiles (repack_weights.py) for %s\n",
+            path, dir);
+    fprintf(stderr, "error: cannot open column-SoA weights\n");
+    exit(1);
+  }
+  if (fseek(f, 0, SEEK_END) != 0 || ftell(f) != (long)expected || fseek(f, 0, SEEK_SET) != 0) {
+    fprintf(stderr, "%s has the wrong size (expected %zu bytes)\n", path, expected);
+    fprintf(stderr, "error: invalid column-SoA weights\n");
+    exit(1);
+  }
+  void *buf = malloc(expected);
+  if (!buf || fread(buf, 1, expected, f) != expected) {
+    fprintf(stderr, "error: cannot read column-SoA weights\n");
+    exit(1);
+  }
+  fclose(f);
+  return buf;
+}
+
+// Geometry of the column-SoA blobs: 256-output tiles of 128-wide heads.
+static void fused_geometry_check(int hidden, int n_q_heads, int n_kv_heads, int head_dim) {
+  if (head_dim != 128 || hidden % 256 || n_q_heads % 2 || n_q_heads * head_dim != hidden ||
+      n_kv_heads < 1 || n_q_heads % n_kv_heads) {
+    fprintf(stderr, "error: column-SoA tiles need head_dim 128, paired heads and hidden = "
+                    "heads*128 (got hidden %d, %d/%d heads, head_dim %d)\n",
+            hidden, n_q_heads, n_kv_heads, head_dim);
+    exit(1);
+  }
+}
+
+extern "C" SI_API fused_weights_t si_ref_fused_weights_load(const char *dir, int use_tcm,
+                                                            int block, int hidden,
+                                                            int n_q_heads, int n_kv_heads) {
+  (void)use_tcm;
+  (void)block;
+  fused_geometry_check(hidden, n_q_heads, n_kv_heads, 128);
+  const size_t tile = (size_t)(hidden / 32) * 5120;
+  fused_weights_t fw;
+  memset(&fw, 0, sizeof(fw));
+  fw.tcm_fd = -1;
+  fw.q = static_cast<uint8_t *>(ref_load_blob(dir, "q.colsoa", (size_t)(n_q_heads / 2) * tile));
+  fw.kv = static_cast<uint8_t *>(ref_load_blob(dir, "kv.colsoa", (size_t)n_kv_heads * tile));
+  fw.o = static_cast<uint8_t *>(ref_load_blob(dir, "o.colsoa", (size_t)(n_q_heads / 2) * tile));
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  g_blob_bytes[fw.q] = (size_t)(n_q_heads / 2) * tile;
+  g_blob_bytes[fw.kv] = (size_t)n_kv_heads * tile;
+  g_blob_bytes[fw.o] = (size_t)(n_q_heads / 2) * tile;
+  return fw;
+}
+
+extern "C" SI_API void fused_weights_free(fused_weights_t *fw) {
+  if (!fw) return;
+  {
+    std::lock_guard<std::mutex> lk(g_ref_mu);
+    auto it = g_fused_layers.find(fw->q);
+    if (it != g_fused_layers.end()) {
+      si_layer_free(it->second);
+      g_fused_layers.erase(it);
+    }
+    for (const void *b : {(const void *)fw->q, (const void *)fw->kv, (const void *)fw->o}) {
+      auto bb = g_blob_bytes.find(b);
+      if (bb == g_blob_bytes.end()) continue;
+      ref_forget_tiles(b, static_cast<const char *>(b) + bb->second);
+      g_blob_bytes.erase(bb);
+    }
+  }
+  free(fw->q);
+  free(fw->kv);
+  free(fw->o);
+  memset(fw, 0, sizeof(*fw));
+  fw->tcm_fd = -1;
+}
+
+// Device layer from column-SoA tiles (weights) and layer_t (norm, biases):
+// the tiles are uploaded once and unpacked on the GPU into the fused QKV and O
+// matrices of the row-tile layout.
+static si_layer *ref_fused_layer(si_ctx *c, const si_dims &d, const layer_t *l,
+                                 const fused_weights_t *fw) {
+  auto it = g_fused_layers.find(fw->q);
+  if (it != g_fused_layers.end() && it->second->d.hidden == d.hidden &&
+      it->second->d.n_q_heads == d.n_q_heads && it->second->d.n_kv_heads == d.n_kv_heads)
+    return it->second;
+  if (it != g_fused_layers.end()) {
+    si_layer_free(it->second);
+    g_fused_layers.erase(it);
+  }
+  const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
+  const int KB = H / 32;
+  const size_t tile = (size_t)KB * 5120;
+  const size_t qb = (size_t)(d.n_q_heads / 2) * tile, kvb = (size_t)d.n_kv_heads * tile;
+  const char *w = "column-SoA layer";
+  si_layer *L = new si_layer();
+  L->ctx = c;
+  L->d = d;
+  uint8_t *dev = nullptr;
+  ref_ck(cudaMalloc(&dev, qb + kvb + qb), w);
+  ref_ck(cudaMemcpyAsync(dev, fw->q, qb, cudaMemcpyHostToDevice, c->stream), w);
+  ref_ck(cudaMemcpyAsync(dev + qb, fw->kv, kvb, cudaMemcpyHostToDevice, c->stream), w);
+  ref_ck(cudaMemcpyAsync(dev + qb + kvb, fw->o, qb, cudaMemcpyHostToDevice, c->stream), w);
+  if (matrix_alloc(c, QD + 2 * KVD, H, &L->qkv) != SI_OK || matrix_alloc(c, H, QD, &L->o) != SI_OK)
+    ref_die(w);
+  ref_ck(si::launch_colsoa_to_rt(dev, 0, QD, 0, KB, H, tile, 0, L->qkv->nib, L->qkv->scl,
+                                 c->stream), w);
+  ref_ck(si::launch_colsoa_to_rt(dev + qb, 1, 2 * KVD, QD, KB, H, tile, KVD, L->qkv->nib,
+                                 L->qkv->scl, c->stream), w);
+  ref_ck(si::launch_colsoa_to_rt(dev + qb + kvb, 2, H, 0, QD / 32, H, tile, 0, L->o->nib,
+                                 L->o->scl, c->stream), w);
+  if (l->bq || l->bk || l->bv) {
+    std::vector<float> b((size_t)QD + 2 * KVD, 0.0f);
+    if (l->bq) memcpy(b.data(), l->bq, (size_t)QD * 4);
+    if (l->bk) memcpy(b.data() + QD, l->bk, (size_t)KVD * 4);
+    if (l->bv) memcpy(b.data() + QD + KVD, l->bv, (size_t)KVD * 4);
+    if (upload_f32(c, b.data(), b.size(), &L->bias_qkv) != SI_OK) ref_die(w);
+    ref_ck(cudaStreamSynchronize(c->stream), w);
+  }
+  if (upload_f32(c, l->norm, H, &L->norm) != SI_OK) ref_die(w);
+  ref_ck(cudaStreamSynchronize(c->stream), w);
+  cudaFree(dev);
+  g_fused_layers[fw->q] = L;
+  return L;
+}
+
+extern "C" SI_API fused_stats_t si_ref_run_layer_fused(
+    const layer_t *l, const fused_weights_t *fw, const float *x, uint16_t *kc, uint16_t *vc,
+    int context, float *output, float *attn_capture, block_q8_0 *q8_capture, int hidden,
+    int n_q_heads, int n_kv_heads, int head_dim, float theta, float eps) {
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  fused_stats_t st;
+  memset(&st, 0, sizeof(st));
+  fused_geometry_check(hidden, n_q_heads, n_kv_heads, head_dim);
+  if (!l || !fw || !fw->q || !fw->kv || !fw->o) {
+    fprintf(stderr, "error: run_layer_fused: missing weights\n");
+    exit(1);
+  }
+  if (context < 1 || context > 32768) {
+    fprintf(stderr, "error: Context must be 1..32768\n");
+    exit(1);
+  }
+  si_ctx *c = ref_ctx(head_dim, theta);
+  si_dims d{hidden, n_q_heads, n_kv_heads, head_dim, 0, theta, eps};
+  si_layer *L = ref_fused_layer(c, d, l, fw);
+  st.phase = ref_step(c, L, x, kc, vc, context, output, attn_capture, q8_capture,
+                      "run_layer_fused");
+  return st;
+}
+
+extern "C" SI_API void si_ref_pf_workspace_open(pf_workspace_t *p, int ntok, int hidden) {
+  memset(p, 0, sizeof(*p));
+  p->capacity = ntok;
+  const size_t nb = (size_t)ntok * (hidden / 32);
+  p->xin = static_cast<block_q8_0 *>(malloc(nb * sizeof(block_q8_0)));
+  p->oq = static_cast<block_q8_0 *>(malloc(nb * sizeof(block_q8_0)));
+  p->acc = static_cast<float *>(malloc((size_t)ntok * 256 * sizeof(float)));
+  p->cv = static_cast<float *>(malloc((size_t)ntok * 64 * sizeof(float)));
+  p->sv = static_cast<float *>(malloc((size_t)ntok * 64 * sizeof(float)));
+  if (ntok < 1 || !p->xin || !p->oq || !p->acc || !p->cv || !p->sv) {
+    fprintf(stderr, "error: cannot allocate the prefill workspace\n");
+    exit(1);
+  }
+}
+
+extern "C" SI_API void pf_workspace_close(pf_workspace_t *p) {
+  if (!p) return;
+  free(p->xin);
+  free(p->oq);
+  free(p->acc);
+  free(p->cv);
+  free(p->sv);
+  memset(p, 0, sizeof(*p));
+}
+
+extern "C" SI_API void si_ref_pf_run_batch(const layer_t *l, const fused_weights_t *fw,
+                                           rt_ai_pipeline_t *a, pf_workspace_t *p,
+                                           const float *x, int ntok, int prefix, uint16_t *kc,
+                                           uint16_t *vc, float *output, int hidden,
+                                           int n_q_heads, int n_kv_heads, int head_dim,
+                                           float theta, float eps) {
+  (void)a;
+  std::lock_guard<std::mutex> lk(g_ref_mu);
+  // The reference's own precondition (prefill_weight_stationary.h:187-189),
+  // without its TCM / AI-DMA ownership checks.
+  if (!p || ntok < 1 || ntok > p->capacity || prefix < 0 || prefix > 32768 - ntok) {
+    fprintf(stderr, "error: Invalid prefill configuration\n");
+    exit(1);
+  }
+  fused_geometry_check(hidden, n_q_heads, n_kv_heads, head_dim);
+  if (!l || !fw || !fw->q || !fw->kv || !fw->o || !x || !kc || !vc || !output) {
+    fprintf(stderr, "error: pf_run_batch: missing arguments\n");
+    exit(1);
+  }
+  const char *w = "pf_run_batch";
+  si_ctx *c = ref_ctx(head_dim, theta);
+  si_dims d{hidden, n_q_heads, n_kv_heads, head_dim, 0, theta, eps};
+  si_layer *L = ref_fused_layer(c, d, l, fw);
+  si_kv *kv = ref_kv(c, d, prefix + ntok);
+  const size_t row = (size_t)n_kv_heads * head_dim;
+  if (prefix > 0) {
+    ref_ck(cudaMemcpyAsync(kv->k, kc, (size_t)prefix * row * 2, cudaMemcpyHostToDevice, c->stream), w);
+    ref_ck(cudaMemcpyAsync(kv->v, vc, (size_t)prefix * row * 2, cudaMemcpyHostToDevice, c->stream), w);
+  }
+  const size_t n = (size_t)ntok * hidden;
+  char *s = ref_scratch(n * 8 + 1024);
+  float *xd = reinterpret_cast<float *>(s), *yd = xd + n;
+  ref_ck(cudaMemcpyAsync(xd, x, n * 4, cudaMemcpyHostToDevice, c->stream), w);
+  if (run_step(c, L, kv, xd, ntok, nullptr, nullptr, 0, prefix, yd, SI_LAYER_ATTN, nullptr,
+               false) != SI_OK)
+    ref_die(w);
+  ref_ck(cudaMemcpyAsync(output, yd, n * 4, cudaMemcpyDeviceToHost, c->stream), w);
+  const size_t first = (size_t)prefix * row, cnt = (size_t)ntok * row;
+  ref_ck(cudaMemcpyAsync(kc + first, (uint16_t *)kv->k + first, cnt * 2, cudaMemcpyDeviceToHost, c->stream), w);
+  ref_ck(cudaMemcpyAsync(vc + first, (uint16_t *)kv->v + first, cnt * 2, cudaMemcpyDeviceToHost, c->stream), w);
+  ref_ck(cudaStreamSynchronize(c->stream), w);
+  if (si_ctx_status(c) != SI_OK) ref_die(w);
 }

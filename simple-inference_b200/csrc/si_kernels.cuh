@@ -24,6 +24,18 @@ cudaError_t launch_q8_to_blocks(const int8_t *qs, const uint16_t *d, int M, int 
 cudaError_t launch_q8_from_blocks(const uint8_t *blocks, int M, int K, int8_t *qs, uint16_t *d,
                                   cudaStream_t s);
 
+// Column-SoA tiles of repack_weights.py -> row-tile SoA rows [row0, row0+nrows)
+// of a matrix with KB blocks per row.  kind 0 = Q pair tiles, 1 = K|V group
+// tiles (destination: kv_rows K rows then kv_rows V rows), 2 = O pair x output
+// subtiles of a model with `hidden` outputs.
+cudaError_t launch_colsoa_to_rt(const uint8_t *tiles, int kind, int nrows, int row0, int KB,
+                                int hidden, size_t tile_bytes, int kv_rows, uint8_t *nib,
+                                uint16_t *scl, cudaStream_t s);
+// fused_column_matvec on one column-SoA tile: out[256] (+)= blocks in order.
+cudaError_t launch_colsoa_matvec(const uint8_t *tile, const uint8_t *x_blocks, int nblocks,
+                                 const float *bias_lo, const float *bias_hi, float *out, int add,
+                                 cudaStream_t s);
+
 // ---- norm_q8.cu -------------------------------------------------------------
 cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_t *d,
                                cudaStream_t s);
