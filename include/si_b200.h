@@ -295,6 +295,39 @@ SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const 
 SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const float *x_dev,
                                 int ntok, int prefix, float *y_dev, int mode);
 
+/* ------------------------------------------------------------------------ */
+/* Tensor parallelism (multi-layer 72B configuration over 2/4/8 GPUs).       */
+/* One process per GPU.  Q/K/V and gate/up are split by rows (whole heads;    */
+/* 128-row units of the MLP, uneven by at most one unit), o and down by       */
+/* columns; each row-parallel projection is followed by one NCCL all-reduce   */
+/* of its fp32 partial sums on the context's stream, then the residual add.   */
+/* Cross-rank summation changes the fp32 order: layer outputs agree with one  */
+/* GPU to the 1e-3 layer bar, not bit for bit.  Not in the reference.         */
+/* ------------------------------------------------------------------------ */
+typedef struct si_tp si_tp;
+/* Units [*first, *first + *count) of `units` owned by rank (host only). */
+SI_API void si_tp_split(int units, int rank, int world, int *first, int *count);
+/* ncclGetUniqueId into 128 bytes, to be shared with every rank. */
+SI_API si_status si_tp_unique_id(void *id128);
+SI_API si_status si_tp_create(si_ctx *ctx, const void *id128, int rank, int world, si_tp **out);
+SI_API void si_tp_free(si_tp *tp);
+/* The shard's dims (heads / world, this rank's MLP rows) and the first MLP
+ * row it owns.  Needs heads divisible by world and intermediate % 128 == 0. */
+SI_API si_status si_tp_local_dims(const si_dims *full, int rank, int world, si_dims *local,
+                                  int *mlp_first);
+/* This rank's shard of si_layer_synth(full, seed): equal to the same slices
+ * of the whole layer. */
+SI_API si_status si_layer_tp_synth(si_ctx *ctx, const si_dims *full, uint64_t seed, int rank,
+                                   int world, si_layer **out);
+/* Steps on a shard (KV cache created with the local dims); x and y are the
+ * full hidden vectors, identical on every rank. */
+SI_API si_status si_decode_step_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,
+                                       const float *x_dev, int batch, const int *ctx_lens,
+                                       float *y_dev, int mode);
+SI_API si_status si_prefill_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv, int seq,
+                                   const float *x_dev, int ntok, int prefix, float *y_dev,
+                                   int mode);
+
 /* CUDA-graph capture of a sequence of calls on the context's stream (no host
  * synchronisation may happen between begin and end: the *_dev matrix/Q8 calls
  * qualify).  Replays run the captured kernels with no launch gaps. */

@@ -62,14 +62,19 @@ __device__ __forceinline__ float normal_from(uint64_t h) {
 // Seeded synthetic Q4_0 weights written straight into the SoA layout.  Values
 // ~N(0, std) are quantised with the GGUF Q4_0 rule: d = (signed value of
 // max|x|) / -8 stored fp16, q = min(15, (int)(x/d + 8.5)).
+// Rows [row0, row0+rows) x blocks [cb0, cb0+KB) of a seeded matrix with
+// full_KB blocks per row: every block's values depend only on (seed, its index
+// in the full matrix), so a shard generated alone equals the same slice of the
+// whole matrix.
 __global__ void k_synth_q4(int rows, int KB, uint64_t seed, float stdv, uint8_t *__restrict__ nib,
-                           uint16_t *__restrict__ scl) {
+                           uint16_t *__restrict__ scl, int row0, int cb0, int full_KB) {
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)rows * KB) return;
   int row = (int)(i / KB), b = (int)(i % KB);
+  const size_t gi = (size_t)(row0 + row) * full_KB + cb0 + b;
   float x[32];
   float amax = 0.0f, smax = 0.0f;
-  uint64_t base = mix64(seed) ^ ((uint64_t)i << 5);
+  uint64_t base = mix64(seed) ^ ((uint64_t)gi << 5);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     x[j] = normal_from(mix64(base + j)) * stdv;
@@ -93,9 +98,11 @@ __global__ void k_synth_q4(int rows, int KB, uint64_t seed, float stdv, uint8_t 
   scl[slot] = f32_to_f16(d);
 }
 
-__global__ void k_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float stdv) {
+// Elements [i0, i0+n) of a seeded vector.
+__global__ void k_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float stdv,
+                            size_t i0) {
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = mean + stdv * normal_from(mix64(mix64(seed) + i));
+  if (i < n) dst[i] = mean + stdv * normal_from(mix64(mix64(seed) + i0 + i));
 }
 
 __global__ void k_synth_kv(void *dst, size_t n, int f32, uint64_t seed, float stdv) {
@@ -144,15 +151,16 @@ cudaError_t launch_unpack_to_gguf(const uint8_t *nib, const uint16_t *scl, int r
   return cudaGetLastError();
 }
 cudaError_t launch_synth_q4(int rows, int KB, uint64_t seed, float stdv, uint8_t *nib,
-                            uint16_t *scl, cudaStream_t s) {
+                            uint16_t *scl, cudaStream_t s, int row0, int cb0, int full_KB) {
   size_t n = (size_t)rows * KB;
-  k_synth_q4<<<nblk(n, 128), 128, 0, s>>>(rows, KB, seed, stdv, nib, scl);
+  k_synth_q4<<<nblk(n, 128), 128, 0, s>>>(rows, KB, seed, stdv, nib, scl, row0, cb0,
+                                          full_KB > 0 ? full_KB : KB);
   return cudaGetLastError();
 }
 cudaError_t launch_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float stdv,
-                             cudaStream_t s) {
+                             cudaStream_t s, size_t i0) {
   if (n == 0) return cudaSuccess;
-  k_synth_f32<<<nblk(n, 256), 256, 0, s>>>(dst, n, seed, mean, stdv);
+  k_synth_f32<<<nblk(n, 256), 256, 0, s>>>(dst, n, seed, mean, stdv, i0);
   return cudaGetLastError();
 }
 cudaError_t launch_synth_kv(void *dst, size_t n, int f32, uint64_t seed, float stdv,

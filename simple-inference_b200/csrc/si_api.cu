@@ -4,6 +4,8 @@
 // the layer schedules.  Every computation is a kernel from the other .cu files;
 // there is no CPU compute path.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdarg>
@@ -122,6 +124,53 @@ struct si_layer {
   si_dims d{};
   si_matrix *qkv = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
   float *bias_qkv = nullptr, *norm = nullptr, *norm2 = nullptr;
+};
+
+// NCCL is opened on first use instead of being linked: a process that already
+// loaded an NCCL (PyTorch bundles its own, newer one) keeps using that copy,
+// and processes that never use tensor parallelism never load one.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId *);
+  ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
+  ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                             ncclComm_t, cudaStream_t);
+  ncclResult_t (*comm_destroy)(ncclComm_t);
+  const char *(*error_string)(ncclResult_t);
+};
+
+static const NcclApi *nccl_api() {
+  static std::mutex mu;
+  static NcclApi api{};
+  static int state = 0;  // 0 untried, 1 ok, -1 unavailable
+  std::lock_guard<std::mutex> lk(mu);
+  if (state == 0) {
+    state = -1;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (h) {
+      api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+      api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+      api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+      api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+      api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy &&
+          api.error_string)
+        state = 1;
+    }
+  }
+  return state == 1 ? &api : nullptr;
+}
+
+#define SI_NCCL(api, call, what)                                                       \
+  do {                                                                                  \
+    ncclResult_t r_ = (call);                                                           \
+    if (r_ != ncclSuccess) return fail(SI_ERR_CUDA, "%s: %s", what, (api)->error_string(r_)); \
+  } while (0)
+
+// Tensor-parallel group: one NCCL communicator per rank (one rank per GPU).
+struct si_tp {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
 };
 
 struct si_kv {
@@ -860,9 +909,22 @@ StepBuffers carve(void *base, const si_dims &d, int T, int nsplit) {
 // Events bracketing the phases of one step, for the reference's phase_t.
 enum { EV_START, EV_RMS, EV_QKV, EV_ROPE, EV_ATTN, EV_Q8O, EV_OPROJ, EV_MLP, EV_COUNT };
 
+// In-place sum of a row-parallel projection's partial outputs over the TP group.
+static si_status tp_allreduce(si_ctx *ctx, si_tp *tp, float *buf, size_t n) {
+  const NcclApi *api = nccl_api();
+  SI_CHECK(api, "NCCL is not available");
+  SI_NCCL(api, api->all_reduce(buf, buf, n, ncclFloat32, ncclSum, tp->comm, ctx->stream),
+          "ncclAllReduce");
+  return SI_OK;
+}
+
+// One layer step.  With tp, the layer holds this rank's shard (its Q/KV heads
+// and its slice of the MLP); the O and down projections then produce partial
+// sums, which are all-reduced before the residual adds.
 static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, int T,
                           const int *seq_host, const int *ctx_host, int seq0, int prefix,
-                          float *y, int mode, const si_captures *cap, bool timing) {
+                          float *y, int mode, const si_captures *cap, bool timing,
+                          si_tp *tp = nullptr) {
   const si_dims &d = l->d;
   const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
   SI_CHECK(mode == SI_LAYER_ATTN || mode == SI_LAYER_FULL, "bad layer mode");
@@ -949,17 +1011,31 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
   if (cap && cap->attn_q8)
     SI_CUDA(si::launch_q8_to_blocks(b.aq, b.ad, T, QD, reinterpret_cast<uint8_t *>(cap->attn_q8), s));
   // 6. Output projection (qwen_one_layer.c:275); the decoder layer adds the residual.
+  const size_t TH = (size_t)T * H;
   if (mode == SI_LAYER_ATTN) {
     SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, y, -1));
+    if (tp) SI_TRY(tp_allreduce(ctx, tp, y, TH));
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
   } else {
-    SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, x, b.h, -1));
+    if (tp) {
+      SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, b.h, -1));
+      SI_TRY(tp_allreduce(ctx, tp, b.h, TH));
+      SI_CUDA(si::launch_add(x, b.h, b.h, TH, s));
+    } else {
+      SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, x, b.h, -1));
+    }
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
     // 7. MLP: rmsnorm2 + Q8 -> gate/up + SiLU*mul + Q8 -> down + residual.
     SI_CUDA(si::launch_rmsnorm_q8(b.h, l->norm2, T, H, d.rms_eps, nullptr, b.hq, b.hd, s));
     SI_TRY(si_gateup_q8_dev(ctx, l->gate, l->up, b.hq, b.hd, T, b.actq, b.actd, nullptr));
-    SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, b.h, y, -1));
+    if (tp) {
+      SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, nullptr, y, -1));
+      SI_TRY(tp_allreduce(ctx, tp, y, TH));
+      SI_CUDA(si::launch_add(b.h, y, y, TH, s));
+    } else {
+      SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, b.h, y, -1));
+    }
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
   }
   return SI_OK;
@@ -1704,4 +1780,170 @@ extern "C" SI_API void si_ref_pf_run_batch(const layer_t *l, const fused_weights
   ref_ck(cudaMemcpyAsync(vc + first, (uint16_t *)kv->v + first, cnt * 2, cudaMemcpyDeviceToHost, c->stream), w);
   ref_ck(cudaStreamSynchronize(c->stream), w);
   if (si_ctx_status(c) != SI_OK) ref_die(w);
+}
+
+// ----------------------------------------------------------------------------
+// tensor parallelism (one process per GPU, NCCL over NVLink)
+// ----------------------------------------------------------------------------
+extern "C" SI_API void si_tp_split(int units, int rank, int world, int *first, int *count) {
+  if (world < 1 || rank < 0 || rank >= world || units < 0) {
+    if (first) *first = 0;
+    if (count) *count = 0;
+    return;
+  }
+  const int q = units / world, r = units % world;
+  if (first) *first = rank * q + (rank < r ? rank : r);
+  if (count) *count = q + (rank < r ? 1 : 0);
+}
+
+extern "C" SI_API si_status si_tp_unique_id(void *id_out) {
+  SI_CHECK(id_out, "null id buffer");
+  const NcclApi *api = nccl_api();
+  if (!api) return fail(SI_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  SI_NCCL(api, api->get_unique_id(&id), "ncclGetUniqueId");
+  memcpy(id_out, &id, sizeof(id));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_tp_create(si_ctx *ctx, const void *id, int rank, int world,
+                                         si_tp **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(id && out && world >= 1 && rank >= 0 && rank < world, "bad TP arguments");
+  const NcclApi *api = nccl_api();
+  if (!api) return fail(SI_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  si_tp *tp = new si_tp();
+  tp->rank = rank;
+  tp->world = world;
+  ncclResult_t r = api->comm_init_rank(&tp->comm, world, uid, rank);
+  if (r != ncclSuccess) {
+    delete tp;
+    return fail(SI_ERR_CUDA, "ncclCommInitRank: %s", api->error_string(r));
+  }
+  *out = tp;
+  return SI_OK;
+}
+
+extern "C" SI_API void si_tp_free(si_tp *tp) {
+  if (!tp) return;
+  if (tp->comm && nccl_api()) nccl_api()->comm_destroy(tp->comm);
+  delete tp;
+}
+
+extern "C" SI_API si_status si_tp_local_dims(const si_dims *full, int rank, int world,
+                                             si_dims *local, int *mlp_first) {
+  SI_TRY(check_dims(full));
+  SI_CHECK(local && world >= 1 && rank >= 0 && rank < world, "bad TP arguments");
+  SI_CHECK(full->n_q_heads % world == 0 && full->n_kv_heads % world == 0,
+           "%d query / %d KV heads do not split over %d ranks", full->n_q_heads,
+           full->n_kv_heads, world);
+  SI_CHECK(full->intermediate % 128 == 0, "intermediate %d is not a multiple of 128",
+           full->intermediate);
+  *local = *full;
+  local->n_q_heads = full->n_q_heads / world;
+  local->n_kv_heads = full->n_kv_heads / world;
+  int first = 0, count = 0;
+  si_tp_split(full->intermediate / 128, rank, world, &first, &count);
+  SI_CHECK(full->intermediate == 0 || count > 0, "too many ranks for the MLP");
+  local->intermediate = count * 128;
+  if (mlp_first) *mlp_first = first * 128;
+  return SI_OK;
+}
+
+// This rank's shard of the layer si_layer_synth(full, seed) makes: the same
+// seeded weights, generated only for the owned rows / columns.
+extern "C" SI_API si_status si_layer_tp_synth(si_ctx *ctx, const si_dims *full, uint64_t seed,
+                                              int rank, int world, si_layer **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(out, "null output handle");
+  si_dims d{};
+  int i0 = 0;
+  SI_TRY(si_tp_local_dims(full, rank, world, &d, &i0));
+  SI_CHECK(full->intermediate > 0, "the TP layer needs its MLP");
+  const int H = full->hidden, D = full->head_dim;
+  const int QD = full->n_q_heads * D, KVD = full->n_kv_heads * D;
+  const int qd = d.n_q_heads * D, kvd = d.n_kv_heads * D, I = d.intermediate;
+  const int q0 = rank * qd, kv0 = rank * kvd;
+  const int KBH = H / 32;
+  cudaStream_t s = ctx->stream;
+  const float wstd = 0.02f;
+  si_layer *l = new si_layer();
+  l->ctx = ctx;
+  l->d = d;
+  si_status st = SI_OK;
+  auto rows_at = [](si_matrix *m, int row) {  // row offsets are multiples of 32
+    return std::make_pair(m->nib + (size_t)(row / 32) * (m->cols / 32) * 32 * 16,
+                          m->scl + (size_t)(row / 32) * (m->cols / 32) * 32);
+  };
+  do {
+    if ((st = matrix_alloc(ctx, qd + 2 * kvd, H, &l->qkv)) != SI_OK) break;
+    const uint64_t sq = seed * 16 + 1;
+    auto p0 = rows_at(l->qkv, 0), p1 = rows_at(l->qkv, qd), p2 = rows_at(l->qkv, qd + kvd);
+    if (si::launch_synth_q4(qd, KBH, sq, wstd, p0.first, p0.second, s, q0, 0, KBH) ||
+        si::launch_synth_q4(kvd, KBH, sq, wstd, p1.first, p1.second, s, QD + kv0, 0, KBH) ||
+        si::launch_synth_q4(kvd, KBH, sq, wstd, p2.first, p2.second, s, QD + KVD + kv0, 0, KBH)) {
+      st = fail(SI_ERR_CUDA, "qkv shard");
+      break;
+    }
+    if ((st = matrix_alloc(ctx, H, qd, &l->o)) != SI_OK) break;
+    if (si::launch_synth_q4(H, qd / 32, seed * 16 + 2, wstd, l->o->nib, l->o->scl, s, 0, q0 / 32,
+                            QD / 32)) {
+      st = fail(SI_ERR_CUDA, "o shard");
+      break;
+    }
+    if (cudaMalloc(&l->bias_qkv, (size_t)(qd + 2 * kvd) * 4) != cudaSuccess ||
+        cudaMalloc(&l->norm, (size_t)H * 4) != cudaSuccess ||
+        cudaMalloc(&l->norm2, (size_t)H * 4) != cudaSuccess) {
+      st = fail(SI_ERR_OOM, "layer vectors");
+      break;
+    }
+    const uint64_t sb = seed * 16 + 3;
+    if (si::launch_synth_f32(l->bias_qkv, qd, sb, 0.0f, 0.02f, s, q0) ||
+        si::launch_synth_f32(l->bias_qkv + qd, kvd, sb, 0.0f, 0.02f, s, QD + kv0) ||
+        si::launch_synth_f32(l->bias_qkv + qd + kvd, kvd, sb, 0.0f, 0.02f, s, QD + KVD + kv0) ||
+        si::launch_synth_f32(l->norm, H, seed * 16 + 4, 1.0f, 0.02f, s) ||
+        si::launch_synth_f32(l->norm2, H, seed * 16 + 8, 1.0f, 0.02f, s)) {
+      st = fail(SI_ERR_CUDA, "layer vectors");
+      break;
+    }
+    if ((st = matrix_alloc(ctx, I, H, &l->gate)) != SI_OK ||
+        (st = matrix_alloc(ctx, I, H, &l->up)) != SI_OK ||
+        (st = matrix_alloc(ctx, H, I, &l->down)) != SI_OK)
+      break;
+    if (si::launch_synth_q4(I, KBH, seed * 16 + 5, wstd, l->gate->nib, l->gate->scl, s, i0, 0, KBH) ||
+        si::launch_synth_q4(I, KBH, seed * 16 + 6, wstd, l->up->nib, l->up->scl, s, i0, 0, KBH) ||
+        si::launch_synth_q4(H, I / 32, seed * 16 + 7, wstd, l->down->nib, l->down->scl, s, 0,
+                            i0 / 32, full->intermediate / 32)) {
+      st = fail(SI_ERR_CUDA, "MLP shard");
+      break;
+    }
+    st = si_ctx_synchronize(ctx);
+  } while (0);
+  if (st != SI_OK) {
+    si_layer_free(l);
+    return st;
+  }
+  *out = l;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_decode_step_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,
+                                                  const float *x, int batch, const int *ctx_lens,
+                                                  float *y, int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(tp && l && kv && ctx_lens, "null argument");
+  SI_CHECK(batch > 0 && batch <= kv->batch, "batch %d exceeds the KV cache's %d", batch, kv->batch);
+  std::vector<int> seqs(batch);
+  for (int i = 0; i < batch; ++i) seqs[i] = i;
+  return run_step(ctx, l, kv, x, batch, seqs.data(), ctx_lens, 0, 0, y, mode, nullptr, false, tp);
+}
+
+extern "C" SI_API si_status si_prefill_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,
+                                              int seq, const float *x, int ntok, int prefix,
+                                              float *y, int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(tp && l && kv, "null argument");
+  return run_step(ctx, l, kv, x, ntok, nullptr, nullptr, seq, prefix, y, mode, nullptr, false, tp);
 }

@@ -13,10 +13,15 @@ cudaError_t launch_repack_gguf(const uint8_t *gguf, int rows, int KB, uint8_t *n
                                uint16_t *scl, cudaStream_t s);
 cudaError_t launch_unpack_to_gguf(const uint8_t *nib, const uint16_t *scl, int rows, int KB,
                                   uint8_t *gguf, cudaStream_t s);
+// Seeded synthetic Q4_0 rows [row0, row0+rows) x blocks [cb0, cb0+KB) of a
+// matrix with full_KB blocks per row (0: full_KB = KB), written to a matrix of
+// exactly `rows` x KB blocks.
 cudaError_t launch_synth_q4(int rows, int KB, uint64_t seed, float std, uint8_t *nib,
-                            uint16_t *scl, cudaStream_t s);
+                            uint16_t *scl, cudaStream_t s, int row0 = 0, int cb0 = 0,
+                            int full_KB = 0);
+// Elements [i0, i0+n) of a seeded N(mean, std) vector.
 cudaError_t launch_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float std,
-                             cudaStream_t s);
+                             cudaStream_t s, size_t i0 = 0);
 cudaError_t launch_synth_kv(void *dst, size_t n, int f32, uint64_t seed, float std,
                             cudaStream_t s);
 cudaError_t launch_q8_to_blocks(const int8_t *qs, const uint16_t *d, int M, int K,

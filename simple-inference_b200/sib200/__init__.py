@@ -106,6 +106,15 @@ def lib() -> C.CDLL:
         "si_decode_step_dev": (i32, [vp, vp, vp, vp, i32, vp, vp, i32, C.POINTER(Captures)]),
         "si_prefill": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_prefill_dev": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
+        "si_tp_split": (None, [i32, i32, i32, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "si_tp_unique_id": (i32, [vp]),
+        "si_tp_create": (i32, [vp, vp, i32, i32, pp]),
+        "si_tp_free": (None, [vp]),
+        "si_tp_local_dims": (i32, [C.POINTER(Dims), i32, i32, C.POINTER(Dims),
+                                   C.POINTER(C.c_int)]),
+        "si_layer_tp_synth": (i32, [vp, C.POINTER(Dims), u64, i32, i32, pp]),
+        "si_decode_step_tp_dev": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
+        "si_prefill_tp_dev": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_attention_decode_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, vp, vp]),
         "si_graph_begin": (i32, [vp]),
         "si_graph_end": (i32, [vp, pp]),
@@ -243,6 +252,20 @@ class Context:
         check(self.L.si_layer_synth(self.h, C.byref(dm), seed, C.byref(h)), "si_layer_synth")
         return Layer(self, h, dims)
 
+    def tp(self, uid: bytes, rank: int, world: int) -> "TP":
+        """Join the tensor-parallel group identified by uid (from tp_unique_id)."""
+        h = C.c_void_p()
+        buf = C.create_string_buffer(bytes(uid), 128)
+        check(self.L.si_tp_create(self.h, buf, rank, world, C.byref(h)), "si_tp_create")
+        return TP(self, h, rank, world)
+
+    def layer_tp_synth(self, full: dict, seed: int, rank: int, world: int) -> "Layer":
+        dm = Dims.of(full)
+        h = C.c_void_p()
+        check(self.L.si_layer_tp_synth(self.h, C.byref(dm), seed, rank, world, C.byref(h)),
+              "si_layer_tp_synth")
+        return Layer(self, h, tp_local_dims(full, rank, world)[0])
+
     def kv(self, dims: dict, batch: int, max_ctx: int, kv_f32: bool) -> "KV":
         dm = Dims.of(dims)
         h = C.c_void_p()
@@ -345,6 +368,49 @@ class Layer:
     def prefill_dev(self, kv: "KV", seq, x, ntok, prefix, y, mode=SI_LAYER_ATTN):
         check(self.ctx.L.si_prefill_dev(self.ctx.h, self.h, kv.h, seq, _p(x), ntok, prefix,
                                         _p(y), mode), "si_prefill_dev")
+
+
+def tp_split(units: int, rank: int, world: int) -> tuple[int, int]:
+    """(first, count) of the units rank owns (host-only; no GPU needed)."""
+    f, c = C.c_int(), C.c_int()
+    lib().si_tp_split(units, rank, world, C.byref(f), C.byref(c))
+    return f.value, c.value
+
+
+def tp_local_dims(full: dict, rank: int, world: int) -> tuple[dict, int]:
+    """Shard dims and first owned MLP row (host-only)."""
+    dm, out, first = Dims.of(full), Dims(), C.c_int()
+    check(lib().si_tp_local_dims(C.byref(dm), rank, world, C.byref(out), C.byref(first)),
+          "si_tp_local_dims")
+    d = dict(full)
+    d.update(n_q_heads=out.n_q_heads, n_kv_heads=out.n_kv_heads, intermediate=out.intermediate)
+    return d, first.value
+
+
+def tp_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().si_tp_unique_id(buf), "si_tp_unique_id")
+    return buf.raw
+
+
+class TP:
+    def __init__(self, ctx: Context, h, rank, world):
+        self.ctx, self.h, self.rank, self.world = ctx, h, rank, world
+
+    def decode_dev(self, layer: "Layer", kv: "KV", x, ctx_lens, y, mode=SI_LAYER_FULL):
+        lens = (C.c_int * len(ctx_lens))(*ctx_lens)
+        check(self.ctx.L.si_decode_step_tp_dev(self.ctx.h, self.h, layer.h, kv.h, _p(x),
+                                               len(ctx_lens), lens, _p(y), mode),
+              "si_decode_step_tp_dev")
+
+    def prefill_dev(self, layer: "Layer", kv: "KV", seq, x, ntok, prefix, y, mode=SI_LAYER_FULL):
+        check(self.ctx.L.si_prefill_tp_dev(self.ctx.h, self.h, layer.h, kv.h, seq, _p(x), ntok,
+                                           prefix, _p(y), mode), "si_prefill_tp_dev")
+
+    def free(self):
+        if self.h:
+            self.ctx.L.si_tp_free(self.h)
+            self.h = None
 
 
 class KV:
