@@ -258,6 +258,9 @@ SI_API si_status si_layer_upload(si_ctx *ctx, const si_dims *dims, const si_laye
 SI_API si_status si_layer_synth(si_ctx *ctx, const si_dims *dims, uint64_t seed, si_layer **out);
 SI_API void si_layer_free(si_layer *l);
 SI_API si_status si_layer_matrix(si_layer *l, int which, si_matrix **out); /* 0 qkv,1 o,2 gate,3 up,4 down */
+/* Copy the layer's norm, norm2 and fused Q|K|V bias to host arrays (NULL skips). */
+SI_API si_status si_layer_vectors_download(si_ctx *ctx, const si_layer *l, float *norm,
+                                           float *norm2, float *bias_qkv);
 
 /* KV cache [batch][max_ctx][Hkv][D], fp16 (kv_f32=0, the reference's format,
  * attention_kernels.h:43-44) or fp32. */

@@ -56,6 +56,16 @@ struct KvRow<D, false> {
   }
 };
 
+// Splits of a token's context depend on its own length only (128 keys per
+// split, at most 64 splits), never on how many tokens share the launch, so a
+// token's attention is bit-identical in a prefill, a batched decode or a
+// decode of its own.
+constexpr int kSplitKeys = 128, kMaxSplits = 64;
+__host__ __device__ __forceinline__ int splits_for(int L) {
+  int s = (L + kSplitKeys - 1) / kSplitKeys;
+  return s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
+}
+
 template <int D, bool KVF32>
 __global__ void __launch_bounds__(kAttnWarps * 32) k_attn_split(const AttnArgs a) {
   pdl_trigger();
@@ -68,7 +78,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32) k_attn_split(const AttnArgs a
   const int seq = a.tok_seq ? a.tok_seq[t] : a.seq0;
   int L = a.tok_ctx ? a.tok_ctx[t] : a.ctx0 + t;
   L = min(L, a.max_ctx);
-  const int chunk = (max(L, 0) + a.nsplit - 1) / a.nsplit;
+  const int ns = splits_for(L);
+  if (split >= ns) return;  // this token needs fewer splits than the grid has
+  const int chunk = (max(L, 0) + ns - 1) / ns;
   const int j0 = split * chunk, j1 = min(max(L, 0), j0 + chunk);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
 
@@ -145,8 +157,10 @@ __global__ void k_attn_combine(const AttnArgs a) {
   pdl_trigger();
   pdl_wait();
   const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
-  const int D = a.head_dim, S = a.nsplit;
-  const float *p = a.part + ((size_t)t * a.n_q_heads + h) * S * (D + 2);
+  const int D = a.head_dim;
+  const int L = min(a.tok_ctx ? a.tok_ctx[t] : a.ctx0 + t, a.max_ctx);
+  const int S = splits_for(L);
+  const float *p = a.part + ((size_t)t * a.n_q_heads + h) * a.nsplit * (D + 2);
   float M = -INFINITY;
   for (int s = 0; s < S; ++s) M = fmaxf(M, p[(size_t)s * (D + 2)]);
   float Ls = 0.0f, Os = 0.0f;
@@ -174,12 +188,9 @@ size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit) {
 }
 
 int attn_pick_splits(int T, int n_kv_heads, int max_len) {
-  int ctas = T * n_kv_heads;
-  int want = (2 * 148 + ctas - 1) / ctas;
-  int cap = (max_len + 63) / 64;
-  int s = want < cap ? want : cap;
-  if (s > 64) s = 64;
-  return s < 1 ? 1 : s;
+  (void)T;
+  (void)n_kv_heads;
+  return splits_for(max_len);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s) {

@@ -700,6 +700,20 @@ extern "C" SI_API si_status si_layer_upload(si_ctx *ctx, const si_dims *d, const
   return SI_OK;
 }
 
+extern "C" SI_API si_status si_layer_vectors_download(si_ctx *ctx, const si_layer *l, float *norm,
+                                                      float *norm2, float *bias_qkv) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l, "null layer");
+  const si_dims &d = l->d;
+  const size_t H = d.hidden, nb = (size_t)(d.n_q_heads + 2 * d.n_kv_heads) * d.head_dim;
+  if (norm && l->norm) SI_CUDA(cudaMemcpyAsync(norm, l->norm, H * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (norm2 && l->norm2) SI_CUDA(cudaMemcpyAsync(norm2, l->norm2, H * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (bias_qkv && l->bias_qkv)
+    SI_CUDA(cudaMemcpyAsync(bias_qkv, l->bias_qkv, nb * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
 extern "C" SI_API si_status si_layer_synth(si_ctx *ctx, const si_dims *d, uint64_t seed,
                                            si_layer **out) {
   SI_TRY(set_device(ctx));

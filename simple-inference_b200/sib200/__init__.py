@@ -11,6 +11,8 @@ import ctypes as C
 import os
 import subprocess
 
+import numpy as np
+
 from . import synth  # noqa: F401
 
 PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -96,6 +98,7 @@ def lib() -> C.CDLL:
         "si_layer_synth": (i32, [vp, C.POINTER(Dims), u64, pp]),
         "si_layer_free": (None, [vp]),
         "si_layer_matrix": (i32, [vp, i32, pp]),
+        "si_layer_vectors_download": (i32, [vp, vp, vp, vp, vp]),
         "si_kv_create": (i32, [vp, C.POINTER(Dims), i32, i32, i32, pp]),
         "si_kv_free": (None, [vp]),
         "si_kv_write": (i32, [vp, vp, i32, i32, i32, vp, vp]),
@@ -308,6 +311,12 @@ class Matrix:
     def download(self, out):
         check(self.ctx.L.si_matrix_download(self.ctx.h, self.h, _p(out)), "si_matrix_download")
 
+    def download_gguf(self):
+        """GGUF row-major Q4_0 bytes as a new numpy array."""
+        out = np.zeros(self.rows * (self.cols // 32) * 18, np.uint8)
+        self.download(out)
+        return out
+
     def layout(self):
         nib, scl = C.c_void_p(), C.c_void_p()
         check(self.ctx.L.si_matrix_layout(self.h, C.byref(nib), C.byref(scl)), "si_matrix_layout")
@@ -328,6 +337,27 @@ class Matrix:
 class Layer:
     def __init__(self, ctx: Context, h, dims):
         self.ctx, self.h, self.dims = ctx, h, dims
+
+    def host(self) -> dict:
+        """The layer as a host dict in the reference's formats (GGUF Q4_0 rows,
+        fp32 vectors), e.g. for checking a synthetic layer against the oracle."""
+        d = self.dims
+        H, D = d["hidden"], d["head_dim"]
+        QD, KVD = d["n_q_heads"] * D, d["n_kv_heads"] * D
+        norm, norm2 = np.zeros(H, np.float32), np.zeros(H, np.float32)
+        bias = np.zeros(QD + 2 * KVD, np.float32)
+        check(self.ctx.L.si_layer_vectors_download(self.ctx.h, self.h, _p(norm), _p(norm2),
+                                                   _p(bias)), "si_layer_vectors_download")
+        qkv = self.matrix(0).download_gguf()
+        rb = H // 32 * 18
+        out = {"wq": qkv[:QD * rb], "wk": qkv[QD * rb:(QD + KVD) * rb],
+               "wv": qkv[(QD + KVD) * rb:], "wo": self.matrix(1).download_gguf(),
+               "norm": norm, "bq": bias[:QD], "bk": bias[QD:QD + KVD], "bv": bias[QD + KVD:],
+               "w_gate": None, "w_up": None, "w_down": None, "norm2": None}
+        if d.get("intermediate", 0) > 0:
+            out.update(w_gate=self.matrix(2).download_gguf(), w_up=self.matrix(3).download_gguf(),
+                       w_down=self.matrix(4).download_gguf(), norm2=norm2)
+        return out
 
     def matrix(self, which: int) -> Matrix:
         m = C.c_void_p()
