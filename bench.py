@@ -42,6 +42,11 @@ PREFILL_M = 2048
 COPIES = 10
 METRIC = "Qwen layer prefill tok/s + decode µs/token; % of HBM / int8-TC roofline"
 INT8_SPEC_TOPS = 4500.0  # B200 dense int8 tensor-core spec; not in MEASURED_PEAKS.json
+SWEEP_M = (1, 16, 128, 512, 2048)  # BASELINE config 1 token counts
+# DRAM bytes (read + write) per launch of each prefill GEMM at M = 2048, from one
+# ncu capture of this bench's first prefill step
+# (profiles/gemm_q4q8_prefill_config1.md); re-measure when the kernels change.
+NCU_TRAFFIC = {"qkv": 5371136, "o": 4920320, "gateup": 19192320, "down": 28481536}
 
 
 def peaks():
@@ -246,7 +251,8 @@ def run_ours(args, rank, world, local_rank):
     M = PREFILL_M
     b = ps.buffers(M)
     steps, per_kernel = graphs_for(M, b)
-    log("graphs captured")
+    kernels_per_step = steps[0].kernels()  # counted from the captured graph
+    log(f"graphs captured ({kernels_per_step} kernels per step)")
     for i in range(args.warmup):
         steps[i % COPIES].launch()
     barrier_sync()
@@ -272,6 +278,22 @@ def run_ours(args, rank, world, local_rank):
     td = max_over_ranks(td)
     kd = kernel_times(dper_kernel, 20)
     log(f"decode kernels {kd}")
+
+    # ---- the config-1 token sweep (device time per step, 10 weight copies) ----
+    sweep = {1: td / dsteps, M: t / args.steps}
+    for Ms in SWEEP_M:
+        if Ms in sweep:
+            continue
+        bs = ps.buffers(Ms)
+        ps.step(bs, Ms, 0)
+        ctx.sync()
+        g = ctx.capture(lambda: [ps.step(bs, Ms, c) for c in range(COPIES)])
+        g.launch()
+        ts = time_region(torch, stream, lambda i: g.launch(), 3) / (3 * COPIES)
+        sweep[Ms] = max_over_ranks(ts)
+        g.free()
+        del bs
+    log(f"sweep {sweep}")
 
     # ---- end to end through the C ABI with pinned host buffers ---------------
     hx = torch.randn(M, H).pin_memory()
@@ -327,10 +349,12 @@ def run_ours(args, rank, world, local_rank):
                      "frac": round(fl[dom_p] / kt[dom_p] / 1e12 / INT8_SPEC_TOPS, 4),
                      "peak_src": "spec (dense int8; MEASURED_PEAKS.json has no int8 figure)",
                      "all": {n: round(fl[n] / kt[n] / 1e12, 2) for n in fl},
-                     "traffic": None},
+                     "traffic": NCU_TRAFFIC.get(dom_p)},
         "e2e": {"value": round(world * M * args.steps / te, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": kernels_per_step * args.steps,
+        "sweep": {str(m): {"ms_per_step": round(sweep[m] * 1e3, 4),
+                           "tok_s": round(world * m / sweep[m], 1)} for m in SWEEP_M},
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:

@@ -339,6 +339,8 @@ SI_API si_status si_graph_begin(si_ctx *ctx);
 SI_API si_status si_graph_end(si_ctx *ctx, si_graph **out);
 SI_API si_status si_graph_launch(si_ctx *ctx, si_graph *g);
 SI_API void si_graph_free(si_graph *g);
+/* Number of kernel launches a replay performs (-1 on error). */
+SI_API int si_graph_kernel_nodes(const si_graph *g);
 
 /* Decode attention alone (parity): q [B][Hq][D] after RoPE. */
 SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *dims,

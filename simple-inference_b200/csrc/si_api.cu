@@ -328,6 +328,20 @@ extern "C" SI_API si_status si_graph_launch(si_ctx *ctx, si_graph *g) {
   return SI_OK;
 }
 
+extern "C" SI_API int si_graph_kernel_nodes(const si_graph *g) {
+  if (!g || !g->graph) return -1;
+  size_t n = 0;
+  if (cudaGraphGetNodes(g->graph, nullptr, &n) != cudaSuccess) return -1;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n && cudaGraphGetNodes(g->graph, nodes.data(), &n) != cudaSuccess) return -1;
+  int k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+  }
+  return k;
+}
+
 extern "C" SI_API void si_graph_free(si_graph *g) {
   if (!g) return;
   if (g->exec) cudaGraphExecDestroy(g->exec);
@@ -469,6 +483,19 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
   return a;
 }
 
+// Kernel choice by token count.  The tcgen05 GEMM keeps each output's
+// block-ordered sum inside one CTA, so a 128-row tile costs K/32 pipelined
+// block steps whatever M is, and few tiles leave SMs idle; the GEMV computes
+// the per-block terms in parallel and then runs a short serial add chain, but
+// re-reads the weights once per 8 tokens.  Measured on B200 at the 1.5B
+// shapes: the GEMM is faster from 128 tokens on, or earlier once it has at
+// least 64 tiles (the gate/up pair at 32 tokens).
+static bool prefer_gemm(int row_tiles, int M) {
+  if (M <= 8) return false;
+  const int tiles = row_tiles * ((M + 127) / 128);
+  return M >= 128 || tiles >= 64;
+}
+
 static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
                         int M, const float *bias, const float *resid, float *out, int kernel) {
   SI_CHECK(w && qs && d && out, "null pointer");
@@ -477,7 +504,8 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
   a.bias = bias;
   a.resid = resid;
   a.out = out;
-  if (kernel < 0) kernel = (M > 8 && si::gemm_tc_supported(w->rows, w->cols, M)) ? 1 : 0;
+  if (kernel < 0)
+    kernel = (prefer_gemm(w->rows / 128, M) && si::gemm_tc_supported(w->rows, w->cols, M)) ? 1 : 0;
   if (kernel == 1) {
     if (!si::gemm_tc_supported(w->rows, w->cols, M))
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
@@ -599,7 +627,8 @@ extern "C" SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate,
   a.out = act_f32;
   a.act_qs = act_qs;
   a.act_d = act_d;
-  if (M > 8 && si::gemm_tc_supported(gate->rows, gate->cols, M)) {
+  if (prefer_gemm(gate->rows / 64, M) && si::gemm_tc_supported(2 * gate->rows, gate->cols, M) &&
+      gate->rows % 64 == 0) {
     SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(gate->cols, M)));
     a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, true, ctx->stream));

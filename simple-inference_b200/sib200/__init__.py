@@ -109,6 +109,7 @@ def lib() -> C.CDLL:
         "si_decode_step_dev": (i32, [vp, vp, vp, vp, i32, vp, vp, i32, C.POINTER(Captures)]),
         "si_prefill": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_prefill_dev": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32]),
+        "si_graph_kernel_nodes": (i32, [vp]),
         "si_tp_split": (None, [i32, i32, i32, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "si_tp_unique_id": (i32, [vp]),
         "si_tp_create": (i32, [vp, vp, i32, i32, pp]),
@@ -289,6 +290,10 @@ class Graph:
 
     def launch(self):
         check(self.ctx.L.si_graph_launch(self.ctx.h, self.h), "si_graph_launch")
+
+    def kernels(self) -> int:
+        """Kernel launches per replay."""
+        return self.ctx.L.si_graph_kernel_nodes(self.h)
 
     def free(self):
         if self.h:

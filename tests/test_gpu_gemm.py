@@ -82,7 +82,7 @@ def test_gemm_swiglu_epilogue(si_ctx, oc, M):
     mg, mu = si_ctx.matrix(g, I, H), si_ctx.matrix(u, I, H)
     qs, d, blocks = q8_dev(si_ctx, x)
     aq, ad, af = z(M * I, torch.int8), z(M * I // 32, torch.int16), z(M * I, torch.float32)
-    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af)   # M > 8 -> tcgen05 path
+    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af)   # 140 pair tiles -> tcgen05 path
     si_ctx.status()
     act = af.cpu().numpy().reshape(M, I)
     blk = z(M * I // 32 * 34, torch.uint8)
