@@ -13,8 +13,9 @@
 // accumulators (512 columns) let the MMA run up to four blocks ahead of the
 // rescale.  The accumulators are pre-set to the integer 0x4B400000 and the MMA
 // accumulates onto it, so each read-back is already the float C + 16*isum; one
-// exact FMA per element folds that into round(isum*dw), then a scalar
-// round-to-nearest multiply by dx and add keep the reference's rounding.
+// exact FMA per element folds that into round(isum*dw), then a
+// round-to-nearest multiply by dx (packed in pairs) and a scalar add keep the
+// reference's rounding.
 //
 // The kernel is persistent (one CTA per SM, tiles visited token-tile fastest)
 // so the TMA / unpack / MMA / epilogue pipeline never drains between tiles.
@@ -332,8 +333,9 @@ constexpr int NCH = NC / CW;  // chunks per block
 static_assert(NCH >= 2 && NCH % 2 == 0, "chunk double-buffering needs an even chunk count");
 
 // One CW-column chunk h of the rescale: acc[h*CW + c] += ((C+D)*dw16 - C*dw16) * dx.
-// The fold is a packed FMA (exact, see above); product and sum stay scalar so
-// both keep the reference's separate roundings.
+// The fold is a packed FMA (exact, see above) and the product a packed
+// multiply; the sum stays scalar so product and sum keep the reference's
+// separate roundings.
 __device__ __forceinline__ void rescale(float (&acc)[NC], int h, const uint32_t (&d)[CW],
                                         const float4 *dx4, float2 dw2, float2 nc2) {
 #pragma unroll
@@ -343,10 +345,14 @@ __device__ __forceinline__ void rescale(float (&acc)[NC], int h, const uint32_t 
     const float2 f1 = make_float2(__uint_as_float(d[4 * c4 + 2]), __uint_as_float(d[4 * c4 + 3]));
     const float2 p0 = fma2_rn(f0, dw2, nc2), p1 = fma2_rn(f1, dw2, nc2);
     const int a = h * CW + 4 * c4;
-    acc[a] = __fadd_rn(acc[a], __fmul_rn(p0.x, x.x));
-    acc[a + 1] = __fadd_rn(acc[a + 1], __fmul_rn(p0.y, x.y));
-    acc[a + 2] = __fadd_rn(acc[a + 2], __fmul_rn(p1.x, x.z));
-    acc[a + 3] = __fadd_rn(acc[a + 3], __fmul_rn(p1.y, x.w));
+    // Packed product, scalar sum: with both packed, ptxas fuses them into one
+    // packed FMA (a single rounding) despite the explicit .rn -- measured here;
+    // either one packed alone keeps both roundings.
+    const float2 q0 = mul2_rn(p0, make_float2(x.x, x.y)), q1 = mul2_rn(p1, make_float2(x.z, x.w));
+    acc[a] = __fadd_rn(acc[a], q0.x);
+    acc[a + 1] = __fadd_rn(acc[a + 1], q0.y);
+    acc[a + 2] = __fadd_rn(acc[a + 2], q1.x);
+    acc[a + 3] = __fadd_rn(acc[a + 3], q1.y);
   }
 }
 
