@@ -40,6 +40,7 @@
 
 #include "si_common.cuh"
 #include "si_kernels.cuh"
+#include "si_tma.cuh"
 
 namespace si {
 namespace tc {
@@ -89,74 +90,6 @@ struct Params {
 // ---------------------------------------------------------------------------
 // PTX helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes (or the hint, 0.5 ms, runs out) instead of spinning on issue slots.
-__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(500000u)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false if the 2 s deadline passes or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_sleep(bar, parity)) {
-    if (*abort) return false;
-    if (globaltimer() - t0 > 2000000000ull) return false;
-  }
-  return true;
-}
-// The same for a whole warp: every lane polls (each observes the phase itself),
-// and all lanes leave together.  A dependent mbarrier wait costs a few hundred
-// cycles on B200 even when the phase is already complete, so the kernel keeps
-// them to one or two per 4-block stage and issues independent ones together.
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort) {
-  const bool ok = mbar_wait(bar, parity, abort);
-  return __all_sync(0xffffffffu, ok) != 0;
-}
-__device__ __forceinline__ bool mbar_wait2_warp(uint32_t b1, uint32_t p1, uint32_t b2, uint32_t p2,
-                                                volatile int *abort) {
-  const bool t1 = mbar_try(b1, p1), t2 = mbar_try(b2, p2);  // both in flight at once
-  bool ok = true;
-  if (!t1) ok = mbar_wait(b1, p1, abort);
-  if (ok && !t2) ok = mbar_wait(b2, p2, abort);
-  return __all_sync(0xffffffffu, ok) != 0;
-}
 // Release / acquire on a shared-memory counter: the cheap path for the
 // epilogue -> MMA "accumulator free" signal (a plain load to spin on).
 __device__ __forceinline__ void smem_add_release(int *p, int v) {
@@ -182,14 +115,6 @@ __device__ __forceinline__ bool counter_wait(const int *p, int target, volatile 
     }
   }
 }
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
                                             int c2, int c3, uint32_t bar) {
   asm volatile(
@@ -197,9 +122,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -687,32 +609,10 @@ __global__ void k_scales_t(const uint16_t *__restrict__ xd, int M, int KB, int M
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-static bool encode(CUtensorMap *m, CUtensorMapDataType dt, int rank, const void *base,
-                   const cuuint64_t *dims, const cuuint64_t *strides, const cuuint32_t *box,
-                   CUtensorMapSwizzle swz) {
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  return encode_fn()(m, dt, rank, const_cast<void *>(base), dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace tc
 
 bool gemm_tc_supported(int N, int K, int M) {
-  return M >= 1 && K % 128 == 0 && N % 128 == 0 && tc::encode_fn() != nullptr;
+  return M >= 1 && K % 128 == 0 && N % 128 == 0 && tma_encode_fn() != nullptr;
 }
 
 size_t gemm_tc_scratch_bytes(int K, int M) {
@@ -742,11 +642,11 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   cuuint64_t dA[2] = {(cuuint64_t)KB * 64, (cuuint64_t)rt};
   cuuint64_t sA[1] = {(cuuint64_t)KB * 512};
   cuuint32_t bA[2] = {256, (cuuint32_t)per};
-  if (!encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dA, sA, bA,
+  if (!tma_encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dA, sA, bA,
               CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   if (swiglu) {
-    if (!encode(&tmA2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dA, sA, bA,
+    if (!tma_encode(&tmA2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dA, sA, bA,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   } else {
@@ -755,13 +655,13 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   cuuint64_t dB[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
   cuuint64_t sB[1] = {(cuuint64_t)a.K};
   cuuint32_t bB[2] = {128, (cuuint32_t)BN};
-  if (!encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.xq, dB, sB, bB,
+  if (!tma_encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.xq, dB, sB, bB,
               CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   cuuint64_t dD[2] = {(cuuint64_t)Mp, (cuuint64_t)KB};
   cuuint64_t sD[1] = {(cuuint64_t)Mp * 4};
   cuuint32_t bD[2] = {(cuuint32_t)BN, (cuuint32_t)KBS};
-  if (!encode(&tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dT, dD, sD, bD,
+  if (!tma_encode(&tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dT, dD, sD, bD,
               CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   // Weight scales [rows/32][KB][32] fp16 as a 2-D view (KB*32, rows/32); box =
@@ -769,11 +669,11 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   cuuint64_t dS[2] = {(cuuint64_t)KB * 32, (cuuint64_t)rt};
   cuuint64_t sS[1] = {(cuuint64_t)KB * 64};
   cuuint32_t bS[2] = {128, (cuuint32_t)per};
-  if (!encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
+  if (!tma_encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
               CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   if (swiglu) {
-    if (!encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
+    if (!tma_encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   } else {

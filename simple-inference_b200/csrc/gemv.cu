@@ -6,274 +6,203 @@
 //
 // Mapping.  One CTA owns an RW-row slice (32, 16 or 8 rows) of one 32-row
 // tile of the SoA layout and the whole K range, for up to MT tokens; narrow
-// slices give matrices with few tiles enough CTAs to fill the GPU.  Weights,
-// their scales and the int8 activations stream through a shared-memory ring
-// of chunks filled by cp.async (16-byte pieces: a slice of one block is RW*16
-// contiguous bytes).  The ring holds up to 8 chunks: for the small decode
-// matrices the whole slice is requested at once; the activation scales of the
-// CTA's tokens are staged once.  The 8 warps
-// split each chunk of blocks and compute the per-block terms in parallel: the
-// int32 block sums are exact, and each term ((float)isum*dw)*dx is rounded
-// exactly as the reference rounds it.  The terms go to shared memory; then one
-// thread per (token, row) adds them to its running sum in block order, while
-// the other warps go on to the next chunk.  The result is bit-identical to the
+// slices give matrices with few tiles enough CTAs to fill the GPU.  The slice
+// streams through a shared-memory ring of up to 8 chunks of CB blocks: one
+// thread issues three 2-D TMA loads per chunk (nibbles RW*16 B x CB, their
+// fp16 scales, the int8 activations of the chunk's blocks) on the stage's
+// mbarrier, so the ring keeps all but one of its chunks in flight for the cost
+// of a few instructions.  Eight compute warps take the chunk's (row, block) pieces and
+// compute the terms in parallel: the int32 block sums are exact and each term
+// ((float)isum*dw)*dx is rounded exactly as the reference rounds it.  The
+// terms go to shared memory, where dedicated merge warps -- one thread per
+// (token, row) -- add them to the running sums in block order while the
+// compute warps go on to the next chunk.  The result is bit-identical to the
 // reference's serial loop.
 //
-// SwiGLU mode runs the gate and up tiles of the same rows through the CTA,
-// then forms act = silu(g) * u and quantises it to Q8_0 directly: the 32 rows
-// of a tile are exactly one Q8 block of the down projection's input.
+// SwiGLU mode streams the gate rows and then the up rows of the same slice
+// through the ring, then forms act = silu(g) * u and quantises it to Q8_0
+// directly: the 32 rows of a tile are exactly one Q8 block of the down
+// projection's input.
 #include "si_common.cuh"
 #include "si_kernels.cuh"
+#include "si_tma.cuh"
 
 namespace si {
 
 namespace {
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kMaxStages = 8;         // chunks in the shared-memory ring, at most
-constexpr size_t kSmemBudget = 200 * 1024;
+constexpr int kComputeWarps = 8;
+constexpr int kStages = 4;                // ring depth, at most
+constexpr size_t kRingBudget = 96 * 1024; // keeps two CTAs per SM when the slice is long
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
   float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
   return __fmul_rn(s, u);
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(dst)),
-               "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// Wait until at most n of this thread's copy groups are still pending.
-__device__ __forceinline__ void cp_async_wait_n(int n) {
-  switch (n) {
-    case 0: cp_async_wait<0>(); break;
-    case 1: cp_async_wait<1>(); break;
-    case 2: cp_async_wait<2>(); break;
-    case 3: cp_async_wait<3>(); break;
-    case 4: cp_async_wait<4>(); break;
-    case 5: cp_async_wait<5>(); break;
-    case 6: cp_async_wait<6>(); break;
-    default: cp_async_wait<7>(); break;
-  }
-}
-
 // Shape of one instantiation.  A chunk is CB blocks of the RW-row slice; the
-// thread (warp w, lane = bo*RW + rl) owns pieces u < U of each chunk: block
-// (w*U + u)*BPL + bo, row rl -- for loading and for computing.
-template <int MT, int U, int RW>
+// compute thread (warp w < 8, lane = bo*RW + rl) owns pieces u < U of each
+// chunk: block (w*U + u)*BPL + bo, row rl.  Term buffers stay <= 32 KB.
+template <int MT, int RW>
 struct Shape {
   static constexpr int BPL = SI_RT / RW;
-  static constexpr int CB = kWarps * U * BPL;
-  static constexpr int NIB = CB * RW * 16;      // bytes of nibbles per chunk
-  static constexpr int SCL = CB * RW * 2;       // bytes of scales per chunk
-  static constexpr int ACT = MT * CB * 32;      // bytes of int8 activations per chunk
+  static constexpr int CB0 = (4096 / (MT * RW)) < (1024 / RW) ? 4096 / (MT * RW) : 1024 / RW;
+  static constexpr int CB = CB0 < 64 ? CB0 : 64;            // nibbles <= 16 KB per stage
+  static constexpr int U = CB / (kComputeWarps * BPL);
+  static constexpr int MW = (MT * RW + 31) / 32;            // merge warps
+  static constexpr int THREADS = (kComputeWarps + MW) * 32;
+  static constexpr int NIB = CB * RW * 16;                  // [CB][RW][16 B]
+  static constexpr int SCL = CB * RW * 2;                   // [CB][RW] fp16
+  static constexpr int ACT = MT * CB * 32;                  // [MT][CB][32 B]
   static constexpr int STAGE = NIB + SCL + ACT;
-  static constexpr int TERMS = MT * CB * RW;    // floats per term buffer
-  // Shared memory: a ring of ns chunks, two term buffers, then the activation
-  // scales [MT][KB] fp16.
-  static constexpr size_t TERM_BYTES = 2 * TERMS * sizeof(float);
-  static size_t smem(int ns, int KB) {
-    return (size_t)ns * STAGE + TERM_BYTES + (size_t)MT * KB * sizeof(uint16_t);
-  }
-  static_assert(SCL / 16 <= kThreads, "one 16-byte scale piece per thread at most");
+  static constexpr int TERMS = MT * CB * RW;                // floats per term buffer
+  // Shared memory: ns ring stages, two term buffers, 128 B of barriers and
+  // flags, the activation scales [MT][KB] fp16, alignment slack.
+  __host__ __device__ static size_t fixed(int ns) { return (size_t)ns * STAGE + 2 * TERMS * sizeof(float) + 128; }
+  static size_t smem(int ns, int KB) { return fixed(ns) + (size_t)MT * KB * sizeof(uint16_t) + 128; }
+  static_assert(U >= 1 && U * kComputeWarps * BPL == CB, "chunk shape");
+  static_assert(NIB % 128 == 0 && SCL % 128 == 0 && ACT % 128 == 0, "TMA destinations");
 };
 
-// Streams the RW-row slice (rows r0.. of tile `tile`) of one matrix -- or, with
-// SWIGLU, of the gate matrix followed by the up matrix as blocks [0, KB) and
-// [KB, 2KB) -- and returns in merge thread t < RW*mcount (token t/RW, row t%RW)
-// the in-order sums: `first` gets bias + the terms of blocks [0, KB), the
-// return value those of [KB, 2KB) (SWIGLU) or the same sum (otherwise).
-template <int MT, int U, int RW, bool SWIGLU>
-__device__ __forceinline__ float slice_dot(const GemvArgs &a, int tile, int r0, int m0,
-                                           int mcount, float &first, uint8_t *smem, int ns) {
-  using S = Shape<MT, U, RW>;
-  constexpr int CB = S::CB, BPL = S::BPL;
-  const int KB = a.K / 32;
-  const int NB = SWIGLU ? 2 * KB : KB;  // blocks streamed
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bo = lane / RW, rl = lane % RW;
-  const int tm = threadIdx.x / RW, tr = threadIdx.x % RW;  // merge role: token, row
-  const int nchunks = (NB + CB - 1) / CB;
-  uint8_t *ring = smem;
-  float *T = reinterpret_cast<float *>(smem + (size_t)ns * S::STAGE);
-  uint16_t *dxs = reinterpret_cast<uint16_t *>(smem + (size_t)ns * S::STAGE + S::TERM_BYTES);
-  const size_t tile_off = (size_t)tile * KB * SI_RT;
-
-  // Weights and their scales of chunk c (no kernel writes them).
-  auto issue_w = [&](int c) {
-    if (c < nchunks) {
-      uint8_t *st = ring + (size_t)(c % ns) * S::STAGE;
-      uint4 *nb = reinterpret_cast<uint4 *>(st);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int bl = (warp * U + u) * BPL + bo;
-        const int b = c * CB + bl;
-        if (b < NB) {
-          const bool second = SWIGLU && b >= KB;
-          const uint8_t *src = second ? a.nib2 : a.nib;
-          const int bb = second ? b - KB : b;
-          cp_async16(nb + bl * RW + rl,
-                     src + ((tile_off + (size_t)bb * SI_RT + r0 + rl) << 4));
-        }
-      }
-      // Scales: 8 rows (16 bytes) per piece.
-      constexpr int PIECES = S::SCL / 16, PPB = RW / 8;
-      if (threadIdx.x < PIECES) {
-        const int bl = threadIdx.x / PPB, rg = (threadIdx.x % PPB) * 8;
-        const int b = c * CB + bl;
-        if (b < NB) {
-          const bool second = SWIGLU && b >= KB;
-          const uint16_t *src = second ? a.scl2 : a.scl;
-          const int bb = second ? b - KB : b;
-          cp_async16(st + S::NIB + (size_t)(bl * RW + rg) * 2,
-                     src + tile_off + (size_t)bb * SI_RT + r0 + rg);
-        }
-      }
-    }
-  };
-  // int8 activations of chunk c's blocks: [token][block][32 B].
-  auto issue_a = [&](int c) {
-    if (c < nchunks) {
-      uint8_t *st = ring + (size_t)(c % ns) * S::STAGE;
-      for (int i = threadIdx.x; i < mcount * CB * 2; i += kThreads) {
-        const int m = i / (CB * 2), bl = (i / 2) % CB, h = i & 1;
-        const int b = c * CB + bl;
-        if (b < NB) {
-          const int bx = (SWIGLU && b >= KB) ? b - KB : b;
-          cp_async16(st + S::NIB + S::SCL + ((size_t)(m * CB + bl) * 32 + h * 16),
-                     a.xq + (size_t)(m0 + m) * a.K + (size_t)bx * 32 + h * 16);
-        }
-      }
-    }
-  };
-
-  // Copy groups: one per prologue chunk (weights only), then one with the
-  // prologue chunks' activations, then one per later chunk (weights and
-  // activations); empty groups keep the count uniform.  The weights of the
-  // prologue chunks are requested before the previous kernel has finished.
-  for (int c = 0; c < ns - 1; ++c) {
-    issue_w(c);
-    cp_async_commit();
-  }
-  pdl_wait();
-  float acc = 0.0f;
-  if (!SWIGLU && a.bias && tm < mcount) acc = a.bias[tile * SI_RT + r0 + tr];
-  for (int c = 0; c < ns - 1; ++c) issue_a(c);
-  cp_async_commit();
-  // All activation scales of the CTA's tokens, once (visible after the first
-  // barrier of the chunk loop).
-  for (int i = threadIdx.x; i < mcount * KB; i += kThreads)
-    dxs[i] = a.xd[(size_t)(m0 + i / KB) * KB + i % KB];
-  for (int c = 0; c < nchunks; ++c) {
-    issue_w(c + ns - 1);
-    issue_a(c + ns - 1);
-    cp_async_commit();
-    // Chunk c's data is in group c (prologue weights) and the activation group,
-    // or in group c+1 for later chunks: at most min(c+1, ns-1) newer groups.
-    cp_async_wait_n(c + 1 < ns - 1 ? c + 1 : ns - 1);
-    __syncthreads();  // chunk c landed for every thread; term buffer c&1 is free
-    const uint8_t *st = ring + (size_t)(c % ns) * S::STAGE;
-    const uint4 *nb = reinterpret_cast<const uint4 *>(st);
-    const uint16_t *sb = reinterpret_cast<const uint16_t *>(st + S::NIB);
-    const int4 *ab = reinterpret_cast<const int4 *>(st + S::NIB + S::SCL);
-    float *Tb = T + (size_t)(c & 1) * S::TERMS;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int bl = (warp * U + u) * BPL + bo;
-      const int b = c * CB + bl;
-      if (b < NB) {
-        const int bx = (SWIGLU && b >= KB) ? b - KB : b;  // activation block
-        const uint4 w = nb[bl * RW + rl];
-        const float dw = f16_to_f32(sb[bl * RW + rl]);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          if (m < mcount) {
-            const int4 a0 = ab[(m * CB + bl) * 2], a1 = ab[(m * CB + bl) * 2 + 1];
-            const float dx = f16_to_f32(dxs[m * KB + bx]);
-            const int is = block_isum(w, a0, a1);
-            Tb[((size_t)m * CB + bl) * RW + rl] = block_term(is, dw, dx);
-            if (!SWIGLU && a.isum_out)
-              a.isum_out[((size_t)(m0 + m) * a.N + (size_t)tile * SI_RT + r0 + rl) * KB + b] = is;
-          }
-        }
-      }
-    }
-    __syncthreads();  // terms of chunk c visible
-    if (tm < mcount) {
-      // The adds are a serial chain; load the terms 16 at a time ahead of it
-      // so only the add latency remains.
-      const int nvalid = min(CB, NB - c * CB);
-      const float *Tm = Tb + (size_t)tm * CB * RW + tr;
-      // Register double buffer: the next 16 terms are loaded while the current
-      // 16 are added.
-      int j = 0;
-      float v[16], w[16];
-      if (nvalid >= 16) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = Tm[q * RW];
-      }
-      for (; j + 16 <= nvalid; j += 16) {
-        const bool next = j + 32 <= nvalid;
-        if (next) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) w[q] = Tm[(j + 16 + q) * RW];
-        }
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if (SWIGLU && c * CB + j + q == KB) {
-            first = acc;
-            acc = 0.0f;
-          }
-          acc = __fadd_rn(acc, v[q]);
-        }
-        if (next) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = w[q];
-        }
-      }
-      for (; j < nvalid; ++j) {
-        if (SWIGLU && c * CB + j == KB) {
-          first = acc;
-          acc = 0.0f;
-        }
-        acc = __fadd_rn(acc, Tm[j * RW]);
-      }
-    }
-  }
-  cp_async_wait<0>();
-  if (!SWIGLU) first = acc;
-  return acc;
-}
-
 // Grid: (N/32 tiles x 32/RW row slices, token groups of MT).
-template <int MT, int U, int RW, bool SWIGLU>
-__global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a, int ns) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int SLICES = SI_RT / RW;
+template <int MT, int RW, bool SWIGLU>
+__global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
+    k_gemv(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
+           const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
+           const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
+  using S = Shape<MT, RW>;
+  constexpr int CB = S::CB, BPL = S::BPL, U = S::U, SLICES = SI_RT / RW;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+  float *T = reinterpret_cast<float *>(smem + ns * S::STAGE);          // [2][MT][CB][RW]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(T + 2 * S::TERMS);      // [ns]
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + kStages);
+  uint16_t *dxs = reinterpret_cast<uint16_t *>(smem + S::fixed(ns));    // [MT][KB]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x / SLICES, r0 = (blockIdx.x % SLICES) * RW;
-  const int m0 = blockIdx.y * MT;
-  const int mcount = min(MT, a.M - m0);
-  const int tm = threadIdx.x / RW, tr = threadIdx.x % RW;
-  const int row = tile * SI_RT + r0 + tr;
+  const int m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
+  const int KB = a.K / 32;
+  const int npass = (KB + CB - 1) / CB;                 // chunks per matrix
+  const int nchunks = SWIGLU ? 2 * npass : npass;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
 
   pdl_trigger();
-  float gate = 0.0f;
-  const float acc = slice_dot<MT, U, RW, SWIGLU>(a, tile, r0, m0, mcount, gate, smem, ns);
-  if (tm >= mcount) return;
+
+  // Chunk c: pass c / npass (gate, then up), blocks [cc*CB, cc*CB + CB).
+  auto load_weights = [&](int c) {
+    const int pass = c / npass, cc = c % npass, slot = c % ns;
+    uint8_t *st = smem + slot * S::STAGE;
+    const int y = tile * KB + cc * CB;
+    mbar_expect_tx(bar(slot), S::STAGE);
+    tma_load_2d(smem_u32(st), pass ? &tmN2 : &tmN, r0 * 2, y, bar(slot));
+    tma_load_2d(smem_u32(st + S::NIB), pass ? &tmS2 : &tmS, r0, y, bar(slot));
+  };
+  auto load_acts = [&](int c) {
+    const int cc = c % npass, slot = c % ns;
+    tma_load_2d(smem_u32(smem + slot * S::STAGE + S::NIB + S::SCL), &tmX, cc * CB * 4, m0,
+                bar(slot));
+  };
+  // Thread 0 owns the barriers until the block barrier below: it sets them up
+  // and requests the weights of the first chunks right away -- before the
+  // previous kernel (which may still be running) has produced the activations.
+  const int pre = nchunks < ns - 1 ? nchunks : ns - 1;
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    for (int i = 0; i < ns; ++i) mbar_init(bar(i), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int c = 0; c < pre; ++c) load_weights(c);
+  }
+  pdl_wait();
+  if (threadIdx.x == 0)
+    for (int c = 0; c < pre; ++c) load_acts(c);
+  for (int i = threadIdx.x; i < mcount * KB; i += blockDim.x)
+    dxs[i] = a.xd[(size_t)(m0 + i / KB) * KB + i % KB];
+
+  // Merge role: thread (token tm, row tr) of the merge warps.
+  const bool merger = warp >= kComputeWarps;
+  const int mt = threadIdx.x - kComputeWarps * 32;
+  const int tm = mt / RW, tr = mt % RW;
+  const bool merging = merger && tm < mcount;
+  float acc = 0.0f, first = 0.0f;
+  if (!SWIGLU && merging && a.bias) acc = a.bias[tile * SI_RT + r0 + tr];
+  __syncthreads();  // dxs visible
+
+  const int bo = lane / RW, rl = lane % RW;
+  for (int c = 0; c < nchunks; ++c) {
+    if (threadIdx.x == 0 && c + ns - 1 < nchunks) {
+      load_weights(c + ns - 1);
+      load_acts(c + ns - 1);
+    }
+    const int cc = c % npass, slot = c % ns;
+    bool ok = true;
+    if (!merger) {
+      ok = mbar_wait(bar(slot), (c / ns) & 1, abort_flag);
+      if (ok) {
+        const uint8_t *st = smem + slot * S::STAGE;
+        const uint4 *nb = reinterpret_cast<const uint4 *>(st);
+        const uint16_t *sb = reinterpret_cast<const uint16_t *>(st + S::NIB);
+        const int4 *ab = reinterpret_cast<const int4 *>(st + S::NIB + S::SCL);
+        float *Tb = T + (size_t)(c & 1) * S::TERMS;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int bl = (warp * U + u) * BPL + bo;
+          const int bx = cc * CB + bl;  // block within the matrix
+          if (bx < KB) {
+            const uint4 w = nb[bl * RW + rl];
+            const float dw = f16_to_f32(sb[bl * RW + rl]);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              if (m < mcount) {
+                const int4 a0 = ab[(m * CB + bl) * 2], a1 = ab[(m * CB + bl) * 2 + 1];
+                const float dx = f16_to_f32(dxs[m * KB + bx]);
+                const int is = block_isum(w, a0, a1);
+                Tb[((size_t)m * CB + bl) * RW + rl] = block_term(is, dw, dx);
+                if (!SWIGLU && a.isum_out)
+                  a.isum_out[((size_t)(m0 + m) * a.N + (size_t)tile * SI_RT + r0 + rl) * KB + bx] =
+                      is;
+              }
+            }
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+    // Terms of chunk c visible; stage c's ring slot is free for chunk c+ns.
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+      return;
+    }
+    if (merging) {
+      // The adds are a serial chain; load the terms 16 at a time ahead of it.
+      const int nvalid = min(CB, KB - cc * CB);
+      const float *Tm = T + (size_t)(c & 1) * S::TERMS + (size_t)tm * CB * RW + tr;
+      if (SWIGLU && c == npass) {  // the up rows begin
+        first = acc;
+        acc = 0.0f;
+      }
+      int j = 0;
+      for (; j + 16 <= nvalid; j += 16) {
+        float v[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[q] = Tm[(j + q) * RW];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) acc = __fadd_rn(acc, v[q]);
+      }
+      for (; j < nvalid; ++j) acc = __fadd_rn(acc, Tm[j * RW]);
+    }
+  }
+  if (!merging) return;
+  const int row = tile * SI_RT + r0 + tr;
   const size_t o = (size_t)(m0 + tm) * a.N + row;
   if (!SWIGLU) {
     a.out[o] = a.resid ? __fadd_rn(a.resid[o], acc) : acc;
   } else {
-    // RW == 32: warp m holds token m's 32 outputs of the tile, one Q8 block.
-    const float act = silu_mul(gate, acc);
+    // RW == 32: merge warp m holds token m's 32 outputs of the tile, one Q8 block.
+    const float act = silu_mul(first, acc);
     if (a.out) a.out[o] = act;
     uint16_t d16;
     const int8_t q = q8_lane(act, d16);
@@ -282,52 +211,80 @@ __global__ void __launch_bounds__(kThreads) k_gemv(const GemvArgs a, int ns) {
   }
 }
 
-template <int MT, int U, int RW, bool SWIGLU>
+template <int MT, int RW, bool SWIGLU>
 cudaError_t run(const GemvArgs &a, cudaStream_t s) {
   static_assert(!SWIGLU || RW == SI_RT, "the SwiGLU Q8 epilogue needs whole 32-row tiles");
-  static_assert(MT * RW <= kThreads, "one merge thread per (token, row)");
-  using S = Shape<MT, U, RW>;
-  // Ring depth: every chunk of the slice in flight at once when it fits (the
-  // small decode matrices are latency-bound), else as many as the budget holds.
-  const int KB = a.K / 32, NB = SWIGLU ? 2 * KB : KB;
-  const int nchunks = (NB + S::CB - 1) / S::CB;
-  int ns = nchunks < 2 ? 2 : (nchunks > kMaxStages ? kMaxStages : nchunks);
-  while (ns > 2 && S::smem(ns, KB) > kSmemBudget) --ns;
+  using S = Shape<MT, RW>;
+  const int KB = a.K / 32, tiles = a.N / SI_RT;
+  // Ring depth: every chunk of the slice in flight at once when the ring fits
+  // the budget (decode matrices are latency-bound), else as many as it holds,
+  // at least 3.
+  const int nchunks = ((KB + S::CB - 1) / S::CB) * (SWIGLU ? 2 : 1);
+  int ns = nchunks < 2 ? 2 : (nchunks < kStages ? nchunks : kStages);
+  while (ns > 3 && (size_t)ns * S::STAGE > kRingBudget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = k_gemv<MT, U, RW, SWIGLU>;
+  // Nibbles [tiles*KB blocks][32 rows x 16 B] as (64 x u64, tiles*KB); scales
+  // [tiles*KB][32] fp16; activations [M][K] int8 as (K/8 x u64, M).
+  CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
+  const cuuint64_t dN[2] = {64, (cuuint64_t)tiles * KB}, sN[1] = {512};
+  const cuuint32_t bN[2] = {(cuuint32_t)RW * 2, (cuuint32_t)S::CB};
+  const cuuint64_t dS[2] = {32, (cuuint64_t)tiles * KB}, sS[1] = {64};
+  const cuuint32_t bS[2] = {(cuuint32_t)RW, (cuuint32_t)S::CB};
+  const cuuint64_t dX[2] = {(cuuint64_t)a.K / 8, (cuuint64_t)a.M}, sX[1] = {(cuuint64_t)a.K};
+  const cuuint32_t bX[2] = {(cuuint32_t)S::CB * 4, (cuuint32_t)MT};
+  if (!tma_encode(&tmN, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dN, sN, bN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.xq, dX, sX, bX,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (SWIGLU) {
+    if (!tma_encode(&tmN2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dN, sN, bN,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !tma_encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    tmN2 = tmN;
+    tmS2 = tmS;
+  }
+  auto kern = k_gemv<MT, RW, SWIGLU>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid(a.N / SI_RT * (SI_RT / RW), (a.M + MT - 1) / MT);
-  return launch_pdl(kern, grid, dim3(kThreads), smem, s, a, ns);
+  dim3 grid(tiles * (SI_RT / RW), (a.M + MT - 1) / MT);
+  return launch_pdl(kern, grid, dim3(S::THREADS), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
 }
 
 // Row slices per tile: enough CTAs to occupy every SM when the matrix has few
 // 32-row tiles (the decode projections of the smaller models).
-template <int MT, int U, bool SWIGLU>
+template <int MT, bool SWIGLU>
 cudaError_t pick_rows(const GemvArgs &a, cudaStream_t s) {
-  if (SWIGLU) return run<MT, U, 32, true>(a, s);
+  if (SWIGLU) return run<MT, 32, true>(a, s);
   const int tiles = a.N / SI_RT;
-  if (tiles < 160) return run<MT, U, 8, false>(a, s);
-  if (tiles < 320) return run<MT, U, 16, false>(a, s);
-  return run<MT, U, 32, false>(a, s);
+  if (tiles < 160) return run<MT, 8, false>(a, s);
+  if (tiles < 320) return run<MT, 16, false>(a, s);
+  return run<MT, 32, false>(a, s);
 }
 
 template <bool SWIGLU>
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t s) {
-  if (a.M <= 1) return pick_rows<1, 4, SWIGLU>(a, s);
-  if (a.M <= 2) return pick_rows<2, 4, SWIGLU>(a, s);
-  if (a.M <= 4) return pick_rows<4, 2, SWIGLU>(a, s);
-  return pick_rows<8, 2, SWIGLU>(a, s);
+  if (a.M <= 1) return pick_rows<1, SWIGLU>(a, s);
+  if (a.M <= 2) return pick_rows<2, SWIGLU>(a, s);
+  if (a.M <= 4) return pick_rows<4, SWIGLU>(a, s);
+  return pick_rows<8, SWIGLU>(a, s);
 }
 }  // namespace
 
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   if (a.M <= 0) return cudaSuccess;
-  if ((reinterpret_cast<uintptr_t>(a.nib) | reinterpret_cast<uintptr_t>(a.scl)) & 15)
+  if (!tma_encode_fn()) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(a.nib) | reinterpret_cast<uintptr_t>(a.scl) |
+       reinterpret_cast<uintptr_t>(a.xq)) & 15)
     return cudaErrorInvalidValue;
   if (swiglu && ((reinterpret_cast<uintptr_t>(a.nib2) | reinterpret_cast<uintptr_t>(a.scl2)) & 15))
     return cudaErrorInvalidValue;
