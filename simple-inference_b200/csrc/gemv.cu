@@ -153,12 +153,16 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
           if (bx < KB) {
             const uint4 w = nb[bl * RW + rl];
             const float dw = f16_to_f32(sb[bl * RW + rl]);
+            const int lo[4] = {lo_nib_s8x16(w.x), lo_nib_s8x16(w.y), lo_nib_s8x16(w.z),
+                               lo_nib_s8x16(w.w)};
+            const int hi[4] = {hi_nib_s8x16(w.x), hi_nib_s8x16(w.y), hi_nib_s8x16(w.z),
+                               hi_nib_s8x16(w.w)};
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
               if (m < mcount) {
                 const int4 a0 = ab[(m * CB + bl) * 2], a1 = ab[(m * CB + bl) * 2 + 1];
                 const float dx = f16_to_f32(dxs[m * KB + bx]);
-                const int is = block_isum(w, a0, a1);
+                const int is = block_isum_unpacked(lo, hi, a0, a1);
                 Tb[((size_t)m * CB + bl) * RW + rl] = block_term(is, dw, dx);
                 if (!SWIGLU && a.isum_out)
                   a.isum_out[((size_t)(m0 + m) * a.N + (size_t)tile * SI_RT + r0 + rl) * KB + bx] =
