@@ -264,14 +264,16 @@ cudaError_t run(const GemvArgs &a, cudaStream_t s) {
   return launch_pdl(kern, grid, dim3(S::THREADS), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
 }
 
-// Row slices per tile: enough CTAs to occupy every SM when the matrix has few
-// 32-row tiles (the decode projections of the smaller models).
+// Row slices per tile: whole 32-row tiles whenever there are enough of them
+// for every SM (each CTA then streams one contiguous region: measured 10-20%
+// faster than split tiles on the 7B/72B matrices), narrower slices only to
+// give matrices with few tiles (the smaller models) enough CTAs.
 template <int MT, bool SWIGLU>
 cudaError_t pick_rows(const GemvArgs &a, cudaStream_t s) {
   if (SWIGLU) return run<MT, 32, true>(a, s);
   const int tiles = a.N / SI_RT;
-  if (tiles < 160) return run<MT, 8, false>(a, s);
-  if (tiles < 320) return run<MT, 16, false>(a, s);
+  if (tiles < 74) return run<MT, 8, false>(a, s);
+  if (tiles < 148) return run<MT, 16, false>(a, s);
   return run<MT, 32, false>(a, s);
 }
 

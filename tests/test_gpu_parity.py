@@ -85,7 +85,8 @@ def test_gemv_golden_bit_exact(si_ctx, golden, oc):
 
 @pytest.mark.parametrize("N,K,M", [(2048, 1536, 1), (1536, 8960, 2), (256, 896, 3),
                                    (128, 4864, 5), (512, 3584, 8), (96, 1536, 13),
-                                   (5120, 512, 2), (10240, 256, 3), (32, 32, 1)])
+                                   (5120, 512, 2), (10240, 256, 3), (32, 32, 1),
+                                   (3072, 640, 4), (2368, 320, 1)])
 def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
     rng = np.random.default_rng(N + K + M)
     w = synth.random_q4(rng, N, K)
