@@ -201,12 +201,103 @@ def time_region(torch, stream, fn, steps):
     return start.elapsed_time(end) / 1e3
 
 
+# ---------------------------------------------------------------------------
+# 8 Qwen2.5-72B layers, tensor-parallel over the ranks
+# ---------------------------------------------------------------------------
+CONFIG4 = dict(hidden=8192, n_q_heads=64, n_kv_heads=8, head_dim=128, intermediate=29568,
+               rope_theta=1e6, rms_eps=1e-6)
+TP_LAYERS, TP_PREFILL, TP_BATCH, TP_DECODE = 8, 4096, 8, 256
+TP_MAX_CTX = TP_PREFILL + TP_DECODE
+
+
+def q4_bytes(n, k):
+    return n * k // 32 * 18
+
+
+def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
+    """The layer stack at TP = world: a 4096-token prefill of sequence 0, then 256
+    decode steps of a batch of 8 (sequence 0 continues its prefill; the other 7
+    hold seeded N(0,1) fp32 histories of 4096 positions).  Each rank holds its
+    heads and its slice of the MLP; the O and down partial sums are all-reduced
+    over NCCL.  Times are device times on the library stream, max over ranks;
+    decode steps are launched eagerly (host context lengths every step)."""
+    import sib200
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    if world > 1:
+        import torch.distributed as tdist
+        box = [sib200.tp_unique_id() if rank == 0 else None]
+        tdist.broadcast_object_list(box, src=0)
+        uid = box[0]
+    else:
+        uid = sib200.tp_unique_id()
+    tp = ctx.tp(uid, rank, world)
+    d, _ = sib200.tp_local_dims(CONFIG4, rank, world)
+    layers = [ctx.layer_tp_synth(CONFIG4, 4 + 1000 * i, rank, world) for i in range(TP_LAYERS)]
+    kvs = [ctx.kv(d, TP_BATCH, TP_MAX_CTX, True) for _ in range(TP_LAYERS)]
+    for i, kv in enumerate(kvs):
+        kv.fill_synth(4 + 1000 * i, 1.0, TP_PREFILL)
+    Hd = CONFIG4["hidden"]
+    g = torch.Generator(device="cuda").manual_seed(4)
+    xp = [torch.randn(TP_PREFILL, Hd, device="cuda", generator=g), torch.empty(TP_PREFILL, Hd, device="cuda")]
+    xd = [torch.randn(TP_BATCH, Hd, device="cuda", generator=g), torch.empty(TP_BATCH, Hd, device="cuda")]
+    x0 = xd[0].clone()
+    torch.cuda.synchronize()
+
+    def prefill(_=0):
+        for j, (layer, kv) in enumerate(zip(layers, kvs)):
+            tp.prefill_dev(layer, kv, 0, xp[j % 2], TP_PREFILL, 0, xp[(j + 1) % 2])
+
+    def decode(step):
+        lens = [TP_PREFILL + step + 1] * TP_BATCH
+        for j, (layer, kv) in enumerate(zip(layers, kvs)):
+            tp.decode_dev(layer, kv, xd[j % 2], lens, xd[(j + 1) % 2])
+
+    prefill()
+    barrier_sync()
+    reps = 2
+    tpf = max_over_ranks(time_region(torch, stream, prefill, reps)) / reps
+    for s in range(3):
+        decode(s)
+    xd[0].copy_(x0)
+    barrier_sync()
+    tdec = max_over_ranks(time_region(torch, stream, decode, TP_DECODE)) / TP_DECODE
+    ctx.status()
+    ok = bool(torch.isfinite(xd[0]).all().item()) and bool(torch.isfinite(xp[0]).all().item())
+
+    D, QD, KVD = CONFIG4["head_dim"], d["n_q_heads"] * CONFIG4["head_dim"], d["n_kv_heads"] * CONFIG4["head_dim"]
+    Il = d["intermediate"]
+    wlayer = q4_bytes(QD + 2 * KVD, Hd) + q4_bytes(Hd, QD) + q4_bytes(2 * Il, Hd) + q4_bytes(Hd, Il)
+    mean_ctx = TP_PREFILL + (TP_DECODE + 1) / 2
+    kv_read = TP_BATCH * mean_ctx * KVD * 2 * 4
+    per_step = TP_LAYERS * (wlayer + kv_read)
+    res = {
+        "workload": "BASELINE config 4: 8 Qwen2.5-72B layers (hidden 8192, 64 Q / 8 KV heads, "
+                    "intermediate 29568), Q4_0 weights, fp32 KV; column-sharded QKV/gate/up, "
+                    "row-sharded o/down, NCCL all-reduce after each row-parallel projection",
+        "tp": world, "finite": ok,
+        "prefill": {"tokens": TP_PREFILL, "ms": round(tpf * 1e3, 3),
+                    "tok_s": round(TP_PREFILL / tpf, 1)},
+        "decode": {"batch": TP_BATCH, "steps": TP_DECODE,
+                   "context": f"{TP_PREFILL + 1}..{TP_MAX_CTX}",
+                   "us_per_step": round(tdec * 1e6, 2),
+                   "us_per_token": round(tdec * 1e6 / TP_BATCH, 3),
+                   "tok_s": round(TP_BATCH / tdec, 1),
+                   "hbm_bytes_per_step_per_rank": int(per_step),
+                   "achieved_gbs_per_rank": round(per_step / tdec / 1e9, 1)},
+        "timing": "CUDA events on the library stream, max over ranks; eager launches",
+    }
+    for o in kvs + layers:
+        o.free()
+    tp.free()
+    return res
+
+
 def run_ours(args, rank, world, local_rank):
     import gc
     import torch
     import sib200
     torch.cuda.set_device(local_rank)
-    ctx = sib200.Context(local_rank, max_positions=4096, rope_theta=1e6, head_dim=128)
+    ctx = sib200.Context(local_rank, max_positions=TP_MAX_CTX, rope_theta=1e6, head_dim=128)
     stream = torch.cuda.ExternalStream(ctx.stream)
     ps = ProjectionSet(ctx, torch, COPIES)
     dist = world > 1
@@ -357,6 +448,11 @@ def run_ours(args, rank, world, local_rank):
                            "tok_s": round(world * m / sweep[m], 1)} for m in SWEEP_M},
         "clocks": clk.summary(),
     }
+    if not args.no_tp:
+        log("tp config 4")
+        result["tp_config4"] = run_tp_config4(args, rank, world, ctx, torch, barrier_sync,
+                                              max_over_ranks)
+        log(f"tp {result['tp_config4']}")
     if rank == 0 and not args.no_cpu_baseline:
         log("cpu baseline")
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
@@ -487,6 +583,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the config-4 tensor-parallel stack")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

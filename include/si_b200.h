@@ -246,7 +246,8 @@ SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate, const si_m
                                   const int8_t *qs_dev, const uint16_t *d_dev, int M,
                                   int8_t *act_qs_dev, uint16_t *act_d_dev, float *act_f32_dev);
 /* RMSNorm over rows of x [M][n] (qwen_one_layer.c:164-169) with optional fp32
- * output and fused Q8 output. */
+ * output and fused Q8 output.  x, w and out 16-byte aligned, qs 4-byte aligned
+ * (SI_ERR_CUDA otherwise). */
 SI_API si_status si_rmsnorm_q8_dev(si_ctx *ctx, const float *x_dev, const float *w_dev, int M,
                                    int n, float eps, float *out_dev, int8_t *qs_dev,
                                    uint16_t *d_dev);

@@ -4,151 +4,267 @@
 // call: per head h, group = h / (Hq/Hkv); score_t = (q . k_t) * (1/sqrtf(D)); an
 // online max/normaliser; out = sum_t softmax_t * v_t.  The standard variant
 // (attention_kernels.h:33-78) computes the same function with materialised scores.
+// The causal prefill gives query token t of a prefill the context
+// prefix + t + 1 (prefill_weight_stationary.h:173-177).
 //
-// GPU form (flash-decoding): the context of each (query token, KV head) is split
-// into nsplit chunks, one CTA per chunk.  A CTA holds the G = Hq/Hkv queries of
-// its group in registers (lane = D/32 dims) and streams its chunk of K/V once:
-// each K/V row is read once for all G heads.  Warps take tokens round-robin and
-// keep their own (max, normaliser, accumulator) per head; the warps, then the
-// chunks, are merged with the usual rescaling by exp(m_i - m).  Summation order
-// differs from the reference's serial loop, so results agree to fp32 rounding
-// (the reference's own standard-vs-flash check uses 1e-5 + 1e-4*|x|).
-// The same kernel serves causal prefill: query token t of a prefill sees
-// context prefix + t + 1 (prefill_weight_stationary.h:173-177).
+// Order of the arithmetic.  Every (query token, head) is evaluated by one fixed
+// procedure whatever kernel runs it and however many tokens share the launch,
+// so a token's output is bit-identical in a prefill, a batched decode and a
+// decode of its own:
+//   * keys in sub-tiles of 32 aligned positions, splits of 4 sub-tiles (128);
+//   * score = fmaf chain over d = 0..D-1 from 0, times 1/sqrt(D); keys at or
+//     past the context length are -inf;
+//   * per sub-tile: m = max, p = expf(s - m), l = xor-butterfly sum of p over the
+//     32 lanes (16, 8, 4, 2, 1), o[d] = fmaf chain over the keys in order from 0;
+//   * the sub-tiles of a split, then the splits, merged in order by
+//     M' = max(M, m), a = expf(M - M'), b = expf(m - M'), L = fmaf(L, a, l*b),
+//     O = fmaf(O, a, o*b); out = O / L.
+// The reference's serial loop sums in another order, so results agree with it
+// to fp32 rounding (its own standard-vs-flash check uses 1e-5 + 1e-4*|x|).
+//
+// Kernels.  Decode (any token count, per-token context lengths): one CTA per
+// (split, KV head, token), one warp per sub-tile; a warp stages its 32 K rows
+// in shared memory with cp.async (16-byte chunks XOR-swizzled by row so that
+// lane = key reads are conflict-free), scores all G = Hq/Hkv heads of the group
+// with lane = key, and accumulates P.V with lane = dims straight from the
+// V rows (coalesced).  Splits of a token are merged by k_attn_combine.
+// Prefill (contiguous tokens of one sequence): one CTA per (64 query rows =
+// 64/G tokens x G heads, KV head) walks the splits in order with K and V tiles
+// of 128 keys in shared memory, S = Q.K^T and P.V as register-tiled fp32 FMA
+// chains, and the same merges, so it needs no split scratch.
 #include "si_common.cuh"
 #include "si_kernels.cuh"
+#include "si_tma.cuh"
 
 namespace si {
 
 namespace {
-constexpr int kAttnWarps = 4;
 constexpr int kMaxGroup = 8;
+constexpr int kSub = 32;           // keys per sub-tile
+constexpr int kSplitKeys = 128;    // keys per split
+constexpr int kSubPerSplit = kSplitKeys / kSub;
+constexpr int kPrefillRows = 64;   // query rows (token x head) per prefill CTA
+constexpr int kPrefillThreads = 256;
+constexpr int kPrefillMinTokens = 16;
 
-template <int D, bool KVF32>
-struct KvRow;
-template <int D>
-struct KvRow<D, true> {
-  static constexpr int N = D / 32;
-  __device__ static void load(const void *base, size_t off, int lane, float (&v)[N]) {
-    const float *p = static_cast<const float *>(base) + off + lane * N;
-    if constexpr (N == 4) {
-      float4 x = __ldg(reinterpret_cast<const float4 *>(p));
-      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-    } else {
-      float2 x = __ldg(reinterpret_cast<const float2 *>(p));
-      v[0] = x.x; v[1] = x.y;
-    }
-  }
-};
-template <int D>
-struct KvRow<D, false> {
-  static constexpr int N = D / 32;
-  __device__ static void load(const void *base, size_t off, int lane, float (&v)[N]) {
-    const uint16_t *p = static_cast<const uint16_t *>(base) + off + lane * N;
-    if constexpr (N == 4) {
-      uint2 x = __ldg(reinterpret_cast<const uint2 *>(p));
-      v[0] = f16_to_f32((uint16_t)x.x); v[1] = f16_to_f32((uint16_t)(x.x >> 16));
-      v[2] = f16_to_f32((uint16_t)x.y); v[3] = f16_to_f32((uint16_t)(x.y >> 16));
-    } else {
-      uint32_t x = __ldg(reinterpret_cast<const uint32_t *>(p));
-      v[0] = f16_to_f32((uint16_t)x); v[1] = f16_to_f32((uint16_t)(x >> 16));
-    }
-  }
-};
-
-// Splits of a token's context depend on its own length only (128 keys per
-// split, at most 64 splits), never on how many tokens share the launch, so a
-// token's attention is bit-identical in a prefill, a batched decode or a
-// decode of its own.
-constexpr int kSplitKeys = 128, kMaxSplits = 64;
 __host__ __device__ __forceinline__ int splits_for(int L) {
-  int s = (L + kSplitKeys - 1) / kSplitKeys;
-  return s < 1 ? 1 : (s > kMaxSplits ? kMaxSplits : s);
+  const int s = (L + kSplitKeys - 1) / kSplitKeys;
+  return s < 1 ? 1 : s;
 }
 
-template <int D, bool KVF32>
-__global__ void __launch_bounds__(kAttnWarps * 32) k_attn_split(const AttnArgs a) {
+__device__ __forceinline__ void merge_ml(float &M, float &L, float m, float l, float &a,
+                                         float &b) {
+  const float Mn = fmaxf(M, m);
+  a = expf(__fsub_rn(M, Mn));
+  b = expf(__fsub_rn(m, Mn));
+  L = fmaf(L, a, __fmul_rn(l, b));
+  M = Mn;
+}
+__device__ __forceinline__ float merge_o(float O, float a, float o, float b) {
+  return fmaf(O, a, __fmul_rn(o, b));
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Four consecutive elements of a K/V row as floats (fp16 rows convert exactly).
+template <bool F32>
+__device__ __forceinline__ float4 load4(const void *p) {
+  if constexpr (F32) {
+    return *reinterpret_cast<const float4 *>(p);
+  } else {
+    const uint2 x = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(f16_to_f32((uint16_t)x.x), f16_to_f32((uint16_t)(x.x >> 16)),
+                       f16_to_f32((uint16_t)x.y), f16_to_f32((uint16_t)(x.y >> 16)));
+  }
+}
+
+__device__ __forceinline__ int ctx_of(const AttnArgs &a, int t) {
+  const int L = a.tok_ctx ? a.tok_ctx[t] : a.ctx0 + t;
+  return L < a.max_ctx ? L : a.max_ctx;
+}
+
+// ---------------------------------------------------------------------------
+// decode: one CTA per (split, KV head, token), one warp per sub-tile
+// ---------------------------------------------------------------------------
+template <int D, bool F32>
+struct DecShape {
+  static constexpr int ES = F32 ? 4 : 2;
+  static constexpr int RB = D * ES;     // bytes per K row
+  static constexpr int CPR = RB / 16;   // 16-byte chunks per row (8..32)
+  static constexpr int Q = kMaxGroup * D * 4;
+  static constexpr int KW = kSub * RB;  // one warp's K rows (>= its G x D merge floats)
+  static constexpr int P = kSub * kMaxGroup * 4;
+  static constexpr int bytes() { return Q + kSubPerSplit * (KW + P) + kSubPerSplit * kMaxGroup * 8; }
+  static_assert(CPR >= 8, "the row swizzle needs at least 8 chunks per row");
+  static_assert(KW >= kMaxGroup * D * 4, "the merge floats must fit over the K rows");
+};
+
+template <int D, bool F32>
+__global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a) {
+  using S = DecShape<D, F32>;
+  constexpr int NV = D / 32;  // dims per lane in P.V
+  extern __shared__ __align__(16) uint8_t smem[];
+  float *q_s = reinterpret_cast<float *>(smem);                       // [G][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *k_w = smem + S::Q + warp * S::KW;                           // [32][RB] swizzled
+  float *p_w = reinterpret_cast<float *>(smem + S::Q + kSubPerSplit * S::KW) +
+               warp * kSub * kMaxGroup;                                // [32][8]
+  float2 *ml_s = reinterpret_cast<float2 *>(smem + S::Q + kSubPerSplit * (S::KW + S::P));
+
   pdl_trigger();
   pdl_wait();
-  constexpr int N = D / 32;
   const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int Hq = a.n_q_heads, Hkv = a.n_kv_heads;
-  const int G = Hq / Hkv;
+  const int Hq = a.n_q_heads, Hkv = a.n_kv_heads, G = Hq / Hkv;
   const int seq = a.tok_seq ? a.tok_seq[t] : a.seq0;
-  int L = a.tok_ctx ? a.tok_ctx[t] : a.ctx0 + t;
-  L = min(L, a.max_ctx);
+  const int L = ctx_of(a, t);
   const int ns = splits_for(L);
   if (split >= ns) return;  // this token needs fewer splits than the grid has
-  const int chunk = (max(L, 0) + ns - 1) / ns;
-  const int j0 = split * chunk, j1 = min(max(L, 0), j0 + chunk);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+  const int key0 = (split * kSubPerSplit + warp) * kSub;
+  const int nvalid = L - key0 < 0 ? 0 : (L - key0 > kSub ? kSub : L - key0);
+  const size_t rowstride = (size_t)Hkv * D;
+  const size_t base = (size_t)seq * a.max_ctx * rowstride + (size_t)kvh * D;
+  const uint8_t *kg = static_cast<const uint8_t *>(a.kc) + base * S::ES;
+  const uint8_t *vg = static_cast<const uint8_t *>(a.vc) + base * S::ES;
 
-  float q[kMaxGroup][N], o[kMaxGroup][N], m[kMaxGroup], l[kMaxGroup];
+  // This warp's K rows into shared memory; the group's queries.
+  for (int i = lane; i < nvalid * S::CPR; i += 32) {
+    const int r = i / S::CPR, c = i % S::CPR;
+    cp_async16(smem_u32(k_w + r * S::RB + ((c ^ (r & 7)) << 4)),
+               kg + ((size_t)(key0 + r) * rowstride) * S::ES + c * 16, 16);
+  }
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x)
+    q_s[i] = a.q[((size_t)t * Hq + kvh * G) * D + i];
+  cp_async_wait_all();
+  __syncthreads();
+
+  float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][NV];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      o[g][i] = 0.0f;
-      q[g][i] = g < G ? a.q[((size_t)t * Hq + kvh * G + g) * D + lane * N + i] : 0.0f;
-    }
+    for (int j = 0; j < NV; ++j) o[g][j] = 0.0f;
   }
-  const size_t rowstride = (size_t)Hkv * D;
-  const size_t base = ((size_t)seq * a.max_ctx) * rowstride + (size_t)kvh * D;
-  for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-    float k[N], v[N];
-    KvRow<D, KVF32>::load(a.kc, base + (size_t)j * rowstride, lane, k);
-    KvRow<D, KVF32>::load(a.vc, base + (size_t)j * rowstride, lane, v);
+  if (nvalid > 0) {
+    // Scores, lane = key.
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+    float s[kMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) s[g] = 0.0f;
+    const uint8_t *kr = k_w + lane * S::RB;
+#pragma unroll 4
+    for (int c4 = 0; c4 < D / 4; ++c4) {
+      // dims 4*c4 .. 4*c4+3 live in chunk (4*c4*ES)/16 at byte (4*c4*ES)%16
+      const int byte = c4 * 4 * S::ES;
+      const int c = byte >> 4;
+      const float4 k = load4<F32>(kr + (((c ^ (lane & 7)) << 4) | (byte & 15)));
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) {
+        if (g < G) {
+          const float4 q = *reinterpret_cast<const float4 *>(q_s + g * D + c4 * 4);
+          s[g] = fmaf(q.x, k.x, s[g]);
+          s[g] = fmaf(q.y, k.y, s[g]);
+          s[g] = fmaf(q.z, k.z, s[g]);
+          s[g] = fmaf(q.w, k.w, s[g]);
+        }
+      }
+    }
+    const bool valid = lane < nvalid;
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
       if (g < G) {
-        float p = 0.0f;
+        const float sc = valid ? __fmul_rn(s[g], scale) : -INFINITY;
+        m[g] = warp_max(sc);
+        const float p = expf(__fsub_rn(sc, m[g]));
+        l[g] = warp_sum(p);
+        p_w[lane * kMaxGroup + g] = p;
+      }
+    }
+    __syncwarp();
+    // P.V, lane = dims NV*lane .. NV*lane+NV-1, keys in order.
+    const uint8_t *vr = vg + (size_t)key0 * rowstride * S::ES + lane * NV * S::ES;
+    for (int k0 = 0; k0 < nvalid; k0 += 8) {
+      float v[8][NV];
 #pragma unroll
-        for (int i = 0; i < N; ++i) p = fmaf(q[g][i], k[i], p);
+      for (int k = 0; k < 8; ++k) {
+        if (k0 + k < nvalid) {
+          const uint8_t *p = vr + (size_t)(k0 + k) * rowstride * S::ES;
+          if constexpr (NV == 4) {
+            const float4 x = load4<F32>(p);
+            v[k][0] = x.x; v[k][1] = x.y; v[k][2] = x.z; v[k][3] = x.w;
+          } else if constexpr (F32) {
+            const float2 x = *reinterpret_cast<const float2 *>(p);
+            v[k][0] = x.x; v[k][1] = x.y;
+          } else {
+            const uint32_t x = *reinterpret_cast<const uint32_t *>(p);
+            v[k][0] = f16_to_f32((uint16_t)x); v[k][1] = f16_to_f32((uint16_t)(x >> 16));
+          }
+        }
+      }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
-        float s = p * scale;
-        float mn = fmaxf(m[g], s);
-        float corr = expf(m[g] - mn);
-        float e = expf(s - mn);
-        l[g] = fmaf(l[g], corr, e);
+      for (int k = 0; k < 8; ++k) {
+        if (k0 + k < nvalid) {
+          const float4 pa = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup);
+          const float4 pb = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup + 4);
+          const float pk[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-        for (int i = 0; i < N; ++i) o[g][i] = fmaf(o[g][i], corr, e * v[i]);
-        m[g] = mn;
+          for (int g = 0; g < kMaxGroup; ++g)
+            if (g < G)
+#pragma unroll
+              for (int j = 0; j < NV; ++j) o[g][j] = fmaf(pk[g], v[k][j], o[g][j]);
+        }
       }
     }
   }
-  // Merge the warps of this CTA.
-  __shared__ float sm_m[kAttnWarps][kMaxGroup], sm_l[kAttnWarps][kMaxGroup];
-  __shared__ float sm_o[kAttnWarps][kMaxGroup][D];
-  if (lane == 0)
-    for (int g = 0; g < G; ++g) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+  // Merge the sub-tiles of this split in order (warp 0 first).
+  __syncwarp();
+  float *o_w = reinterpret_cast<float *>(k_w);  // [G][D], over this warp's K rows
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g)
     if (g < G)
 #pragma unroll
-      for (int i = 0; i < N; ++i) sm_o[warp][g][lane * N + i] = o[g][i];
+      for (int j = 0; j < NV; ++j) o_w[g * D + lane * NV + j] = o[g][j];
+  if (lane == 0)
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g)
+      if (g < G) ml_s[warp * kMaxGroup + g] = make_float2(m[g], l[g]);
   __syncthreads();
+  const int nsub = (L - split * kSplitKeys + kSub - 1) / kSub;  // valid sub-tiles, >= 1
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    int g = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][g]);
-    float Ls = 0.0f, Os = 0.0f;
-    if (M != -INFINITY)
-      for (int w = 0; w < kAttnWarps; ++w) {
-        float f = expf(sm_m[w][g] - M);
-        Ls = fmaf(sm_l[w][g], f, Ls);
-        Os = fmaf(sm_o[w][g][d], f, Os);
-      }
+    const int g = idx / D, d = idx % D;
+    float2 ml = ml_s[g];
+    float M = ml.x, Ls = ml.y;
+    float O = reinterpret_cast<const float *>(smem + S::Q)[g * D + d];
+    for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
+      ml = ml_s[w * kMaxGroup + g];
+      float fa, fb;
+      merge_ml(M, Ls, ml.x, ml.y, fa, fb);
+      O = merge_o(O, fa, reinterpret_cast<const float *>(smem + S::Q + w * S::KW)[g * D + d], fb);
+    }
     const int h = kvh * G + g;
-    if (a.nsplit == 1) {
-      a.out[((size_t)t * Hq + h) * D + d] = Ls > 0.0f ? Os / Ls : 0.0f;
+    if (a.nsplit == 1) {  // no combine pass follows
+      a.out[((size_t)t * Hq + h) * D + d] = __fdiv_rn(O, Ls);
     } else {
       float *p = a.part + (((size_t)t * Hq + h) * a.nsplit + split) * (D + 2);
       if (d == 0) { p[0] = M; p[1] = Ls; }
-      p[2 + d] = Os;
+      p[2 + d] = O;
     }
   }
 }
@@ -158,26 +274,286 @@ __global__ void k_attn_combine(const AttnArgs a) {
   pdl_wait();
   const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
   const int D = a.head_dim;
-  const int L = min(a.tok_ctx ? a.tok_ctx[t] : a.ctx0 + t, a.max_ctx);
-  const int S = splits_for(L);
+  const int S = splits_for(ctx_of(a, t));
   const float *p = a.part + ((size_t)t * a.n_q_heads + h) * a.nsplit * (D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, p[(size_t)s * (D + 2)]);
-  float Ls = 0.0f, Os = 0.0f;
-  if (M != -INFINITY)
-    for (int s = 0; s < S; ++s) {
-      const float *ps = p + (size_t)s * (D + 2);
-      float f = expf(ps[0] - M);
-      Ls = fmaf(ps[1], f, Ls);
-      Os = fmaf(ps[2 + d], f, Os);
+  float M = p[0], Ls = p[1], O = p[2 + d];
+  for (int s = 1; s < S; ++s) {
+    const float *ps = p + (size_t)s * (D + 2);
+    float fa, fb;
+    merge_ml(M, Ls, ps[0], ps[1], fa, fb);
+    O = merge_o(O, fa, ps[2 + d], fb);
+  }
+  a.out[((size_t)t * a.n_q_heads + h) * D + d] = __fdiv_rn(O, Ls);
+}
+
+// ---------------------------------------------------------------------------
+// prefill: one CTA per (64 query rows, KV head), splits in order
+// ---------------------------------------------------------------------------
+template <int D, bool F32>
+struct PfShape {
+  static constexpr int ES = F32 ? 4 : 2;
+  static constexpr int QS = D + 4;                  // q row stride (floats)
+  static constexpr int KS = D + 16 / ES;            // k row stride (elements), +16 B
+  static constexpr int SS = kSplitKeys + 4;         // score row stride (floats)
+  static constexpr int Q = kPrefillRows * QS * 4;
+  static constexpr int K = kSplitKeys * KS * ES;
+  static constexpr int V = kSplitKeys * D * ES;
+  static constexpr int SC = kPrefillRows * SS * 4;
+  // per row: running (M, L), sub-tile (m, l) x4, sub-tile factors (a, b) x4,
+  // split factors (a, b)
+  static constexpr int ROW = kPrefillRows * (2 + 8 + 8 + 2) * 4;
+  static constexpr int bytes() { return Q + K + V + SC + ROW; }
+};
+
+template <int D, bool F32>
+__global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnArgs a) {
+  using S = PfShape<D, F32>;
+  constexpr int DG = D / 16;   // dims per thread in P.V (two float4 for D = 128)
+  extern __shared__ __align__(16) uint8_t smem[];
+  float *q_s = reinterpret_cast<float *>(smem);
+  uint8_t *k_s = smem + S::Q;
+  uint8_t *v_s = smem + S::Q + S::K;
+  float *s_s = reinterpret_cast<float *>(smem + S::Q + S::K + S::V);
+  float *rw = reinterpret_cast<float *>(smem + S::Q + S::K + S::V + S::SC);
+  float *run_m = rw, *run_l = rw + kPrefillRows;
+  float *sub_m = rw + 2 * kPrefillRows, *sub_l = sub_m + 4 * kPrefillRows;
+  float *fa_s = sub_l + 4 * kPrefillRows, *fb_s = fa_s + 4 * kPrefillRows;
+  float *sa_s = fb_s + 4 * kPrefillRows, *sb_s = sa_s + kPrefillRows;
+
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hq = a.n_q_heads, Hkv = a.n_kv_heads, G = Hq / Hkv;
+  const int TQ = kPrefillRows / G, R = TQ * G;
+  const int tile = gridDim.x - 1 - blockIdx.x;  // longest contexts first
+  const int kvh = blockIdx.y;
+  const int t0 = tile * TQ;
+  const int tlast = min(a.T, t0 + TQ) - 1;
+  const int Lmax = min(a.ctx0 + tlast, a.max_ctx);
+  const int nsplit = splits_for(Lmax);
+  const size_t rowstride = (size_t)Hkv * D;
+  const size_t base = (size_t)a.seq0 * a.max_ctx * rowstride + (size_t)kvh * D;
+  const uint8_t *kg = static_cast<const uint8_t *>(a.kc) + base * S::ES;
+  const uint8_t *vg = static_cast<const uint8_t *>(a.vc) + base * S::ES;
+  auto row_ctx = [&](int r) {  // context of row r, 0 for padding rows
+    const int t = t0 + r / G;
+    return (r < R && t <= tlast) ? min(a.ctx0 + t, a.max_ctx) : 0;
+  };
+
+  for (int i = tid; i < kPrefillRows * (D / 4); i += kPrefillThreads) {
+    const int r = i / (D / 4), c = i % (D / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row_ctx(r) > 0) {
+      const int t = t0 + r / G, h = kvh * G + r % G;
+      v = *reinterpret_cast<const float4 *>(a.q + ((size_t)t * Hq + h) * D + c * 4);
     }
-  a.out[((size_t)t * a.n_q_heads + h) * D + d] = Ls > 0.0f ? Os / Ls : 0.0f;
+    *reinterpret_cast<float4 *>(q_s + r * S::QS + c * 4) = v;
+  }
+
+  // QK^T tiling: rows rg + 16i (i < 4), keys kq + 16j (j < 8).
+  const int rg = tid & 15, kq = tid >> 4;
+  // P.V tiling: rows rg + 16i, dims dq*4 + 64*jj (jj < DG/4).
+  const int dq = tid >> 4;
+  int Lr[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) Lr[i] = row_ctx(rg + 16 * i);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+  float O[4][DG];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < DG; ++j) O[i][j] = 0.0f;
+
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const int key0 = sp * kSplitKeys;
+    const int nkeys = min(kSplitKeys, Lmax - key0);
+    __syncthreads();  // previous split done with the tiles
+    constexpr int CPR = D * S::ES / 16;
+    for (int i = tid; i < kSplitKeys * CPR; i += kPrefillThreads) {
+      const int r = i / CPR, c = i % CPR;
+      const bool ok = r < nkeys;
+      const size_t off = ((size_t)(ok ? key0 + r : 0) * rowstride) * S::ES + c * 16;
+      cp_async16(smem_u32(k_s + r * S::KS * S::ES + c * 16), kg + off, ok ? 16 : 0);
+      cp_async16(smem_u32(v_s + r * D * S::ES + c * 16), vg + off, ok ? 16 : 0);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // Scores.
+    {
+      float acc[4][8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
+      for (int c4 = 0; c4 < D / 4; ++c4) {
+        float4 q[4], k[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          q[i] = *reinterpret_cast<const float4 *>(q_s + (rg + 16 * i) * S::QS + c4 * 4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          k[j] = load4<F32>(k_s + ((kq + 16 * j) * S::KS + c4 * 4) * S::ES);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc[i][j] = fmaf(q[i].x, k[j].x, acc[i][j]);
+            acc[i][j] = fmaf(q[i].y, k[j].y, acc[i][j]);
+            acc[i][j] = fmaf(q[i].z, k[j].z, acc[i][j]);
+            acc[i][j] = fmaf(q[i].w, k[j].w, acc[i][j]);
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int key = kq + 16 * j;
+          s_s[(rg + 16 * i) * S::SS + key] =
+              key0 + key < Lr[i] ? __fmul_rn(acc[i][j], scale) : -INFINITY;
+        }
+    }
+    __syncthreads();
+
+    // Sub-tile softmax, lane = key: warp w takes rows 8w .. 8w+7.
+    for (int task = 0; task < 8 * kSubPerSplit; ++task) {
+      const int r = warp * 8 + task / kSubPerSplit, u = task % kSubPerSplit;
+      const int Lrow = row_ctx(r);
+      float *sp_row = s_s + r * S::SS + u * kSub;
+      if (key0 + u * kSub < Lrow) {
+        const float sc = sp_row[lane];
+        const float mx = warp_max(sc);
+        const float p = expf(__fsub_rn(sc, mx));
+        const float ls = warp_sum(p);
+        sp_row[lane] = p;
+        if (lane == 0) { sub_m[r * 4 + u] = mx; sub_l[r * 4 + u] = ls; }
+      } else {
+        sp_row[lane] = 0.0f;
+      }
+    }
+    __syncthreads();
+    // Merge factors per row: sub-tiles of this split, then the split itself.
+    if (tid < kPrefillRows) {
+      const int r = tid, Lrow = row_ctx(r);
+      if (key0 < Lrow) {
+        float M = sub_m[r * 4], Ls = sub_l[r * 4];
+        for (int u = 1; u < kSubPerSplit && key0 + u * kSub < Lrow; ++u)
+          merge_ml(M, Ls, sub_m[r * 4 + u], sub_l[r * 4 + u], fa_s[r * 4 + u], fb_s[r * 4 + u]);
+        if (sp == 0) {
+          run_m[r] = M;
+          run_l[r] = Ls;
+        } else {
+          float rm = run_m[r], rl = run_l[r];
+          merge_ml(rm, rl, M, Ls, sa_s[r], sb_s[r]);
+          run_m[r] = rm;
+          run_l[r] = rl;
+        }
+      }
+    }
+    __syncthreads();
+
+    // P.V per sub-tile, merged into the split, then into the running output.
+    float Os[4][DG];
+    for (int u = 0; u < kSubPerSplit && key0 + u * kSub < Lmax; ++u) {
+      float acc[4][DG];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < DG; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
+      for (int k = 0; k < kSub; ++k) {
+        const int kk = u * kSub + k;
+        float p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = s_s[(rg + 16 * i) * S::SS + kk];
+#pragma unroll
+        for (int jj = 0; jj < DG / 4; ++jj) {
+          const float4 v = load4<F32>(v_s + (kk * D + dq * 4 + 64 * jj) * S::ES);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[i][jj * 4 + 0] = fmaf(p[i], v.x, acc[i][jj * 4 + 0]);
+            acc[i][jj * 4 + 1] = fmaf(p[i], v.y, acc[i][jj * 4 + 1]);
+            acc[i][jj * 4 + 2] = fmaf(p[i], v.z, acc[i][jj * 4 + 2]);
+            acc[i][jj * 4 + 3] = fmaf(p[i], v.w, acc[i][jj * 4 + 3]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = rg + 16 * i;
+        if (key0 + u * kSub < Lr[i]) {
+          if (u == 0) {
+#pragma unroll
+            for (int j = 0; j < DG; ++j) Os[i][j] = acc[i][j];
+          } else {
+            const float fa = fa_s[r * 4 + u], fb = fb_s[r * 4 + u];
+#pragma unroll
+            for (int j = 0; j < DG; ++j) Os[i][j] = merge_o(Os[i][j], fa, acc[i][j], fb);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = rg + 16 * i;
+      if (key0 < Lr[i]) {
+        if (sp == 0) {
+#pragma unroll
+          for (int j = 0; j < DG; ++j) O[i][j] = Os[i][j];
+        } else {
+          const float fa = sa_s[r], fb = sb_s[r];
+#pragma unroll
+          for (int j = 0; j < DG; ++j) O[i][j] = merge_o(O[i][j], fa, Os[i][j], fb);
+        }
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = rg + 16 * i;
+    if (Lr[i] > 0) {
+      const int t = t0 + r / G, h = kvh * G + r % G;
+      const float Ls = run_l[r];
+      float *out = a.out + ((size_t)t * Hq + h) * D;
+#pragma unroll
+      for (int jj = 0; jj < DG / 4; ++jj) {
+        float4 y;
+        y.x = __fdiv_rn(O[i][jj * 4 + 0], Ls);
+        y.y = __fdiv_rn(O[i][jj * 4 + 1], Ls);
+        y.z = __fdiv_rn(O[i][jj * 4 + 2], Ls);
+        y.w = __fdiv_rn(O[i][jj * 4 + 3], Ls);
+        *reinterpret_cast<float4 *>(out + dq * 4 + 64 * jj) = y;
+      }
+    }
+  }
+}
+
+bool use_prefill(const AttnArgs &a) { return !a.tok_ctx && !a.tok_seq && a.T >= kPrefillMinTokens; }
+
+template <class K>
+cudaError_t with_smem(K kern, int bytes) {
+  return bytes > 48 * 1024
+             ? cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)
+             : cudaSuccess;
 }
 
 template <int D, bool F32>
 cudaError_t run(const AttnArgs &a, cudaStream_t s) {
-  dim3 grid(a.nsplit, a.n_kv_heads, a.T);
-  cudaError_t e = launch_pdl(k_attn_split<D, F32>, grid, dim3(kAttnWarps * 32), 0, s, a);
+  if (use_prefill(a)) {
+    using P = PfShape<D, F32>;
+    const int G = a.n_q_heads / a.n_kv_heads, TQ = kPrefillRows / G;
+    cudaError_t e = with_smem(k_attn_prefill<D, F32>, P::bytes());
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_attn_prefill<D, F32>, dim3((a.T + TQ - 1) / TQ, a.n_kv_heads),
+                      dim3(kPrefillThreads), P::bytes(), s, a);
+  }
+  using Sd = DecShape<D, F32>;
+  cudaError_t e = with_smem(k_attn_dec<D, F32>, Sd::bytes());
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(k_attn_dec<D, F32>, dim3(a.nsplit, a.n_kv_heads, a.T),
+                 dim3(kSubPerSplit * 32), Sd::bytes(), s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
   return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D), 0, s, a);
 }
@@ -187,15 +563,20 @@ size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit) {
   return nsplit > 1 ? (size_t)T * n_q_heads * nsplit * (head_dim + 2) : 0;
 }
 
-int attn_pick_splits(int T, int n_kv_heads, int max_len) {
-  (void)T;
-  (void)n_kv_heads;
+int attn_pick_splits(int T, bool decode_form, int max_len) {
+  // The prefill kernel walks the splits itself; the decode kernel needs the
+  // largest split count of the launch.
+  if (!decode_form && T >= kPrefillMinTokens) return 1;
   return splits_for(max_len);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  if (a.n_q_heads / a.n_kv_heads > kMaxGroup) return cudaErrorInvalidValue;
+  if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads ||
+      a.n_q_heads / a.n_kv_heads > kMaxGroup)
+    return cudaErrorInvalidValue;
+  if (!use_prefill(a) && a.nsplit < splits_for(a.tok_ctx ? 1 : min(a.ctx0 + a.T - 1, a.max_ctx)))
+    return cudaErrorInvalidValue;
   if (a.head_dim == 128) return a.kv_f32 ? run<128, true>(a, s) : run<128, false>(a, s);
   if (a.head_dim == 64) return a.kv_f32 ? run<64, true>(a, s) : run<64, false>(a, s);
   return cudaErrorInvalidValue;

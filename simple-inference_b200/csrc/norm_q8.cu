@@ -43,24 +43,38 @@ __global__ void k_q8_quantize(const float *__restrict__ x, size_t nblocks,
   }
 }
 
-// One CTA per row.  out (fp32) and the Q8 pair are each optional.
-__global__ void __launch_bounds__(256) k_rmsnorm_q8(const float *__restrict__ x,
-                                                    const float *__restrict__ w, int n, float eps,
-                                                    float *__restrict__ out,
-                                                    int8_t *__restrict__ qs,
-                                                    uint16_t *__restrict__ d) {
+// One CTA per row, the row held in registers (VPT float4 per thread) so it is
+// read once; thread t holds float4 t + j*blockDim, so the eight float4 of a
+// Q8 block sit in eight adjacent lanes.  out (fp32) and the Q8 pair are each
+// optional.
+template <int VPT>
+__global__ void __launch_bounds__(1024) k_rmsnorm_q8(const float *__restrict__ x,
+                                                     const float *__restrict__ w, int n, float eps,
+                                                     float *__restrict__ out,
+                                                     int8_t *__restrict__ qs,
+                                                     uint16_t *__restrict__ d) {
   pdl_trigger();
   pdl_wait();
-  const int row = blockIdx.x;
-  const float *xr = x + (size_t)row * n;
+  const int row = blockIdx.x, n4 = n / 4;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)row * n);
+  float4 v[VPT];
   double ss = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    double v = (double)xr[i];
-    ss = __dadd_rn(ss, __dmul_rn(v, v));
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const double a = v[j].x, b = v[j].y, c = v[j].z, e = v[j].w;
+    ss = __dadd_rn(ss, __dmul_rn(a, a));
+    ss = __dadd_rn(ss, __dmul_rn(b, b));
+    ss = __dadd_rn(ss, __dmul_rn(c, c));
+    ss = __dadd_rn(ss, __dmul_rn(e, e));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  __shared__ double part[8];
+  __shared__ double part[32];
   __shared__ float s_inv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) part[warp] = ss;
@@ -68,22 +82,42 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float *__restrict__ x,
   if (threadIdx.x == 0) {
     double t = 0.0;
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t = __dadd_rn(t, part[i]);
-    float mean = (float)__ddiv_rn(t, (double)n);
+    const float mean = (float)__ddiv_rn(t, (double)n);
     s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   }
   __syncthreads();
   const float inv = s_inv;
-  const int nblocks = n / 32;
-  for (int b = warp; b < nblocks; b += (int)(blockDim.x >> 5)) {
-    int i = b * 32 + lane;
-    float v = __fmul_rn(xr[i], inv);
-    if (w) v = __fmul_rn(v, w[i]);
-    if (out) out[(size_t)row * n + i] = v;
+  const float4 *wr = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    const bool ok = i < n4;  // uniform over each 8-lane Q8 group (n4 % 8 == 0)
+    float4 y = make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv),
+                           __fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv));
+    if (w && ok) {
+      const float4 g = wr[i];
+      y = make_float4(__fmul_rn(y.x, g.x), __fmul_rn(y.y, g.y), __fmul_rn(y.z, g.z),
+                      __fmul_rn(y.w, g.w));
+    }
+    if (out && ok) reinterpret_cast<float4 *>(out + (size_t)row * n)[i] = y;
     if (qs) {
-      uint16_t d16;
-      int8_t q = q8_lane(v, d16);
-      qs[(size_t)row * n + i] = q;
-      if (lane == 0) d[(size_t)row * nblocks + b] = d16;
+      unsigned m = max(max(__float_as_uint(fabsf(y.x)), __float_as_uint(fabsf(y.y))),
+                       max(__float_as_uint(fabsf(y.z)), __float_as_uint(fabsf(y.w))));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      if (ok) {
+        const float dd = __fdiv_rn(__uint_as_float(m), 127.0f);
+        const float qi = dd == 0.0f ? 0.0f : __fdiv_rn(1.0f, dd);
+        auto q = [&](float e) {
+          int t = __float2int_rn(__fmul_rn(e, qi));
+          t = t > 127 ? 127 : (t < -127 ? -127 : t);
+          return (uint32_t)(t & 0xFF);
+        };
+        const size_t gi = (size_t)row * n4 + i;
+        reinterpret_cast<uint32_t *>(qs)[gi] = q(y.x) | q(y.y) << 8 | q(y.z) << 16 | q(y.w) << 24;
+        if ((i & 7) == 0) d[gi >> 3] = f32_to_f16(dd);
+      }
     }
   }
 }
@@ -112,7 +146,25 @@ cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_
 cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, float eps,
                               float *out, int8_t *qs, uint16_t *d, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
-  return launch_pdl(k_rmsnorm_q8, dim3(M), dim3(256), 0, s, x, w, n, eps, out, qs, d);
+  if (n % 4 || (qs && n % 32) || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(qs) & 3) ||
+      (reinterpret_cast<uintptr_t>(d) & 1))
+    return cudaErrorMisalignedAddress;
+  // Threads: a multiple of 32 with at most 4 float4 each up to 1024 threads.
+  const int n4 = n / 4;
+  int threads = ((n4 + 3) / 4 + 31) / 32 * 32;
+  threads = threads < 128 ? 128 : (threads > 1024 ? 1024 : threads);
+  const int vpt = (n4 + threads - 1) / threads;
+  const dim3 g(M), b(threads);
+  switch (vpt) {
+    case 1: return launch_pdl(k_rmsnorm_q8<1>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    case 2: return launch_pdl(k_rmsnorm_q8<2>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    case 3: return launch_pdl(k_rmsnorm_q8<3>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    case 4: return launch_pdl(k_rmsnorm_q8<4>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    case 5: case 6: case 7: case 8:
+      return launch_pdl(k_rmsnorm_q8<8>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_add(const float *a, const float *b, float *y, size_t n, cudaStream_t s) {

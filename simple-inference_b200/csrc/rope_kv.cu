@@ -13,56 +13,55 @@
 
 namespace si {
 
-__global__ void k_rope_kv(const RopeKvArgs a) {
+// One thread per rotated pair: grid (T, ceil((Hq + Hkv) * D/2 / 256)); pairs
+// [0, Hq*D/2) are query pairs, the rest key pairs (each also moves V's pair).
+__global__ void __launch_bounds__(256) k_rope_kv(const RopeKvArgs a) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
   const int D = a.head_dim, half = D / 2;
   const int Hq = a.n_q_heads, Hkv = a.n_kv_heads;
   const int QD = Hq * D, KVD = Hkv * D;
+  const int idx = blockIdx.y * blockDim.x + threadIdx.x;
+  if (idx >= (Hq + Hkv) * half) return;
   const int seq = a.tok_seq ? a.tok_seq[t] : a.seq0;
   const int pos = a.tok_pos ? a.tok_pos[t] : a.pos0 + t;
   const float *row = a.qkv + (size_t)t * (QD + 2 * KVD);
   // Positions are validated on the host; an out-of-table position is never
   // dereferenced (the row is left unrotated and nothing is appended).
   if (pos < 0 || pos >= a.max_positions) return;
-  const float *ct = a.cos_tab + (size_t)pos * half;
-  const float *st = a.sin_tab + (size_t)pos * half;
-  // Rotated queries.
-  for (int idx = threadIdx.x; idx < Hq * half; idx += blockDim.x) {
-    int h = idx / half, i = idx % half;
-    float x0 = row[h * D + i], x1 = row[h * D + i + half];
-    float c = ct[i], s = st[i];
+  const int h = idx / half, i = idx % half;
+  const float c = a.cos_tab[(size_t)pos * half + i], s = a.sin_tab[(size_t)pos * half + i];
+  if (h < Hq) {  // rotated query
+    const float x0 = row[h * D + i], x1 = row[h * D + i + half];
     float *q = a.q_out + (size_t)t * QD + h * D;
     q[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
     q[i + half] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+    return;
   }
   if (!a.kc || pos >= a.max_ctx) return;  // rotation only (reference rope()), or no cache slot
-  const size_t slot = ((size_t)seq * a.max_ctx + pos) * KVD;
-  for (int idx = threadIdx.x; idx < Hkv * half; idx += blockDim.x) {
-    int h = idx / half, i = idx % half;
-    const float *k = row + QD + h * D;
-    const float *v = row + QD + KVD + h * D;
-    float x0 = k[i], x1 = k[i + half];
-    float c = ct[i], s = st[i];
-    float k0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    float k1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
-    size_t o = slot + (size_t)h * D + i;
-    if (a.kv_f32) {
-      float *kc = static_cast<float *>(a.kc), *vc = static_cast<float *>(a.vc);
-      kc[o] = k0; kc[o + half] = k1;
-      vc[o] = v[i]; vc[o + half] = v[i + half];
-    } else {
-      uint16_t *kc = static_cast<uint16_t *>(a.kc), *vc = static_cast<uint16_t *>(a.vc);
-      kc[o] = f32_to_f16(k0); kc[o + half] = f32_to_f16(k1);
-      vc[o] = f32_to_f16(v[i]); vc[o + half] = f32_to_f16(v[i + half]);
-    }
+  const int kh = h - Hq;
+  const float *k = row + QD + kh * D;
+  const float *v = row + QD + KVD + kh * D;
+  const float x0 = k[i], x1 = k[i + half];
+  const float k0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  const float k1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+  const size_t o = ((size_t)seq * a.max_ctx + pos) * KVD + (size_t)kh * D + i;
+  if (a.kv_f32) {
+    float *kc = static_cast<float *>(a.kc), *vc = static_cast<float *>(a.vc);
+    kc[o] = k0; kc[o + half] = k1;
+    vc[o] = v[i]; vc[o + half] = v[i + half];
+  } else {
+    uint16_t *kc = static_cast<uint16_t *>(a.kc), *vc = static_cast<uint16_t *>(a.vc);
+    kc[o] = f32_to_f16(k0); kc[o + half] = f32_to_f16(k1);
+    vc[o] = f32_to_f16(v[i]); vc[o + half] = f32_to_f16(v[i + half]);
   }
 }
 
 cudaError_t launch_rope_kv(const RopeKvArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  return launch_pdl(k_rope_kv, dim3(a.T), dim3(256), 0, s, a);
+  const int pairs = (a.n_q_heads + a.n_kv_heads) * (a.head_dim / 2);
+  return launch_pdl(k_rope_kv, dim3(a.T, (pairs + 255) / 256), dim3(256), 0, s, a);
 }
 
 }  // namespace si

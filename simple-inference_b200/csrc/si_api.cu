@@ -107,8 +107,10 @@ struct si_ctx {
   DevBuf work;                  // layer-schedule arena
   DevBuf idx;                   // per-token index arrays
   DevBuf gemm;                  // tcgen05 GEMM scratch (transposed activation scales)
-  int *pinned_idx = nullptr;    // host staging for idx
+  int *pinned_idx = nullptr;    // host staging for idx: kIdxSlots slots of pinned_idx_n ints
   size_t pinned_idx_n = 0;
+  cudaEvent_t idx_ev[4] = {};   // per slot: its host->device copy has run
+  unsigned idx_calls = 0;
   cudaEvent_t ev[12] = {};
 };
 
@@ -270,6 +272,8 @@ extern "C" SI_API void si_ctx_destroy(si_ctx *c) {
   c->idx.release();
   c->gemm.release();
   if (c->pinned_idx) cudaFreeHost(c->pinned_idx);
+  for (cudaEvent_t e : c->idx_ev)
+    if (e) cudaEventDestroy(e);
   for (auto &e : c->ev)
     if (e) cudaEventDestroy(e);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -954,6 +958,7 @@ enum { EV_START, EV_RMS, EV_QKV, EV_ROPE, EV_ATTN, EV_Q8O, EV_OPROJ, EV_MLP, EV_
 
 // In-place sum of a row-parallel projection's partial outputs over the TP group.
 static si_status tp_allreduce(si_ctx *ctx, si_tp *tp, float *buf, size_t n) {
+  if (tp->world == 1) return SI_OK;  // a one-rank group's sum is the partial sum
   const NcclApi *api = nccl_api();
   SI_CHECK(api, "NCCL is not available");
   SI_NCCL(api, api->all_reduce(buf, buf, n, ncclFloat32, ncclSum, tp->comm, ctx->stream),
@@ -992,29 +997,39 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
              "prefill range [%d, %d) exceeds the cache", prefix, prefix + T);
     max_len = prefix + T;
   }
-  const int nsplit = si::attn_pick_splits(T, d.n_kv_heads, max_len);
+  const int nsplit = si::attn_pick_splits(T, ctx_host != nullptr, max_len);
   SI_TRY(ctx->work.reserve(step_bytes(d, T, nsplit, true)));
   StepBuffers b = carve(ctx->work.p, d, T, nsplit);
   cudaStream_t s = ctx->stream;
 
-  // Per-token sequence / position / context arrays for the decode form.
+  // Per-token sequence / position / context arrays for the decode form, staged
+  // through a ring of pinned slots: a slot is rewritten only after its previous
+  // copy has run, so the host can queue several steps ahead without draining
+  // the stream.
   if (ctx_host) {
+    constexpr int kIdxSlots = 4;
     size_t n = (size_t)3 * T;
     if (ctx->pinned_idx_n < n) {
+      SI_CUDA(cudaStreamSynchronize(s));  // old slots may still be in flight
       if (ctx->pinned_idx) cudaFreeHost(ctx->pinned_idx);
       ctx->pinned_idx = nullptr;
       ctx->pinned_idx_n = 0;
-      SI_CUDA(cudaMallocHost(&ctx->pinned_idx, n * sizeof(int)));
+      SI_CUDA(cudaMallocHost(&ctx->pinned_idx, kIdxSlots * n * sizeof(int)));
       ctx->pinned_idx_n = n;
+      for (cudaEvent_t &e : ctx->idx_ev)
+        if (!e) SI_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
-    SI_CUDA(cudaStreamSynchronize(s));  // the staging buffer may still be in flight
+    const unsigned slot = ctx->idx_calls++ % kIdxSlots;
+    int *stage = ctx->pinned_idx + slot * ctx->pinned_idx_n;
+    SI_CUDA(cudaEventSynchronize(ctx->idx_ev[slot]));
     for (int t = 0; t < T; ++t) {
-      ctx->pinned_idx[t] = seq_host[t];
-      ctx->pinned_idx[T + t] = ctx_host[t] - 1;
-      ctx->pinned_idx[2 * T + t] = ctx_host[t];
+      stage[t] = seq_host[t];
+      stage[T + t] = ctx_host[t] - 1;
+      stage[2 * T + t] = ctx_host[t];
     }
     SI_TRY(ctx->idx.reserve(n * sizeof(int)));
-    SI_CUDA(cudaMemcpyAsync(ctx->idx.p, ctx->pinned_idx, n * sizeof(int), cudaMemcpyHostToDevice, s));
+    SI_CUDA(cudaMemcpyAsync(ctx->idx.p, stage, n * sizeof(int), cudaMemcpyHostToDevice, s));
+    SI_CUDA(cudaEventRecord(ctx->idx_ev[slot], s));
     b.tok_seq = static_cast<int *>(ctx->idx.p);
     b.tok_pos = b.tok_seq + T;
     b.tok_ctx = b.tok_seq + 2 * T;
@@ -1177,7 +1192,7 @@ extern "C" SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, cons
     SI_CHECK(ctx_lens[i] >= 0 && ctx_lens[i] <= kv->max_ctx, "context out of range");
     max_len = ctx_lens[i] > max_len ? ctx_lens[i] : max_len;
   }
-  const int nsplit = si::attn_pick_splits(batch, d->n_kv_heads, max_len);
+  const int nsplit = si::attn_pick_splits(batch, true, max_len);
   size_t part = si::attn_part_floats(batch, d->n_q_heads, d->head_dim, nsplit);
   size_t n = (size_t)2 * batch;
   SI_TRY(ctx->work.reserve(part * 4 + 1024));
@@ -1324,8 +1339,9 @@ extern "C" SI_API void si_ref_rmsnorm(const float *input, const float *weight, f
                                       float eps) {
   std::lock_guard<std::mutex> lk(g_ref_mu);
   si_ctx *c = ref_ctx(HDIM, ROPE_BASE);
-  char *s = ref_scratch((size_t)n * 12 + 1024);
-  float *x = reinterpret_cast<float *>(s), *w = x + n, *o = w + n;
+  const size_t n4 = ((size_t)n + 3) & ~(size_t)3;  // 16-byte aligned vectors
+  char *s = ref_scratch(n4 * 12 + 1024);
+  float *x = reinterpret_cast<float *>(s), *w = x + n4, *o = w + n4;
   ref_ck(cudaMemcpyAsync(x, input, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "rmsnorm");
   if (weight) ref_ck(cudaMemcpyAsync(w, weight, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream), "rmsnorm");
   ref_ck(si::launch_rmsnorm_q8(x, weight ? w : nullptr, 1, n, eps, o, nullptr, nullptr, c->stream), "rmsnorm");

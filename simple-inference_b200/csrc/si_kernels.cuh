@@ -105,7 +105,9 @@ struct AttnArgs {
   int nsplit;
 };
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
-int attn_pick_splits(int T, int n_kv_heads, int max_len);
+// Splits the launch needs: 1 when the prefill kernel runs (contiguous tokens
+// of one sequence, T >= 16), else ceil(max_len / 128).
+int attn_pick_splits(int T, bool decode_form, int max_len);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
 
 }  // namespace si

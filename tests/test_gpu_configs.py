@@ -122,3 +122,38 @@ def test_config3_batched_decode(si_ctx, oc):
         assert_layer_close(want, Y[b].cpu().numpy(), LAYER_RTOL, f"sequence {b}")
     kv.free()
     layer.free()
+
+
+@pytest.mark.parametrize("hq,hkv,hd", [(14, 2, 64), (12, 2, 128), (8, 8, 128), (16, 2, 128)])
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_prefill_kernel_equals_decode_kernel(hq, hkv, hd, kv_f32):
+    """The flash-style prefill attention (contiguous tokens, splits walked in one
+    CTA) and the split decode attention (one token per step) evaluate a token by
+    the same procedure: a 150-token prefill after a 130-position history (three
+    splits, ragged last query tile) equals 150 decode steps bit for bit, for
+    group sizes 7, 6, 1 and 8, head_dim 64 and 128, fp16 and fp32 caches."""
+    import sib200
+    dims = dict(hidden=hq * hd, n_q_heads=hq, n_kv_heads=hkv, head_dim=hd, intermediate=0,
+                rope_theta=1e6, rms_eps=1e-6)
+    prefix, ntok = 130, 150
+    L = prefix + ntok
+    ctx = sib200.Context(0, 4096, 1e6, hd)
+    try:
+        layer = ctx.layer_synth(dims, 11 + hq)
+        g = torch.Generator("cuda").manual_seed(hq + hkv)
+        X = torch.randn(ntok, dims["hidden"], device="cuda", generator=g)
+        ya, yb = torch.zeros_like(X), torch.zeros_like(X)
+        kva, kvb = ctx.kv(dims, 1, L, kv_f32), ctx.kv(dims, 1, L, kv_f32)
+        kva.fill_synth(7, 1.0, prefix)
+        kvb.fill_synth(7, 1.0, prefix)
+        torch.cuda.synchronize()
+        layer.prefill_dev(kva, 0, X, ntok, prefix, ya, sib200.SI_LAYER_ATTN)
+        for t in range(ntok):
+            layer.decode_dev(kvb, X[t], [prefix + t + 1], yb[t], sib200.SI_LAYER_ATTN)
+        ctx.status()
+        assert torch.isfinite(ya).all()
+        assert torch.equal(ya, yb)
+        for o in (kva, kvb, layer):
+            o.free()
+    finally:
+        ctx.close()
