@@ -217,7 +217,9 @@ SI_API si_status si_q8_from_blocks_dev(si_ctx *ctx, const block_q8_0 *blocks_dev
 SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                const uint16_t *d_dev, int M, const float *bias_dev,
                                float *out_dev);
-/* Force a kernel: 0 = CUDA-core GEMV, 1 = tcgen05 GEMM. */
+/* Force a kernel: 0 = GEMV (its form picked by M), 1 = tcgen05 GEMM,
+ * 2 = GEMV in its tensor-core (mma.sync s8) form, 3 = GEMV in its dp4a form.
+ * Every kernel returns the same bits. */
 SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                       const uint16_t *d_dev, int M, const float *bias_dev,
                                       float *out_dev, int kernel);
@@ -245,6 +247,11 @@ SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_
 SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate, const si_matrix *up,
                                   const int8_t *qs_dev, const uint16_t *d_dev, int M,
                                   int8_t *act_qs_dev, uint16_t *act_d_dev, float *act_f32_dev);
+/* The same with a forced kernel (-1 = by M; otherwise as si_matmul_dev_kernel). */
+SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix *gate, const si_matrix *up,
+                                         const int8_t *qs_dev, const uint16_t *d_dev, int M,
+                                         int8_t *act_qs_dev, uint16_t *act_d_dev,
+                                         float *act_f32_dev, int kernel);
 /* RMSNorm over rows of x [M][n] (qwen_one_layer.c:164-169) with optional fp32
  * output and fused Q8 output.  x, w and out 16-byte aligned, qs 4-byte aligned
  * (SI_ERR_CUDA otherwise). */

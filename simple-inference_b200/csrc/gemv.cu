@@ -215,6 +215,271 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core form (3..16 tokens per CTA).  One CTA per 32-row tile and the
+// whole K range, warp w owning rows 8w..8w+7.  Per block, one mma.sync
+// m16n8k32 (s8 x s8 -> s32) takes the tokens as its 16 M-rows (A, from the
+// activation stage) and the warp's 8 weight rows as its N-columns: lane
+// (g, c) holds nibble word c of row 8w+g, whose low nibbles are elements
+// 4c..4c+3 and high nibbles 16+4c..16+4c+3 -- exactly the two B registers of
+// the fragment.  The result is the exact 16*isum of every (token, row) pair
+// of the block, in registers: lane (g, c) owns tokens g (and g+8) x rows 2c,
+// 2c+1, and adds their terms ((float)isum*dw)*dx in block order as it goes.
+// No term buffers and no merge warps; the arithmetic per output is the same
+// serial chain as the reference's, so the result is bit-identical to the
+// dp4a form and to matvec_q4q8.  The weights stream through the same TMA
+// ring as the dp4a form (CB = 17 blocks per chunk: an odd multiple of the
+// 32-byte activation block keeps the A-fragment loads at two-way bank
+// conflicts).  The per-block rescale has to see every block's integer sum,
+// which mma.sync returns in registers; a tcgen05 MMA would put each block's
+// sums in tensor memory and need a round trip per block.
+template <int MT, bool SWIGLU>
+struct MmaShape {
+  static constexpr int CB = 17;                       // blocks per chunk
+  static constexpr int W = SWIGLU ? 2 : 1;            // weight streams
+  static constexpr int NIB = CB * SI_RT * 16;         // [CB][32 rows][16 B]
+  static constexpr int SCL = (CB * SI_RT * 2 + 127) / 128 * 128;  // [CB][32] fp16, padded
+  static constexpr int ACT = MT * CB * 32;            // [MT][CB][32 B]
+  static constexpr int WS = NIB + SCL;                // one weight stream
+  static constexpr int STAGE = W * WS + ACT;
+  static constexpr int TX = W * (NIB + CB * SI_RT * 2) + ACT;  // bytes the TMA boxes deliver
+  static constexpr int THREADS = 128;
+  // ring, barriers and flags, the per-warp amax of the Q8 epilogue, the
+  // activation scales transposed to [KB][MT] fp16, alignment slack
+  static size_t smem(int ns, int KB) {
+    return (size_t)ns * STAGE + 128 + 4 * MT * 4 + (size_t)KB * MT * 2 + 128;
+  }
+  static_assert(NIB % 128 == 0 && WS % 128 == 0 && ACT % 128 == 0, "TMA destinations");
+};
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+template <int MT, bool SWIGLU>
+__global__ void __launch_bounds__(MmaShape<MT, SWIGLU>::THREADS)
+    k_gemv_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
+               const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
+               const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
+  using S = MmaShape<MT, SWIGLU>;
+  constexpr int CB = S::CB, NT = MT / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [ns <= 8]
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 8);
+  unsigned *red = reinterpret_cast<unsigned *>(smem + ns * S::STAGE + 128);  // [4][MT]
+  uint16_t *dxs = reinterpret_cast<uint16_t *>(red + 4 * MT);              // [KB][MT]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int tile = blockIdx.x, m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
+  const int KB = a.K / 32, nchunks = (KB + CB - 1) / CB;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+
+  pdl_trigger();
+  auto load_weights = [&](int ci) {
+    const int slot = ci % ns;
+    uint8_t *st = smem + slot * S::STAGE;
+    const int y = tile * KB + ci * CB;
+    mbar_expect_tx(bar(slot), S::TX);
+    tma_load_2d(smem_u32(st), &tmN, 0, y, bar(slot));
+    tma_load_2d(smem_u32(st + S::NIB), &tmS, 0, y, bar(slot));
+    if (SWIGLU) {
+      tma_load_2d(smem_u32(st + S::WS), &tmN2, 0, y, bar(slot));
+      tma_load_2d(smem_u32(st + S::WS + S::NIB), &tmS2, 0, y, bar(slot));
+    }
+  };
+  auto load_acts = [&](int ci) {
+    const int slot = ci % ns;
+    tma_load_2d(smem_u32(smem + slot * S::STAGE + S::W * S::WS), &tmX, ci * CB * 4, m0, bar(slot));
+  };
+  const int pre = nchunks < ns - 1 ? nchunks : ns - 1;
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    for (int i = 0; i < ns; ++i) mbar_init(bar(i), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int ci = 0; ci < pre; ++ci) load_weights(ci);
+  }
+  pdl_wait();
+  if (threadIdx.x == 0)
+    for (int ci = 0; ci < pre; ++ci) load_acts(ci);
+  for (int i = threadIdx.x; i < MT * KB; i += blockDim.x) {
+    const int m = i / KB, blk = i % KB;
+    dxs[blk * MT + m] = m < mcount ? a.xd[(size_t)(m0 + m) * KB + blk] : (uint16_t)0;
+  }
+
+  const int rowl = 8 * warp + 2 * c;  // this lane's first row within the tile
+  const int row = tile * SI_RT + rowl;
+  float acc[NT][2], accu[NT][2];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      acc[t][j] = (!SWIGLU && a.bias) ? a.bias[row + j] : 0.0f;
+      accu[t][j] = 0.0f;
+    }
+  __syncthreads();  // dxs visible
+
+  for (int ci = 0; ci < nchunks; ++ci) {
+    if (threadIdx.x == 0 && ci + ns - 1 < nchunks) {
+      load_weights(ci + ns - 1);
+      load_acts(ci + ns - 1);
+    }
+    const int slot = ci % ns;
+    const bool ok = mbar_wait(bar(slot), (ci / ns) & 1, abort_flag);
+    if (ok) {
+      const uint8_t *st = smem + slot * S::STAGE;
+      const uint8_t *act = st + S::W * S::WS;
+      const int nb = min(CB, KB - ci * CB);
+#pragma unroll
+      for (int bl = 0; bl < CB; ++bl) {
+        if (bl < nb) {
+          const int bx = ci * CB + bl;
+          const uint32_t *ar = reinterpret_cast<const uint32_t *>(act + (g * CB + bl) * 32);
+          const uint32_t a0 = ar[c], a2 = ar[4 + c];
+          uint32_t a1 = 0, a3 = 0;
+          if (NT == 2) {
+            const uint32_t *ar8 = reinterpret_cast<const uint32_t *>(act + ((g + 8) * CB + bl) * 32);
+            a1 = ar8[c];
+            a3 = ar8[4 + c];
+          }
+          float dx[NT];
+#pragma unroll
+          for (int t = 0; t < NT; ++t) dx[t] = f16_to_f32(dxs[bx * MT + g + 8 * t]);
+#pragma unroll
+          for (int wi = 0; wi < S::W; ++wi) {
+            const uint8_t *ws = st + wi * S::WS;
+            const uint32_t wn =
+                *reinterpret_cast<const uint32_t *>(ws + bl * 512 + (8 * warp + g) * 16 + 4 * c);
+            int d[4];
+            mma_s8_16832(d, a0, a1, a2, a3, (uint32_t)lo_nib_s8x16(wn), (uint32_t)hi_nib_s8x16(wn));
+            const uint32_t dwp = *reinterpret_cast<const uint32_t *>(ws + S::NIB + (bl * 32 + rowl) * 2);
+            const float dw0 = f16_to_f32((uint16_t)dwp), dw1 = f16_to_f32((uint16_t)(dwp >> 16));
+            float(&ac)[NT][2] = wi == 0 ? acc : accu;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              ac[t][0] = __fadd_rn(ac[t][0], block_term(d[2 * t] >> 4, dw0, dx[t]));
+              ac[t][1] = __fadd_rn(ac[t][1], block_term(d[2 * t + 1] >> 4, dw1, dx[t]));
+            }
+            if (!SWIGLU && a.isum_out) {
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const int tok = g + 8 * t;
+                if (tok < mcount) {
+                  int32_t *io = a.isum_out + ((size_t)(m0 + tok) * a.N + row) * KB + bx;
+                  io[0] = d[2 * t] >> 4;
+                  io[KB] = d[2 * t + 1] >> 4;
+                }
+              }
+            }
+          }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+    // Chunk consumed by every warp: its ring slot is free for chunk ci + ns.
+    if (!__syncthreads_and(ok)) {
+      if (threadIdx.x == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+      return;
+    }
+  }
+
+  if (!SWIGLU) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int tok = g + 8 * t;
+      if (tok < mcount) {
+        const size_t o = (size_t)(m0 + tok) * a.N + row;
+        float2 v = make_float2(acc[t][0], acc[t][1]);
+        if (a.resid) {
+          v.x = __fadd_rn(a.resid[o], v.x);
+          v.y = __fadd_rn(a.resid[o + 1], v.y);
+        }
+        *reinterpret_cast<float2 *>(a.out + o) = v;
+      }
+    }
+  } else {
+    // act = silu(g) * u; the tile's 32 rows of a token are one Q8 block.
+    float act[NT][2];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      act[t][0] = silu_mul(acc[t][0], accu[t][0]);
+      act[t][1] = silu_mul(acc[t][1], accu[t][1]);
+      unsigned m = max(__float_as_uint(fabsf(act[t][0])), __float_as_uint(fabsf(act[t][1])));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      if (c == 0) red[warp * MT + g + 8 * t] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int tok = g + 8 * t;
+      if (tok >= mcount) continue;
+      const unsigned mb = max(max(red[tok], red[MT + tok]), max(red[2 * MT + tok], red[3 * MT + tok]));
+      const float d = __fdiv_rn(__uint_as_float(mb), 127.0f);
+      const float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+      const size_t o = (size_t)(m0 + tok) * a.N + row;
+      if (a.out) *reinterpret_cast<float2 *>(a.out + o) = make_float2(act[t][0], act[t][1]);
+      auto q8 = [&](float e) {
+        int q = __float2int_rn(__fmul_rn(e, inv));
+        q = q > 127 ? 127 : (q < -127 ? -127 : q);
+        return (uint32_t)(q & 0xFF);
+      };
+      *reinterpret_cast<uint16_t *>(a.act_qs + o) = (uint16_t)(q8(act[t][0]) | q8(act[t][1]) << 8);
+      if (warp == 0 && c == 0) a.act_d[(size_t)(m0 + tok) * (a.N / 32) + tile] = f32_to_f16(d);
+    }
+  }
+}
+
+template <int MT, bool SWIGLU>
+cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
+  using S = MmaShape<MT, SWIGLU>;
+  const int KB = a.K / 32, tiles = a.N / SI_RT;
+  const int nchunks = (KB + S::CB - 1) / S::CB;
+  int ns = nchunks < 2 ? 2 : (nchunks < kStages ? nchunks : kStages);
+  const size_t smem = S::smem(ns, KB);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
+  const cuuint64_t dN[2] = {64, (cuuint64_t)tiles * KB}, sN[1] = {512};
+  const cuuint32_t bN[2] = {64, (cuuint32_t)S::CB};
+  const cuuint64_t dS[2] = {32, (cuuint64_t)tiles * KB}, sS[1] = {64};
+  const cuuint32_t bS[2] = {32, (cuuint32_t)S::CB};
+  const cuuint64_t dX[2] = {(cuuint64_t)a.K / 8, (cuuint64_t)a.M}, sX[1] = {(cuuint64_t)a.K};
+  const cuuint32_t bX[2] = {(cuuint32_t)S::CB * 4, (cuuint32_t)MT};
+  if (!tma_encode(&tmN, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dN, sN, bN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.xq, dX, sX, bX,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (SWIGLU) {
+    if (!tma_encode(&tmN2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dN, sN, bN,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !tma_encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    tmN2 = tmN;
+    tmS2 = tmS;
+  }
+  auto kern = k_gemv_mma<MT, SWIGLU>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(tiles, (a.M + MT - 1) / MT);
+  return launch_pdl(kern, grid, dim3(S::THREADS), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
+}
+
 template <int MT, int RW, bool SWIGLU>
 cudaError_t run(const GemvArgs &a, cudaStream_t s) {
   static_assert(!SWIGLU || RW == SI_RT, "the SwiGLU Q8 epilogue needs whole 32-row tiles");
@@ -279,6 +544,10 @@ cudaError_t pick_rows(const GemvArgs &a, cudaStream_t s) {
 
 template <bool SWIGLU>
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t s) {
+  // The tensor-core form from 3 tokens on (or when asked for); the dp4a form
+  // for 1-2 tokens, where its per-token cost is lower than one mma per block.
+  const bool mma = a.variant == kGemvMma || (a.variant == kGemvAuto && a.M >= 3);
+  if (mma) return a.M <= 8 ? run_mma<8, SWIGLU>(a, s) : run_mma<16, SWIGLU>(a, s);
   if (a.M <= 1) return pick_rows<1, SWIGLU>(a, s);
   if (a.M <= 2) return pick_rows<2, SWIGLU>(a, s);
   if (a.M <= 4) return pick_rows<4, SWIGLU>(a, s);

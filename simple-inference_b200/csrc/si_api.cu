@@ -510,6 +510,8 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
   a.out = out;
   if (kernel < 0)
     kernel = (prefer_gemm(w->rows / 128, M) && si::gemm_tc_supported(w->rows, w->cols, M)) ? 1 : 0;
+  if (kernel == 2) a.variant = si::kGemvMma;
+  if (kernel == 3) a.variant = si::kGemvDp4a;
   if (kernel == 1) {
     if (!si::gemm_tc_supported(w->rows, w->cols, M))
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
@@ -534,7 +536,8 @@ extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w
                                                  const int8_t *qs, const uint16_t *d, int M,
                                                  const float *bias, float *out, int kernel) {
   SI_TRY(set_device(ctx));
-  SI_CHECK(kernel == 0 || kernel == 1, "kernel must be 0 (GEMV) or 1 (tcgen05 GEMM)");
+  SI_CHECK(kernel >= 0 && kernel <= 3,
+           "kernel must be 0 (GEMV), 1 (tcgen05 GEMM), 2 (GEMV, mma form) or 3 (GEMV, dp4a form)");
   return matmul(ctx, w, qs, d, M, bias, nullptr, out, kernel);
 }
 
@@ -618,11 +621,24 @@ extern "C" SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, 
   return SI_OK;
 }
 
+extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix *gate,
+                                                    const si_matrix *up, const int8_t *qs,
+                                                    const uint16_t *d, int M, int8_t *act_qs,
+                                                    uint16_t *act_d, float *act_f32, int kernel);
+
 extern "C" SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate,
                                              const si_matrix *up, const int8_t *qs,
                                              const uint16_t *d, int M, int8_t *act_qs,
                                              uint16_t *act_d, float *act_f32) {
+  return si_gateup_q8_dev_kernel(ctx, gate, up, qs, d, M, act_qs, act_d, act_f32, -1);
+}
+
+extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix *gate,
+                                                    const si_matrix *up, const int8_t *qs,
+                                                    const uint16_t *d, int M, int8_t *act_qs,
+                                                    uint16_t *act_d, float *act_f32, int kernel) {
   SI_TRY(set_device(ctx));
+  SI_CHECK(kernel >= -1 && kernel <= 3, "bad kernel selector %d", kernel);
   SI_CHECK(gate && up && qs && d && act_qs && act_d, "null pointer");
   SI_CHECK(gate->rows == up->rows && gate->cols == up->cols, "gate/up shape mismatch");
   si::GemvArgs a = gemv_args(gate, qs, d, M);
@@ -631,8 +647,14 @@ extern "C" SI_API si_status si_gateup_q8_dev(si_ctx *ctx, const si_matrix *gate,
   a.out = act_f32;
   a.act_qs = act_qs;
   a.act_d = act_d;
-  if (prefer_gemm(gate->rows / 64, M) && si::gemm_tc_supported(2 * gate->rows, gate->cols, M) &&
-      gate->rows % 64 == 0) {
+  const bool gemm_ok = si::gemm_tc_supported(2 * gate->rows, gate->cols, M) && gate->rows % 64 == 0;
+  if (kernel < 0) kernel = prefer_gemm(gate->rows / 64, M) && gemm_ok ? 1 : 0;
+  if (kernel == 2) a.variant = si::kGemvMma;
+  if (kernel == 3) a.variant = si::kGemvDp4a;
+  if (kernel == 1) {
+    if (!gemm_ok)
+      return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support gate/up %dx%d at M=%d",
+                  gate->rows, gate->cols, M);
     SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(gate->cols, M)));
     a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, true, ctx->stream));

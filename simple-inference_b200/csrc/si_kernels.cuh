@@ -67,7 +67,9 @@ struct GemvArgs {
   int32_t *isum_out;       // [M][N][K/32] block partial sums (parity), or null
   int *err;                // context device error word (bounded waits), or null
   float *scratch;          // tcgen05 GEMM: gemm_tc_scratch_bytes() of device memory
+  int variant;             // GEMV form: kGemvAuto, kGemvDp4a or kGemvMma
 };
+enum { kGemvAuto = 0, kGemvDp4a = 1, kGemvMma = 2 };
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
 
 // ---- gemm_tc.cu (tcgen05) ------------------------------------------------------

@@ -93,6 +93,7 @@ def lib() -> C.CDLL:
         "si_matmul_tc_static_dev": (i32, [vp, vp, vp, vp, i32, vp, vp]),
         "si_block_isums_dev": (i32, [vp, vp, vp, i32, vp]),
         "si_gateup_q8_dev": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, vp]),
+        "si_gateup_q8_dev_kernel": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, vp, i32]),
         "si_rmsnorm_q8_dev": (i32, [vp, vp, vp, i32, i32, f32, vp, vp, vp]),
         "si_layer_upload": (i32, [vp, C.POINTER(Dims), C.POINTER(LayerHost), pp]),
         "si_layer_synth": (i32, [vp, C.POINTER(Dims), u64, pp]),
@@ -233,9 +234,15 @@ class Context:
     def block_isums(self, w: "Matrix", qs, M, out):
         check(self.L.si_block_isums_dev(self.h, w.h, _p(qs), M, _p(out)), "si_block_isums_dev")
 
-    def gateup_q8(self, gate, up, qs, d, M, act_qs, act_d, act_f32=None):
-        check(self.L.si_gateup_q8_dev(self.h, gate.h, up.h, _p(qs), _p(d), M, _p(act_qs),
-                                      _p(act_d), _p(act_f32)), "si_gateup_q8_dev")
+    def gateup_q8(self, gate, up, qs, d, M, act_qs, act_d, act_f32=None,
+                  kernel: int | None = None):
+        if kernel is None:
+            check(self.L.si_gateup_q8_dev(self.h, gate.h, up.h, _p(qs), _p(d), M, _p(act_qs),
+                                          _p(act_d), _p(act_f32)), "si_gateup_q8_dev")
+        else:
+            check(self.L.si_gateup_q8_dev_kernel(self.h, gate.h, up.h, _p(qs), _p(d), M,
+                                                 _p(act_qs), _p(act_d), _p(act_f32), kernel),
+                  "si_gateup_q8_dev_kernel")
 
     def rmsnorm_q8(self, x, w, M, n, eps, out=None, qs=None, d=None):
         check(self.L.si_rmsnorm_q8_dev(self.h, _p(x), _p(w), M, n, eps, _p(out), _p(qs), _p(d)),

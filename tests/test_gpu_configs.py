@@ -28,7 +28,9 @@ LAYER_RTOL = 1e-3
 
 
 def z(n, dt=torch.float32):
-    return torch.zeros(n, dtype=dt, device="cuda")
+    t = torch.zeros(n, dtype=dt, device="cuda")
+    torch.cuda.synchronize()  # the fill runs on torch's stream, the kernels on the library's
+    return t
 
 
 @pytest.mark.parametrize("M", [16, 128, 512])
@@ -59,10 +61,12 @@ def test_config2_prefill_then_decode(si_ctx, oc):
     # Prefill all 2048 tokens at once ...
     kva = si_ctx.kv(DIMS_7B, 1, L, False)
     ya = torch.zeros(ntok, DIMS_7B["hidden"], device="cuda")
+    torch.cuda.synchronize()
     layer.prefill_dev(kva, 0, X[:ntok], ntok, 0, ya, sib200.SI_LAYER_FULL)
     # ... and token by token.
     kvb = si_ctx.kv(DIMS_7B, 1, L, False)
     yb = torch.zeros_like(ya)
+    torch.cuda.synchronize()
     for t in range(ntok):
         layer.decode_dev(kvb, X[t], [t + 1], yb[t], sib200.SI_LAYER_FULL)
     si_ctx.status()
@@ -77,6 +81,7 @@ def test_config2_prefill_then_decode(si_ctx, oc):
     np.testing.assert_array_equal(va, vb)
     # Decode after the prefill, checked against the oracle on the last step.
     yd = torch.zeros(ndec, DIMS_7B["hidden"], device="cuda")
+    torch.cuda.synchronize()
     for i in range(ndec):
         layer.decode_dev(kva, X[ntok + i], [ntok + i + 1], yd[i], sib200.SI_LAYER_FULL)
     si_ctx.status()
@@ -113,6 +118,7 @@ def test_config3_batched_decode(si_ctx, oc):
         one = si_ctx.kv(DIMS_7B, 1, ctx_len, True)
         one.write(0, 0, k[:ctx_len - 1], v[:ctx_len - 1])
         y1 = torch.zeros(DIMS_7B["hidden"], device="cuda")
+        torch.cuda.synchronize()
         layer.decode_dev(one, X[b], [ctx_len], y1, sib200.SI_LAYER_FULL)
         si_ctx.status()
         assert torch.equal(y1, Y[b]), f"sequence {b}: batched != single"

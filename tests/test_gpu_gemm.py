@@ -21,7 +21,9 @@ def dev(a):
 
 
 def z(n, dt):
-    return torch.zeros(n, dtype=dt, device="cuda")
+    t = torch.zeros(n, dtype=dt, device="cuda")
+    torch.cuda.synchronize()  # the fill runs on torch's stream, the kernels on the library's
+    return t
 
 
 def q8_dev(ctx, x):

@@ -27,7 +27,11 @@ def dev(a):
 
 
 def empty(n, dtype):
-    return torch.zeros(n, dtype=dtype, device="cuda")
+    """A zeroed device buffer; the fill runs on torch's stream, so wait for it
+    before a library call on the library's stream writes the buffer."""
+    t = torch.zeros(n, dtype=dtype, device="cuda")
+    torch.cuda.synchronize()
+    return t
 
 
 def host(ctx, t):
@@ -83,11 +87,16 @@ def test_gemv_golden_bit_exact(si_ctx, golden, oc):
     np.testing.assert_array_equal(host(si_ctx, isum).reshape(256, 48), golden["mv_isum"])
 
 
+@pytest.mark.parametrize("kernel", [0, 2, 3], ids=["auto", "mma", "dp4a"])
 @pytest.mark.parametrize("N,K,M", [(2048, 1536, 1), (1536, 8960, 2), (256, 896, 3),
                                    (128, 4864, 5), (512, 3584, 8), (96, 1536, 13),
                                    (5120, 512, 2), (10240, 256, 3), (32, 32, 1),
-                                   (3072, 640, 4), (2368, 320, 1)])
-def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
+                                   (3072, 640, 4), (2368, 320, 1), (256, 1536, 16),
+                                   (160, 544, 21)])
+def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M, kernel):
+    """Both GEMV forms (dp4a; mma.sync with tokens as the 16 M-rows) against the
+    oracle's matvec_q4q8, element for element; K = 544 and 32 exercise a ragged
+    last chunk of the 17-block ring, M = 21 two token groups of 16."""
     rng = np.random.default_rng(N + K + M)
     w = synth.random_q4(rng, N, K)
     x = rng.standard_normal((M, K)).astype(np.float32)
@@ -95,23 +104,43 @@ def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
     m = si_ctx.matrix(w, N, K)
     qs, d, blocks = gpu_q8(si_ctx, x)
     out = empty(M * N, torch.float32)
-    si_ctx.matmul(m, qs, d, M, dev(bias), out, kernel=0)
+    si_ctx.matmul(m, qs, d, M, dev(bias), out, kernel=kernel)
     got = host(si_ctx, out).reshape(M, N)
     for t in range(M):
         np.testing.assert_array_equal(got[t], oc.matvec(w, blocks[t], K, N, bias))
 
 
-def test_gateup_silu_q8(si_ctx, oc):
+@pytest.mark.parametrize("N,K", [(8192, 8192), (10240, 8192), (8192, 29568), (4608, 3584)])
+@pytest.mark.parametrize("M", [3, 8, 16])
+def test_gemv_mma_equals_dp4a_large(si_ctx, N, K, M):
+    """At the 7B/72B decode shapes the two GEMV forms return the same bits."""
+    m = si_ctx.matrix_synth(N, K, seed=N + K + M)
+    x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
+    torch.cuda.synchronize()
+    qs, d = empty(M * K, torch.int8), empty(M * K // 32, torch.int16)
+    si_ctx.q8_quantize(x, M, K, qs, d)
+    a, b = empty(M * N, torch.float32), empty(M * N, torch.float32)
+    si_ctx.matmul(m, qs, d, M, None, a, kernel=2)
+    si_ctx.matmul(m, qs, d, M, None, b, kernel=3)
+    si_ctx.status()
+    assert torch.isfinite(a).all() and torch.equal(a, b)
+    m.free()
+
+
+@pytest.mark.parametrize("kernel,M", [(None, 3), (2, 3), (3, 3), (2, 8), (3, 8), (2, 11),
+                                      (3, 11), (2, 1)])
+def test_gateup_silu_q8(si_ctx, oc, kernel, M):
     rng = np.random.default_rng(5)
-    H, I, M = 896, 4864, 3
+    H, I = 896, 4864
     g, u = synth.random_q4(rng, I, H), synth.random_q4(rng, I, H)
     x = rng.standard_normal((M, H)).astype(np.float32)
     mg, mu = si_ctx.matrix(g, I, H), si_ctx.matrix(u, I, H)
     qs, d, blocks = gpu_q8(si_ctx, x)
     aq, ad, af = empty(M * I, torch.int8), empty(M * I // 32, torch.int16), empty(M * I, torch.float32)
-    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af)
+    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af, kernel=kernel)
     act = host(si_ctx, af).reshape(M, I)
     ablk = torch.zeros(M * I // 32 * 34, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
     si_ctx.q8_to_blocks(aq, ad, M, I, ablk)
     ablk = host(si_ctx, ablk).reshape(M, -1)
     for t in range(M):
@@ -326,3 +355,25 @@ def test_bad_context_is_rejected_cleanly(si_ctx, oc):
     si_ctx.status()                      # device error word is clean; context still usable
     gl.decode(kv, x, [3], y)
     assert np.all(np.isfinite(y))
+
+
+@pytest.mark.parametrize("I,H", [(18944, 3584), (3712, 8192)])
+@pytest.mark.parametrize("M", [3, 8, 16])
+def test_gateup_mma_equals_dp4a(si_ctx, I, H, M):
+    """SwiGLU + Q8 epilogue: both GEMV forms return the same activation bits."""
+    mg, mu = si_ctx.matrix_synth(I, H, seed=I + M), si_ctx.matrix_synth(I, H, seed=H + M)
+    x = torch.randn(M, H, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
+    torch.cuda.synchronize()
+    qs, d = empty(M * H, torch.int8), empty(M * H // 32, torch.int16)
+    si_ctx.q8_quantize(x, M, H, qs, d)
+    out = []
+    for kernel in (2, 3):
+        aq, ad = empty(M * I, torch.int8), empty(M * I // 32, torch.int16)
+        af = empty(M * I, torch.float32)
+        si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af, kernel=kernel)
+        out.append((aq, ad, af))
+    si_ctx.status()
+    for p, q in zip(*out):
+        assert torch.equal(p, q)
+    mg.free()
+    mu.free()
