@@ -149,6 +149,13 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
     cp_async16(smem_u32(k_w + r * S::RB + ((c ^ (r & 7)) << 4)),
                kg + ((size_t)(key0 + r) * rowstride) * S::ES + c * 16, 16);
   }
+  // This warp's V rows into L2 while the scores are computed (P.V then reads
+  // them straight from global memory, lane = dims).
+  constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
+  for (int i = lane; i < nvalid * LPR; i += 32) {
+    const uint8_t *p = vg + ((size_t)(key0 + i / LPR) * rowstride) * S::ES + (i % LPR) * 128;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+  }
   for (int i = threadIdx.x; i < G * D; i += blockDim.x)
     q_s[i] = a.q[((size_t)t * Hq + kvh * G) * D + i];
   cp_async_wait_all();
@@ -277,7 +284,24 @@ __global__ void k_attn_combine(const AttnArgs a) {
   const int S = splits_for(ctx_of(a, t));
   const float *p = a.part + ((size_t)t * a.n_q_heads + h) * a.nsplit * (D + 2);
   float M = p[0], Ls = p[1], O = p[2 + d];
-  for (int s = 1; s < S; ++s) {
+  int s = 1;
+  for (; s + 8 <= S; s += 8) {  // eight splits' loads in flight, merged in order
+    float mm[8], ll[8], oo[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float *ps = p + (size_t)(s + j) * (D + 2);
+      mm[j] = ps[0];
+      ll[j] = ps[1];
+      oo[j] = ps[2 + d];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float fa, fb;
+      merge_ml(M, Ls, mm[j], ll[j], fa, fb);
+      O = merge_o(O, fa, oo[j], fb);
+    }
+  }
+  for (; s < S; ++s) {
     const float *ps = p + (size_t)s * (D + 2);
     float fa, fb;
     merge_ml(M, Ls, ps[0], ps[1], fa, fb);

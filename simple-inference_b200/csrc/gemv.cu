@@ -23,6 +23,8 @@
 // through the ring, then forms act = silu(g) * u and quantises it to Q8_0
 // directly: the 32 rows of a tile are exactly one Q8 block of the down
 // projection's input.
+#include <type_traits>
+
 #include "si_common.cuh"
 #include "si_kernels.cuh"
 #include "si_tma.cuh"
@@ -217,39 +219,64 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
 
 // ---------------------------------------------------------------------------
 // Tensor-core form (3..16 tokens per CTA).  One CTA per 32-row tile and the
-// whole K range, warp w owning rows 8w..8w+7.  Per block, one mma.sync
-// m16n8k32 (s8 x s8 -> s32) takes the tokens as its 16 M-rows (A, from the
-// activation stage) and the warp's 8 weight rows as its N-columns: lane
-// (g, c) holds nibble word c of row 8w+g, whose low nibbles are elements
-// 4c..4c+3 and high nibbles 16+4c..16+4c+3 -- exactly the two B registers of
-// the fragment.  The result is the exact 16*isum of every (token, row) pair
-// of the block, in registers: lane (g, c) owns tokens g (and g+8) x rows 2c,
-// 2c+1, and adds their terms ((float)isum*dw)*dx in block order as it goes.
-// No term buffers and no merge warps; the arithmetic per output is the same
-// serial chain as the reference's, so the result is bit-identical to the
-// dp4a form and to matvec_q4q8.  The weights stream through the same TMA
-// ring as the dp4a form (CB = 17 blocks per chunk: an odd multiple of the
-// 32-byte activation block keeps the A-fragment loads at two-way bank
-// conflicts).  The per-block rescale has to see every block's integer sum,
-// which mma.sync returns in registers; a tcgen05 MMA would put each block's
-// sums in tensor memory and need a round trip per block.
+// whole K range.  Per block and 16-row group, one mma.sync m16n8k32
+// (s8 x s8 -> s32) per 8 tokens takes the weight rows as its 16 M-rows: lane
+// (g, c) holds nibble word c of rows g and g+8, whose low nibbles are elements
+// 4c..4c+3 and high nibbles 16+4c..16+4c+3 -- exactly the four A registers of
+// the fragment -- and the B fragment is token g's activation bytes 4c..4c+3
+// and 16+4c..16+4c+3.  The result is the exact 16*isum of every (row, token)
+// pair of the block, in registers: lane (g, c) owns rows g, g+8 x tokens 2c,
+// 2c+1 of each octet.
+//
+// Order.  Each output is bias + term(block 0) + term(block 1) + ... added one
+// at a time, the reference's serial chain, so the result is bit-identical to
+// the dp4a form and to matvec_q4q8.  The terms themselves are independent, so
+// the CTA runs four phases of warps per 16-row group: phase k computes the
+// terms of chunks k, k+4, ... into registers while the other phases compute
+// theirs, then waits on a named barrier for the running sums of the previous
+// chunk (phase k-1), adds its chunk's terms in block order, and hands the sums
+// on through shared memory to phase k+1.  Only the adds are serial.
+//
+// Terms.  term = ((float)isum * dw) * dx is computed as
+// ((float)(16*isum) * dw) * (dx/16): 16*isum is exact in fp32 and scaling by a
+// power of two commutes with rounding, so both products round exactly as the
+// reference's do; dx/16 is kept per (block, token) in shared memory.
+//
+// Pipeline.  A producer warp streams the tile through a ring of 5-8 chunks of
+// CB blocks (nibbles, fp16 scales and the chunk's activations: three or five
+// 2-D TMA loads on the stage's full barrier); the two warps of a phase release
+// a stage on its empty barrier.  CB = 9 or 5 (1 mod 4) keeps the B-fragment
+// loads at two-way bank conflicts.  The per-block rescale has to see every
+// block's integer sums, which mma.sync returns in registers; a tcgen05 MMA
+// would put each block's sums in tensor memory and need a round trip per block.
+constexpr int kMmaPhases = 4;
+constexpr int kMmaGroups = 2;                                  // 16-row groups per tile
+constexpr int kMmaWarps = kMmaPhases * kMmaGroups + 1;         // + producer
+constexpr size_t kMmaRingBudget = 96 * 1024;
+
 template <int MT, bool SWIGLU>
 struct MmaShape {
-  static constexpr int CB = 17;                       // blocks per chunk
   static constexpr int W = SWIGLU ? 2 : 1;            // weight streams
+  static constexpr int NT = MT / 8;                   // token octets
+  // A chunk's terms stay in registers until the hand-off (36-80 per lane);
+  // mma groups of GB blocks in flight.
+  static constexpr int CB = W * NT == 1 ? 9 : 5;      // blocks per chunk
+  static constexpr int GB = W * NT == 1 ? 3 : 1;
+  static constexpr int MINB = NT == 2 ? 1 : 2;        // CTAs per SM the registers allow
   static constexpr int NIB = CB * SI_RT * 16;         // [CB][32 rows][16 B]
   static constexpr int SCL = (CB * SI_RT * 2 + 127) / 128 * 128;  // [CB][32] fp16, padded
   static constexpr int ACT = MT * CB * 32;            // [MT][CB][32 B]
-  static constexpr int WS = NIB + SCL;                // one weight stream
-  static constexpr int STAGE = W * WS + ACT;
+  static constexpr int WS = (NIB + SCL + 127) / 128 * 128;        // one weight stream
+  static constexpr int STAGE = W * WS + (ACT + 127) / 128 * 128;
   static constexpr int TX = W * (NIB + CB * SI_RT * 2) + ACT;  // bytes the TMA boxes deliver
-  static constexpr int THREADS = 128;
-  // ring, barriers and flags, the per-warp amax of the Q8 epilogue, the
-  // activation scales transposed to [KB][MT] fp16, alignment slack
+  static constexpr int NV = W * NT * 4;               // sums per lane
+  static constexpr int ACCS = kMmaGroups * 32 * NV;   // hand-off floats
+  // ring, 256 B of barriers and flags, hand-off sums, the per-warp amax of
+  // the Q8 epilogue, dx/16 per (block, token) as fp32, slack
   static size_t smem(int ns, int KB) {
-    return (size_t)ns * STAGE + 128 + 4 * MT * 4 + (size_t)KB * MT * 2 + 128;
+    return (size_t)ns * STAGE + 256 + ACCS * 4 + kMmaGroups * MT * 4 + (size_t)KB * MT * 4 + 128;
   }
-  static_assert(NIB % 128 == 0 && WS % 128 == 0 && ACT % 128 == 0, "TMA destinations");
+  static_assert(NIB % 128 == 0 && WS % 128 == 0 && STAGE % 128 == 0, "TMA destinations");
 };
 
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -259,182 +286,301 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 template <int MT, bool SWIGLU>
-__global__ void __launch_bounds__(MmaShape<MT, SWIGLU>::THREADS)
+__global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
     k_gemv_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
                const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
   using S = MmaShape<MT, SWIGLU>;
-  constexpr int CB = S::CB, NT = MT / 8;
+  constexpr int CB = S::CB, NT = S::NT, W = S::W, NV = S::NV, P = kMmaPhases;
+  constexpr int HAND = 2 * kMmaGroups * 32;  // threads in one hand-off
+  // Named barriers: 1..P hand-offs (id 1+k: into phase k), P+1 the compute
+  // warps' start, P+2 the Q8 epilogue's warps.
+  constexpr int kBarStart = P + 1, kBarEpi = P + 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [ns <= 8]
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 8);
-  unsigned *red = reinterpret_cast<unsigned *>(smem + ns * S::STAGE + 128);  // [4][MT]
-  uint16_t *dxs = reinterpret_cast<uint16_t *>(red + 4 * MT);              // [KB][MT]
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [8]
+  uint64_t *empty = full + 8;                                            // [8]
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + 8);
+  float *acc_s = reinterpret_cast<float *>(smem + ns * S::STAGE + 256);  // [group][lane][NV]
+  unsigned *red = reinterpret_cast<unsigned *>(acc_s + S::ACCS);         // [group][MT]
+  float *dxs = reinterpret_cast<float *>(red + kMmaGroups * MT);         // [KB][MT], dx/16
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int tile = blockIdx.x, m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
   const int KB = a.K / 32, nchunks = (KB + CB - 1) / CB;
-  auto bar = [&](int i) { return smem_u32(bars + i); };
+  auto fb = [&](int i) { return smem_u32(full + i); };
+  auto eb = [&](int i) { return smem_u32(empty + i); };
 
   pdl_trigger();
-  auto load_weights = [&](int ci) {
-    const int slot = ci % ns;
-    uint8_t *st = smem + slot * S::STAGE;
-    const int y = tile * KB + ci * CB;
-    mbar_expect_tx(bar(slot), S::TX);
-    tma_load_2d(smem_u32(st), &tmN, 0, y, bar(slot));
-    tma_load_2d(smem_u32(st + S::NIB), &tmS, 0, y, bar(slot));
-    if (SWIGLU) {
-      tma_load_2d(smem_u32(st + S::WS), &tmN2, 0, y, bar(slot));
-      tma_load_2d(smem_u32(st + S::WS + S::NIB), &tmS2, 0, y, bar(slot));
-    }
-  };
-  auto load_acts = [&](int ci) {
-    const int slot = ci % ns;
-    tma_load_2d(smem_u32(smem + slot * S::STAGE + S::W * S::WS), &tmX, ci * CB * 4, m0, bar(slot));
-  };
-  const int pre = nchunks < ns - 1 ? nchunks : ns - 1;
   if (threadIdx.x == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
-    for (int i = 0; i < ns; ++i) mbar_init(bar(i), 1);
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(fb(i), 1);
+      mbar_init(eb(i), kMmaGroups);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int ci = 0; ci < pre; ++ci) load_weights(ci);
   }
-  pdl_wait();
-  if (threadIdx.x == 0)
-    for (int ci = 0; ci < pre; ++ci) load_acts(ci);
-  for (int i = threadIdx.x; i < MT * KB; i += blockDim.x) {
-    const int m = i / KB, blk = i % KB;
-    dxs[blk * MT + m] = m < mcount ? a.xd[(size_t)(m0 + m) * KB + blk] : (uint16_t)0;
-  }
+  __syncthreads();
 
-  const int rowl = 8 * warp + 2 * c;  // this lane's first row within the tile
-  const int row = tile * SI_RT + rowl;
-  float acc[NT][2], accu[NT][2];
-#pragma unroll
-  for (int t = 0; t < NT; ++t)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      acc[t][j] = (!SWIGLU && a.bias) ? a.bias[row + j] : 0.0f;
-      accu[t][j] = 0.0f;
-    }
-  __syncthreads();  // dxs visible
-
-  for (int ci = 0; ci < nchunks; ++ci) {
-    if (threadIdx.x == 0 && ci + ns - 1 < nchunks) {
-      load_weights(ci + ns - 1);
-      load_acts(ci + ns - 1);
-    }
-    const int slot = ci % ns;
-    const bool ok = mbar_wait(bar(slot), (ci / ns) & 1, abort_flag);
-    if (ok) {
-      const uint8_t *st = smem + slot * S::STAGE;
-      const uint8_t *act = st + S::W * S::WS;
-      const int nb = min(CB, KB - ci * CB);
-#pragma unroll
-      for (int bl = 0; bl < CB; ++bl) {
-        if (bl < nb) {
-          const int bx = ci * CB + bl;
-          const uint32_t *ar = reinterpret_cast<const uint32_t *>(act + (g * CB + bl) * 32);
-          const uint32_t a0 = ar[c], a2 = ar[4 + c];
-          uint32_t a1 = 0, a3 = 0;
-          if (NT == 2) {
-            const uint32_t *ar8 = reinterpret_cast<const uint32_t *>(act + ((g + 8) * CB + bl) * 32);
-            a1 = ar8[c];
-            a3 = ar8[4 + c];
-          }
-          float dx[NT];
-#pragma unroll
-          for (int t = 0; t < NT; ++t) dx[t] = f16_to_f32(dxs[bx * MT + g + 8 * t]);
-#pragma unroll
-          for (int wi = 0; wi < S::W; ++wi) {
-            const uint8_t *ws = st + wi * S::WS;
-            const uint32_t wn =
-                *reinterpret_cast<const uint32_t *>(ws + bl * 512 + (8 * warp + g) * 16 + 4 * c);
-            int d[4];
-            mma_s8_16832(d, a0, a1, a2, a3, (uint32_t)lo_nib_s8x16(wn), (uint32_t)hi_nib_s8x16(wn));
-            const uint32_t dwp = *reinterpret_cast<const uint32_t *>(ws + S::NIB + (bl * 32 + rowl) * 2);
-            const float dw0 = f16_to_f32((uint16_t)dwp), dw1 = f16_to_f32((uint16_t)(dwp >> 16));
-            float(&ac)[NT][2] = wi == 0 ? acc : accu;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              ac[t][0] = __fadd_rn(ac[t][0], block_term(d[2 * t] >> 4, dw0, dx[t]));
-              ac[t][1] = __fadd_rn(ac[t][1], block_term(d[2 * t + 1] >> 4, dw1, dx[t]));
-            }
-            if (!SWIGLU && a.isum_out) {
-#pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                const int tok = g + 8 * t;
-                if (tok < mcount) {
-                  int32_t *io = a.isum_out + ((size_t)(m0 + tok) * a.N + row) * KB + bx;
-                  io[0] = d[2 * t] >> 4;
-                  io[KB] = d[2 * t + 1] >> 4;
-                }
-              }
-            }
-          }
+  if (warp == kMmaWarps - 1) {
+    // ---- producer ----------------------------------------------------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+      auto weights = [&](int ci) {
+        const int slot = ci % ns;
+        uint8_t *st = smem + slot * S::STAGE;
+        const int y = tile * KB + ci * CB;
+        mbar_expect_tx(fb(slot), S::TX);
+        tma_load_2d(smem_u32(st), &tmN, 0, y, fb(slot));
+        tma_load_2d(smem_u32(st + S::NIB), &tmS, 0, y, fb(slot));
+        if (SWIGLU) {
+          tma_load_2d(smem_u32(st + S::WS), &tmN2, 0, y, fb(slot));
+          tma_load_2d(smem_u32(st + S::WS + S::NIB), &tmS2, 0, y, fb(slot));
         }
+      };
+      auto acts = [&](int ci) {
+        tma_load_2d(smem_u32(smem + (ci % ns) * S::STAGE + W * S::WS), &tmX, ci * CB * 4, m0,
+                    fb(ci % ns));
+      };
+      // The first ring's weights go out before the previous kernel has
+      // produced the activations.
+      const int pre = nchunks < ns ? nchunks : ns;
+      for (int ci = 0; ci < pre; ++ci) weights(ci);
+      pdl_wait();
+      for (int ci = 0; ci < pre; ++ci) acts(ci);
+      for (int ci = pre; ci < nchunks; ++ci) {
+        if (!mbar_wait(eb(ci % ns), ((ci / ns) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          break;
+        }
+        weights(ci);
+        acts(ci);
       }
-    } else {
+    }
+    return;
+  }
+
+  // ---- compute warps: phase k, 16-row group rg ---------------------------
+  const int k = warp / kMmaGroups, rg = warp % kMmaGroups;
+  pdl_wait();
+  {
+    // Eight independent loads in flight per thread (a K of 29568 has 7392
+    // scales per 8 tokens).
+    constexpr int NTH = (kMmaWarps - 1) * 32;
+    for (int i0 = threadIdx.x; i0 < MT * KB; i0 += 8 * NTH) {
+      uint16_t v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * NTH, m = i / KB, blk = i % KB;
+        v[j] = (i < MT * KB && m < mcount) ? a.xd[(size_t)(m0 + m) * KB + blk] : (uint16_t)0;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + j * NTH;
+        if (i < MT * KB) dxs[(i % KB) * MT + i / KB] = __fmul_rn(f16_to_f32(v[j]), 0.0625f);
+      }
+    }
+  }
+  named_sync(kBarStart, (kMmaWarps - 1) * 32);  // dxs visible
+
+  const int r0 = tile * SI_RT + 16 * rg + g;  // this lane's rows r0 and r0 + 8
+  // sums [stream][octet][row half][token of the pair]
+  float acc[W][NT][2][2];
+  bool ok = true;
+  int last = -1;  // the chunk whose sums this warp holds at the end
+  for (int ci = k; ci < nchunks; ci += P) {
+    const int slot = ci % ns;
+    const bool got = ok && mbar_wait(fb(slot), (ci / ns) & 1, abort_flag);
+    if (!got) {
+      ok = false;
       *abort_flag = 1;
     }
-    // Chunk consumed by every warp: its ring slot is free for chunk ci + ns.
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
-      return;
+    const uint8_t *st = smem + slot * S::STAGE;
+    const uint8_t *act = st + W * S::WS;
+    const int nb = min(CB, KB - ci * CB);
+    float t[CB][W][NT][2][2];
+    auto group = [&](auto nbc, int bl0) {
+      constexpr int NB = decltype(nbc)::value;
+      int d[NB][W][NT][4];
+      uint32_t dwp[NB][W][2];
+      float2 dx[NB][NT];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+        const int bl = bl0 + j, bx = ci * CB + bl;
+        uint32_t b[NT][2];
+#pragma unroll
+        for (int q = 0; q < NT; ++q) {
+          const uint32_t *ar = reinterpret_cast<const uint32_t *>(act + ((g + 8 * q) * CB + bl) * 32);
+          b[q][0] = ar[c];
+          b[q][1] = ar[4 + c];
+          dx[j][q] = *reinterpret_cast<const float2 *>(dxs + bx * MT + 8 * q + 2 * c);
+        }
+#pragma unroll
+        for (int wi = 0; wi < W; ++wi) {
+          const uint8_t *ws = st + wi * S::WS;
+          const uint8_t *wr = ws + bl * 512 + (16 * rg + g) * 16 + 4 * c;
+          const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wr);
+          const uint32_t w8 = *reinterpret_cast<const uint32_t *>(wr + 8 * 16);
+          const uint32_t a0 = (uint32_t)lo_nib_s8x16(w0), a2 = (uint32_t)hi_nib_s8x16(w0);
+          const uint32_t a1 = (uint32_t)lo_nib_s8x16(w8), a3 = (uint32_t)hi_nib_s8x16(w8);
+#pragma unroll
+          for (int q = 0; q < NT; ++q) mma_s8_16832(d[j][wi][q], a0, a1, a2, a3, b[q][0], b[q][1]);
+          const uint16_t *sr = reinterpret_cast<const uint16_t *>(ws + S::NIB) + bl * 32 + 16 * rg + g;
+          dwp[j][wi][0] = sr[0];
+          dwp[j][wi][1] = sr[8];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NB; ++j) {
+#pragma unroll
+        for (int wi = 0; wi < W; ++wi) {
+          const float dw[2] = {f16_to_f32((uint16_t)dwp[j][wi][0]),
+                               f16_to_f32((uint16_t)dwp[j][wi][1])};
+#pragma unroll
+          for (int q = 0; q < NT; ++q)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              t[bl0 + j][wi][q][h][0] = block_term(d[j][wi][q][2 * h], dw[h], dx[j][q].x);
+              t[bl0 + j][wi][q][h][1] = block_term(d[j][wi][q][2 * h + 1], dw[h], dx[j][q].y);
+            }
+        }
+        if (!SWIGLU && a.isum_out) {
+          const int bx = ci * CB + bl0 + j;
+#pragma unroll
+          for (int q = 0; q < NT; ++q)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int tok = 8 * q + 2 * c + e;
+                if (tok < mcount)
+                  a.isum_out[((size_t)(m0 + tok) * a.N + r0 + 8 * h) * KB + bx] =
+                      d[j][0][q][2 * h + e] >> 4;
+              }
+        }
+      }
+    };
+    if (got) {
+      if (nb == CB) {
+#pragma unroll
+        for (int bl0 = 0; bl0 + S::GB <= CB; bl0 += S::GB)
+          group(std::integral_constant<int, S::GB>{}, bl0);
+#pragma unroll
+        for (int bl = CB / S::GB * S::GB; bl < CB; ++bl) group(std::integral_constant<int, 1>{}, bl);
+      } else {
+#pragma unroll
+        for (int bl = 0; bl < CB; ++bl)
+          if (bl < nb) group(std::integral_constant<int, 1>{}, bl);
+      }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(eb(slot));  // stage free for the producer
+    // Running sums of the previous chunk, then this chunk's terms in order.
+    float *ac = &acc[0][0][0][0];
+    if (ci == 0) {
+#pragma unroll
+      for (int wi = 0; wi < W; ++wi)
+#pragma unroll
+        for (int q = 0; q < NT; ++q)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+              acc[wi][q][h][e] = (!SWIGLU && a.bias) ? a.bias[r0 + 8 * h] : 0.0f;
+    } else {
+      named_sync(1 + k, HAND);
+      const float *src = acc_s + (rg * 32 + lane) * NV;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) ac[i] = src[i];
+    }
+    if (got) {
+#pragma unroll
+      for (int bl = 0; bl < CB; ++bl)
+        if (bl < nb) {
+          const float *tb = &t[bl][0][0][0][0];
+#pragma unroll
+          for (int i = 0; i < NV; ++i) ac[i] = __fadd_rn(ac[i], tb[i]);
+        }
+    }
+    if (ci + 1 < nchunks) {
+      float *dst = acc_s + (rg * 32 + lane) * NV;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) dst[i] = ac[i];
+      named_arrive(1 + (k + 1) % P, HAND);
+    }
+    last = ci;
+  }
+  if (last != nchunks - 1) return;  // another phase holds the final sums
+  if (*abort_flag) ok = false;
+  if (!ok) {
+    if (lane == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+    return;
   }
 
   if (!SWIGLU) {
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const int tok = g + 8 * t;
-      if (tok < mcount) {
-        const size_t o = (size_t)(m0 + tok) * a.N + row;
-        float2 v = make_float2(acc[t][0], acc[t][1]);
-        if (a.resid) {
-          v.x = __fadd_rn(a.resid[o], v.x);
-          v.y = __fadd_rn(a.resid[o + 1], v.y);
+    for (int q = 0; q < NT; ++q)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = 8 * q + 2 * c + e;
+        if (tok >= mcount) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const size_t o = (size_t)(m0 + tok) * a.N + r0 + 8 * h;
+          float v = acc[0][q][h][e];
+          if (a.resid) v = __fadd_rn(a.resid[o], v);
+          a.out[o] = v;
         }
-        *reinterpret_cast<float2 *>(a.out + o) = v;
       }
-    }
   } else {
-    // act = silu(g) * u; the tile's 32 rows of a token are one Q8 block.
-    float act[NT][2];
+    // act = silu(g) * u; the tile's 32 rows of a token are one Q8 block,
+    // spread over this phase's warps (16 rows each, rows g and g+8 per lane).
+    float act[NT][2][2];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      act[t][0] = silu_mul(acc[t][0], accu[t][0]);
-      act[t][1] = silu_mul(acc[t][1], accu[t][1]);
-      unsigned m = max(__float_as_uint(fabsf(act[t][0])), __float_as_uint(fabsf(act[t][1])));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
-      if (c == 0) red[warp * MT + g + 8 * t] = m;
-    }
-    __syncthreads();
+    for (int q = 0; q < NT; ++q)
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const int tok = g + 8 * t;
-      if (tok >= mcount) continue;
-      const unsigned mb = max(max(red[tok], red[MT + tok]), max(red[2 * MT + tok], red[3 * MT + tok]));
-      const float d = __fdiv_rn(__uint_as_float(mb), 127.0f);
-      const float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-      const size_t o = (size_t)(m0 + tok) * a.N + row;
-      if (a.out) *reinterpret_cast<float2 *>(a.out + o) = make_float2(act[t][0], act[t][1]);
-      auto q8 = [&](float e) {
-        int q = __float2int_rn(__fmul_rn(e, inv));
-        q = q > 127 ? 127 : (q < -127 ? -127 : q);
-        return (uint32_t)(q & 0xFF);
-      };
-      *reinterpret_cast<uint16_t *>(a.act_qs + o) = (uint16_t)(q8(act[t][0]) | q8(act[t][1]) << 8);
-      if (warp == 0 && c == 0) a.act_d[(size_t)(m0 + tok) * (a.N / 32) + tile] = f32_to_f16(d);
-    }
+      for (int e = 0; e < 2; ++e) {
+        unsigned m = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          act[q][h][e] = silu_mul(acc[0][q][h][e], acc[1][q][h][e]);
+          m = max(m, __float_as_uint(fabsf(act[q][h][e])));
+        }
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (g == 0) red[rg * MT + 8 * q + 2 * c + e] = m;
+      }
+    named_sync(kBarEpi, kMmaGroups * 32);
+#pragma unroll
+    for (int q = 0; q < NT; ++q)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = 8 * q + 2 * c + e;
+        if (tok >= mcount) continue;
+        const unsigned mb = max(red[tok], red[MT + tok]);
+        const float d = __fdiv_rn(__uint_as_float(mb), 127.0f);
+        const float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const size_t o = (size_t)(m0 + tok) * a.N + r0 + 8 * h;
+          if (a.out) a.out[o] = act[q][h][e];
+          int v = __float2int_rn(__fmul_rn(act[q][h][e], inv));
+          v = v > 127 ? 127 : (v < -127 ? -127 : v);
+          a.act_qs[o] = (int8_t)v;
+        }
+        if (rg == 0 && g == 0) a.act_d[(size_t)(m0 + tok) * (a.N / 32) + tile] = f32_to_f16(d);
+      }
   }
 }
 
@@ -442,8 +588,8 @@ template <int MT, bool SWIGLU>
 cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
   using S = MmaShape<MT, SWIGLU>;
   const int KB = a.K / 32, tiles = a.N / SI_RT;
-  const int nchunks = (KB + S::CB - 1) / S::CB;
-  int ns = nchunks < 2 ? 2 : (nchunks < kStages ? nchunks : kStages);
+  int ns = 8;
+  while (ns > 5 && (size_t)ns * S::STAGE > kMmaRingBudget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
@@ -477,7 +623,7 @@ cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
   }
   dim3 grid(tiles, (a.M + MT - 1) / MT);
-  return launch_pdl(kern, grid, dim3(S::THREADS), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
+  return launch_pdl(kern, grid, dim3(kMmaWarps * 32), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
 }
 
 template <int MT, int RW, bool SWIGLU>
