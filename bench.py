@@ -256,11 +256,19 @@ def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
     barrier_sync()
     reps = 2
     tpf = max_over_ranks(time_region(torch, stream, prefill, reps)) / reps
-    for s in range(3):
-        decode(s)
-    xd[0].copy_(x0)
-    barrier_sync()
-    tdec = max_over_ranks(time_region(torch, stream, decode, TP_DECODE)) / TP_DECODE
+    def time_decode():
+        for s in range(3):
+            decode(s)
+        xd[0].copy_(x0)
+        barrier_sync()
+        return max_over_ranks(time_region(torch, stream, decode, TP_DECODE)) / TP_DECODE
+
+    tdec = time_decode()  # row-parallel sums fused into the projections (world > 1)
+    tdec_nccl = None
+    if world > 1:
+        tp.set_options(fused=False)
+        tdec_nccl = time_decode()
+        tp.set_options(fused=True)
     ctx.status()
     ok = bool(torch.isfinite(xd[0]).all().item()) and bool(torch.isfinite(xp[0]).all().item())
 
@@ -273,7 +281,8 @@ def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
     res = {
         "workload": "BASELINE config 4: 8 Qwen2.5-72B layers (hidden 8192, 64 Q / 8 KV heads, "
                     "intermediate 29568), Q4_0 weights, fp32 KV; column-sharded QKV/gate/up, "
-                    "row-sharded o/down, NCCL all-reduce after each row-parallel projection",
+                    "row-sharded o/down; decode adds the row-parallel partial sums through "
+                    "NVLink peer stores fused into the projection, prefill through NCCL",
         "tp": world, "finite": ok,
         "prefill": {"tokens": TP_PREFILL, "ms": round(tpf * 1e3, 3),
                     "tok_s": round(TP_PREFILL / tpf, 1)},
@@ -283,7 +292,10 @@ def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
                    "us_per_token": round(tdec * 1e6 / TP_BATCH, 3),
                    "tok_s": round(TP_BATCH / tdec, 1),
                    "hbm_bytes_per_step_per_rank": int(per_step),
-                   "achieved_gbs_per_rank": round(per_step / tdec / 1e9, 1)},
+                   "achieved_gbs_per_rank": round(per_step / tdec / 1e9, 1),
+                   "reduction": "fused into the projection (peer stores + flags)" if world > 1
+                                else "none (one rank)",
+                   "us_per_step_nccl_allreduce": round(tdec_nccl * 1e6, 2) if tdec_nccl else None},
         "timing": "CUDA events on the library stream, max over ranks; eager launches",
     }
     for o in kvs + layers:

@@ -310,10 +310,17 @@ SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, co
 /* Tensor parallelism (multi-layer 72B configuration over 2/4/8 GPUs).       */
 /* One process per GPU.  Q/K/V and gate/up are split by rows (whole heads;    */
 /* 128-row units of the MLP, uneven by at most one unit), o and down by       */
-/* columns; each row-parallel projection is followed by one NCCL all-reduce   */
-/* of its fp32 partial sums on the context's stream, then the residual add.   */
-/* Cross-rank summation changes the fp32 order: layer outputs agree with one  */
-/* GPU to the 1e-3 layer bar, not bit for bit.  Not in the reference.         */
+/* columns, so each row-parallel projection leaves partial sums to be added  */
+/* across the ranks.  Decode-sized steps (at most 16 tokens) fuse that       */
+/* exchange into the projection: its GEMV stores the partial sums into every */
+/* rank's receive slot over NVLink (CUDA IPC mappings of one buffer per rank, */
+/* set up by the first such step, a collective call) and a second kernel    */
+/* waits for every rank's flag (bounded; SI_ERR_TIMEOUT past the limit) and   */
+/* adds the slots in rank order and the residual.  Larger steps use one NCCL  */
+/* all-reduce on the context's stream, then the residual add.  Cross-rank     */
+/* summation changes the fp32 order: layer outputs agree with one GPU to the  */
+/* 1e-3 layer bar, not bit for bit; every rank holds identical outputs.       */
+/* The context that creates a group must outlive it.  Not in the reference.   */
 /* ------------------------------------------------------------------------ */
 typedef struct si_tp si_tp;
 /* Units [*first, *first + *count) of `units` owned by rank (host only). */
@@ -321,7 +328,15 @@ SI_API void si_tp_split(int units, int rank, int world, int *first, int *count);
 /* ncclGetUniqueId into 128 bytes, to be shared with every rank. */
 SI_API si_status si_tp_unique_id(void *id128);
 SI_API si_status si_tp_create(si_ctx *ctx, const void *id128, int rank, int world, si_tp **out);
+/* Collective when the group has fused buffers: every rank frees together. */
 SI_API void si_tp_free(si_tp *tp);
+/* fused = 0 sends every row-parallel projection through NCCL; timeout_ms
+ * bounds the fused reduction's wait for the other ranks (default 5000). */
+SI_API si_status si_tp_set_options(si_tp *tp, int fused, int timeout_ms);
+/* Runs the fused reduction's bounded wait against a flag that nothing sets,
+ * on this GPU alone: returns SI_ERR_TIMEOUT after about timeout_us and leaves
+ * the context usable (a check of the failure path, no other rank needed). */
+SI_API si_status si_tp_probe_wait(si_ctx *ctx, int timeout_us);
 /* The shard's dims (heads / world, this rank's MLP rows) and the first MLP
  * row it owns.  Needs heads divisible by world and intermediate % 128 == 0. */
 SI_API si_status si_tp_local_dims(const si_dims *full, int rank, int world, si_dims *local,

@@ -527,7 +527,49 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
     return;
   }
 
-  if (!SWIGLU) {
+  if (!SWIGLU && a.peer.world > 0) {
+    // Row-parallel tensor parallelism: the partial sums go to this rank's slot
+    // on every rank (peer stores over NVLink); the CTA that finishes last
+    // raises this rank's flag everywhere once every CTA's stores are visible.
+    // The tile's sums are gathered in shared memory first ([token][32 rows],
+    // over the hand-off area, free once both warps have read their sums), so
+    // each token's 32 rows cross NVLink as one 128-byte line.
+    const PeerOut &pr = a.peer;
+    const size_t slot0 = ((size_t)(pr.epoch & 1) * pr.world + pr.rank) * pr.slot;
+    named_sync(kBarEpi, kMmaGroups * 32);
+    float *tile_s = acc_s;  // MT * 32 floats == S::ACCS
+#pragma unroll
+    for (int q = 0; q < NT; ++q)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          tile_s[(8 * q + 2 * c + e) * 32 + 16 * rg + g + 8 * h] = acc[0][q][h][e];
+    named_sync(kBarEpi, kMmaGroups * 32);
+    const int et = rg * 32 + lane;  // 0..63: token et / 8, rows 4 * (et % 8) ..
+    for (int i = et; i < mcount * 8; i += kMmaGroups * 32) {
+      const int tok = i / 8, r4 = (i % 8) * 4;
+      const float4 v = *reinterpret_cast<const float4 *>(tile_s + tok * 32 + r4);
+      const size_t o = slot0 + (size_t)(m0 + tok) * a.N + (size_t)tile * SI_RT + r4;
+      for (int dst = 0; dst < pr.world; ++dst)
+        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(pr.base[dst] + kPeerData) + o) = v;
+    }
+    __threadfence_system();
+    named_sync(kBarEpi, kMmaGroups * 32);
+    if (rg == 0 && lane == 0) {
+      unsigned *ticket = reinterpret_cast<unsigned *>(pr.base[pr.rank] + kPeerTicket);
+      const unsigned total = gridDim.x * gridDim.y;
+      if (atomicAdd(ticket, 1u) == total - 1) {
+        *ticket = 0;
+        __threadfence_system();
+        for (int dst = 0; dst < pr.world; ++dst) {
+          unsigned long long *f =
+              reinterpret_cast<unsigned long long *>(pr.base[dst] + kPeerFlags + pr.rank * 128);
+          asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(pr.epoch) : "memory");
+        }
+      }
+    }
+  } else if (!SWIGLU) {
 #pragma unroll
     for (int q = 0; q < NT; ++q)
 #pragma unroll
@@ -692,7 +734,9 @@ template <bool SWIGLU>
 cudaError_t dispatch(const GemvArgs &a, cudaStream_t s) {
   // The tensor-core form from 3 tokens on (or when asked for); the dp4a form
   // for 1-2 tokens, where its per-token cost is lower than one mma per block.
-  const bool mma = a.variant == kGemvMma || (a.variant == kGemvAuto && a.M >= 3);
+  const bool mma = a.variant == kGemvMma || (a.variant == kGemvAuto && a.M >= 3) ||
+                   a.peer.world > 0;
+  if (a.peer.world > 0 && (SWIGLU || a.M > 16)) return cudaErrorInvalidValue;
   if (mma) return a.M <= 8 ? run_mma<8, SWIGLU>(a, s) : run_mma<16, SWIGLU>(a, s);
   if (a.M <= 1) return pick_rows<1, SWIGLU>(a, s);
   if (a.M <= 2) return pick_rows<2, SWIGLU>(a, s);

@@ -7,6 +7,8 @@
 // fp64 sum only in the last bits of a double, far below the float rounding.
 #include "si_common.cuh"
 #include "si_kernels.cuh"
+#include "si_peer.cuh"
+#include "si_tma.cuh"
 
 namespace si {
 
@@ -48,11 +50,11 @@ __global__ void k_q8_quantize(const float *__restrict__ x, size_t nblocks,
 // Q8 block sit in eight adjacent lanes.  out (fp32) and the Q8 pair are each
 // optional.
 template <int VPT>
-__global__ void __launch_bounds__(1024) k_rmsnorm_q8(const float *__restrict__ x,
+__global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
                                                      const float *__restrict__ w, int n, float eps,
                                                      float *__restrict__ out,
                                                      int8_t *__restrict__ qs,
-                                                     uint16_t *__restrict__ d) {
+                                                     uint16_t *__restrict__ d, const RmsPeer rp) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x, n4 = n / 4;
@@ -63,6 +65,29 @@ __global__ void __launch_bounds__(1024) k_rmsnorm_q8(const float *__restrict__ x
   for (int j = 0; j < VPT; ++j) {
     const int i = threadIdx.x + j * blockDim.x;
     v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (rp.p.world > 0) {
+    // h = x + the ranks' partial sums, added in rank order (tp_peer.cu's order).
+    if (!tp_wait_flags(rp.p, rp.timeout_ns, rp.err)) return;
+    const float4 *recv = reinterpret_cast<const float4 *>(
+        reinterpret_cast<const float *>(rp.p.base[rp.p.rank] + kPeerData) +
+        (size_t)(rp.p.epoch & 1) * rp.p.world * rp.p.slot + (size_t)row * n);
+    const size_t slot4 = (size_t)rp.p.slot / 4;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      if (i < n4) {
+        float4 sum = __ldcg(recv + i);
+        for (int src = 1; src < rp.p.world; ++src) {
+          const float4 o = __ldcg(recv + src * slot4 + i);
+          sum = make_float4(__fadd_rn(sum.x, o.x), __fadd_rn(sum.y, o.y), __fadd_rn(sum.z, o.z),
+                            __fadd_rn(sum.w, o.w));
+        }
+        v[j] = make_float4(__fadd_rn(v[j].x, sum.x), __fadd_rn(v[j].y, sum.y),
+                           __fadd_rn(v[j].z, sum.z), __fadd_rn(v[j].w, sum.w));
+        reinterpret_cast<float4 *>(rp.h_out + (size_t)row * n)[i] = v[j];
+      }
+    }
   }
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -144,25 +169,33 @@ cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_
 }
 
 cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, float eps,
-                              float *out, int8_t *qs, uint16_t *d, cudaStream_t s) {
+                              float *out, int8_t *qs, uint16_t *d, cudaStream_t s,
+                              const RmsPeer *rpp) {
+  RmsPeer rp{};
+  if (rpp) {
+    rp = *rpp;
+    if (rp.p.world < 1 || rp.p.world > kPeerMaxWorld || (size_t)M * n > (size_t)rp.p.slot ||
+        !rp.h_out || (reinterpret_cast<uintptr_t>(rp.h_out) & 15) || rp.p.slot % 4)
+      return cudaErrorInvalidValue;
+  }
   if (M == 0) return cudaSuccess;
   if (n % 4 || (qs && n % 32) || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(qs) & 3) ||
       (reinterpret_cast<uintptr_t>(d) & 1))
     return cudaErrorMisalignedAddress;
-  // Threads: a multiple of 32 with at most 4 float4 each up to 1024 threads.
+  // Threads: a multiple of 32 with at most 4 float4 each up to 512 threads.
   const int n4 = n / 4;
   int threads = ((n4 + 3) / 4 + 31) / 32 * 32;
-  threads = threads < 128 ? 128 : (threads > 1024 ? 1024 : threads);
+  threads = threads < 128 ? 128 : (threads > 512 ? 512 : threads);
   const int vpt = (n4 + threads - 1) / threads;
   const dim3 g(M), b(threads);
   switch (vpt) {
-    case 1: return launch_pdl(k_rmsnorm_q8<1>, g, b, 0, s, x, w, n, eps, out, qs, d);
-    case 2: return launch_pdl(k_rmsnorm_q8<2>, g, b, 0, s, x, w, n, eps, out, qs, d);
-    case 3: return launch_pdl(k_rmsnorm_q8<3>, g, b, 0, s, x, w, n, eps, out, qs, d);
-    case 4: return launch_pdl(k_rmsnorm_q8<4>, g, b, 0, s, x, w, n, eps, out, qs, d);
+    case 1: return launch_pdl(k_rmsnorm_q8<1>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 2: return launch_pdl(k_rmsnorm_q8<2>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 3: return launch_pdl(k_rmsnorm_q8<3>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 4: return launch_pdl(k_rmsnorm_q8<4>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
     case 5: case 6: case 7: case 8:
-      return launch_pdl(k_rmsnorm_q8<8>, g, b, 0, s, x, w, n, eps, out, qs, d);
+      return launch_pdl(k_rmsnorm_q8<8>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -136,6 +136,8 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
   ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
                              ncclComm_t, cudaStream_t);
+  ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t);
   ncclResult_t (*comm_destroy)(ncclComm_t);
   const char *(*error_string)(ncclResult_t);
 };
@@ -153,10 +155,11 @@ static const NcclApi *nccl_api() {
       api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
       api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
       api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+      api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
       api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
       api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
-      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy &&
-          api.error_string)
+      if (api.get_unique_id && api.comm_init_rank && api.all_reduce && api.all_gather &&
+          api.comm_destroy && api.error_string)
         state = 1;
     }
   }
@@ -170,9 +173,19 @@ static const NcclApi *nccl_api() {
   } while (0)
 
 // Tensor-parallel group: one NCCL communicator per rank (one rank per GPU).
+// With fused row-parallel projections (the default when world > 1), each rank
+// also holds one symmetric buffer (flags, CTA ticket, receive slots; see
+// si::PeerOut) that every other rank maps through a CUDA IPC handle.
 struct si_tp {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  si_ctx *ctx = nullptr;               // the context that created the group
+  int fused = 1;                       // fused GEMV + peer reduction for T <= 16
+  unsigned long long timeout_ns = 5000000000ull;
+  char *sym = nullptr;                 // own symmetric buffer
+  char *peer[si::kPeerMaxWorld] = {};  // every rank's buffer as mapped here
+  int slot = 0;                        // floats per receive slot
+  unsigned long long epoch = 0;        // fused calls so far
 };
 
 struct si_kv {
@@ -988,6 +1001,115 @@ static si_status tp_allreduce(si_ctx *ctx, si_tp *tp, float *buf, size_t n) {
   return SI_OK;
 }
 
+// Collective: every rank calls it at the same point.  A one-int all-reduce
+// on the group's stream, waited for, as a barrier between the ranks.
+static si_status tp_barrier(si_ctx *ctx, si_tp *tp, void *scratch_dev) {
+  const NcclApi *api = nccl_api();
+  SI_CHECK(api, "NCCL is not available");
+  SI_NCCL(api, api->all_reduce(scratch_dev, scratch_dev, 1, ncclInt32, ncclSum, tp->comm,
+                               ctx->stream),
+          "ncclAllReduce");
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
+// Collective: unmaps the peers' buffers and frees this rank's, once no rank
+// can still write into it.
+static si_status tp_sym_release(si_ctx *ctx, si_tp *tp) {
+  if (!tp->sym) return SI_OK;
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  for (int r = 0; r < tp->world; ++r)
+    if (r != tp->rank && tp->peer[r]) cudaIpcCloseMemHandle(tp->peer[r]);
+  SI_TRY(tp_barrier(ctx, tp, tp->sym + si::kPeerTicket + 64));
+  cudaFree(tp->sym);
+  tp->sym = nullptr;
+  for (char *&p : tp->peer) p = nullptr;
+  tp->slot = 0;
+  return SI_OK;
+}
+
+// Collective: a symmetric buffer with receive slots of at least `slot`
+// floats on every rank, mapped by every other rank (CUDA IPC handles
+// exchanged with an NCCL all-gather).
+static si_status tp_sym_reserve(si_ctx *ctx, si_tp *tp, int slot) {
+  if (tp->sym && tp->slot >= slot) return SI_OK;
+  SI_TRY(tp_sym_release(ctx, tp));
+  const size_t bytes = si::kPeerData + (size_t)2 * tp->world * slot * sizeof(float);
+  SI_CUDA(cudaMalloc(&tp->sym, bytes));
+  SI_CUDA(cudaMemset(tp->sym, 0, si::kPeerData));
+  tp->slot = slot;
+  tp->epoch = 0;
+  cudaIpcMemHandle_t h;
+  SI_CUDA(cudaIpcGetMemHandle(&h, tp->sym));
+  static_assert(sizeof(cudaIpcMemHandle_t) <= 64, "IPC handle size");
+  char *xchg = tp->sym + si::kPeerData;  // the slots are not in use yet
+  SI_CUDA(cudaMemcpyAsync(xchg + (size_t)tp->rank * 64, &h, sizeof(h), cudaMemcpyHostToDevice,
+                          ctx->stream));
+  const NcclApi *api = nccl_api();
+  SI_CHECK(api, "NCCL is not available");
+  SI_NCCL(api, api->all_gather(xchg + (size_t)tp->rank * 64, xchg, 64, ncclUint8, tp->comm,
+                               ctx->stream),
+          "ncclAllGather");
+  std::vector<char> all((size_t)tp->world * 64);
+  SI_CUDA(cudaMemcpyAsync(all.data(), xchg, all.size(), cudaMemcpyDeviceToHost, ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  for (int r = 0; r < tp->world; ++r) {
+    if (r == tp->rank) {
+      tp->peer[r] = tp->sym;
+      continue;
+    }
+    cudaIpcMemHandle_t hr;
+    memcpy(&hr, all.data() + (size_t)r * 64, sizeof(hr));
+    void *p = nullptr;
+    SI_CUDA(cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess));
+    tp->peer[r] = static_cast<char *>(p);
+  }
+  // Every rank's flags are zero and its mappings open before any rank writes.
+  SI_TRY(tp_barrier(ctx, tp, tp->sym + si::kPeerTicket + 64));
+  return SI_OK;
+}
+
+// A row-parallel projection of a TP layer: out = resid + the sum over ranks of
+// x.W_r.  Decode-sized steps (T <= 16) fuse the exchange into the GEMV (peer
+// stores + flags) and add the slots in tp_peer.cu's combine kernel; larger
+// steps run the GEMM, an NCCL all-reduce and the residual add.
+static bool tp_fused(const si_tp *tp, int T) {
+  return tp->world > 1 && tp->fused && T <= 16 && tp->world <= si::kPeerMaxWorld;
+}
+
+// The GEMV half of a fused row-parallel projection: partial sums to every
+// rank's receive slot; *po describes them for the consuming kernel.
+static si_status tp_gemv_peer(si_ctx *ctx, si_tp *tp, const si_matrix *w, const int8_t *qs,
+                              const uint16_t *d, int T, si::PeerOut *po) {
+  const int n = T * w->rows;
+  SI_TRY(tp_sym_reserve(ctx, tp, 16 * w->rows > n ? 16 * w->rows : n));
+  si::GemvArgs a = gemv_args(w, qs, d, T);
+  a.variant = si::kGemvMma;
+  a.peer.world = tp->world;
+  a.peer.rank = tp->rank;
+  a.peer.slot = tp->slot;
+  a.peer.epoch = ++tp->epoch;
+  for (int r = 0; r < tp->world; ++r) a.peer.base[r] = tp->peer[r];
+  SI_CUDA(si::launch_gemv(a, false, ctx->stream));
+  *po = a.peer;
+  return SI_OK;
+}
+
+static si_status tp_rowparallel(si_ctx *ctx, si_tp *tp, const si_matrix *w, const int8_t *qs,
+                                const uint16_t *d, int T, const float *resid, float *out) {
+  const size_t n = (size_t)T * w->rows;
+  if (tp_fused(tp, T)) {
+    si::PeerOut po;
+    SI_TRY(tp_gemv_peer(ctx, tp, w, qs, d, T, &po));
+    SI_CUDA(si::launch_tp_combine(po, resid, out, n, tp->timeout_ns, ctx->err, ctx->stream));
+    return SI_OK;
+  }
+  SI_TRY(matmul(ctx, w, qs, d, T, nullptr, nullptr, out, -1));
+  SI_TRY(tp_allreduce(ctx, tp, out, n));
+  SI_CUDA(si::launch_add(resid, out, out, n, ctx->stream));
+  return SI_OK;
+}
+
 // One layer step.  With tp, the layer holds this rank's shard (its Q/KV heads
 // and its slice of the MLP); the O and down projections then produce partial
 // sums, which are all-reduced before the residual adds.
@@ -1093,26 +1215,37 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
   // 6. Output projection (qwen_one_layer.c:275); the decoder layer adds the residual.
   const size_t TH = (size_t)T * H;
   if (mode == SI_LAYER_ATTN) {
-    SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, y, -1));
-    if (tp) SI_TRY(tp_allreduce(ctx, tp, y, TH));
+    if (tp) {
+      SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, y, -1));
+      SI_TRY(tp_allreduce(ctx, tp, y, TH));
+    } else {
+      SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, y, -1));
+    }
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
   } else {
-    if (tp) {
-      SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, nullptr, b.h, -1));
-      SI_TRY(tp_allreduce(ctx, tp, b.h, TH));
-      SI_CUDA(si::launch_add(x, b.h, b.h, TH, s));
+    bool normed = false;
+    if (tp && tp_fused(tp, T)) {
+      // The ranks' o partial sums, the residual and rmsnorm2 + Q8 in one kernel.
+      si::RmsPeer rp{};
+      SI_TRY(tp_gemv_peer(ctx, tp, l->o, b.aq, b.ad, T, &rp.p));
+      rp.h_out = b.h;
+      rp.timeout_ns = tp->timeout_ns;
+      rp.err = ctx->err;
+      SI_CUDA(si::launch_rmsnorm_q8(x, l->norm2, T, H, d.rms_eps, nullptr, b.hq, b.hd, s, &rp));
+      normed = true;
+    } else if (tp) {
+      SI_TRY(tp_rowparallel(ctx, tp, l->o, b.aq, b.ad, T, x, b.h));
     } else {
       SI_TRY(matmul(ctx, l->o, b.aq, b.ad, T, nullptr, x, b.h, -1));
     }
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_OPROJ], s));
     // 7. MLP: rmsnorm2 + Q8 -> gate/up + SiLU*mul + Q8 -> down + residual.
-    SI_CUDA(si::launch_rmsnorm_q8(b.h, l->norm2, T, H, d.rms_eps, nullptr, b.hq, b.hd, s));
+    if (!normed)
+      SI_CUDA(si::launch_rmsnorm_q8(b.h, l->norm2, T, H, d.rms_eps, nullptr, b.hq, b.hd, s));
     SI_TRY(si_gateup_q8_dev(ctx, l->gate, l->up, b.hq, b.hd, T, b.actq, b.actd, nullptr));
     if (tp) {
-      SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, nullptr, y, -1));
-      SI_TRY(tp_allreduce(ctx, tp, y, TH));
-      SI_CUDA(si::launch_add(b.h, y, y, TH, s));
+      SI_TRY(tp_rowparallel(ctx, tp, l->down, b.actq, b.actd, T, b.h, y));
     } else {
       SI_TRY(matmul(ctx, l->down, b.actq, b.actd, T, nullptr, b.h, y, -1));
     }
@@ -1898,6 +2031,7 @@ extern "C" SI_API si_status si_tp_create(si_ctx *ctx, const void *id, int rank, 
   si_tp *tp = new si_tp();
   tp->rank = rank;
   tp->world = world;
+  tp->ctx = ctx;
   ncclResult_t r = api->comm_init_rank(&tp->comm, world, uid, rank);
   if (r != ncclSuccess) {
     delete tp;
@@ -1909,8 +2043,39 @@ extern "C" SI_API si_status si_tp_create(si_ctx *ctx, const void *id, int rank, 
 
 extern "C" SI_API void si_tp_free(si_tp *tp) {
   if (!tp) return;
+  if (tp->sym && tp->ctx && set_device(tp->ctx) == SI_OK) tp_sym_release(tp->ctx, tp);
   if (tp->comm && nccl_api()) nccl_api()->comm_destroy(tp->comm);
   delete tp;
+}
+
+extern "C" SI_API si_status si_tp_set_options(si_tp *tp, int fused, int timeout_ms) {
+  SI_CHECK(tp && timeout_ms > 0, "bad TP options");
+  tp->fused = fused != 0;
+  tp->timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_tp_probe_wait(si_ctx *ctx, int timeout_us) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(timeout_us > 0 && timeout_us <= 10000000, "timeout out of range");
+  // A two-rank group whose other rank never writes: this rank's buffer stands
+  // for both, its flags stay zero, and the combine's wait must give up.
+  char *buf = nullptr;
+  SI_CUDA(cudaMalloc(&buf, si::kPeerData + 2 * 2 * 32 * sizeof(float)));
+  SI_CUDA(cudaMemset(buf, 0, si::kPeerData));
+  si::PeerOut p{};
+  p.world = 2;
+  p.rank = 0;
+  p.slot = 32;
+  p.epoch = 1;
+  p.base[0] = p.base[1] = buf;
+  float *y = reinterpret_cast<float *>(buf + si::kPeerData);
+  cudaError_t e = si::launch_tp_combine(p, nullptr, y, 32, (unsigned long long)timeout_us * 1000ull,
+                                        ctx->err, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(buf);
+  if (e != cudaSuccess) return fail(SI_ERR_CUDA, "probe: %s", cudaGetErrorString(e));
+  return si_ctx_status(ctx);
 }
 
 extern "C" SI_API si_status si_tp_local_dims(const si_dims *full, int rank, int world,

@@ -6,6 +6,22 @@
 
 namespace si {
 
+// Row-parallel tensor parallelism: where a GEMV's partial sums go instead of
+// `out` -- every rank's receive slot -- and how its last CTA signals them.
+// Each rank holds one symmetric buffer: flags[src] (u64 epochs, 128 B apart)
+// at kPeerFlags, a CTA ticket at kPeerTicket, receive slots
+// [2 parities][world][slot floats] at kPeerData.
+constexpr int kPeerMaxWorld = 8;
+constexpr size_t kPeerFlags = 0, kPeerTicket = 1024, kPeerData = 4096;
+struct PeerOut {
+  char *base[kPeerMaxWorld];  // each rank's buffer as mapped in this process (own included)
+  int world;                  // 0: no peer output
+  int rank;
+  int slot;                   // floats per receive slot (>= M * N)
+  unsigned long long epoch;   // this call's number, 1, 2, ...; parity picks the slot set
+};
+
+
 // ---- layout.cu -------------------------------------------------------------
 // GGUF Q4_0 rows [rows][KB] x 18 B  ->  row-tile SoA: nib [rows/32][KB][32][16]
 // (each byte XOR 0x88) and scl [rows/32][KB][32] fp16.
@@ -44,8 +60,19 @@ cudaError_t launch_colsoa_matvec(const uint8_t *tile, const uint8_t *x_blocks, i
 // ---- norm_q8.cu -------------------------------------------------------------
 cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_t *d,
                                cudaStream_t s);
+// With rp (tensor parallelism, decode): x is the residual and the row is
+// first h = x + the sum over ranks (rank order) of the receive slots of
+// rp->p.epoch, after the bounded wait for every rank's flag; h is written to
+// rp->h_out and normalised.
+struct RmsPeer {
+  PeerOut p;
+  float *h_out;
+  unsigned long long timeout_ns;
+  int *err;
+};
 cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, float eps,
-                              float *out, int8_t *qs, uint16_t *d, cudaStream_t s);
+                              float *out, int8_t *qs, uint16_t *d, cudaStream_t s,
+                              const RmsPeer *rp = nullptr);
 // y = a + b elementwise (residual), fp32, round-to-nearest.
 cudaError_t launch_add(const float *a, const float *b, float *y, size_t n, cudaStream_t s);
 
@@ -68,6 +95,7 @@ struct GemvArgs {
   int *err;                // context device error word (bounded waits), or null
   float *scratch;          // tcgen05 GEMM: gemm_tc_scratch_bytes() of device memory
   int variant;             // GEMV form: kGemvAuto, kGemvDp4a or kGemvMma
+  PeerOut peer;            // tensor-core form only: partial sums to every rank's slot
 };
 enum { kGemvAuto = 0, kGemvDp4a = 1, kGemvMma = 2 };
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
@@ -111,5 +139,11 @@ size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
 // of one sequence, T >= 16), else ceil(max_len / 128).
 int attn_pick_splits(int T, bool decode_form, int max_len);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
+
+// ---- tp_peer.cu --------------------------------------------------------------
+// y[i] = resid[i] + sum over ranks (in rank order) of the receive slots of
+// epoch `epoch`, after a bounded wait (timeout_ns) for every rank's flag.
+cudaError_t launch_tp_combine(const PeerOut &p, const float *resid, float *y, size_t n,
+                              unsigned long long timeout_ns, int *err, cudaStream_t s);
 
 }  // namespace si

@@ -1,0 +1,53 @@
+// tp_peer.cu -- the reduction half of the fused row-parallel projection.
+//
+// Tensor parallelism (no counterpart in the single-core reference; its layer
+// is qwen_one_layer.c:245-280) splits QKV/gate/up by output rows and O/down
+// by input rows, so the O and down projections leave partial sums that every
+// rank must add.  Instead of a separate all-reduce, the projection's own GEMV
+// writes its partial sums straight into every rank's receive slot over NVLink
+// (peer stores from the tensor-core GEMV's epilogue, tile by tile as the
+// tiles finish) and its last CTA raises this rank's flag on every rank; this
+// kernel then waits for all ranks' flags, adds the slots in rank order and
+// the residual.  Every rank sums in the same
+// order, so all ranks hold bit-identical hidden states.
+//
+// The wait is bounded: past timeout_ns the kernel records SI_ERR_TIMEOUT in
+// the context's error word and returns without writing y, so a rank that
+// never arrives ends in an error on the host instead of a hung GPU.
+#include "si_common.cuh"
+#include "si_kernels.cuh"
+#include "si_peer.cuh"
+#include "si_tma.cuh"
+
+namespace si {
+
+namespace {
+__global__ void __launch_bounds__(256) k_tp_combine(const PeerOut p, const float *resid,
+                                                    float *y, size_t n,
+                                                    unsigned long long timeout_ns, int *err) {
+  pdl_trigger();
+  pdl_wait();
+  if (!tp_wait_flags(p, timeout_ns, err)) return;
+  const char *own = p.base[p.rank];
+  const float *recv = reinterpret_cast<const float *>(own + kPeerData) +
+                      (size_t)(p.epoch & 1) * p.world * p.slot;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float s = __ldcg(recv + i);
+    for (int src = 1; src < p.world; ++src) s = __fadd_rn(s, __ldcg(recv + (size_t)src * p.slot + i));
+    y[i] = resid ? __fadd_rn(resid[i], s) : s;
+  }
+}
+}  // namespace
+
+cudaError_t launch_tp_combine(const PeerOut &p, const float *resid, float *y, size_t n,
+                              unsigned long long timeout_ns, int *err, cudaStream_t s) {
+  if (p.world < 1 || p.world > kPeerMaxWorld || p.rank < 0 || p.rank >= p.world ||
+      n > (size_t)p.slot)
+    return cudaErrorInvalidValue;
+  const unsigned blocks = (unsigned)((n + 1023) / 1024);
+  return launch_pdl(k_tp_combine, dim3(blocks < 1 ? 1 : blocks), dim3(256), 0, s, p, resid, y, n,
+                    timeout_ns, err);
+}
+
+}  // namespace si

@@ -19,6 +19,8 @@ PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_PATH = os.path.join(PKG_DIR, "lib", "libsi_b200.so")
 
 SI_OK = 0
+SI_ERR_INVALID, SI_ERR_CUDA, SI_ERR_OOM, SI_ERR_NO_DEVICE = 1, 2, 3, 4
+SI_ERR_DEVICE, SI_ERR_TIMEOUT, SI_ERR_IO, SI_ERR_UNSUPPORTED = 5, 6, 7, 8
 SI_LAYER_ATTN, SI_LAYER_FULL = 0, 1
 
 
@@ -115,6 +117,8 @@ def lib() -> C.CDLL:
         "si_tp_unique_id": (i32, [vp]),
         "si_tp_create": (i32, [vp, vp, i32, i32, pp]),
         "si_tp_free": (None, [vp]),
+        "si_tp_set_options": (i32, [vp, i32, i32]),
+        "si_tp_probe_wait": (i32, [vp, i32]),
         "si_tp_local_dims": (i32, [C.POINTER(Dims), i32, i32, C.POINTER(Dims),
                                    C.POINTER(C.c_int)]),
         "si_layer_tp_synth": (i32, [vp, C.POINTER(Dims), u64, i32, i32, pp]),
@@ -269,6 +273,10 @@ class Context:
         buf = C.create_string_buffer(bytes(uid), 128)
         check(self.L.si_tp_create(self.h, buf, rank, world, C.byref(h)), "si_tp_create")
         return TP(self, h, rank, world)
+
+    def tp_probe_wait(self, timeout_us: int) -> int:
+        """Status of the fused TP reduction's bounded wait on a flag nothing sets."""
+        return self.L.si_tp_probe_wait(self.h, timeout_us)
 
     def layer_tp_synth(self, full: dict, seed: int, rank: int, world: int) -> "Layer":
         dm = Dims.of(full)
@@ -448,6 +456,9 @@ class TP:
     def prefill_dev(self, layer: "Layer", kv: "KV", seq, x, ntok, prefix, y, mode=SI_LAYER_FULL):
         check(self.ctx.L.si_prefill_tp_dev(self.ctx.h, self.h, layer.h, kv.h, seq, _p(x), ntok,
                                            prefix, _p(y), mode), "si_prefill_tp_dev")
+
+    def set_options(self, fused: bool = True, timeout_ms: int = 5000):
+        check(self.ctx.L.si_tp_set_options(self.h, int(fused), timeout_ms), "si_tp_set_options")
 
     def free(self):
         if self.h:

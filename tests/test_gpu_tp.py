@@ -1,11 +1,13 @@
-"""Tensor parallelism over NCCL on two GPUs: the sharded layer (one process per
-GPU, all-reduce after the O and down projections) against the same layer on
-one GPU, for a batch-1 decode step (GEMV path) and a 40-token prefill
-(tcgen05 GEMM path).  Cross-rank summation reorders the fp32 sums, so the bar
-is the layer bar, 1e-3.  Skipped on hosts with fewer than two GPUs.
+"""Tensor parallelism on two GPUs: the sharded layer (one process per GPU)
+against the same layer on one GPU, for decode steps (GEMV path) and a
+40-token prefill (tcgen05 GEMM path).  Decode runs both ways the group can
+add the row-parallel partial sums: fused into the projection (peer stores over
+NVLink plus a flag-gated combine kernel) and through NCCL's all-reduce.
+Five consecutive decode steps exercise both receive-slot parities and the
+flag epochs.  Cross-rank summation reorders the fp32 sums, so the bar is the
+layer bar, 1e-3; both ranks must hold identical outputs.  Skipped on hosts
+with fewer than two GPUs.
 """
-import os
-
 import numpy as np
 import pytest
 
@@ -16,7 +18,7 @@ pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
 
 FULL = dict(hidden=1024, n_q_heads=8, n_kv_heads=2, head_dim=128, intermediate=2816,
             rope_theta=1e6, rms_eps=1e-6)
-SEED, CTX, PREFIX, NTOK, L = 5, 37, 11, 40, 64
+SEED, CTX, PREFIX, NTOK, L, STEPS, BATCH = 5, 37, 11, 40, 64, 5, 3
 
 
 def _inputs():
@@ -24,28 +26,40 @@ def _inputs():
     kvd = FULL["n_kv_heads"] * FULL["head_dim"]
     k = (rng.standard_normal((L, kvd)) * 0.5).astype(np.float32)
     v = (rng.standard_normal((L, kvd)) * 0.5).astype(np.float32)
-    x = rng.standard_normal(FULL["hidden"]).astype(np.float32)
+    x = rng.standard_normal((STEPS, BATCH, FULL["hidden"])).astype(np.float32)
     X = rng.standard_normal((NTOK, FULL["hidden"])).astype(np.float32)
     return k, v, x, X
 
 
-def _run(ctx, step, dims, k, v, x, X):
-    """Decode at context CTX (history CTX-1) and prefill NTOK tokens after PREFIX."""
-    import sib200
+def _decode(ctx, step, dims, k, v, x):
+    """STEPS decode steps of BATCH sequences from context CTX on."""
     kvd = dims["n_kv_heads"] * dims["head_dim"]
+    kv = ctx.kv(dims, BATCH, L, True)
+    for b in range(BATCH):
+        kv.write(b, 0, np.ascontiguousarray(k[:CTX - 1, :kvd]), np.ascontiguousarray(v[:CTX - 1, :kvd]))
     out = []
-    for kind in ("decode", "prefill"):
-        kv = ctx.kv(dims, 1, L, True)
-        hist = CTX - 1 if kind == "decode" else PREFIX
-        kv.write(0, 0, np.ascontiguousarray(k[:hist, :kvd]), np.ascontiguousarray(v[:hist, :kvd]))
-        xin = torch.from_numpy(x if kind == "decode" else X).cuda()
+    for s in range(STEPS):
+        xin = torch.from_numpy(x[s]).cuda()
         y = torch.zeros_like(xin)
         torch.cuda.synchronize()
-        step(kind, kv, xin, y)
+        step(kv, xin, [CTX + s] * BATCH, y)
         ctx.status()
         out.append(y.cpu().numpy())
-        kv.free()
-    return out
+    kv.free()
+    return np.stack(out)
+
+
+def _prefill(ctx, step, dims, k, v, X):
+    kvd = dims["n_kv_heads"] * dims["head_dim"]
+    kv = ctx.kv(dims, 1, L, True)
+    kv.write(0, 0, np.ascontiguousarray(k[:PREFIX, :kvd]), np.ascontiguousarray(v[:PREFIX, :kvd]))
+    xin = torch.from_numpy(X).cuda()
+    y = torch.zeros_like(xin)
+    torch.cuda.synchronize()
+    step(kv, xin, y)
+    ctx.status()
+    kv.free()
+    return y.cpu().numpy()
 
 
 def _rank(rank, world, uid, path):
@@ -56,29 +70,26 @@ def _rank(rank, world, uid, path):
     d, _ = sib200.tp_local_dims(FULL, rank, world)
     kvd = d["n_kv_heads"] * d["head_dim"]
     sl = slice(rank * kvd, (rank + 1) * kvd)
+    ks, vs = np.ascontiguousarray(k[:, sl]), np.ascontiguousarray(v[:, sl])
     tp = ctx.tp(uid, rank, world)
     layer = ctx.layer_tp_synth(FULL, SEED, rank, world)
-
-    def tp_step(kind, kv, xin, y):
-        if kind == "decode":
-            tp.decode_dev(layer, kv, xin, [CTX], y)
-        else:
-            tp.prefill_dev(layer, kv, 0, xin, NTOK, PREFIX, y)
-
-    got = _run(ctx, tp_step, d, np.ascontiguousarray(k[:, sl]), np.ascontiguousarray(v[:, sl]),
-               x, X)
+    dec = lambda kv, xin, lens, y: tp.decode_dev(layer, kv, xin, lens, y)
+    fused = _decode(ctx, dec, d, ks, vs, x)
+    tp.set_options(fused=False)
+    nccl = _decode(ctx, dec, d, ks, vs, x)
+    tp.set_options(fused=True)
+    pre = _prefill(ctx, lambda kv, xin, y: tp.prefill_dev(layer, kv, 0, xin, NTOK, PREFIX, y), d,
+                   ks, vs, X)
+    np.save(f"{path}.rank{rank}.npy", fused)
     if rank == 0:
         full = ctx.layer_synth(FULL, SEED)
-
-        def one_step(kind, kv, xin, y):
-            if kind == "decode":
-                full.decode_dev(kv, xin, [CTX], y, sib200.SI_LAYER_FULL)
-            else:
-                full.prefill_dev(kv, 0, xin, NTOK, PREFIX, y, sib200.SI_LAYER_FULL)
-
-        want = _run(ctx, one_step, FULL, k, v, x, X)
-        np.save(path, np.concatenate([want[0][None], got[0][None]]))
-        np.save(path + ".prefill.npy", np.stack([want[1], got[1]]))
+        one_dec = _decode(ctx, lambda kv, xin, lens, y: full.decode_dev(kv, xin, lens, y,
+                                                                        sib200.SI_LAYER_FULL),
+                          FULL, k, v, x)
+        one_pre = _prefill(ctx, lambda kv, xin, y: full.prefill_dev(kv, 0, xin, NTOK, PREFIX, y,
+                                                                    sib200.SI_LAYER_FULL),
+                           FULL, k, v, X)
+        np.savez(path, one_dec=one_dec, fused=fused, nccl=nccl, one_pre=one_pre, pre=pre)
         full.free()
     layer.free()
     tp.free()
@@ -91,10 +102,28 @@ def test_tp2_layer_matches_one_gpu(tmp_path):
     import sib200
     import torch.multiprocessing as mp
     uid = sib200.tp_unique_id()
-    path = str(tmp_path / "decode.npy")
+    path = str(tmp_path / "tp")
     mp.spawn(_rank, args=(2, uid, path), nprocs=2, join=True)
-    want, got = np.load(path)
-    assert_layer_close(want, got, 1e-3, "TP=2 decode step")
-    pw, pg = np.load(path + ".prefill.npy")
+    r = np.load(path + ".npz")
+    for s in range(STEPS):
+        for b in range(BATCH):
+            assert_layer_close(r["one_dec"][s, b], r["fused"][s, b], 1e-3, f"fused step {s} seq {b}")
+            assert_layer_close(r["one_dec"][s, b], r["nccl"][s, b], 1e-3, f"NCCL step {s} seq {b}")
+    # every rank sums the slots in the same order: identical hidden states
+    np.testing.assert_array_equal(np.load(path + ".rank0.npy"), np.load(path + ".rank1.npy"))
     for t in range(NTOK):
-        assert_layer_close(pw[t], pg[t], 1e-3, f"TP=2 prefill token {t}")
+        assert_layer_close(r["one_pre"][t], r["pre"][t], 1e-3, f"TP=2 prefill token {t}")
+
+
+def test_fused_reduction_wait_times_out(si_ctx):
+    """The fused reduction's wait for other ranks is bounded: against a flag
+    that nothing sets it returns SI_ERR_TIMEOUT, and the context stays usable."""
+    import sib200
+    assert si_ctx.tp_probe_wait(20000) == sib200.SI_ERR_TIMEOUT
+    si_ctx.status()
+    x = torch.randn(64, device="cuda")
+    qs = torch.zeros(64, dtype=torch.int8, device="cuda")
+    d = torch.zeros(2, dtype=torch.int16, device="cuda")
+    torch.cuda.synchronize()
+    si_ctx.q8_quantize(x, 1, 64, qs, d)
+    si_ctx.status()
