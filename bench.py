@@ -580,6 +580,30 @@ def run_reference(args, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def probe_config4_layer():
+    """One Qwen2.5-72B layer on GPU 0 (TP = 1): three decode steps of a batch
+    of 8 at context 4097.. and one 4096-token prefill, no timing -- the
+    workload the config-4 ncu summaries capture."""
+    import torch
+    import sib200
+    torch.cuda.set_device(0)
+    ctx = sib200.Context(0, max_positions=TP_MAX_CTX, rope_theta=1e6, head_dim=128)
+    layer = ctx.layer_synth(CONFIG4, 4)
+    kv = ctx.kv(CONFIG4, TP_BATCH, TP_MAX_CTX, True)
+    kv.fill_synth(4, 1.0, TP_PREFILL)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(TP_BATCH, CONFIG4["hidden"], device="cuda", generator=g)
+    xp = torch.randn(TP_PREFILL, CONFIG4["hidden"], device="cuda", generator=g)
+    y, yp = torch.empty_like(x), torch.empty_like(xp)
+    torch.cuda.synchronize()
+    for i in range(3):
+        layer.decode_dev(kv, x, [TP_PREFILL + 1 + i] * TP_BATCH, y, sib200.SI_LAYER_FULL)
+    layer.prefill_dev(kv, 0, xp, TP_PREFILL, 0, yp, sib200.SI_LAYER_FULL)
+    ctx.sync()
+    ctx.status()
+    print("ok")
+
+
 def log(msg):
     if os.environ.get("SI_BENCH_VERBOSE"):
         print(f"[bench] {msg}", file=sys.stderr, flush=True)
@@ -596,8 +620,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="skip the config-4 tensor-parallel stack")
+    ap.add_argument("--probe", choices=["config4-layer"],
+                    help="run one untimed workload for a profiler and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.probe == "config4-layer":
+        probe_config4_layer()
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

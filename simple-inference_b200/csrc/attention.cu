@@ -254,16 +254,28 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
       if (g < G) ml_s[warp * kMaxGroup + g] = make_float2(m[g], l[g]);
   __syncthreads();
   const int nsub = (L - split * kSplitKeys + kSub - 1) / kSub;  // valid sub-tiles, >= 1
+  // The merge factors depend on the head only: one thread per head runs the
+  // (max, sum) chain once; every output element then applies them.
+  float2 *fab = reinterpret_cast<float2 *>(q_s);  // [G][4] (the queries are no longer read)
+  __shared__ float2 mls[kMaxGroup];
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float M = ml_s[g].x, Ls = ml_s[g].y;
+    for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
+      float fa, fb;
+      merge_ml(M, Ls, ml_s[w * kMaxGroup + g].x, ml_s[w * kMaxGroup + g].y, fa, fb);
+      fab[g * kSubPerSplit + w] = make_float2(fa, fb);
+    }
+    mls[g] = make_float2(M, Ls);
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int g = idx / D, d = idx % D;
-    float2 ml = ml_s[g];
-    float M = ml.x, Ls = ml.y;
+    const float M = mls[g].x, Ls = mls[g].y;
     float O = reinterpret_cast<const float *>(smem + S::Q)[g * D + d];
     for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
-      ml = ml_s[w * kMaxGroup + g];
-      float fa, fb;
-      merge_ml(M, Ls, ml.x, ml.y, fa, fb);
-      O = merge_o(O, fa, reinterpret_cast<const float *>(smem + S::Q + w * S::KW)[g * D + d], fb);
+      const float2 f = fab[g * kSubPerSplit + w];
+      O = merge_o(O, f.x, reinterpret_cast<const float *>(smem + S::Q + w * S::KW)[g * D + d], f.y);
     }
     const int h = kvh * G + g;
     if (a.nsplit == 1) {  // no combine pass follows
@@ -283,31 +295,33 @@ __global__ void k_attn_combine(const AttnArgs a) {
   const int D = a.head_dim;
   const int S = splits_for(ctx_of(a, t));
   const float *p = a.part + ((size_t)t * a.n_q_heads + h) * a.nsplit * (D + 2);
-  float M = p[0], Ls = p[1], O = p[2 + d];
+  // Merge factors per split: one (max, sum) chain, run by thread 0 with the
+  // splits' pairs loaded into shared memory first; every d then applies them.
+  extern __shared__ float2 fs[];  // [S]: (m, l), then (a, b); [S] = final (M, L)
+  for (int s = d; s < S; s += blockDim.x)
+    fs[s] = make_float2(p[(size_t)s * (D + 2)], p[(size_t)s * (D + 2) + 1]);
+  __syncthreads();
+  if (d == 0) {
+    float M = fs[0].x, Ls = fs[0].y;
+    for (int s = 1; s < S; ++s) {
+      float fa, fb;
+      merge_ml(M, Ls, fs[s].x, fs[s].y, fa, fb);
+      fs[s] = make_float2(fa, fb);
+    }
+    fs[S] = make_float2(M, Ls);
+  }
+  __syncthreads();
+  float O = p[2 + d];
   int s = 1;
   for (; s + 8 <= S; s += 8) {  // eight splits' loads in flight, merged in order
-    float mm[8], ll[8], oo[8];
+    float oo[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float *ps = p + (size_t)(s + j) * (D + 2);
-      mm[j] = ps[0];
-      ll[j] = ps[1];
-      oo[j] = ps[2 + d];
-    }
+    for (int j = 0; j < 8; ++j) oo[j] = p[(size_t)(s + j) * (D + 2) + 2 + d];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float fa, fb;
-      merge_ml(M, Ls, mm[j], ll[j], fa, fb);
-      O = merge_o(O, fa, oo[j], fb);
-    }
+    for (int j = 0; j < 8; ++j) O = merge_o(O, fs[s + j].x, oo[j], fs[s + j].y);
   }
-  for (; s < S; ++s) {
-    const float *ps = p + (size_t)s * (D + 2);
-    float fa, fb;
-    merge_ml(M, Ls, ps[0], ps[1], fa, fb);
-    O = merge_o(O, fa, ps[2 + d], fb);
-  }
-  a.out[((size_t)t * a.n_q_heads + h) * D + d] = __fdiv_rn(O, Ls);
+  for (; s < S; ++s) O = merge_o(O, fs[s].x, p[(size_t)s * (D + 2) + 2 + d], fs[s].y);
+  a.out[((size_t)t * a.n_q_heads + h) * D + d] = __fdiv_rn(O, fs[S].y);
 }
 
 // ---------------------------------------------------------------------------
@@ -579,7 +593,8 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
   e = launch_pdl(k_attn_dec<D, F32>, dim3(a.nsplit, a.n_kv_heads, a.T),
                  dim3(kSubPerSplit * 32), Sd::bytes(), s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
-  return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D), 0, s, a);
+  return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D),
+                    (size_t)(a.nsplit + 1) * sizeof(float2), s, a);
 }
 }  // namespace
 

@@ -1,0 +1,370 @@
+// gemm_mma.cu -- Q4_0 x Q8_0 projection for many tokens (prefill, batched
+// decode) on the tensor cores through mma.sync, with the reference's exact
+// per-block rescale in registers.
+//
+// Reference: matvec_q4q8 (qwen_one_layer.c:148-162) per token: out[n] = bias[n]
+// followed, block by block IN ORDER, by out[n] += ((float)isum * dw) * dx.
+//
+// Mapping.  A CTA owns 128 weight rows (four 32-row tiles; for SwiGLU the
+// gate and the up rows of two tiles) x 128 tokens and the whole K range.
+// Sixteen compute warps: warp w takes 16 rows (row group w % 8) x 64 tokens
+// (half w / 8).  Per K block (32 = one Q4_0 block) a warp issues eight mma.sync
+// m16n8k32 s8 x s8 -> s32 with the weight rows as M (lane (g, c) holds nibble
+// word c of rows g and g+8: low nibbles are elements 4c..4c+3, high nibbles
+// 16+4c..16+4c+3, exactly the A fragment) and eight tokens per mma as N; each
+// returns the block's exact 16*isum for 16 rows x 8 tokens.  The terms are
+// formed and added at once, block by block, so every output is the
+// reference's serial chain and bit-identical to the GEMV and to matvec_q4q8:
+//   f = float(0x4B400000 + 16*isum) = 1.5*2^23 + 16*isum (exact),
+//   fma(f, dw/16, -1.5*2^23*dw/16) = round(isum*dw) (both addends exact),
+//   * dx (packed .rn multiply), then one scalar add per output.
+// A producer warp streams 8-block chunks through a three-stage ring with one
+// mbarrier per stage (2-D TMA loads: the four row tiles' nibbles and scales,
+// the activations as two 128-byte-swizzled boxes -- the B-fragment loads of
+// eight tokens then hit 32 distinct banks -- and the fp32 activation scales,
+// transposed to [block][token] by a small kernel first); the compute warps
+// release a stage through an empty barrier.  Only the nibble unpack, one
+// mma per 16x8x32 and ~12 fp32/int operations per 4 outputs run per block.
+#include <type_traits>
+
+#include "si_common.cuh"
+#include "si_kernels.cuh"
+#include "si_tma.cuh"
+
+namespace si {
+
+namespace {
+constexpr int kGmTok = 128, kGmCB = 8, kGmStages = 3;
+constexpr int kGmTiles = 4;  // 32-row tiles per CTA (SwiGLU: two gate + two up)
+constexpr int kGmCompute = 16, kGmThreads = (kGmCompute + 1) * 32;
+// Stage layout (bytes): activations 2 x [128 tokens][128 B] swizzled, nibbles
+// 4 x [8 blocks][32 rows][16 B], weight scales 4 x [8][32] fp16, activation
+// scales [8 blocks][128 tokens] fp32.
+constexpr int kGmAct = kGmTok * 128, kGmNib = kGmCB * 512, kGmScl = kGmCB * 64;
+constexpr int kGmDx = kGmCB * kGmTok * 4;
+constexpr int kGmOffNib = 2 * kGmAct, kGmOffScl = kGmOffNib + kGmTiles * kGmNib;
+constexpr int kGmOffDx = kGmOffScl + kGmTiles * kGmScl;
+constexpr int kGmStage = kGmOffDx + kGmDx;
+constexpr int kGmTx = kGmStage;
+constexpr size_t kGmSmem = (size_t)kGmStages * kGmStage + 256 + 1024;
+static_assert(kGmStage % 1024 == 0, "swizzled boxes need 1024-byte alignment");
+static_assert((size_t)kGmStages * kGmStage + 256 + 1024 <= 227 * 1024, "shared memory");
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// Packed .rn arithmetic: each half is one IEEE operation with its own
+// rounding, and explicit instructions are never contracted.
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kGmThreads, 1)
+    k_gemm_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
+               const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
+               const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmD,
+               const GemvArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGmStages * kGmStage);
+  uint64_t *empty = full + kGmStages;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kGmStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int m0 = blockIdx.x * kGmTok;
+  // Row tiles of this CTA: SwiGLU -> gate tiles rt0, rt0+1 and the same up
+  // tiles; else four consecutive tiles.
+  const int rt0 = (SWIGLU ? 2 : kGmTiles) * blockIdx.y;
+  const int KB = a.K / 32, nchunks = (KB + kGmCB - 1) / kGmCB;
+  auto fb = [&](int i) { return smem_u32(full + i); };
+  auto eb = [&](int i) { return smem_u32(empty + i); };
+
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGmStages; ++i) {
+      mbar_init(fb(i), 1);
+      mbar_init(eb(i), kGmCompute);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == kGmCompute) {
+    // ---- producer ----------------------------------------------------------
+    if (lane == 0) {
+      auto weights = [&](int ci) {
+        const int slot = ci % kGmStages;
+        uint8_t *st = smem + slot * kGmStage;
+        mbar_expect_tx(fb(slot), kGmTx);
+#pragma unroll
+        for (int t = 0; t < kGmTiles; ++t) {
+          // SwiGLU: slots 0, 1 gate tiles rt0, rt0+1; slots 2, 3 the up tiles.
+          const bool up = SWIGLU && t >= 2;
+          const int y = (rt0 + (SWIGLU ? (t & 1) : t)) * KB + ci * kGmCB;
+          tma_load_2d(smem_u32(st + kGmOffNib + t * kGmNib), up ? &tmN2 : &tmN, 0, y, fb(slot));
+          tma_load_2d(smem_u32(st + kGmOffScl + t * kGmScl), up ? &tmS2 : &tmS, 0, y, fb(slot));
+        }
+      };
+      auto acts = [&](int ci) {
+        const int slot = ci % kGmStages;
+        uint8_t *st = smem + slot * kGmStage;
+        tma_load_2d(smem_u32(st), &tmX, ci * kGmCB * 4, m0, fb(slot));
+        tma_load_2d(smem_u32(st + kGmAct), &tmX, ci * kGmCB * 4 + 16, m0, fb(slot));
+        tma_load_2d(smem_u32(st + kGmOffDx), &tmD, m0, ci * kGmCB, fb(slot));
+      };
+      const int pre = nchunks < kGmStages ? nchunks : kGmStages;
+      for (int ci = 0; ci < pre; ++ci) weights(ci);
+      pdl_wait();
+      for (int ci = 0; ci < pre; ++ci) acts(ci);
+      for (int ci = pre; ci < nchunks; ++ci) {
+        if (!mbar_wait(eb(ci % kGmStages), ((ci / kGmStages) - 1) & 1, abort_flag)) {
+          *abort_flag = 1;
+          break;
+        }
+        weights(ci);
+        acts(ci);
+      }
+    }
+    return;
+  }
+
+  // ---- compute warps -------------------------------------------------------
+  pdl_wait();
+  const int rg = warp & 7, th = warp >> 3;   // 16-row group, 64-token half
+  const int tsel = rg >> 1, hrow = (rg & 1) * 16;  // tile slot (0..3) and row offset in it
+  const int tok0 = th * 64;                  // first token of this warp within the CTA
+  // Output row of this lane's accumulators (h = 0: row g, h = 1: row g + 8).
+  const int row = (rt0 + (SWIGLU ? (tsel & 1) : tsel)) * SI_RT + hrow + g;
+  float acc[8][2][2];  // [n-tile][row half][token of the pair]
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float b = (!SWIGLU && a.bias) ? a.bias[row + 8 * h] : 0.0f;
+      acc[j][h][0] = b;
+      acc[j][h][1] = b;
+    }
+  const float kMagic = 12582912.0f;  // 1.5 * 2^23
+  bool ok = true;
+  for (int ci = 0; ci < nchunks; ++ci) {
+    const int slot = ci % kGmStages;
+    ok = ok && mbar_wait(fb(slot), (ci / kGmStages) & 1, abort_flag);
+    if (ok) {
+      const uint8_t *st = smem + slot * kGmStage;
+      const uint8_t *nib = st + kGmOffNib + tsel * kGmNib;
+      const uint16_t *scl = reinterpret_cast<const uint16_t *>(st + kGmOffScl + tsel * kGmScl);
+      const float *dxs = reinterpret_cast<const float *>(st + kGmOffDx);
+      const int nb = min(kGmCB, KB - ci * kGmCB);
+#pragma unroll 1
+      for (int bl = 0; bl < nb; ++bl) {
+        const uint8_t *wr = nib + bl * 512 + (hrow + g) * 16 + 4 * c;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wr);
+        const uint32_t w8 = *reinterpret_cast<const uint32_t *>(wr + 8 * 16);
+        const uint32_t a0 = (uint32_t)lo_nib_s8x16(w0), a2 = (uint32_t)hi_nib_s8x16(w0);
+        const uint32_t a1 = (uint32_t)lo_nib_s8x16(w8), a3 = (uint32_t)hi_nib_s8x16(w8);
+        // dw/16 of rows g and g+8 and the exact -1.5*2^23*dw/16.
+        const float dw0 = __fmul_rn(f16_to_f32(scl[bl * 32 + hrow + g]), 0.0625f);
+        const float dw1 = __fmul_rn(f16_to_f32(scl[bl * 32 + hrow + g + 8]), 0.0625f);
+        const float2 dwa = make_float2(dw0, dw0), dwb = make_float2(dw1, dw1);
+        const float2 nca = make_float2(-kMagic * dw0, -kMagic * dw0);
+        const float2 ncb = make_float2(-kMagic * dw1, -kMagic * dw1);
+        // Activation rows: token t's block bl is 32 bytes in box bl / 4, its two
+        // 16-byte chunks 2*(bl % 4) and +1 swizzled by t & 7 (== g here).
+        const uint8_t *abox = st + (bl >> 2) * kGmAct;
+        const int ch0 = ((2 * (bl & 3)) ^ g) << 4, ch1 = ((2 * (bl & 3) + 1) ^ g) << 4;
+#pragma unroll
+        for (int j0 = 0; j0 < 8; j0 += 4) {  // four n-tiles' mmas in flight, then their terms
+        int d[4][4];
+#pragma unroll
+        for (int j = j0; j < j0 + 4; ++j) {
+          const uint8_t *ar = abox + (tok0 + 8 * j + g) * 128;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t *>(ar + ch0 + 4 * c);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t *>(ar + ch1 + 4 * c);
+          mma_s8(d[j - j0], a0, a1, a2, a3, b0, b1);
+        }
+#pragma unroll
+        for (int j = j0; j < j0 + 4; ++j) {
+          const float2 dx = *reinterpret_cast<const float2 *>(dxs + bl * kGmTok + tok0 + 8 * j + 2 * c);
+          const int *dj = d[j - j0];
+          const float2 fa = make_float2(__int_as_float(0x4B400000 + dj[0]),
+                                        __int_as_float(0x4B400000 + dj[1]));
+          const float2 fbv = make_float2(__int_as_float(0x4B400000 + dj[2]),
+                                         __int_as_float(0x4B400000 + dj[3]));
+          const float2 ta = mul2_rn(fma2_rn(fa, dwa, nca), dx);
+          const float2 tb = mul2_rn(fma2_rn(fbv, dwb, ncb), dx);
+          acc[j][0][0] = __fadd_rn(acc[j][0][0], ta.x);
+          acc[j][0][1] = __fadd_rn(acc[j][0][1], ta.y);
+          acc[j][1][0] = __fadd_rn(acc[j][1][0], tb.x);
+          acc[j][1][1] = __fadd_rn(acc[j][1][1], tb.y);
+        }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(eb(slot));
+  }
+  if (!ok || *abort_flag) {
+    if (lane == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+    return;
+  }
+
+  const int mcount = min(kGmTok, a.M - m0);
+  if (!SWIGLU) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tl = tok0 + 8 * j + 2 * c + e;
+        if (tl >= mcount) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const size_t o = (size_t)(m0 + tl) * a.N + row + 8 * h;
+          float v = acc[j][h][e];
+          if (a.resid) v = __fadd_rn(a.resid[o], v);
+          a.out[o] = v;
+        }
+      }
+    return;
+  }
+  // SwiGLU: the gate warps (row groups 0-3) hand their sums to the up warps
+  // (4-7, the same rows) through shared memory (the ring is idle now: every
+  // stage has been consumed by every warp once this barrier passes).
+  constexpr int kBar = 1, kBarN = kGmCompute * 32;
+  asm volatile("bar.sync %0, %1;" ::"r"(kBar), "r"(kBarN) : "memory");
+  float *gs = reinterpret_cast<float *>(smem);                      // [64 rows][128 tokens]
+  unsigned *red = reinterpret_cast<unsigned *>(gs + 64 * kGmTok);   // [2 tiles][2 halves][128]
+  const int rl = (rg & 3) * 16 + g;  // row within the CTA's 64 gate (or up) rows
+  if (rg < 4) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          gs[(rl + 8 * h) * kGmTok + tok0 + 8 * j + 2 * c + e] = acc[j][h][e];
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(kBar), "r"(kBarN) : "memory");
+  float act[8][2][2];
+  if (rg >= 4) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        unsigned m = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float gv = gs[(rl + 8 * h) * kGmTok + tok0 + 8 * j + 2 * c + e];
+          act[j][h][e] = silu_mul(gv, acc[j][h][e]);
+          m = max(m, __float_as_uint(fabsf(act[j][h][e])));
+        }
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (g == 0) red[(rg - 4) * kGmTok + tok0 + 8 * j + 2 * c + e] = m;
+      }
+  }
+  asm volatile("bar.sync %0, %1;" ::"r"(kBar), "r"(kBarN) : "memory");
+  if (rg < 4) return;
+  const int pt = (rg - 4) >> 1;        // which of the two tiles
+  const int tile = rt0 + pt;
+  const int rt = hrow + g;             // row within that tile
+  const unsigned *rp = red + pt * 2 * kGmTok;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int tl = tok0 + 8 * j + 2 * c + e;
+      if (tl >= mcount) continue;
+      const unsigned mb = max(rp[tl], rp[kGmTok + tl]);
+      const float dq = __fdiv_rn(__uint_as_float(mb), 127.0f);
+      const float inv = dq == 0.0f ? 0.0f : __fdiv_rn(1.0f, dq);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const size_t o = (size_t)(m0 + tl) * a.N + tile * SI_RT + rt + 8 * h;
+        if (a.out) a.out[o] = act[j][h][e];
+        int q = __float2int_rn(__fmul_rn(act[j][h][e], inv));
+        q = q > 127 ? 127 : (q < -127 ? -127 : q);
+        a.act_qs[o] = (int8_t)q;
+      }
+      if ((rg & 1) == 0 && g == 0) a.act_d[(size_t)(m0 + tl) * (a.N / 32) + tile] = f32_to_f16(dq);
+    }
+}
+}  // namespace
+
+bool gemm_mma_supported(int N, int K, int M, bool swiglu) {
+  return M >= 1 && K % 32 == 0 && (swiglu ? N % 64 == 0 : N % 128 == 0) &&
+         tma_encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_mma(const GemvArgs &a, bool swiglu, cudaStream_t s) {
+  if (a.M <= 0) return cudaSuccess;
+  if (!gemm_mma_supported(a.N, a.K, a.M, swiglu) || !a.scratch) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.xq) | reinterpret_cast<uintptr_t>(a.nib) |
+       reinterpret_cast<uintptr_t>(a.scratch) | reinterpret_cast<uintptr_t>(a.scl)) & 15)
+    return cudaErrorInvalidValue;
+  if (swiglu && ((reinterpret_cast<uintptr_t>(a.nib2) | reinterpret_cast<uintptr_t>(a.scl2)) & 15))
+    return cudaErrorInvalidValue;
+  const int KB = a.K / 32, Mp = (a.M + 3) & ~3, tiles = a.N / SI_RT;
+  cudaError_t e = launch_scales_t(a.xd, a.M, KB, a.scratch, s);
+  if (e != cudaSuccess) return e;
+  CUtensorMap tmN, tmN2, tmS, tmS2, tmX, tmD;
+  const cuuint64_t dN[2] = {64, (cuuint64_t)tiles * KB}, sN[1] = {512};
+  const cuuint32_t bN[2] = {64, (cuuint32_t)kGmCB};
+  const cuuint64_t dS[2] = {32, (cuuint64_t)tiles * KB}, sS[1] = {64};
+  const cuuint32_t bS[2] = {32, (cuuint32_t)kGmCB};
+  const cuuint64_t dX[2] = {(cuuint64_t)a.K / 8, (cuuint64_t)a.M}, sX[1] = {(cuuint64_t)a.K};
+  const cuuint32_t bX[2] = {16, (cuuint32_t)kGmTok};
+  const cuuint64_t dD[2] = {(cuuint64_t)Mp, (cuuint64_t)KB}, sD[1] = {(cuuint64_t)Mp * 4};
+  const cuuint32_t bD[2] = {(cuuint32_t)kGmTok, (cuuint32_t)kGmCB};
+  if (!tma_encode(&tmN, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dN, sN, bN,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl, dS, sS, bS,
+                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !tma_encode(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.xq, dX, sX, bX,
+                  CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tma_encode(&tmD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.scratch, dD, sD, bD,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  if (swiglu) {
+    if (!tma_encode(&tmN2, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib2, dN, sN, bN,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !tma_encode(&tmS2, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.scl2, dS, sS, bS,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  } else {
+    tmN2 = tmN;
+    tmS2 = tmS;
+  }
+  auto kern = swiglu ? k_gemm_mma<true> : k_gemm_mma<false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGmSmem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((a.M + kGmTok - 1) / kGmTok, swiglu ? tiles / 2 : tiles / kGmTiles);
+  return launch_pdl(kern, grid, dim3(kGmThreads), kGmSmem, s, tmN, tmN2, tmS, tmS2, tmX, tmD, a);
+}
+
+}  // namespace si

@@ -611,6 +611,11 @@ __global__ void k_scales_t(const uint16_t *__restrict__ xd, int M, int KB, int M
 // ---------------------------------------------------------------------------
 }  // namespace tc
 
+cudaError_t launch_scales_t(const uint16_t *xd, int M, int KB, float *dT, cudaStream_t s) {
+  const int Mp = (M + 3) & ~3;
+  return launch_pdl(tc::k_scales_t, dim3((Mp + 127) / 128, KB), dim3(128), 0, s, xd, M, KB, Mp, dT);
+}
+
 bool gemm_tc_supported(int N, int K, int M) {
   return M >= 1 && K % 128 == 0 && N % 128 == 0 && tma_encode_fn() != nullptr;
 }

@@ -500,18 +500,14 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
   return a;
 }
 
-// Kernel choice by token count.  The tcgen05 GEMM keeps each output's
-// block-ordered sum inside one CTA, so a 128-row tile costs K/32 pipelined
-// block steps whatever M is, and few tiles leave SMs idle; the GEMV computes
-// the per-block terms in parallel and then runs a short serial add chain, but
-// re-reads the weights once per 8 tokens.  Measured on B200 at the 1.5B
-// shapes: the GEMM is faster from 128 tokens on, or earlier once it has at
-// least 64 tiles (the gate/up pair at 32 tokens).
-static bool prefer_gemm(int row_tiles, int M) {
-  if (M <= 8) return false;
-  const int tiles = row_tiles * ((M + 127) / 128);
-  return M >= 128 || tiles >= 64;
-}
+// Kernel choice for M tokens (measured on B200 at the 1.5B/7B/72B shapes):
+// the GEMV streams the weights once per 16 tokens, the GEMM keeps every
+// output's block-ordered sum in one warp and tiles 128 rows x 128 tokens.
+// The SwiGLU pair (two matrices, the Q8 epilogue) favours the GEMM from 64
+// tokens on, single matrices from 256.  The mma.sync GEMM outruns the tcgen05
+// one at every measured shape (its rescale runs straight from registers), so
+// it is the default where its shape rules allow.
+static bool prefer_gemm(bool swiglu, int M) { return M >= (swiglu ? 64 : 256); }
 
 static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
                         int M, const float *bias, const float *resid, float *out, int kernel) {
@@ -522,9 +518,20 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
   a.resid = resid;
   a.out = out;
   if (kernel < 0)
-    kernel = (prefer_gemm(w->rows / 128, M) && si::gemm_tc_supported(w->rows, w->cols, M)) ? 1 : 0;
+    kernel = !prefer_gemm(false, M) ? 0
+             : si::gemm_mma_supported(w->rows, w->cols, M, false) ? 4
+             : si::gemm_tc_supported(w->rows, w->cols, M) ? 1 : 0;
   if (kernel == 2) a.variant = si::kGemvMma;
   if (kernel == 3) a.variant = si::kGemvDp4a;
+  if (kernel == 4) {
+    if (!si::gemm_mma_supported(w->rows, w->cols, M, false))
+      return fail(SI_ERR_UNSUPPORTED, "mma GEMM does not support %dx%d at M=%d", w->rows,
+                  w->cols, M);
+    SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(w->cols, M)));
+    a.scratch = static_cast<float *>(ctx->gemm.p);
+    SI_CUDA(si::launch_gemm_mma(a, false, ctx->stream));
+    return SI_OK;
+  }
   if (kernel == 1) {
     if (!si::gemm_tc_supported(w->rows, w->cols, M))
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
@@ -549,8 +556,9 @@ extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w
                                                  const int8_t *qs, const uint16_t *d, int M,
                                                  const float *bias, float *out, int kernel) {
   SI_TRY(set_device(ctx));
-  SI_CHECK(kernel >= 0 && kernel <= 3,
-           "kernel must be 0 (GEMV), 1 (tcgen05 GEMM), 2 (GEMV, mma form) or 3 (GEMV, dp4a form)");
+  SI_CHECK(kernel >= 0 && kernel <= 4,
+           "kernel must be 0 (GEMV), 1 (tcgen05 GEMM), 2 (GEMV, mma form), 3 (GEMV, dp4a form) "
+           "or 4 (mma GEMM)");
   return matmul(ctx, w, qs, d, M, bias, nullptr, out, kernel);
 }
 
@@ -651,7 +659,7 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
                                                     const uint16_t *d, int M, int8_t *act_qs,
                                                     uint16_t *act_d, float *act_f32, int kernel) {
   SI_TRY(set_device(ctx));
-  SI_CHECK(kernel >= -1 && kernel <= 3, "bad kernel selector %d", kernel);
+  SI_CHECK(kernel >= -1 && kernel <= 4, "bad kernel selector %d", kernel);
   SI_CHECK(gate && up && qs && d && act_qs && act_d, "null pointer");
   SI_CHECK(gate->rows == up->rows && gate->cols == up->cols, "gate/up shape mismatch");
   si::GemvArgs a = gemv_args(gate, qs, d, M);
@@ -661,9 +669,21 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
   a.act_qs = act_qs;
   a.act_d = act_d;
   const bool gemm_ok = si::gemm_tc_supported(2 * gate->rows, gate->cols, M) && gate->rows % 64 == 0;
-  if (kernel < 0) kernel = prefer_gemm(gate->rows / 64, M) && gemm_ok ? 1 : 0;
+  if (kernel < 0)
+    kernel = !prefer_gemm(true, M) ? 0
+             : si::gemm_mma_supported(gate->rows, gate->cols, M, true) ? 4
+             : gemm_ok ? 1 : 0;
   if (kernel == 2) a.variant = si::kGemvMma;
   if (kernel == 3) a.variant = si::kGemvDp4a;
+  if (kernel == 4) {
+    if (!si::gemm_mma_supported(gate->rows, gate->cols, M, true))
+      return fail(SI_ERR_UNSUPPORTED, "mma GEMM does not support gate/up %dx%d at M=%d",
+                  gate->rows, gate->cols, M);
+    SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(gate->cols, M)));
+    a.scratch = static_cast<float *>(ctx->gemm.p);
+    SI_CUDA(si::launch_gemm_mma(a, true, ctx->stream));
+    return SI_OK;
+  }
   if (kernel == 1) {
     if (!gemm_ok)
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support gate/up %dx%d at M=%d",

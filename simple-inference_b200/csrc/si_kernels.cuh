@@ -103,6 +103,13 @@ cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
 // ---- gemm_tc.cu (tcgen05) ------------------------------------------------------
 cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s);
 bool gemm_tc_supported(int N, int K, int M);
+// Activation scales fp16 [M][KB] -> fp32 [KB][round_up(M, 4)] (zero padded).
+cudaError_t launch_scales_t(const uint16_t *xd, int M, int KB, float *dT, cudaStream_t s);
+
+// ---- gemm_mma.cu (mma.sync, many tokens) ----------------------------------------
+// Same results and scratch as the tcgen05 GEMM; N % 128 (SwiGLU: % 64), K % 32.
+cudaError_t launch_gemm_mma(const GemvArgs &a, bool swiglu, cudaStream_t s);
+bool gemm_mma_supported(int N, int K, int M, bool swiglu);
 // Scratch the GEMM needs for its transposed fp32 activation scales.
 size_t gemm_tc_scratch_bytes(int K, int M);
 

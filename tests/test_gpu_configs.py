@@ -1,8 +1,8 @@
 """Parity at the full sizes of the BASELINE configurations, through properties
 that do not depend on size plus oracle checks on sampled tokens.
 
-* config 1 (1.5B projection sweep, M in {1, 16, 128, 512, 2048}): the tcgen05
-  GEMM equals the in-order GEMV element for element at M = 16, 128, 512
+* config 1 (1.5B projection sweep, M in {1, 16, 128, 512, 2048}): both GEMMs
+  (tcgen05, mma.sync) equal the in-order GEMV element for element at M = 16, 128, 512
   (M = 2048 is in test_gpu_gemm.py, M = 1 is the GEMV itself).
 * config 2 (7B layer, 2048-token prefill, then decode): the prefill equals 2048
   sequential decode steps (the reference's prefill oracle,
@@ -11,7 +11,7 @@ that do not depend on size plus oracle checks on sampled tokens.
   attention splits depend only on its own context length; the decode steps
   after it match the oracle's decoder layer.
 * config 3 (7B, batch 64, fp32 KV of 4096 positions): the batched decode step
-  (tcgen05 GEMM projections) equals single-sequence decode steps (GEMV) bit
+  (GEMM gate/up projection) equals single-sequence decode steps (GEMV) bit
   for bit, and matches the oracle's decoder layer on sampled sequences.
 """
 import numpy as np
@@ -33,17 +33,18 @@ def z(n, dt=torch.float32):
     return t
 
 
+@pytest.mark.parametrize("kernel", [1, 4], ids=["tcgen05", "mma"])
 @pytest.mark.parametrize("M", [16, 128, 512])
 @pytest.mark.parametrize("name,N,K", [("qkv", 2048, 1536), ("o", 1536, 1536),
                                       ("gate", 8960, 1536), ("down", 1536, 8960)])
-def test_config1_sweep_gemm_equals_gemv(si_ctx, name, N, K, M):
+def test_config1_sweep_gemm_equals_gemv(si_ctx, name, N, K, M, kernel):
     m = si_ctx.matrix_synth(N, K, seed=1000 + N + K)
     x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
     torch.cuda.synchronize()
     qs, d = z(M * K, torch.int8), z(M * K // 32, torch.int16)
     si_ctx.q8_quantize(x, M, K, qs, d)
     a, b = z(M * N), z(M * N)
-    si_ctx.matmul(m, qs, d, M, None, a, kernel=1)
+    si_ctx.matmul(m, qs, d, M, None, a, kernel=kernel)
     si_ctx.matmul(m, qs, d, M, None, b, kernel=0)
     si_ctx.status()
     assert torch.isfinite(a).all() and torch.equal(a, b)

@@ -1,4 +1,5 @@
-"""GPU parity of the tcgen05 Q4_0 x Q8_0 GEMM (prefill / batched decode path).
+"""GPU parity of the Q4_0 x Q8_0 GEMMs (prefill / batched decode path): the
+tcgen05 kernel (kernel=1) and the mma.sync kernel (kernel=4).
 
 The kernel keeps the reference's per-block order (bias, then
 out += ((float)isum*dw)*dx for b = 0..KB-1), so its outputs are compared
@@ -36,9 +37,13 @@ def q8_dev(ctx, x):
     return qs, d, blk.cpu().numpy().reshape(M, -1)
 
 
+@pytest.mark.parametrize("kernel", [1, 4], ids=["tcgen05", "mma"])
 @pytest.mark.parametrize("N,K,M", [(128, 128, 1), (256, 1536, 16), (2048, 1536, 130),
-                                   (128, 8960, 64), (1536, 3584, 257), (896, 4864, 9)])
-def test_gemm_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
+                                   (128, 8960, 64), (1536, 3584, 257), (896, 4864, 9),
+                                   (384, 896, 300)])
+def test_gemm_bit_exact_vs_oracle(si_ctx, oc, N, K, M, kernel):
+    if kernel == 1 and (N % 128 or K % 128):
+        pytest.skip("tcgen05 GEMM needs rows and cols % 128")
     rng = np.random.default_rng(N * 7 + K + M)
     w = synth.random_q4(rng, N, K)
     x = rng.standard_normal((M, K)).astype(np.float32)
@@ -46,7 +51,7 @@ def test_gemm_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
     m = si_ctx.matrix(w, N, K)
     qs, d, blocks = q8_dev(si_ctx, x)
     out = z(M * N, torch.float32)
-    si_ctx.matmul(m, qs, d, M, dev(bias), out, kernel=1)
+    si_ctx.matmul(m, qs, d, M, dev(bias), out, kernel=kernel)
     si_ctx.status()
     got = out.cpu().numpy().reshape(M, N)
     for t in sorted({0, M // 2, M - 1}):
@@ -57,10 +62,11 @@ def test_gemm_bit_exact_vs_oracle(si_ctx, oc, N, K, M):
     np.testing.assert_array_equal(got, ref.cpu().numpy().reshape(M, N))
 
 
+@pytest.mark.parametrize("kernel", [1, 4], ids=["tcgen05", "mma"])
 @pytest.mark.parametrize("name,N,K", [("qkv", 2048, 1536), ("o", 1536, 1536),
                                       ("gate", 8960, 1536), ("down", 1536, 8960)])
-def test_gemm_config1_full_size_equals_gemv(si_ctx, name, N, K):
-    """Config-1 shapes at M = 2048: tcgen05 GEMM == in-order GEMV, every element."""
+def test_gemm_config1_full_size_equals_gemv(si_ctx, name, N, K, kernel):
+    """Config-1 shapes at M = 2048: GEMM == in-order GEMV, every element."""
     M = 2048
     m = si_ctx.matrix_synth(N, K, seed=hash(name) & 0xFFFF)
     x = torch.randn(M, K, device="cuda")
@@ -68,15 +74,16 @@ def test_gemm_config1_full_size_equals_gemv(si_ctx, name, N, K):
     qs, d = z(M * K, torch.int8), z(M * K // 32, torch.int16)
     si_ctx.q8_quantize(x, M, K, qs, d)
     a, b = z(M * N, torch.float32), z(M * N, torch.float32)
-    si_ctx.matmul(m, qs, d, M, None, a, kernel=1)
+    si_ctx.matmul(m, qs, d, M, None, a, kernel=kernel)
     si_ctx.matmul(m, qs, d, M, None, b, kernel=0)
     si_ctx.status()
     assert torch.isfinite(a).all()
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("kernel", [1, 4], ids=["tcgen05", "mma"])
 @pytest.mark.parametrize("M", [16, 200])
-def test_gemm_swiglu_epilogue(si_ctx, oc, M):
+def test_gemm_swiglu_epilogue(si_ctx, oc, M, kernel):
     rng = np.random.default_rng(M)
     H, I = 1536, 8960
     g, u = synth.random_q4(rng, I, H), synth.random_q4(rng, I, H)
@@ -84,8 +91,13 @@ def test_gemm_swiglu_epilogue(si_ctx, oc, M):
     mg, mu = si_ctx.matrix(g, I, H), si_ctx.matrix(u, I, H)
     qs, d, blocks = q8_dev(si_ctx, x)
     aq, ad, af = z(M * I, torch.int8), z(M * I // 32, torch.int16), z(M * I, torch.float32)
-    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af)   # 140 pair tiles -> tcgen05 path
+    si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af, kernel=kernel)
     si_ctx.status()
+    # the same bits as the GEMV's SwiGLU epilogue
+    aq2, ad2, af2 = z(M * I, torch.int8), z(M * I // 32, torch.int16), z(M * I, torch.float32)
+    si_ctx.gateup_q8(mg, mu, qs, d, M, aq2, ad2, af2, kernel=0)
+    si_ctx.status()
+    assert torch.equal(aq, aq2) and torch.equal(ad, ad2) and torch.equal(af, af2)
     act = af.cpu().numpy().reshape(M, I)
     blk = z(M * I // 32 * 34, torch.uint8)
     si_ctx.q8_to_blocks(aq, ad, M, I, blk)
