@@ -10,7 +10,8 @@ of the whole set over M tokens of synthetic activations.
            CUDA events on the library's stream, inputs resident in HBM;
 * e2e    = the same through the C ABI with pinned host buffers: host->device copy
            of the step's two fp32 inputs and device->host copy of its three fp32
-           outputs inside the timed region;
+           outputs inside the timed region, steps pipelined over two buffer sets
+           (copies of neighbouring steps overlap the compute on their own streams);
 * decode = the same set at M = 1 (microseconds per token) in `decode`;
 * roofline: the dominant kernel's algorithmic throughput against MEASURED_PEAKS.json;
 * cpu_baseline: the reference's own matvec_q4q8/quantize_q8 (oracle/_ref when built
@@ -43,10 +44,11 @@ COPIES = 10
 METRIC = "Qwen layer prefill tok/s + decode µs/token; % of HBM / int8-TC roofline"
 INT8_SPEC_TOPS = 4500.0  # B200 dense int8 tensor-core spec; not in MEASURED_PEAKS.json
 SWEEP_M = (1, 16, 128, 512, 2048)  # BASELINE config 1 token counts
-# DRAM bytes (read + write) per launch of each prefill GEMM at M = 2048, from one
-# ncu capture of this bench's first prefill step
-# (profiles/gemm_q4q8_prefill_config1.md); re-measure when the kernels change.
-NCU_TRAFFIC = {"qkv": 5371136, "o": 4920320, "gateup": 19192320, "down": 28481536}
+# DRAM bytes (read + write) per launch of the gate/up GEMM at M = 2048, from one
+# `ncu --set full -k regex:k_gemm_mma -s 2 -c 1` capture of
+# `bench.py --steps 2 --warmup 3 --no-tp --no-cpu-baseline` (its first, cold
+# step); re-measure when the kernel changes.
+NCU_TRAFFIC = {"gateup": 19099136}
 
 
 def peaks():
@@ -399,25 +401,59 @@ def run_ours(args, rank, world, local_rank):
     log(f"sweep {sweep}")
 
     # ---- end to end through the C ABI with pinned host buffers ---------------
+    # Each step copies its two fp32 inputs in from pinned host memory, runs the
+    # projection set and copies its three fp32 outputs back.  Steps are
+    # pipelined over two buffer sets: the host->device copy of step i+1 and the
+    # device->host copy of step i-1 run on their own streams (their own copy
+    # engines) while step i computes; events order every reuse of a buffer.
     hx = torch.randn(M, H).pin_memory()
     ho = torch.randn(M, H).pin_memory()
-    out_q = torch.empty(M, QKV_N).pin_memory()
-    out_o = torch.empty(M, H).pin_memory()
-    out_d = torch.empty(M, H).pin_memory()
+    outs = [(torch.empty(M, QKV_N).pin_memory(), torch.empty(M, H).pin_memory(),
+             torch.empty(M, H).pin_memory()) for _ in range(2)]
+    b2 = ps.buffers(M)
+    ps.step(b2, M, 0)
+    ctx.sync()
+    steps2 = [ctx.capture(lambda c=c: ps.step(b2, M, c)) for c in range(COPIES)]
+    sets = [(b, steps), (b2, steps2)]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
     def e2e_step(i):
-        b["x"].copy_(hx, non_blocking=True)
-        b["oin"].copy_(ho, non_blocking=True)
-        steps[i % COPIES].launch()
-        out_q.copy_(b["qkv"], non_blocking=True)
-        out_o.copy_(b["yo"], non_blocking=True)
-        out_d.copy_(b["yd"], non_blocking=True)
-    with torch.cuda.stream(stream):
-        e2e_step(0)
+        k = i % 2
+        bb, gs = sets[k]
+        s_in.wait_event(ev_comp[k])          # step i-2 has read this set's inputs
+        with torch.cuda.stream(s_in):
+            bb["x"].copy_(hx, non_blocking=True)
+            bb["oin"].copy_(ho, non_blocking=True)
+            ev_in[k].record(s_in)
+        stream.wait_event(ev_in[k])
+        stream.wait_event(ev_out[k])         # step i-2's outputs have left this set
+        gs[i % COPIES].launch()
+        ev_comp[k].record(stream)
+        s_out.wait_event(ev_comp[k])
+        with torch.cuda.stream(s_out):
+            oq, oo, od = outs[k]
+            oq.copy_(bb["qkv"], non_blocking=True)
+            oo.copy_(bb["yo"], non_blocking=True)
+            od.copy_(bb["yd"], non_blocking=True)
+            ev_out[k].record(s_out)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
     barrier_sync()
-    te = time_region(torch, stream, e2e_step, args.steps)
-    te = max_over_ranks(te)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(s_in)
+    for i in range(args.steps):
+        e2e_step(i)
+    e_end.record(s_out)
+    e_end.synchronize()
+    te = max_over_ranks(e_start.elapsed_time(e_end) / 1e3)
     log(f"e2e {te:.4f}s")
+    for g_ in steps2:
+        g_.free()
     h2d = 2 * M * H * 4
     d2h = M * (QKV_N + 2 * H) * 4
 
@@ -436,7 +472,9 @@ def run_ours(args, rank, world, local_rank):
                                "1536x8960), Q4_0 x Q8_0",
                    "prefill_tokens_per_step": M, "parallelism": f"replicas x{world}",
                    "l2": f"{COPIES} weight copies ({COPIES * 26.3:.0f} MB > 2x L2) rotated per step",
-                   "timing": "CUDA graph replays, CUDA events on the library stream"},
+                   "timing": "CUDA graph replays, CUDA events on the library stream",
+                   "e2e": "pinned host buffers; host->device, compute and device->host of "
+                          "neighbouring steps overlap on three streams"},
         "decode": {"us_per_token": round(td / dsteps * 1e6, 3),
                    "kernel_us": {n: round(kd[n] * 1e6, 3) for n in names},
                    "roofline": {"bound": "hbm", "kernel": dom_d,
