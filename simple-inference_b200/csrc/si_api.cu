@@ -502,7 +502,7 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
 
 // Kernel choice for M tokens (measured on B200 at the 1.5B/7B/72B shapes):
 // the GEMV streams the weights once per 16 tokens, the GEMM keeps every
-// output's block-ordered sum in one warp and tiles 128 rows x 128 tokens.
+// output's block-ordered sum in one warp and tiles 128 rows x 64 tokens.
 // The SwiGLU pair (two matrices, the Q8 epilogue) favours the GEMM from 64
 // tokens on, single matrices from 256.  The mma.sync GEMM outruns the tcgen05
 // one at every measured shape (its rescale runs straight from registers), so
