@@ -216,6 +216,71 @@ def q4_bytes(n, k):
     return n * k // 32 * 18
 
 
+DIMS_7B = dict(hidden=3584, n_q_heads=28, n_kv_heads=4, head_dim=128, intermediate=18944,
+               rope_theta=1e6, rms_eps=1e-6)
+
+
+def run_layers_7b(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
+    """BASELINE configs 2 and 3 on each rank (replicas): one Qwen2.5-7B layer.
+    Config 2: a 2048-token prefill (fp16 KV), then 128 sequential decode steps
+    at batch 1.  Config 3: one decode step of 64 sequences with fp32 KV
+    histories of 4096 positions.  Device time, CUDA events on the library
+    stream, max over ranks; decode steps are eager launches."""
+    import sib200
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    layer = ctx.layer_synth(DIMS_7B, 2)
+    H = DIMS_7B["hidden"]
+    g = torch.Generator(device="cuda").manual_seed(2)
+    # config 2
+    ntok, ndec = 2048, 128
+    kv = ctx.kv(DIMS_7B, 1, ntok + ndec, False)
+    X = torch.randn(ntok, H, device="cuda", generator=g)
+    Y = torch.empty_like(X)
+    xd = torch.randn(ndec, H, device="cuda", generator=g)
+    yd = torch.empty_like(xd)
+    torch.cuda.synchronize()
+    pf = lambda _=0: layer.prefill_dev(kv, 0, X, ntok, 0, Y, sib200.SI_LAYER_FULL)
+    pf()
+    barrier_sync()
+    tpf = max_over_ranks(time_region(torch, stream, pf, 3)) / 3
+    dec = lambda i: layer.decode_dev(kv, xd[i], [ntok + i + 1], yd[i], sib200.SI_LAYER_FULL)
+    for i in range(3):
+        dec(i)
+    barrier_sync()
+    tdec = max_over_ranks(time_region(torch, stream, dec, ndec)) / ndec
+    kv.free()
+    # config 3
+    B, L = 64, 4096
+    kv3 = ctx.kv(DIMS_7B, B, L, True)
+    kv3.fill_synth(3, 1.0, L - 1)
+    X3 = torch.randn(B, H, device="cuda", generator=g)
+    Y3 = torch.empty_like(X3)
+    torch.cuda.synchronize()
+    d3 = lambda _=0: layer.decode_dev(kv3, X3, [L] * B, Y3, sib200.SI_LAYER_FULL)
+    for _ in range(3):
+        d3()
+    barrier_sync()
+    t3 = max_over_ranks(time_region(torch, stream, d3, 20)) / 20
+    ctx.status()
+    kv3.free()
+    layer.free()
+    kvb = B * L * DIMS_7B["n_kv_heads"] * DIMS_7B["head_dim"] * 2 * 4
+    return {
+        "config2": {"workload": "BASELINE config 2: one Qwen2.5-7B layer, 2048-token prefill "
+                                "(fp16 KV), then 128 decode steps at batch 1",
+                    "prefill_ms": round(tpf * 1e3, 3),
+                    "prefill_tok_s": round(world * ntok / tpf, 1),
+                    "decode_us_per_token": round(tdec * 1e6, 2)},
+        "config3": {"workload": "BASELINE config 3: one Qwen2.5-7B layer, one decode step of "
+                                "64 sequences with fp32 KV histories of 4096 positions",
+                    "us_per_step": round(t3 * 1e6, 2),
+                    "us_per_token": round(t3 * 1e6 / B, 3),
+                    "tok_s": round(world * B / t3, 1),
+                    "kv_bytes_per_step": kvb},
+        "timing": "CUDA events on the library stream, max over ranks; eager launches",
+    }
+
+
 def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
     """The layer stack at TP = world: a 4096-token prefill of sequence 0, then 256
     decode steps of a batch of 8 (sequence 0 continues its prefill; the other 7
@@ -498,6 +563,9 @@ def run_ours(args, rank, world, local_rank):
                            "tok_s": round(world * m / sweep[m], 1)} for m in SWEEP_M},
         "clocks": clk.summary(),
     }
+    log("configs 2 and 3")
+    result.update(run_layers_7b(args, rank, world, ctx, torch, barrier_sync, max_over_ranks))
+    log(f"configs 2/3 {result['config2']} {result['config3']}")
     if not args.no_tp:
         log("tp config 4")
         result["tp_config4"] = run_tp_config4(args, rank, world, ctx, torch, barrier_sync,

@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
 // power of two commutes with rounding, so both products round exactly as the
 // reference's do; dx/16 is kept per (block, token) in shared memory.
 //
-// Pipeline.  A producer warp streams the tile through a ring of 5-8 chunks of
+// Pipeline.  A producer warp streams the tile through a ring of 5-12 chunks of
 // CB blocks (nibbles, fp16 scales and the chunk's activations: three or five
 // 2-D TMA loads on the stage's full barrier); the two warps of a phase release
 // a stage on its empty barrier.  CB = 9 or 5 (1 mod 4) keeps the B-fragment
@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
 constexpr int kMmaPhases = 4;
 constexpr int kMmaGroups = 2;                                  // 16-row groups per tile
 constexpr int kMmaWarps = kMmaPhases * kMmaGroups + 1;         // + producer
-constexpr size_t kMmaRingBudget = 96 * 1024;
+constexpr int kMmaMaxRing = 12;                                 // stages, at most
+constexpr size_t kMmaCtaBudget = 113 * 1024;  // shared memory that keeps two CTAs per SM
 
 template <int MT, bool SWIGLU>
 struct MmaShape {
@@ -306,9 +307,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
   constexpr int kBarStart = P + 1, kBarEpi = P + 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [8]
-  uint64_t *empty = full + 8;                                            // [8]
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + 8);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [kMmaMaxRing]
+  uint64_t *empty = full + kMmaMaxRing;                                  // [kMmaMaxRing]
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kMmaMaxRing);
   float *acc_s = reinterpret_cast<float *>(smem + ns * S::STAGE + 256);  // [group][lane][NV]
   unsigned *red = reinterpret_cast<unsigned *>(acc_s + S::ACCS);         // [group][MT]
   float *dxs = reinterpret_cast<float *>(red + kMmaGroups * MT);         // [KB][MT], dx/16
@@ -630,8 +631,9 @@ template <int MT, bool SWIGLU>
 cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
   using S = MmaShape<MT, SWIGLU>;
   const int KB = a.K / 32, tiles = a.N / SI_RT;
-  int ns = 8;
-  while (ns > 5 && (size_t)ns * S::STAGE > kMmaRingBudget) --ns;
+  // The deepest ring (5..12 stages) that keeps two CTAs per SM.
+  int ns = kMmaMaxRing;
+  while (ns > 5 && S::smem(ns, KB) > kMmaCtaBudget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
