@@ -31,7 +31,8 @@
 // Prefill (contiguous tokens of one sequence): one CTA per (64 query rows =
 // 64/G tokens x G heads, KV head) walks the splits in order with K and V tiles
 // of 128 keys in shared memory, S = Q.K^T and P.V as register-tiled fp32 FMA
-// chains, and the same merges, so it needs no split scratch.
+// chains (two chains per packed f32x2 FMA), and the same merges, so it needs
+// no split scratch.
 #include "si_common.cuh"
 #include "si_kernels.cuh"
 #include "si_tma.cuh"
@@ -72,6 +73,18 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// Packed fp32 FMA: each half is one IEEE fused multiply-add with its own
+// rounding, exactly as fmaf, two chains per instruction.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
@@ -156,52 +169,65 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
     const uint8_t *p = vg + ((size_t)(key0 + i / LPR) * rowstride) * S::ES + (i % LPR) * 128;
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
   }
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x)
-    q_s[i] = a.q[((size_t)t * Hq + kvh * G) * D + i];
+  // Queries as [D][8 heads] (heads of one dim adjacent, for packed FMAs).
+  for (int i = threadIdx.x; i < kMaxGroup * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    q_s[d * kMaxGroup + h] = h < G ? a.q[((size_t)t * Hq + kvh * G + h) * D + d] : 0.0f;
+  }
   cp_async_wait_all();
   __syncthreads();
 
-  float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][NV];
+  // Heads in pairs (2q, 2q+1): two independent chains per packed FMA; each
+  // chain keeps the order of the procedure above.
+  constexpr int NP = kMaxGroup / 2;
+  float m[kMaxGroup], l[kMaxGroup];
+  float2 o2[NP][NV];
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) o[g][j] = 0.0f;
   }
+#pragma unroll
+  for (int q = 0; q < NP; ++q)
+#pragma unroll
+    for (int j = 0; j < NV; ++j) o2[q][j] = make_float2(0.0f, 0.0f);
   if (nvalid > 0) {
     // Scores, lane = key.
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
-    float s[kMaxGroup];
+    float2 s2[NP];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) s[g] = 0.0f;
+    for (int q = 0; q < NP; ++q) s2[q] = make_float2(0.0f, 0.0f);
     const uint8_t *kr = k_w + lane * S::RB;
-#pragma unroll 4
+#pragma unroll 2
     for (int c4 = 0; c4 < D / 4; ++c4) {
       // dims 4*c4 .. 4*c4+3 live in chunk (4*c4*ES)/16 at byte (4*c4*ES)%16
       const int byte = c4 * 4 * S::ES;
       const int c = byte >> 4;
       const float4 k = load4<F32>(kr + (((c ^ (lane & 7)) << 4) | (byte & 15)));
+      const float kd[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
-      for (int g = 0; g < kMaxGroup; ++g) {
-        if (g < G) {
-          const float4 q = *reinterpret_cast<const float4 *>(q_s + g * D + c4 * 4);
-          s[g] = fmaf(q.x, k.x, s[g]);
-          s[g] = fmaf(q.y, k.y, s[g]);
-          s[g] = fmaf(q.z, k.z, s[g]);
-          s[g] = fmaf(q.w, k.w, s[g]);
-        }
+      for (int e = 0; e < 4; ++e) {
+        const float2 kk = make_float2(kd[e], kd[e]);
+        const float4 qa = *reinterpret_cast<const float4 *>(q_s + (c4 * 4 + e) * kMaxGroup);
+        const float4 qb = *reinterpret_cast<const float4 *>(q_s + (c4 * 4 + e) * kMaxGroup + 4);
+        s2[0] = fma2(make_float2(qa.x, qa.y), kk, s2[0]);
+        if (G > 2) s2[1] = fma2(make_float2(qa.z, qa.w), kk, s2[1]);
+        if (G > 4) s2[2] = fma2(make_float2(qb.x, qb.y), kk, s2[2]);
+        if (G > 6) s2[3] = fma2(make_float2(qb.z, qb.w), kk, s2[3]);
       }
     }
     const bool valid = lane < nvalid;
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
       if (g < G) {
-        const float sc = valid ? __fmul_rn(s[g], scale) : -INFINITY;
+        const float sg = (g & 1) ? s2[g >> 1].y : s2[g >> 1].x;
+        const float sc = valid ? __fmul_rn(sg, scale) : -INFINITY;
         m[g] = warp_max(sc);
         const float p = expf(__fsub_rn(sc, m[g]));
         l[g] = warp_sum(p);
         p_w[lane * kMaxGroup + g] = p;
+      } else {
+        p_w[lane * kMaxGroup + g] = 0.0f;
       }
     }
     __syncwarp();
@@ -230,12 +256,15 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
         if (k0 + k < nvalid) {
           const float4 pa = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup);
           const float4 pb = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup + 4);
-          const float pk[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+          const float2 pp[NP] = {make_float2(pa.x, pa.y), make_float2(pa.z, pa.w),
+                                 make_float2(pb.x, pb.y), make_float2(pb.z, pb.w)};
 #pragma unroll
-          for (int g = 0; g < kMaxGroup; ++g)
-            if (g < G)
+          for (int j = 0; j < NV; ++j) {
+            const float2 vv = make_float2(v[k][j], v[k][j]);
 #pragma unroll
-              for (int j = 0; j < NV; ++j) o[g][j] = fmaf(pk[g], v[k][j], o[g][j]);
+            for (int q = 0; q < NP; ++q)
+              if (2 * q < G) o2[q][j] = fma2(pp[q], vv, o2[q][j]);
+          }
         }
       }
     }
@@ -247,7 +276,8 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   for (int g = 0; g < kMaxGroup; ++g)
     if (g < G)
 #pragma unroll
-      for (int j = 0; j < NV; ++j) o_w[g * D + lane * NV + j] = o[g][j];
+      for (int j = 0; j < NV; ++j)
+        o_w[g * D + lane * NV + j] = (g & 1) ? o2[g >> 1][j].y : o2[g >> 1][j].x;
   if (lane == 0)
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g)
@@ -330,10 +360,9 @@ __global__ void k_attn_combine(const AttnArgs a) {
 template <int D, bool F32>
 struct PfShape {
   static constexpr int ES = F32 ? 4 : 2;
-  static constexpr int QS = D + 4;                  // q row stride (floats)
   static constexpr int KS = D + 16 / ES;            // k row stride (elements), +16 B
-  static constexpr int SS = kSplitKeys + 4;         // score row stride (floats)
-  static constexpr int Q = kPrefillRows * QS * 4;
+  static constexpr int SS = kSplitKeys + 1;         // score row stride (floats)
+  static constexpr int Q = D * kPrefillRows * 4;    // queries as [D][64 rows]
   static constexpr int K = kSplitKeys * KS * ES;
   static constexpr int V = kSplitKeys * D * ES;
   static constexpr int SC = kPrefillRows * SS * 4;
@@ -378,23 +407,27 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnA
     return (r < R && t <= tlast) ? min(a.ctx0 + t, a.max_ctx) : 0;
   };
 
-  for (int i = tid; i < kPrefillRows * (D / 4); i += kPrefillThreads) {
-    const int r = i / (D / 4), c = i % (D / 4);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Queries transposed to [D][64 rows]: four rows of one dim are one float4.
+  for (int i = tid; i < kPrefillRows * D; i += kPrefillThreads) {
+    const int r = i % kPrefillRows, d = i / kPrefillRows;
+    float v = 0.0f;
     if (row_ctx(r) > 0) {
       const int t = t0 + r / G, h = kvh * G + r % G;
-      v = *reinterpret_cast<const float4 *>(a.q + ((size_t)t * Hq + h) * D + c * 4);
+      v = a.q[((size_t)t * Hq + h) * D + d];
     }
-    *reinterpret_cast<float4 *>(q_s + r * S::QS + c * 4) = v;
+    q_s[d * kPrefillRows + r] = v;
   }
 
-  // QK^T tiling: rows rg + 16i (i < 4), keys kq + 16j (j < 8).
+  // QK^T tiling: rows 4*rg .. 4*rg+3 (two packed pairs), keys kq + 16j (j < 8).
   const int rg = tid & 15, kq = tid >> 4;
-  // P.V tiling: rows rg + 16i, dims dq*4 + 64*jj (jj < DG/4).
+  // P.V tiling: rows rg + 16i, dims dq*4 + 64*jj (jj < DG/4), packed in pairs.
   const int dq = tid >> 4;
-  int Lr[4];
+  int Lr[4], Lq[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) Lr[i] = row_ctx(rg + 16 * i);
+  for (int i = 0; i < 4; ++i) {
+    Lr[i] = row_ctx(rg + 16 * i);
+    Lq[i] = row_ctx(4 * rg + i);
+  }
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
   float O[4][DG];
 #pragma unroll
@@ -417,39 +450,41 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnA
     cp_async_wait_all();
     __syncthreads();
 
-    // Scores.
+    // Scores: row pairs (4rg, 4rg+1), (4rg+2, 4rg+3) as packed FMA chains.
     {
-      float acc[4][8];
+      float2 acc[2][8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int p2 = 0; p2 < 2; ++p2)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < 8; ++j) acc[p2][j] = make_float2(0.0f, 0.0f);
 #pragma unroll 2
       for (int c4 = 0; c4 < D / 4; ++c4) {
         float4 q[4], k[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          q[i] = *reinterpret_cast<const float4 *>(q_s + (rg + 16 * i) * S::QS + c4 * 4);
+        for (int e = 0; e < 4; ++e)
+          q[e] = *reinterpret_cast<const float4 *>(q_s + (c4 * 4 + e) * kPrefillRows + 4 * rg);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           k[j] = load4<F32>(k_s + ((kq + 16 * j) * S::KS + c4 * 4) * S::ES);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int e = 0; e < 4; ++e) {
+          const float2 qa = make_float2(q[e].x, q[e].y), qb = make_float2(q[e].z, q[e].w);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            acc[i][j] = fmaf(q[i].x, k[j].x, acc[i][j]);
-            acc[i][j] = fmaf(q[i].y, k[j].y, acc[i][j]);
-            acc[i][j] = fmaf(q[i].z, k[j].z, acc[i][j]);
-            acc[i][j] = fmaf(q[i].w, k[j].w, acc[i][j]);
+            const float kv = e == 0 ? k[j].x : (e == 1 ? k[j].y : (e == 2 ? k[j].z : k[j].w));
+            const float2 kk = make_float2(kv, kv);
+            acc[0][j] = fma2(qa, kk, acc[0][j]);
+            acc[1][j] = fma2(qb, kk, acc[1][j]);
           }
+        }
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int key = kq + 16 * j;
-          s_s[(rg + 16 * i) * S::SS + key] =
-              key0 + key < Lr[i] ? __fmul_rn(acc[i][j], scale) : -INFINITY;
+          const float sv = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
+          s_s[(4 * rg + i) * S::SS + key] = key0 + key < Lq[i] ? __fmul_rn(sv, scale) : -INFINITY;
         }
     }
     __syncthreads();
@@ -494,11 +529,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnA
     // P.V per sub-tile, merged into the split, then into the running output.
     float Os[4][DG];
     for (int u = 0; u < kSubPerSplit && key0 + u * kSub < Lmax; ++u) {
-      float acc[4][DG];
+      float2 acc2[4][DG / 2];  // dim pairs as packed FMA chains
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < DG; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < DG / 2; ++j) acc2[i][j] = make_float2(0.0f, 0.0f);
 #pragma unroll 4
       for (int k = 0; k < kSub; ++k) {
         const int kk = u * kSub + k;
@@ -508,15 +543,23 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnA
 #pragma unroll
         for (int jj = 0; jj < DG / 4; ++jj) {
           const float4 v = load4<F32>(v_s + (kk * D + dq * 4 + 64 * jj) * S::ES);
+          const float2 va = make_float2(v.x, v.y), vb = make_float2(v.z, v.w);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            acc[i][jj * 4 + 0] = fmaf(p[i], v.x, acc[i][jj * 4 + 0]);
-            acc[i][jj * 4 + 1] = fmaf(p[i], v.y, acc[i][jj * 4 + 1]);
-            acc[i][jj * 4 + 2] = fmaf(p[i], v.z, acc[i][jj * 4 + 2]);
-            acc[i][jj * 4 + 3] = fmaf(p[i], v.w, acc[i][jj * 4 + 3]);
+            const float2 pp = make_float2(p[i], p[i]);
+            acc2[i][jj * 2] = fma2(pp, va, acc2[i][jj * 2]);
+            acc2[i][jj * 2 + 1] = fma2(pp, vb, acc2[i][jj * 2 + 1]);
           }
         }
       }
+      float acc[4][DG];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < DG / 2; ++j) {
+          acc[i][2 * j] = acc2[i][j].x;
+          acc[i][2 * j + 1] = acc2[i][j].y;
+        }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = rg + 16 * i;
