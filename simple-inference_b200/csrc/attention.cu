@@ -489,20 +489,33 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) k_attn_prefill(const AttnA
     }
     __syncthreads();
 
-    // Sub-tile softmax, lane = key: warp w takes rows 8w .. 8w+7.
-    for (int task = 0; task < 8 * kSubPerSplit; ++task) {
-      const int r = warp * 8 + task / kSubPerSplit, u = task % kSubPerSplit;
+    // Sub-tile softmax, lane = key: warp w takes rows 8w .. 8w+7, the four
+    // sub-tiles of a row at once so their shuffle chains overlap.
+#pragma unroll 1
+    for (int rr = 0; rr < 8; ++rr) {
+      const int r = warp * 8 + rr;
       const int Lrow = row_ctx(r);
-      float *sp_row = s_s + r * S::SS + u * kSub;
-      if (key0 + u * kSub < Lrow) {
-        const float sc = sp_row[lane];
-        const float mx = warp_max(sc);
-        const float p = expf(__fsub_rn(sc, mx));
-        const float ls = warp_sum(p);
-        sp_row[lane] = p;
-        if (lane == 0) { sub_m[r * 4 + u] = mx; sub_l[r * 4 + u] = ls; }
-      } else {
-        sp_row[lane] = 0.0f;
+      float *srow = s_s + r * S::SS;
+      float sc[kSubPerSplit], mx[kSubPerSplit], p[kSubPerSplit], ls[kSubPerSplit];
+#pragma unroll
+      for (int u = 0; u < kSubPerSplit; ++u) mx[u] = sc[u] = srow[u * kSub + lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < kSubPerSplit; ++u)
+          mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
+#pragma unroll
+      for (int u = 0; u < kSubPerSplit; ++u) ls[u] = p[u] = expf(__fsub_rn(sc[u], mx[u]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < kSubPerSplit; ++u)
+          ls[u] = __fadd_rn(ls[u], __shfl_xor_sync(0xffffffffu, ls[u], o));
+#pragma unroll
+      for (int u = 0; u < kSubPerSplit; ++u) {
+        const bool live = key0 + u * kSub < Lrow;  // else the sub-tile is all masked
+        srow[u * kSub + lane] = live ? p[u] : 0.0f;
+        if (live && lane == 0) { sub_m[r * 4 + u] = mx[u]; sub_l[r * 4 + u] = ls[u]; }
       }
     }
     __syncthreads();
