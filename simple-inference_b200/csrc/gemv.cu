@@ -33,7 +33,8 @@ namespace si {
 
 namespace {
 constexpr int kComputeWarps = 8;
-constexpr int kStages = 4;                // ring depth, at most
+constexpr int kStages = 4;                // ring depth when the slice does not fit whole
+constexpr int kWholeStages = 8;           // ring depth when the whole slice fits
 constexpr size_t kRingBudget = 96 * 1024; // keeps two CTAs per SM when the slice is long
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
   float *T = reinterpret_cast<float *>(smem + ns * S::STAGE);          // [2][MT][CB][RW]
   uint64_t *bars = reinterpret_cast<uint64_t *>(T + 2 * S::TERMS);      // [ns]
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + kStages);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + kWholeStages);
   uint16_t *dxs = reinterpret_cast<uint16_t *>(smem + S::fixed(ns));    // [MT][KB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -681,6 +682,10 @@ cudaError_t run(const GemvArgs &a, cudaStream_t s) {
   const int nchunks = ((KB + S::CB - 1) / S::CB) * (SWIGLU ? 2 : 1);
   int ns = nchunks < 2 ? 2 : (nchunks < kStages ? nchunks : kStages);
   while (ns > 3 && (size_t)ns * S::STAGE > kRingBudget) --ns;
+  // A slice of at most eight chunks that fits the budget whole goes out in
+  // one burst (the small decode matrices: one memory round trip, not two).
+  if (nchunks > ns && nchunks <= kWholeStages && (size_t)nchunks * S::STAGE <= kRingBudget)
+    ns = nchunks;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   // Nibbles [tiles*KB blocks][32 rows x 16 B] as (64 x u64, tiles*KB); scales
