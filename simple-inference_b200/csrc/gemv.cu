@@ -338,8 +338,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
-      auto weights = [&](int ci) {
-        const int slot = ci % ns;
+      // Ring position (slot, wrap) advanced incrementally: ns is a runtime value.
+      auto weights = [&](int ci, int slot) {
         uint8_t *st = smem + slot * S::STAGE;
         const int y = tile * KB + ci * CB;
         mbar_expect_tx(fb(slot), S::TX);
@@ -350,23 +350,27 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
           tma_load_2d(smem_u32(st + S::WS + S::NIB), &tmS2, 0, y, fb(slot));
         }
       };
-      auto acts = [&](int ci) {
-        tma_load_2d(smem_u32(smem + (ci % ns) * S::STAGE + W * S::WS), &tmX, ci * CB * 4, m0,
-                    fb(ci % ns));
+      auto acts = [&](int ci, int slot) {
+        tma_load_2d(smem_u32(smem + slot * S::STAGE + W * S::WS), &tmX, ci * CB * 4, m0, fb(slot));
       };
       // The first ring's weights go out before the previous kernel has
       // produced the activations.
       const int pre = nchunks < ns ? nchunks : ns;
-      for (int ci = 0; ci < pre; ++ci) weights(ci);
+      for (int ci = 0; ci < pre; ++ci) weights(ci, ci);
       pdl_wait();
-      for (int ci = 0; ci < pre; ++ci) acts(ci);
+      for (int ci = 0; ci < pre; ++ci) acts(ci, ci);
+      int slot = 0, wrap = 0;  // chunk ci = ns * (wrap + 1) + slot reuses slot
       for (int ci = pre; ci < nchunks; ++ci) {
-        if (!mbar_wait(eb(ci % ns), ((ci / ns) - 1) & 1, abort_flag)) {
+        if (!mbar_wait(eb(slot), wrap & 1, abort_flag)) {
           *abort_flag = 1;
           break;
         }
-        weights(ci);
-        acts(ci);
+        weights(ci, slot);
+        acts(ci, slot);
+        if (++slot == ns) {
+          slot = 0;
+          ++wrap;
+        }
       }
     }
     return;
@@ -400,9 +404,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
   float acc[W][NT][2][2];
   bool ok = true;
   int last = -1;  // the chunk whose sums this warp holds at the end
+  int slot = k, phase = 0;  // ring position of chunk ci (k < P < ns), advanced below
   for (int ci = k; ci < nchunks; ci += P) {
-    const int slot = ci % ns;
-    const bool got = ok && mbar_wait(fb(slot), (ci / ns) & 1, abort_flag);
+    const bool got = ok && mbar_wait(fb(slot), phase, abort_flag);
     if (!got) {
       ok = false;
       *abort_flag = 1;
@@ -521,6 +525,11 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       named_arrive(1 + (k + 1) % P, HAND);
     }
     last = ci;
+    slot += P;
+    if (slot >= ns) {
+      slot -= ns;
+      phase ^= 1;
+    }
   }
   if (last != nchunks - 1) return;  // another phase holds the final sums
   if (*abort_flag) ok = false;
