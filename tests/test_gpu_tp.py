@@ -1,12 +1,13 @@
-"""Tensor parallelism on two GPUs: the sharded layer (one process per GPU)
+"""Tensor parallelism on two (and, where the host has them, four) GPUs: the
+sharded layer (one process per GPU)
 against the same layer on one GPU, for decode steps (GEMV path) and a
 40-token prefill (tcgen05 GEMM path).  Decode runs both ways the group can
 add the row-parallel partial sums: fused into the projection (peer stores over
 NVLink plus a flag-gated combine kernel) and through NCCL's all-reduce.
 Five consecutive decode steps exercise both receive-slot parities and the
 flag epochs.  Cross-rank summation reorders the fp32 sums, so the bar is the
-layer bar, 1e-3; both ranks must hold identical outputs.  Skipped on hosts
-with fewer than two GPUs.
+layer bar, 1e-3; every rank must hold identical outputs.  Skipped on hosts
+with fewer GPUs than ranks.
 """
 import numpy as np
 import pytest
@@ -16,12 +17,14 @@ from common import assert_layer_close
 torch = pytest.importorskip("torch")
 pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
 
-FULL = dict(hidden=1024, n_q_heads=8, n_kv_heads=2, head_dim=128, intermediate=2816,
-            rope_theta=1e6, rms_eps=1e-6)
+FULLS = {2: dict(hidden=1024, n_q_heads=8, n_kv_heads=2, head_dim=128, intermediate=2816,
+                 rope_theta=1e6, rms_eps=1e-6),
+         4: dict(hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, intermediate=2816,
+                 rope_theta=1e6, rms_eps=1e-6)}
 SEED, CTX, PREFIX, NTOK, L, STEPS, BATCH = 5, 37, 11, 40, 64, 5, 3
 
 
-def _inputs():
+def _inputs(FULL):
     rng = np.random.default_rng(17)
     kvd = FULL["n_kv_heads"] * FULL["head_dim"]
     k = (rng.standard_normal((L, kvd)) * 0.5).astype(np.float32)
@@ -64,9 +67,10 @@ def _prefill(ctx, step, dims, k, v, X):
 
 def _rank(rank, world, uid, path):
     import sib200
+    FULL = FULLS[world]
     torch.cuda.set_device(rank)
     ctx = sib200.Context(rank, 4096, 1e6, 128)
-    k, v, x, X = _inputs()
+    k, v, x, X = _inputs(FULL)
     d, _ = sib200.tp_local_dims(FULL, rank, world)
     kvd = d["n_kv_heads"] * d["head_dim"]
     sl = slice(rank * kvd, (rank + 1) * kvd)
@@ -96,23 +100,26 @@ def _rank(rank, world, uid, path):
     ctx.close()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs two GPUs")
-def test_tp2_layer_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_layer_matches_one_gpu(tmp_path, world):
     import sib200
     import torch.multiprocessing as mp
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     uid = sib200.tp_unique_id()
     path = str(tmp_path / "tp")
-    mp.spawn(_rank, args=(2, uid, path), nprocs=2, join=True)
+    mp.spawn(_rank, args=(world, uid, path), nprocs=world, join=True)
     r = np.load(path + ".npz")
     for s in range(STEPS):
         for b in range(BATCH):
             assert_layer_close(r["one_dec"][s, b], r["fused"][s, b], 1e-3, f"fused step {s} seq {b}")
             assert_layer_close(r["one_dec"][s, b], r["nccl"][s, b], 1e-3, f"NCCL step {s} seq {b}")
     # every rank sums the slots in the same order: identical hidden states
-    np.testing.assert_array_equal(np.load(path + ".rank0.npy"), np.load(path + ".rank1.npy"))
+    for rk in range(1, world):
+        np.testing.assert_array_equal(np.load(path + ".rank0.npy"),
+                                      np.load(path + f".rank{rk}.npy"))
     for t in range(NTOK):
-        assert_layer_close(r["one_pre"][t], r["pre"][t], 1e-3, f"TP=2 prefill token {t}")
+        assert_layer_close(r["one_pre"][t], r["pre"][t], 1e-3, f"TP={world} prefill token {t}")
 
 
 def test_fused_reduction_wait_times_out(si_ctx):
