@@ -360,7 +360,7 @@ def run_tp_config4(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
                    "tok_s": round(TP_BATCH / tdec, 1),
                    "hbm_bytes_per_step_per_rank": int(per_step),
                    "achieved_gbs_per_rank": round(per_step / tdec / 1e9, 1),
-                   "reduction": "fused into the projection (peer stores + flags)" if world > 1
+                   "reduction": "fused into the projection (epoch-tagged peer stores)" if world > 1
                                 else "none (one rank)",
                    "us_per_step_nccl_allreduce": round(tdec_nccl * 1e6, 2) if tdec_nccl else None},
         "timing": "CUDA events on the library stream, max over ranks; eager launches",

@@ -314,9 +314,10 @@ SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, co
 /* across the ranks.  Decode-sized steps (at most 16 tokens) fuse that       */
 /* exchange into the projection: its GEMV stores the partial sums into every */
 /* rank's receive slot over NVLink (CUDA IPC mappings of one buffer per rank, */
-/* set up by the first such step, a collective call) and a second kernel    */
-/* waits for every rank's flag (bounded; SI_ERR_TIMEOUT past the limit) and   */
-/* adds the slots in rank order and the residual.  Larger steps use one NCCL  */
+/* set up by the first such step, a collective call), each value in one      */
+/* 8-byte word tagged with the call's epoch; the consuming kernel waits for   */
+/* the tagged words (bounded; SI_ERR_TIMEOUT past the limit) and adds the     */
+/* slots in rank order and the residual.  Larger steps use one NCCL           */
 /* all-reduce on the context's stream, then the residual add.  Cross-rank     */
 /* summation changes the fp32 order: layer outputs agree with one GPU to the  */
 /* 1e-3 layer bar, not bit for bit; every rank holds identical outputs.       */
@@ -333,7 +334,7 @@ SI_API void si_tp_free(si_tp *tp);
 /* fused = 0 sends every row-parallel projection through NCCL; timeout_ms
  * bounds the fused reduction's wait for the other ranks (default 5000). */
 SI_API si_status si_tp_set_options(si_tp *tp, int fused, int timeout_ms);
-/* Runs the fused reduction's bounded wait against a flag that nothing sets,
+/* Runs the fused reduction's bounded wait against words that nothing writes,
  * on this GPU alone: returns SI_ERR_TIMEOUT after about timeout_us and leaves
  * the context usable (a check of the failure path, no other rank needed). */
 SI_API si_status si_tp_probe_wait(si_ctx *ctx, int timeout_us);

@@ -540,13 +540,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
 
   if (!SWIGLU && a.peer.world > 0) {
     // Row-parallel tensor parallelism: the partial sums go to this rank's slot
-    // on every rank (peer stores over NVLink); the CTA that finishes last
-    // raises this rank's flag everywhere once every CTA's stores are visible.
-    // The tile's sums are gathered in shared memory first ([token][32 rows],
-    // over the hand-off area, free once both warps have read their sums), so
-    // each token's 32 rows cross NVLink as one 128-byte line.
+    // on every rank (peer stores over NVLink), each value in one 8-byte word
+    // with the call's epoch in its upper half -- the reader polls the words
+    // themselves, so there is no fence and no separate flag.  The tile's sums
+    // are gathered in shared memory first ([token][32 rows], over the hand-off
+    // area, free once both warps have read their sums), so each token's 32
+    // rows cross NVLink as 256 contiguous bytes.
     const PeerOut &pr = a.peer;
     const size_t slot0 = ((size_t)(pr.epoch & 1) * pr.world + pr.rank) * pr.slot;
+    const unsigned long long tag = (unsigned long long)(unsigned)pr.epoch << 32;
     named_sync(kBarEpi, kMmaGroups * 32);
     float *tile_s = acc_s;  // MT * 32 floats == S::ACCS
 #pragma unroll
@@ -561,23 +563,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
     for (int i = et; i < mcount * 8; i += kMmaGroups * 32) {
       const int tok = i / 8, r4 = (i % 8) * 4;
       const float4 v = *reinterpret_cast<const float4 *>(tile_s + tok * 32 + r4);
+      const unsigned long long w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
+      const unsigned long long w2 = tag | __float_as_uint(v.z), w3 = tag | __float_as_uint(v.w);
       const size_t o = slot0 + (size_t)(m0 + tok) * a.N + (size_t)tile * SI_RT + r4;
-      for (int dst = 0; dst < pr.world; ++dst)
-        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(pr.base[dst] + kPeerData) + o) = v;
-    }
-    __threadfence_system();
-    named_sync(kBarEpi, kMmaGroups * 32);
-    if (rg == 0 && lane == 0) {
-      unsigned *ticket = reinterpret_cast<unsigned *>(pr.base[pr.rank] + kPeerTicket);
-      const unsigned total = gridDim.x * gridDim.y;
-      if (atomicAdd(ticket, 1u) == total - 1) {
-        *ticket = 0;
-        __threadfence_system();
-        for (int dst = 0; dst < pr.world; ++dst) {
-          unsigned long long *f =
-              reinterpret_cast<unsigned long long *>(pr.base[dst] + kPeerFlags + pr.rank * 128);
-          asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(pr.epoch) : "memory");
-        }
+      for (int dst = 0; dst < pr.world; ++dst) {
+        unsigned long long *wp = reinterpret_cast<unsigned long long *>(pr.base[dst] + kPeerData) + o;
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(wp), "l"(w0), "l"(w1)
+                     : "memory");
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(wp + 2), "l"(w2), "l"(w3)
+                     : "memory");
       }
     }
   } else if (!SWIGLU) {

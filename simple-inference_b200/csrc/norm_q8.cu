@@ -49,7 +49,7 @@ __global__ void k_q8_quantize(const float *__restrict__ x, size_t nblocks,
 // read once; thread t holds float4 t + j*blockDim, so the eight float4 of a
 // Q8 block sit in eight adjacent lanes.  out (fp32) and the Q8 pair are each
 // optional.
-template <int VPT>
+template <int VPT, bool PEER>
 __global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
                                                      const float *__restrict__ w, int n, float eps,
                                                      float *__restrict__ out,
@@ -66,28 +66,31 @@ __global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
     const int i = threadIdx.x + j * blockDim.x;
     v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  if (rp.p.world > 0) {
-    // h = x + the ranks' partial sums, added in rank order (tp_peer.cu's order).
-    if (!tp_wait_flags(rp.p, rp.timeout_ns, rp.err)) return;
-    const float4 *recv = reinterpret_cast<const float4 *>(
-        reinterpret_cast<const float *>(rp.p.base[rp.p.rank] + kPeerData) +
-        (size_t)(rp.p.epoch & 1) * rp.p.world * rp.p.slot + (size_t)row * n);
-    const size_t slot4 = (size_t)rp.p.slot / 4;
+  if (PEER) {
+    // h = x + the ranks' partial sums, added in rank order (tp_peer.cu's order),
+    // each word waited for until it carries this call's epoch.
+    const unsigned long long deadline = globaltimer() + rp.timeout_ns;
+    const unsigned ep = (unsigned)rp.p.epoch;
+    bool bad = false;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int i = threadIdx.x + j * blockDim.x;
       if (i < n4) {
-        float4 sum = __ldcg(recv + i);
-        for (int src = 1; src < rp.p.world; ++src) {
-          const float4 o = __ldcg(recv + src * slot4 + i);
-          sum = make_float4(__fadd_rn(sum.x, o.x), __fadd_rn(sum.y, o.y), __fadd_rn(sum.z, o.z),
-                            __fadd_rn(sum.w, o.w));
-        }
-        v[j] = make_float4(__fadd_rn(v[j].x, sum.x), __fadd_rn(v[j].y, sum.y),
-                           __fadd_rn(v[j].z, sum.z), __fadd_rn(v[j].w, sum.w));
-        reinterpret_cast<float4 *>(rp.h_out + (size_t)row * n)[i] = v[j];
+        const size_t e0 = (size_t)row * n + 4 * i;
+        float sum[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sum[c] = peer_word(peer_slot(rp.p, 0) + e0 + c, ep, deadline, rp.err, bad);
+        for (int src = 1; src < rp.p.world; ++src)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            sum[c] = __fadd_rn(sum[c], peer_word(peer_slot(rp.p, src) + e0 + c, ep, deadline, rp.err, bad));
+        v[j] = make_float4(__fadd_rn(v[j].x, sum[0]), __fadd_rn(v[j].y, sum[1]),
+                           __fadd_rn(v[j].z, sum[2]), __fadd_rn(v[j].w, sum[3]));
+        if (!bad) reinterpret_cast<float4 *>(rp.h_out + (size_t)row * n)[i] = v[j];
       }
     }
+    // A timed-out row is left unwritten; the block's reductions below still
+    // run (every thread reaches them) on whatever the row holds.
   }
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -189,13 +192,19 @@ cudaError_t launch_rmsnorm_q8(const float *x, const float *w, int M, int n, floa
   threads = threads < 128 ? 128 : (threads > 512 ? 512 : threads);
   const int vpt = (n4 + threads - 1) / threads;
   const dim3 g(M), b(threads);
+  const bool peer = rpp != nullptr;
   switch (vpt) {
-    case 1: return launch_pdl(k_rmsnorm_q8<1>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
-    case 2: return launch_pdl(k_rmsnorm_q8<2>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
-    case 3: return launch_pdl(k_rmsnorm_q8<3>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
-    case 4: return launch_pdl(k_rmsnorm_q8<4>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 1: return peer ? launch_pdl(k_rmsnorm_q8<1, true>, g, b, 0, s, x, w, n, eps, out, qs, d, rp)
+                        : launch_pdl(k_rmsnorm_q8<1, false>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 2: return peer ? launch_pdl(k_rmsnorm_q8<2, true>, g, b, 0, s, x, w, n, eps, out, qs, d, rp)
+                        : launch_pdl(k_rmsnorm_q8<2, false>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 3: return peer ? launch_pdl(k_rmsnorm_q8<3, true>, g, b, 0, s, x, w, n, eps, out, qs, d, rp)
+                        : launch_pdl(k_rmsnorm_q8<3, false>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+    case 4: return peer ? launch_pdl(k_rmsnorm_q8<4, true>, g, b, 0, s, x, w, n, eps, out, qs, d, rp)
+                        : launch_pdl(k_rmsnorm_q8<4, false>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
     case 5: case 6: case 7: case 8:
-      return launch_pdl(k_rmsnorm_q8<8>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
+      return peer ? launch_pdl(k_rmsnorm_q8<8, true>, g, b, 0, s, x, w, n, eps, out, qs, d, rp)
+                  : launch_pdl(k_rmsnorm_q8<8, false>, g, b, 0, s, x, w, n, eps, out, qs, d, rp);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -1040,7 +1040,7 @@ static si_status tp_sym_release(si_ctx *ctx, si_tp *tp) {
   SI_CUDA(cudaStreamSynchronize(ctx->stream));
   for (int r = 0; r < tp->world; ++r)
     if (r != tp->rank && tp->peer[r]) cudaIpcCloseMemHandle(tp->peer[r]);
-  SI_TRY(tp_barrier(ctx, tp, tp->sym + si::kPeerTicket + 64));
+  SI_TRY(tp_barrier(ctx, tp, tp->sym + 1024));  // control space below the slots
   cudaFree(tp->sym);
   tp->sym = nullptr;
   for (char *&p : tp->peer) p = nullptr;
@@ -1054,9 +1054,9 @@ static si_status tp_sym_release(si_ctx *ctx, si_tp *tp) {
 static si_status tp_sym_reserve(si_ctx *ctx, si_tp *tp, int slot) {
   if (tp->sym && tp->slot >= slot) return SI_OK;
   SI_TRY(tp_sym_release(ctx, tp));
-  const size_t bytes = si::kPeerData + (size_t)2 * tp->world * slot * sizeof(float);
+  const size_t bytes = si::kPeerData + (size_t)2 * tp->world * slot * sizeof(uint64_t);
   SI_CUDA(cudaMalloc(&tp->sym, bytes));
-  SI_CUDA(cudaMemset(tp->sym, 0, si::kPeerData));
+  SI_CUDA(cudaMemset(tp->sym, 0, bytes));
   tp->slot = slot;
   tp->epoch = 0;
   cudaIpcMemHandle_t h;
@@ -1072,6 +1072,8 @@ static si_status tp_sym_reserve(si_ctx *ctx, si_tp *tp, int slot) {
           "ncclAllGather");
   std::vector<char> all((size_t)tp->world * 64);
   SI_CUDA(cudaMemcpyAsync(all.data(), xchg, all.size(), cudaMemcpyDeviceToHost, ctx->stream));
+  // Receive words start with epoch 0, which no call uses.
+  SI_CUDA(cudaMemsetAsync(xchg, 0, all.size(), ctx->stream));
   SI_CUDA(cudaStreamSynchronize(ctx->stream));
   for (int r = 0; r < tp->world; ++r) {
     if (r == tp->rank) {
@@ -1085,7 +1087,7 @@ static si_status tp_sym_reserve(si_ctx *ctx, si_tp *tp, int slot) {
     tp->peer[r] = static_cast<char *>(p);
   }
   // Every rank's flags are zero and its mappings open before any rank writes.
-  SI_TRY(tp_barrier(ctx, tp, tp->sym + si::kPeerTicket + 64));
+  SI_TRY(tp_barrier(ctx, tp, tp->sym + 1024));  // control space below the slots
   return SI_OK;
 }
 
@@ -2079,17 +2081,18 @@ extern "C" SI_API si_status si_tp_probe_wait(si_ctx *ctx, int timeout_us) {
   SI_TRY(set_device(ctx));
   SI_CHECK(timeout_us > 0 && timeout_us <= 10000000, "timeout out of range");
   // A two-rank group whose other rank never writes: this rank's buffer stands
-  // for both, its flags stay zero, and the combine's wait must give up.
+  // for both, its words keep epoch 0, and the combine's wait must give up.
   char *buf = nullptr;
-  SI_CUDA(cudaMalloc(&buf, si::kPeerData + 2 * 2 * 32 * sizeof(float)));
-  SI_CUDA(cudaMemset(buf, 0, si::kPeerData));
+  const size_t bytes = si::kPeerData + 2 * 2 * 32 * sizeof(uint64_t);
+  SI_CUDA(cudaMalloc(&buf, bytes));
+  SI_CUDA(cudaMemset(buf, 0, bytes));
   si::PeerOut p{};
   p.world = 2;
   p.rank = 0;
   p.slot = 32;
   p.epoch = 1;
   p.base[0] = p.base[1] = buf;
-  float *y = reinterpret_cast<float *>(buf + si::kPeerData);
+  float *y = reinterpret_cast<float *>(buf + 1024);  // control space: 32 floats
   cudaError_t e = si::launch_tp_combine(p, nullptr, y, 32, (unsigned long long)timeout_us * 1000ull,
                                         ctx->err, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);

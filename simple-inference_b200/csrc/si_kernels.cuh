@@ -7,17 +7,18 @@
 namespace si {
 
 // Row-parallel tensor parallelism: where a GEMV's partial sums go instead of
-// `out` -- every rank's receive slot -- and how its last CTA signals them.
-// Each rank holds one symmetric buffer: flags[src] (u64 epochs, 128 B apart)
-// at kPeerFlags, a CTA ticket at kPeerTicket, receive slots
-// [2 parities][world][slot floats] at kPeerData.
+// `out` -- every rank's receive slot.  Each rank holds one symmetric buffer
+// whose receive slots [2 parities][world][slot] of 8-byte words start at
+// kPeerData; a word is (float bits | epoch << 32), stored in one 8-byte
+// write, so a reader that sees this call's epoch in a word has its value (no
+// fence and no separate flag).  The 4 KB below kPeerData is control space.
 constexpr int kPeerMaxWorld = 8;
-constexpr size_t kPeerFlags = 0, kPeerTicket = 1024, kPeerData = 4096;
+constexpr size_t kPeerData = 4096;
 struct PeerOut {
   char *base[kPeerMaxWorld];  // each rank's buffer as mapped in this process (own included)
   int world;                  // 0: no peer output
   int rank;
-  int slot;                   // floats per receive slot (>= M * N)
+  int slot;                   // words per receive slot (>= M * N)
   unsigned long long epoch;   // this call's number, 1, 2, ...; parity picks the slot set
 };
 
@@ -62,8 +63,8 @@ cudaError_t launch_q8_quantize(const float *x, int M, int K, int8_t *qs, uint16_
                                cudaStream_t s);
 // With rp (tensor parallelism, decode): x is the residual and the row is
 // first h = x + the sum over ranks (rank order) of the receive slots of
-// rp->p.epoch, after the bounded wait for every rank's flag; h is written to
-// rp->h_out and normalised.
+// rp->p.epoch (each word waited for, bounded); h is written to rp->h_out and
+// normalised.
 struct RmsPeer {
   PeerOut p;
   float *h_out;
@@ -149,7 +150,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
 
 // ---- tp_peer.cu --------------------------------------------------------------
 // y[i] = resid[i] + sum over ranks (in rank order) of the receive slots of
-// epoch `epoch`, after a bounded wait (timeout_ns) for every rank's flag.
+// epoch `epoch`, each word waited for (bounded by timeout_ns) until it
+// carries the epoch.
 cudaError_t launch_tp_combine(const PeerOut &p, const float *resid, float *y, size_t n,
                               unsigned long long timeout_ns, int *err, cudaStream_t s);
 

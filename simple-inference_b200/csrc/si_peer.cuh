@@ -1,6 +1,7 @@
-// si_peer.cuh -- the bounded wait for every rank's flag of a fused
-// row-parallel projection (see tp_peer.cu), shared by the kernels that
-// consume the receive slots.
+// si_peer.cuh -- reading the receive slots of a fused row-parallel
+// projection (see tp_peer.cu): each 8-byte word is (float bits | epoch << 32),
+// written by its producer in one store; a reader polls a word until it carries
+// the expected epoch, with a time bound.
 #pragma once
 #include "si_common.cuh"
 #include "si_kernels.cuh"
@@ -8,37 +9,29 @@
 
 namespace si {
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
+// Value of word p once it carries `epoch` (low 32 bits).  Past the deadline
+// the thread records SI_ERR_TIMEOUT (6) once, sets *bad and returns 0.
+__device__ __forceinline__ float peer_word(const unsigned long long *p, unsigned epoch,
+                                           unsigned long long deadline, int *err, bool &bad) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  if (bad) return 0.0f;
+  while ((unsigned)(w >> 32) != epoch) {
+    if (globaltimer() > deadline) {
+      bad = true;
+      raise_error(err, 6 /* SI_ERR_TIMEOUT */);
+      return 0.0f;
+    }
+    __nanosleep(32);
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  }
+  return __uint_as_float((unsigned)w);
 }
 
-// Called by every thread of the CTA.  Thread 0 polls this rank's flags until
-// each rank has published p.epoch; past timeout_ns it records SI_ERR_TIMEOUT
-// (6) in err and every thread gets false.
-__device__ __forceinline__ bool tp_wait_flags(const PeerOut &p, unsigned long long timeout_ns,
-                                              int *err) {
-  __shared__ int bad;
-  if (threadIdx.x == 0) {
-    bad = 0;
-    const char *own = p.base[p.rank];
-    const unsigned long long t0 = globaltimer();
-    for (int src = 0; src < p.world && !bad; ++src) {
-      const unsigned long long *f =
-          reinterpret_cast<const unsigned long long *>(own + kPeerFlags + src * 128);
-      while (ld_acquire_sys(f) < p.epoch) {
-        if (globaltimer() - t0 > timeout_ns) {
-          bad = 1;
-          raise_error(err, 6 /* SI_ERR_TIMEOUT */);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
-  __syncthreads();
-  return !bad;
+// Word i of source rank src of this call's slot set, on this rank.
+__device__ __forceinline__ const unsigned long long *peer_slot(const PeerOut &p, int src) {
+  return reinterpret_cast<const unsigned long long *>(p.base[p.rank] + kPeerData) +
+         ((size_t)(p.epoch & 1) * p.world + src) * p.slot;
 }
 
 }  // namespace si

@@ -6,13 +6,14 @@
 // rank must add.  Instead of a separate all-reduce, the projection's own GEMV
 // writes its partial sums straight into every rank's receive slot over NVLink
 // (peer stores from the tensor-core GEMV's epilogue, tile by tile as the
-// tiles finish) and its last CTA raises this rank's flag on every rank; this
-// kernel then waits for all ranks' flags, adds the slots in rank order and
-// the residual.  Every rank sums in the same
+// tiles finish), each value in one 8-byte word together with the call's
+// epoch; this kernel polls the words until they carry the epoch -- the data
+// is its own flag, so no fence or flag hop sits on the critical path -- and
+// adds the slots in rank order and the residual.  Every rank sums in the same
 // order, so all ranks hold bit-identical hidden states.
 //
-// The wait is bounded: past timeout_ns the kernel records SI_ERR_TIMEOUT in
-// the context's error word and returns without writing y, so a rank that
+// The wait is bounded: past timeout_ns a thread records SI_ERR_TIMEOUT in the
+// context's error word and stops without writing its outputs, so a rank that
 // never arrives ends in an error on the host instead of a hung GPU.
 #include "si_common.cuh"
 #include "si_kernels.cuh"
@@ -27,14 +28,15 @@ __global__ void __launch_bounds__(256) k_tp_combine(const PeerOut p, const float
                                                     unsigned long long timeout_ns, int *err) {
   pdl_trigger();
   pdl_wait();
-  if (!tp_wait_flags(p, timeout_ns, err)) return;
-  const char *own = p.base[p.rank];
-  const float *recv = reinterpret_cast<const float *>(own + kPeerData) +
-                      (size_t)(p.epoch & 1) * p.world * p.slot;
+  const unsigned long long deadline = globaltimer() + timeout_ns;
+  const unsigned ep = (unsigned)p.epoch;
+  bool bad = false;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    float s = __ldcg(recv + i);
-    for (int src = 1; src < p.world; ++src) s = __fadd_rn(s, __ldcg(recv + (size_t)src * p.slot + i));
+    float s = peer_word(peer_slot(p, 0) + i, ep, deadline, err, bad);
+    for (int src = 1; src < p.world; ++src)
+      s = __fadd_rn(s, peer_word(peer_slot(p, src) + i, ep, deadline, err, bad));
+    if (bad) return;
     y[i] = resid ? __fadd_rn(resid[i], s) : s;
   }
 }
