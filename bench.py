@@ -710,6 +710,28 @@ def probe_config4_layer():
     print("ok")
 
 
+def probe_config2_decode():
+    """One Qwen2.5-7B layer on GPU 0: three decode steps at batch 1 after a
+    2048-position fp16 history, no timing -- the workload of the config-2
+    decode ncu summaries."""
+    import torch
+    import sib200
+    torch.cuda.set_device(0)
+    ctx = sib200.Context(0, max_positions=TP_MAX_CTX, rope_theta=1e6, head_dim=128)
+    layer = ctx.layer_synth(DIMS_7B, 2)
+    kv = ctx.kv(DIMS_7B, 1, 2176, False)
+    kv.fill_synth(2, 1.0, 2048)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(3, DIMS_7B["hidden"], device="cuda", generator=g)
+    y = torch.empty_like(x)
+    torch.cuda.synchronize()
+    for i in range(3):
+        layer.decode_dev(kv, x[i], [2049 + i], y[i], sib200.SI_LAYER_FULL)
+    ctx.sync()
+    ctx.status()
+    print("ok")
+
+
 def log(msg):
     if os.environ.get("SI_BENCH_VERBOSE"):
         print(f"[bench] {msg}", file=sys.stderr, flush=True)
@@ -726,12 +748,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="skip the config-4 tensor-parallel stack")
-    ap.add_argument("--probe", choices=["config4-layer"],
+    ap.add_argument("--probe", choices=["config4-layer", "config2-decode"],
                     help="run one untimed workload for a profiler and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.probe == "config4-layer":
         probe_config4_layer()
+        return
+    if args.probe == "config2-decode":
+        probe_config2_decode()
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -33,9 +33,8 @@ namespace si {
 
 namespace {
 constexpr int kComputeWarps = 8;
-constexpr int kStages = 4;                // ring depth when the slice does not fit whole
-constexpr int kWholeStages = 8;           // ring depth when the whole slice fits
-constexpr size_t kRingBudget = 96 * 1024; // keeps two CTAs per SM when the slice is long
+constexpr int kMaxRing = 8;               // ring stages, at most
+constexpr size_t kCtaBudget = 113 * 1024; // shared memory that keeps two CTAs per SM
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
   float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
@@ -43,8 +42,8 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // Shape of one instantiation.  A chunk is CB blocks of the RW-row slice; the
-// compute thread (warp w < 8, lane = bo*RW + rl) owns pieces u < U of each
-// chunk: block (w*U + u)*BPL + bo, row rl.  Term buffers stay <= 32 KB.
+// compute thread (compute warp w, lane = bo*RW + rl) owns pieces u < U of each
+// chunk: block (w*U + u)*BPL + bo, row rl.
 template <int MT, int RW>
 struct Shape {
   static constexpr int BPL = SI_RT / RW;
@@ -52,34 +51,57 @@ struct Shape {
   static constexpr int CB = CB0 < 64 ? CB0 : 64;            // nibbles <= 16 KB per stage
   static constexpr int U = CB / (kComputeWarps * BPL);
   static constexpr int MW = (MT * RW + 31) / 32;            // merge warps
-  static constexpr int THREADS = (kComputeWarps + MW) * 32;
+  static constexpr int WARPS = 1 + kComputeWarps + MW;      // producer, compute, merge
+  static constexpr int THREADS = WARPS * 32;
   static constexpr int NIB = CB * RW * 16;                  // [CB][RW][16 B]
   static constexpr int SCL = CB * RW * 2;                   // [CB][RW] fp16
   static constexpr int ACT = MT * CB * 32;                  // [MT][CB][32 B]
   static constexpr int STAGE = NIB + SCL + ACT;
   static constexpr int TERMS = MT * CB * RW;                // floats per term buffer
-  // Shared memory: ns ring stages, two term buffers, 128 B of barriers and
-  // flags, the activation scales [MT][KB] fp16, alignment slack.
-  __host__ __device__ static size_t fixed(int ns) { return (size_t)ns * STAGE + 2 * TERMS * sizeof(float) + 128; }
-  static size_t smem(int ns, int KB) { return fixed(ns) + (size_t)MT * KB * sizeof(uint16_t) + 128; }
+  static constexpr int NTB = TERMS * 4 <= 8192 ? 4 : 2;     // term buffers
+  // Shared memory: ns ring stages, NTB term buffers, 256 B of barriers and the
+  // abort flag, dx/16 as fp32 [KB][MT], alignment slack.
+  __host__ __device__ static size_t fixed(int ns) {
+    return (size_t)ns * STAGE + (size_t)NTB * TERMS * sizeof(float) + 256;
+  }
+  static size_t smem(int ns, int KB) { return fixed(ns) + (size_t)MT * KB * sizeof(float) + 128; }
   static_assert(U >= 1 && U * kComputeWarps * BPL == CB, "chunk shape");
   static_assert(NIB % 128 == 0 && SCL % 128 == 0 && ACT % 128 == 0, "TMA destinations");
 };
 
 // Grid: (N/32 tiles x 32/RW row slices, token groups of MT).
+//
+// Roles.  Warp 0 is the producer: one thread streams the slice's chunks
+// through the ring (three 2-D TMA loads per chunk on the stage's full
+// barrier), refilling a stage as soon as the eight compute warps have
+// released it on its empty barrier.  The compute warps turn a chunk's
+// (row, block) pieces into terms in a term buffer and publish it on that
+// buffer's full barrier; the merge warps -- one thread per (token, row) --
+// add the terms to the running sums in block order and release the buffer.
+// No role waits for another except through these barriers, so the loads of
+// later chunks, the terms of the current one and the adds of the previous
+// one overlap.
+//
+// Term.  ((float)isum * dw) * dx is computed as ((float)(16*isum) * dw) *
+// (dx/16): the dp4a of the pre-shifted nibbles returns 16*isum, exact in fp32,
+// and scaling by a power of two commutes with both roundings (the products
+// stay far inside the normal range), so the term is bit-identical to the
+// reference's.
 template <int MT, int RW, bool SWIGLU>
-__global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
+__global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
     k_gemv(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
            const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
            const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
   using S = Shape<MT, RW>;
-  constexpr int CB = S::CB, BPL = S::BPL, U = S::U, SLICES = SI_RT / RW;
+  constexpr int CB = S::CB, BPL = S::BPL, U = S::U, SLICES = SI_RT / RW, NTB = S::NTB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-  float *T = reinterpret_cast<float *>(smem + ns * S::STAGE);          // [2][MT][CB][RW]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(T + 2 * S::TERMS);      // [ns]
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + kWholeStages);
-  uint16_t *dxs = reinterpret_cast<uint16_t *>(smem + S::fixed(ns));    // [MT][KB]
+  float *T = reinterpret_cast<float *>(smem + ns * S::STAGE);            // [NTB][MT][CB][RW]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(T + NTB * S::TERMS);
+  uint64_t *full = bars, *empty = bars + kMaxRing;                       // [ns] each
+  uint64_t *tfull = bars + 2 * kMaxRing, *tempty = tfull + 4;            // [NTB] each
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tempty + 4);
+  float *dxs = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256);  // [KB][MT]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x / SLICES, r0 = (blockIdx.x % SLICES) * RW;
@@ -87,73 +109,105 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
   const int KB = a.K / 32;
   const int npass = (KB + CB - 1) / CB;                 // chunks per matrix
   const int nchunks = SWIGLU ? 2 * npass : npass;
-  auto bar = [&](int i) { return smem_u32(bars + i); };
+  auto bar = [&](uint64_t *b, int i) { return smem_u32(b + i); };
 
   pdl_trigger();
 
   // Chunk c: pass c / npass (gate, then up), blocks [cc*CB, cc*CB + CB).
-  auto load_weights = [&](int c) {
-    const int pass = c / npass, cc = c % npass, slot = c % ns;
+  auto load_weights = [&](int c, int slot) {
+    const int pass = c >= npass, cc = pass ? c - npass : c;
     uint8_t *st = smem + slot * S::STAGE;
     const int y = tile * KB + cc * CB;
-    mbar_expect_tx(bar(slot), S::STAGE);
-    tma_load_2d(smem_u32(st), pass ? &tmN2 : &tmN, r0 * 2, y, bar(slot));
-    tma_load_2d(smem_u32(st + S::NIB), pass ? &tmS2 : &tmS, r0, y, bar(slot));
+    mbar_expect_tx(bar(full, slot), S::STAGE);
+    tma_load_2d(smem_u32(st), pass ? &tmN2 : &tmN, r0 * 2, y, bar(full, slot));
+    tma_load_2d(smem_u32(st + S::NIB), pass ? &tmS2 : &tmS, r0, y, bar(full, slot));
   };
-  auto load_acts = [&](int c) {
-    const int cc = c % npass, slot = c % ns;
+  auto load_acts = [&](int c, int slot) {
+    const int cc = c >= npass ? c - npass : c;
     tma_load_2d(smem_u32(smem + slot * S::STAGE + S::NIB + S::SCL), &tmX, cc * CB * 4, m0,
-                bar(slot));
+                bar(full, slot));
   };
-  // Thread 0 owns the barriers until the block barrier below: it sets them up
-  // and requests the weights of the first chunks right away -- before the
-  // previous kernel (which may still be running) has produced the activations.
-  const int pre = nchunks < ns - 1 ? nchunks : ns - 1;
+  // Thread 0 sets the barriers up and requests the weights of the first
+  // chunks right away -- before the previous kernel (which may still be
+  // running) has produced the activations.
+  const int pre = nchunks < ns ? nchunks : ns;
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
-    for (int i = 0; i < ns; ++i) mbar_init(bar(i), 1);
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(bar(full, i), 1);
+      mbar_init(bar(empty, i), kComputeWarps * 32);
+    }
+    for (int i = 0; i < NTB; ++i) {
+      mbar_init(bar(tfull, i), kComputeWarps * 32);
+      mbar_init(bar(tempty, i), S::MW * 32);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int c = 0; c < pre; ++c) load_weights(c);
+    for (int c = 0; c < pre; ++c) load_weights(c, c);
   }
   pdl_wait();
   if (threadIdx.x == 0)
-    for (int c = 0; c < pre; ++c) load_acts(c);
-  for (int i = threadIdx.x; i < mcount * KB; i += blockDim.x)
-    dxs[i] = a.xd[(size_t)(m0 + i / KB) * KB + i % KB];
+    for (int c = 0; c < pre; ++c) load_acts(c, c);
+  for (int i = threadIdx.x; i < mcount * KB; i += blockDim.x) {
+    const int m = i / KB, b = i - m * KB;
+    dxs[b * MT + m] = __fmul_rn(f16_to_f32(a.xd[(size_t)(m0 + m) * KB + b]), 0.0625f);
+  }
+  __syncthreads();  // barriers initialised, dxs visible
 
-  // Merge role: thread (token tm, row tr) of the merge warps.
-  const bool merger = warp >= kComputeWarps;
-  const int mt = threadIdx.x - kComputeWarps * 32;
-  const int tm = mt / RW, tr = mt % RW;
-  const bool merging = merger && tm < mcount;
-  float acc = 0.0f, first = 0.0f;
-  if (!SWIGLU && merging && a.bias) acc = a.bias[tile * SI_RT + r0 + tr];
-  __syncthreads();  // dxs visible
-
-  const int bo = lane / RW, rl = lane % RW;
-  for (int c = 0; c < nchunks; ++c) {
-    if (threadIdx.x == 0 && c + ns - 1 < nchunks) {
-      load_weights(c + ns - 1);
-      load_acts(c + ns - 1);
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane != 0) return;
+    int slot = pre == ns ? 0 : pre, phase = 0;
+    int issued = pre;
+    for (int c = pre; c < nchunks; ++c) {
+      if (!mbar_wait(bar(empty, slot), phase, abort_flag)) {
+        *abort_flag = 1;
+        raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+        break;
+      }
+      load_weights(c, slot);
+      load_acts(c, slot);
+      ++issued;
+      if (++slot == ns) { slot = 0; phase ^= 1; }
     }
-    const int cc = c % npass, slot = c % ns;
-    bool ok = true;
-    if (!merger) {
-      ok = mbar_wait(bar(slot), (c / ns) & 1, abort_flag);
-      if (ok) {
-        const uint8_t *st = smem + slot * S::STAGE;
-        const uint4 *nb = reinterpret_cast<const uint4 *>(st);
-        const uint16_t *sb = reinterpret_cast<const uint16_t *>(st + S::NIB);
-        const int4 *ab = reinterpret_cast<const int4 *>(st + S::NIB + S::SCL);
-        float *Tb = T + (size_t)(c & 1) * S::TERMS;
+    if (*abort_flag) {
+      // Let the copies still in flight land before the CTA's shared memory
+      // goes away (bounded: the waits give up after their deadline).
+      const int first = issued > ns ? issued - ns : 0;
+      int none = 0;
+      for (int c = first; c < issued; ++c) mbar_wait(bar(full, c % ns), (c / ns) & 1, &none);
+    }
+    return;
+  }
+
+  if (warp <= kComputeWarps) {
+    // ---- compute ----
+    const int cw = warp - 1;
+    const int bo = lane / RW, rl = lane % RW;
+    const bool want_isum = !SWIGLU && a.isum_out != nullptr;
+    int slot = 0, sp = 0, tb = 0, tp = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int cc = c >= npass ? c - npass : c;
+      bool ok = mbar_wait(bar(full, slot), sp, abort_flag);
+      if (ok && c >= NTB) ok = mbar_wait(bar(tempty, tb), tp ^ 1, abort_flag);
+      if (!ok) {
+        *abort_flag = 1;
+        raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+        return;
+      }
+      const uint8_t *st = smem + slot * S::STAGE;
+      const uint4 *nb = reinterpret_cast<const uint4 *>(st);
+      const uint16_t *sb = reinterpret_cast<const uint16_t *>(st + S::NIB);
+      const int4 *ab = reinterpret_cast<const int4 *>(st + S::NIB + S::SCL);
+      float *Tb = T + tb * S::TERMS;
+      auto pieces = [&](auto whole) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int bl = (warp * U + u) * BPL + bo;
+          const int bl = (cw * U + u) * BPL + bo;
           const int bx = cc * CB + bl;  // block within the matrix
-          if (bx < KB) {
+          if (decltype(whole)::value || bx < KB) {
             const uint4 w = nb[bl * RW + rl];
             const float dw = f16_to_f32(sb[bl * RW + rl]);
             const int lo[4] = {lo_nib_s8x16(w.x), lo_nib_s8x16(w.y), lo_nib_s8x16(w.z),
@@ -162,31 +216,54 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
                                hi_nib_s8x16(w.w)};
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
-              if (m < mcount) {
+              if (MT == 1 || m < mcount) {
                 const int4 a0 = ab[(m * CB + bl) * 2], a1 = ab[(m * CB + bl) * 2 + 1];
-                const float dx = f16_to_f32(dxs[m * KB + bx]);
-                const int is = block_isum_unpacked(lo, hi, a0, a1);
-                Tb[((size_t)m * CB + bl) * RW + rl] = block_term(is, dw, dx);
-                if (!SWIGLU && a.isum_out)
+                int s16 = __dp4a(lo[0], a0.x, 0);
+                s16 = __dp4a(lo[1], a0.y, s16);
+                s16 = __dp4a(lo[2], a0.z, s16);
+                s16 = __dp4a(lo[3], a0.w, s16);
+                s16 = __dp4a(hi[0], a1.x, s16);
+                s16 = __dp4a(hi[1], a1.y, s16);
+                s16 = __dp4a(hi[2], a1.z, s16);
+                s16 = __dp4a(hi[3], a1.w, s16);
+                Tb[(m * CB + bl) * RW + rl] =
+                    __fmul_rn(__fmul_rn((float)s16, dw), dxs[bx * MT + m]);
+                if (want_isum)
                   a.isum_out[((size_t)(m0 + m) * a.N + (size_t)tile * SI_RT + r0 + rl) * KB + bx] =
-                      is;
+                      s16 >> 4;
               }
             }
           }
         }
-      } else {
-        *abort_flag = 1;
-      }
+      };
+      if (cc * CB + CB <= KB) pieces(std::true_type{});
+      else pieces(std::false_type{});
+      mbar_arrive(bar(empty, slot));  // this thread is done with the stage
+      mbar_arrive(bar(tfull, tb));    // and its terms are written
+      if (++slot == ns) { slot = 0; sp ^= 1; }
+      if (++tb == NTB) { tb = 0; tp ^= 1; }
     }
-    // Terms of chunk c visible; stage c's ring slot is free for chunk c+ns.
-    if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+    return;
+  }
+
+  // ---- merge: thread (token tm, row tr) ----
+  const int mt = threadIdx.x - (1 + kComputeWarps) * 32;
+  const int tm = mt / RW, tr = mt % RW;
+  const bool merging = tm < mcount;
+  float acc = 0.0f, first = 0.0f;
+  if (!SWIGLU && merging && a.bias) acc = a.bias[tile * SI_RT + r0 + tr];
+  int tb = 0, tp = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    const int cc = c >= npass ? c - npass : c;
+    if (!mbar_wait(bar(tfull, tb), tp, abort_flag)) {
+      *abort_flag = 1;
+      raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
       return;
     }
     if (merging) {
       // The adds are a serial chain; load the terms 16 at a time ahead of it.
       const int nvalid = min(CB, KB - cc * CB);
-      const float *Tm = T + (size_t)(c & 1) * S::TERMS + (size_t)tm * CB * RW + tr;
+      const float *Tm = T + tb * S::TERMS + tm * CB * RW + tr;
       if (SWIGLU && c == npass) {  // the up rows begin
         first = acc;
         acc = 0.0f;
@@ -201,6 +278,8 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS)
       }
       for (; j < nvalid; ++j) acc = __fadd_rn(acc, Tm[j * RW]);
     }
+    mbar_arrive(bar(tempty, tb));
+    if (++tb == NTB) { tb = 0; tp ^= 1; }
   }
   if (!merging) return;
   const int row = tile * SI_RT + r0 + tr;
@@ -679,16 +758,13 @@ cudaError_t run(const GemvArgs &a, cudaStream_t s) {
   static_assert(!SWIGLU || RW == SI_RT, "the SwiGLU Q8 epilogue needs whole 32-row tiles");
   using S = Shape<MT, RW>;
   const int KB = a.K / 32, tiles = a.N / SI_RT;
-  // Ring depth: every chunk of the slice in flight at once when the ring fits
-  // the budget (decode matrices are latency-bound), else as many as it holds,
-  // at least 3.
+  // Ring depth: the whole slice at once when it fits (the small decode
+  // matrices: one memory round trip), else the deepest ring that keeps two
+  // CTAs per SM, at least three stages.
   const int nchunks = ((KB + S::CB - 1) / S::CB) * (SWIGLU ? 2 : 1);
-  int ns = nchunks < 2 ? 2 : (nchunks < kStages ? nchunks : kStages);
-  while (ns > 3 && (size_t)ns * S::STAGE > kRingBudget) --ns;
-  // A slice of at most eight chunks that fits the budget whole goes out in
-  // one burst (the small decode matrices: one memory round trip, not two).
-  if (nchunks > ns && nchunks <= kWholeStages && (size_t)nchunks * S::STAGE <= kRingBudget)
-    ns = nchunks;
+  int ns = nchunks < kMaxRing ? nchunks : kMaxRing;
+  if (ns < 2) ns = 2;
+  while (ns > 3 && S::smem(ns, KB) > kCtaBudget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   // Nibbles [tiles*KB blocks][32 rows x 16 B] as (64 x u64, tiles*KB); scales
