@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
                const GemvArgs a) {
   using G = Gm<TOK>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *smem = smem_align<1024>(smem_raw);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGmStages * G::Stage);
   uint64_t *empty = full + kGmStages;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kGmStages);

@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
                 const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *smem = smem_align<1024>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KB = p.K / 32;
   const int G = KB / KBS;  // stages per tile

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
   using S = Shape<MT, RW>;
   constexpr int CB = S::CB, BPL = S::BPL, U = S::U, SLICES = SI_RT / RW, NTB = S::NTB;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+  uint8_t *smem = smem_align<128>(smem_raw);
   float *T = reinterpret_cast<float *>(smem + ns * S::STAGE);            // [NTB][MT][CB][RW]
   uint64_t *bars = reinterpret_cast<uint64_t *>(T + NTB * S::TERMS);
   uint64_t *full = bars, *empty = bars + kMaxRing;                       // [ns] each
@@ -367,6 +367,26 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
+// Packed f32x2 arithmetic as explicit .rn PTX: each lane is one IEEE
+// operation with its own rounding (explicit instructions are not contracted).
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -386,7 +406,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
   // warps' start, P+2 the Q8 epilogue's warps.
   constexpr int kBarStart = P + 1, kBarEpi = P + 2;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+  uint8_t *smem = smem_align<128>(smem_raw);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + ns * S::STAGE);   // [kMmaMaxRing]
   uint64_t *empty = full + kMmaMaxRing;                                  // [kMmaMaxRing]
   volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kMmaMaxRing);
@@ -529,14 +549,24 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       for (int j = 0; j < NB; ++j) {
 #pragma unroll
         for (int wi = 0; wi < W; ++wi) {
-          const float dw[2] = {f16_to_f32((uint16_t)dwp[j][wi][0]),
-                               f16_to_f32((uint16_t)dwp[j][wi][1])};
+          // Rows (g, g+8) of one token per packed operation: the bits
+          // 0x4B400000 + d are the float 1.5*2^23 + d (|d| < 2^22), and
+          // fma(f, dw, -1.5*2^23*dw) = round(d * dw) with one rounding -- the
+          // product (float)d * dw without an int-to-float conversion, which
+          // runs on a narrow pipe.  -1.5*2^23*dw is exact (fp16 dw).
+          const float2 dw = make_float2(f16_to_f32((uint16_t)dwp[j][wi][0]),
+                                        f16_to_f32((uint16_t)dwp[j][wi][1]));
+          const float2 nk = mul2_rn(dw, make_float2(-12582912.0f, -12582912.0f));
 #pragma unroll
           for (int q = 0; q < NT; ++q)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              t[bl0 + j][wi][q][h][0] = block_term(d[j][wi][q][2 * h], dw[h], dx[j][q].x);
-              t[bl0 + j][wi][q][h][1] = block_term(d[j][wi][q][2 * h + 1], dw[h], dx[j][q].y);
+            for (int e = 0; e < 2; ++e) {
+              const float dxe = e ? dx[j][q].y : dx[j][q].x;
+              float2 f = make_float2(__int_as_float(0x4B400000 + d[j][wi][q][e]),
+                                     __int_as_float(0x4B400000 + d[j][wi][q][2 + e]));
+              f = mul2_rn(fma2_rn(f, dw, nk), make_float2(dxe, dxe));
+              t[bl0 + j][wi][q][0][e] = f.x;
+              t[bl0 + j][wi][q][1][e] = f.y;
             }
         }
         if (!SWIGLU && a.isum_out) {

@@ -12,6 +12,15 @@ namespace si {
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
+// Aligns a pointer into dynamic shared memory by pointer arithmetic on the
+// __shared__ array itself, so the compiler keeps every access derived from it
+// in the shared window (an integer round trip turns them into generic loads
+// and stores with 64-bit address arithmetic).
+template <unsigned ALIGN>
+__device__ __forceinline__ uint8_t *smem_align(uint8_t *p) {
+  const uint32_t a = smem_u32(p);
+  return p + ((ALIGN - (a & (ALIGN - 1))) & (ALIGN - 1));
+}
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -52,8 +61,11 @@ __device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false if the 2 s deadline passes or another role aborted.
+// The common case -- the phase completes within one suspended try_wait --
+// never reads the global timer.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
   if (mbar_try(bar, parity)) return true;
+  if (mbar_try_sleep(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_sleep(bar, parity)) {
     if (*abort) return false;
@@ -83,6 +95,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() {
