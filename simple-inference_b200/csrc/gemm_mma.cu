@@ -15,9 +15,11 @@
 // returns the block's exact 16*isum for 16 rows x 8 tokens.  The terms are
 // formed and added at once, block by block, so every output is the
 // reference's serial chain and bit-identical to the GEMV and to matvec_q4q8:
-//   f = float(0x4B400000 + 16*isum) = 1.5*2^23 + 16*isum (exact),
+//   f = float(0x4B400000 + 16*isum) = 1.5*2^23 + 16*isum (exact; the mma's
+//       accumulator input adds the 0x4B400000),
 //   fma(f, dw/16, -1.5*2^23*dw/16) = round(isum*dw) (both addends exact),
-//   * dx (packed .rn multiply), then one scalar add per output.
+//   * dx (packed .rn operations over the lane's token pair, each half one
+//   IEEE operation), then one scalar add per output.
 // A producer warp streams 8-block chunks through a three-stage ring with one
 // mbarrier per stage (2-D TMA loads: the four row tiles' nibbles and scales,
 // the activations as two 128-byte-swizzled boxes -- the B-fragment loads of
@@ -54,12 +56,19 @@ struct Gm {
   static_assert(Smem * MinBlocks <= 228 * 1024, "shared memory");
 };
 
+// The accumulator input is the integer 0x4B400000, so each result is
+// 0x4B400000 + 16*isum: the bit pattern of the float 1.5*2^23 + 16*isum.
 __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0x4B400000));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
 }
 // Packed .rn arithmetic: each half is one IEEE operation with its own
 // rounding, and explicit instructions are never contracted.
@@ -163,14 +172,13 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
   const int tok0 = th * 64;                  // first token of this warp within the CTA
   // Output row of this lane's accumulators (h = 0: row g, h = 1: row g + 8).
   const int row = (rt0 + (SWIGLU ? (tsel & 1) : tsel)) * SI_RT + hrow + g;
-  float acc[8][2][2];  // [n-tile][row half][token of the pair]
+  float2 acc[8][2];  // [n-tile][row half]: the lane's token pair
 #pragma unroll
   for (int j = 0; j < 8; ++j)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const float b = (!SWIGLU && a.bias) ? a.bias[row + 8 * h] : 0.0f;
-      acc[j][h][0] = b;
-      acc[j][h][1] = b;
+      acc[j][h] = make_float2(b, b);
     }
   const float kMagic = 12582912.0f;  // 1.5 * 2^23
   bool ok = true;
@@ -198,33 +206,37 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
         const float2 nca = make_float2(-kMagic * dw0, -kMagic * dw0);
         const float2 ncb = make_float2(-kMagic * dw1, -kMagic * dw1);
         // Activation rows: token t's block bl is 32 bytes in box bl / 4, its two
-        // 16-byte chunks 2*(bl % 4) and +1 swizzled by t & 7 (== g here).
-        const uint8_t *abox = st + (bl >> 2) * G::Act;
-        const int ch0 = ((2 * (bl & 3)) ^ g) << 4, ch1 = ((2 * (bl & 3) + 1) ^ g) << 4;
+        // 16-byte chunks 2*(bl % 4) and +1 swizzled by t & 7.  One ldmatrix.x4
+        // gives the B fragments of two n-tiles: this lane addresses token
+        // tok0 + 8*(j + (lane >> 4)) + (lane & 7), chunk 2*(bl % 4) + ((lane >> 3) & 1).
+        const uint32_t bbase =
+            smem_u32(st + (bl >> 2) * G::Act) +
+            (uint32_t)((tok0 + 8 * (lane >> 4) + (lane & 7)) * 128 +
+                       (((2 * (bl & 3) + ((lane >> 3) & 1)) ^ (lane & 7)) << 4));
 #pragma unroll
         for (int j0 = 0; j0 < 8; j0 += 4) {  // four n-tiles' mmas in flight, then their terms
         int d[4][4];
 #pragma unroll
-        for (int j = j0; j < j0 + 4; ++j) {
-          const uint8_t *ar = abox + (tok0 + 8 * j + g) * 128;
-          const uint32_t b0 = *reinterpret_cast<const uint32_t *>(ar + ch0 + 4 * c);
-          const uint32_t b1 = *reinterpret_cast<const uint32_t *>(ar + ch1 + 4 * c);
-          mma_s8(d[j - j0], a0, a1, a2, a3, b0, b1);
+        for (int j = j0; j < j0 + 4; j += 2) {
+          uint32_t b[4];
+          ldsm_x4(b, bbase + j * 8 * 128);
+          mma_s8(d[j - j0], a0, a1, a2, a3, b[0], b[1]);
+          mma_s8(d[j + 1 - j0], a0, a1, a2, a3, b[2], b[3]);
         }
 #pragma unroll
         for (int j = j0; j < j0 + 4; ++j) {
           const float2 dx = *reinterpret_cast<const float2 *>(dxs + bl * TOK + tok0 + 8 * j + 2 * c);
           const int *dj = d[j - j0];
-          const float2 fa = make_float2(__int_as_float(0x4B400000 + dj[0]),
-                                        __int_as_float(0x4B400000 + dj[1]));
-          const float2 fbv = make_float2(__int_as_float(0x4B400000 + dj[2]),
-                                         __int_as_float(0x4B400000 + dj[3]));
+          const float2 fa = make_float2(__int_as_float(dj[0]), __int_as_float(dj[1]));
+          const float2 fbv = make_float2(__int_as_float(dj[2]), __int_as_float(dj[3]));
+          // The running sums stay scalar adds: ptxas contracts a packed
+          // multiply feeding a packed add into one fused operation.
           const float2 ta = mul2_rn(fma2_rn(fa, dwa, nca), dx);
           const float2 tb = mul2_rn(fma2_rn(fbv, dwb, ncb), dx);
-          acc[j][0][0] = __fadd_rn(acc[j][0][0], ta.x);
-          acc[j][0][1] = __fadd_rn(acc[j][0][1], ta.y);
-          acc[j][1][0] = __fadd_rn(acc[j][1][0], tb.x);
-          acc[j][1][1] = __fadd_rn(acc[j][1][1], tb.y);
+          acc[j][0].x = __fadd_rn(acc[j][0].x, ta.x);
+          acc[j][0].y = __fadd_rn(acc[j][0].y, ta.y);
+          acc[j][1].x = __fadd_rn(acc[j][1].x, tb.x);
+          acc[j][1].y = __fadd_rn(acc[j][1].y, tb.y);
         }
         }
             };
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const size_t o = (size_t)(m0 + tl) * a.N + row + 8 * h;
-          float v = acc[j][h][e];
+          float v = e ? acc[j][h].y : acc[j][h].x;
           if (a.resid) v = __fadd_rn(a.resid[o], v);
           a.out[o] = v;
         }
@@ -280,7 +292,7 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int e = 0; e < 2; ++e)
-          gs[(rl + 8 * h) * TOK + tok0 + 8 * j + 2 * c + e] = acc[j][h][e];
+          gs[(rl + 8 * h) * TOK + tok0 + 8 * j + 2 * c + e] = e ? acc[j][h].y : acc[j][h].x;
   }
   asm volatile("bar.sync %0, %1;" ::"r"(kBar), "r"(kBarN) : "memory");
   float act[8][2][2];
@@ -293,7 +305,7 @@ __global__ void __launch_bounds__(Gm<TOK>::Threads, Gm<TOK>::MinBlocks)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const float gv = gs[(rl + 8 * h) * TOK + tok0 + 8 * j + 2 * c + e];
-          act[j][h][e] = silu_mul(gv, acc[j][h][e]);
+          act[j][h][e] = silu_mul(gv, e ? acc[j][h].y : acc[j][h].x);
           m = max(m, __float_as_uint(fabsf(act[j][h][e])));
         }
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 4));

@@ -360,12 +360,15 @@ struct MmaShape {
   static_assert(NIB % 128 == 0 && WS % 128 == 0 && STAGE % 128 == 0, "TMA destinations");
 };
 
+// The accumulator input is the integer 0x4B400000, so each result is
+// 0x4B400000 + 16*isum: the bit pattern of the float 1.5*2^23 + 16*isum.
+constexpr int kMagicBits = 0x4B400000;
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                              uint32_t a3, uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%10,%10,%10,%10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(kMagicBits));
 }
 // Packed f32x2 arithmetic as explicit .rn PTX: each lane is one IEEE
 // operation with its own rounding (explicit instructions are not contracted).
@@ -549,11 +552,12 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       for (int j = 0; j < NB; ++j) {
 #pragma unroll
         for (int wi = 0; wi < W; ++wi) {
-          // Rows (g, g+8) of one token per packed operation: the bits
-          // 0x4B400000 + d are the float 1.5*2^23 + d (|d| < 2^22), and
-          // fma(f, dw, -1.5*2^23*dw) = round(d * dw) with one rounding -- the
-          // product (float)d * dw without an int-to-float conversion, which
-          // runs on a narrow pipe.  -1.5*2^23*dw is exact (fp16 dw).
+          // Rows (g, g+8) of one token per packed operation: the mma result
+          // 0x4B400000 + d (d = 16*isum) is the float 1.5*2^23 + d (|d| <
+          // 2^22), and fma(f, dw, -1.5*2^23*dw) = round(d * dw) with one
+          // rounding -- the product (float)d * dw without an int-to-float
+          // conversion, which runs on a narrow pipe.  -1.5*2^23*dw is exact
+          // (fp16 dw).
           const float2 dw = make_float2(f16_to_f32((uint16_t)dwp[j][wi][0]),
                                         f16_to_f32((uint16_t)dwp[j][wi][1]));
           const float2 nk = mul2_rn(dw, make_float2(-12582912.0f, -12582912.0f));
@@ -562,8 +566,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const float dxe = e ? dx[j][q].y : dx[j][q].x;
-              float2 f = make_float2(__int_as_float(0x4B400000 + d[j][wi][q][e]),
-                                     __int_as_float(0x4B400000 + d[j][wi][q][2 + e]));
+              float2 f = make_float2(__int_as_float(d[j][wi][q][e]),
+                                     __int_as_float(d[j][wi][q][2 + e]));
               f = mul2_rn(fma2_rn(f, dw, nk), make_float2(dxe, dxe));
               t[bl0 + j][wi][q][0][e] = f.x;
               t[bl0 + j][wi][q][1][e] = f.y;
@@ -580,7 +584,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
                 const int tok = 8 * q + 2 * c + e;
                 if (tok < mcount)
                   a.isum_out[((size_t)(m0 + tok) * a.N + r0 + 8 * h) * KB + bx] =
-                      d[j][0][q][2 * h + e] >> 4;
+                      (d[j][0][q][2 * h + e] - kMagicBits) >> 4;
               }
         }
       }
