@@ -20,19 +20,18 @@
 // The kernel is persistent (one CTA per SM, tiles visited token-tile fastest)
 // so the TMA / unpack / MMA / epilogue pipeline never drains between tiles.
 //
-// Warp roles (384 threads):
+// Warp roles (640 threads):
 //   warp 0      TMA producer: packed Q4 nibbles and their fp16 scales, int8
 //               activations (128-byte swizzle) and the stage's fp32
 //               activation scales
 //   warp 1      TMEM allocation; lane 0 issues the MMAs, one commit per stage
 //   warps 2-3   nibble unpack: Q4 -> signed int8 in the 128B-swizzled K-major
 //               layout the MMA reads (byte = 16*(q-8), so sums are 16*isum)
-//   warps 4-11  epilogue (2 per TMEM lane quarter, 64 columns each, read in
-//               double-buffered 32-column chunks): TMEM -> registers, rescale,
+//   warps 4-19  epilogue (4 per TMEM lane quarter, 32 columns each, read in
+//               double-buffered 8-column chunks): TMEM -> registers, rescale,
 //               accumulate, re-arm, store
 // Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  The
-// epilogue hands each accumulator back to the MMA issuer through a shared-
-// memory release counter instead of an mbarrier round trip.  Every wait is
+// epilogue hands each accumulator back to the MMA issuer on an mbarrier.  Every wait is
 // bounded (about 2 s); on expiry the kernel records SI_ERR_TIMEOUT in the
 // context's error word, stops all roles, frees its TMEM and returns.
 #include <cuda.h>
@@ -51,7 +50,7 @@ constexpr int KBS = 4;                    // blocks per stage
 constexpr int STAGES = 4;
 constexpr int NACC = 4;                   // TMEM accumulators (= blocks per stage)
 constexpr uint32_t TMEM_COLS = NACC * BN; // 512
-constexpr int EPI_WARP0 = 4, EPI_WARPS = 8;
+constexpr int EPI_WARP0 = 4, EPI_WARPS = 16;
 constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
 constexpr uint32_t kMagic = 0x4B400000u;  // bits of 12582912.0f = 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
@@ -70,7 +69,7 @@ constexpr int XCHG_BYTES = 64 * BN * 4;      // SwiGLU up-row hand-off, 32 KB
 constexpr int OFF_SW = OFF_DX + STAGES * DX_BYTES;
 constexpr int OFF_XCHG = OFF_SW + STAGES * SW_BYTES;
 constexpr int OFF_BAR = OFF_XCHG + XCHG_BYTES;
-constexpr int NBAR = 4 * STAGES + 2 * NACC;
+constexpr int NBAR = 4 * STAGES + 2 * NACC + NACC;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
 
@@ -90,31 +89,6 @@ struct Params {
 // ---------------------------------------------------------------------------
 // PTX helpers
 // ---------------------------------------------------------------------------
-// Release / acquire on a shared-memory counter: the cheap path for the
-// epilogue -> MMA "accumulator free" signal (a plain load to spin on).
-__device__ __forceinline__ void smem_add_release(int *p, int v) {
-  asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
-               : "memory");
-}
-__device__ __forceinline__ int smem_ld_acquire(const int *p) {
-  int v;
-  asm volatile("ld.acquire.cta.shared::cta.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
-__device__ __forceinline__ bool counter_wait(const int *p, int target, volatile int *abort) {
-  if (smem_ld_acquire(p) >= target) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    // Back off between polls: the poller shares its SM sub-partition with two
-    // epilogue warps, and a hot spin would take a third of their issue slots.
-    __nanosleep(32);
-    if (smem_ld_acquire(p) >= target) return true;
-    if ((i & 1023) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > 2000000000ull) return false;
-    }
-  }
-}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
                                             int c2, int c3, uint32_t bar) {
   asm volatile(
@@ -190,9 +164,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 template <int CW>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[CW]) {
-  if constexpr (CW == 16) tmem_ld16(taddr, r);
+  if constexpr (CW == 8) tmem_ld8(taddr, r);
+  else if constexpr (CW == 16) tmem_ld16(taddr, r);
   else tmem_ld32(taddr, r);
 }
 // 32 columns of this warp's 32 lanes all set to one value, as four 8-column
@@ -250,7 +231,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // ---------------------------------------------------------------------------
 // Columns per epilogue warp: the 4 TMEM lane quarters x (EPI_WARPS / 4) slices.
 constexpr int NC = BN * 4 / EPI_WARPS;
-constexpr int CW = 16;        // columns per TMEM load chunk
+constexpr int CW = 8;         // columns per TMEM load chunk
 constexpr int NCH = NC / CW;  // chunks per block
 static_assert(NCH >= 2 && NCH % 2 == 0, "chunk double-buffering needs an even chunk count");
 
@@ -296,14 +277,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   // stage_empty: the MMAs of the stage finished; dx_empty: the epilogue used
   // the stage's scales; acc_full[h]: accumulators 2h and 2h+1 of a stage
   // written (two commits per stage, so the epilogue starting a stage never
-  // waits on the MMA that the release of its last accumulator unblocks).  The epilogue frees each accumulator through a
-  // shared counter (acc_cnt[j] = EPI_WARPS x uses released), which the MMA
-  // thread spins on with plain loads.
+  // waits on the MMA that the release of its last accumulator unblocks);
+  // acc_empty[j]: every epilogue warp re-armed accumulator j (the MMA thread
+  // sleeps in try_wait rather than polling, so no issue slots go to waiting).
   const int B_TMA = 0, B_AREADY = STAGES, B_SEMPTY = 2 * STAGES, B_DXEMPTY = 3 * STAGES,
-            B_ACCFULL = 4 * STAGES;
+            B_ACCFULL = 4 * STAGES, B_ACCEMPTY = 4 * STAGES + 2 * NACC;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC + 16);
-  int *acc_cnt = reinterpret_cast<int *>(smem + OFF_MISC + 32);  // [NACC]
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -314,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(bar(B_ACCFULL), 1);
     mbar_init(bar(B_ACCFULL + 1), 1);
-    for (int j = 0; j < NACC; ++j) acc_cnt[j] = 0;
+    for (int j = 0; j < NACC; ++j) mbar_init(bar(B_ACCEMPTY + j), EPI_WARPS);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -385,7 +365,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int j = 0; j < KBS && ok; ++j) {
             // Use number `it` of accumulator j needs the epilogue to have
             // (re)armed it with the magic constant it+1 times (each of its warps).
-            if (!counter_wait(&acc_cnt[j], EPI_WARPS * (it + 1), abort_flag)) {
+            if (!mbar_wait(bar(B_ACCEMPTY + j), it & 1, abort_flag)) {
               ok = false;
               break;
             }
@@ -453,7 +433,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
-      for (int j = 0; j < NACC; ++j) smem_add_release(&acc_cnt[j], 1);
+      for (int j = 0; j < NACC; ++j) mbar_arrive(bar(B_ACCEMPTY + j));
     float *xchg = reinterpret_cast<float *>(smem + OFF_XCHG);  // [64 rows][BN]
     int pending = -1;  // accumulator re-armed but not yet handed back to the MMA
     int it = 0;
@@ -505,7 +485,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               tmem_wait_st();
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) smem_add_release(&acc_cnt[pending], 1);
+              if (lane == 0) mbar_arrive(bar(B_ACCEMPTY + pending));
             }
 #pragma unroll
             for (int f = 0; f < NC / 32; ++f) tmem_fill32(ta + 32 * f, kMagic);
