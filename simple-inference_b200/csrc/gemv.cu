@@ -7,17 +7,22 @@
 // Mapping.  One CTA owns an RW-row slice (32, 16 or 8 rows) of one 32-row
 // tile of the SoA layout and the whole K range, for up to MT tokens; narrow
 // slices give matrices with few tiles enough CTAs to fill the GPU.  The slice
-// streams through a shared-memory ring of up to 8 chunks of CB blocks: one
-// thread issues three 2-D TMA loads per chunk (nibbles RW*16 B x CB, their
-// fp16 scales, the int8 activations of the chunk's blocks) on the stage's
-// mbarrier, so the ring keeps all but one of its chunks in flight for the cost
-// of a few instructions.  Eight compute warps take the chunk's (row, block) pieces and
-// compute the terms in parallel: the int32 block sums are exact and each term
-// ((float)isum*dw)*dx is rounded exactly as the reference rounds it.  The
-// terms go to shared memory, where dedicated merge warps -- one thread per
-// (token, row) -- add them to the running sums in block order while the
-// compute warps go on to the next chunk.  The result is bit-identical to the
-// reference's serial loop.
+// streams through a shared-memory ring of up to 8 chunks of CB blocks: a
+// producer thread issues three 2-D TMA loads per chunk (nibbles RW*16 B x CB,
+// their fp16 scales, the int8 activations of the chunk's blocks) on the
+// stage's full mbarrier and refills a stage as soon as its empty mbarrier says
+// the compute warps are done with it.  Eight compute warps take the chunk's
+// (row, block) pieces and compute the terms in parallel: the int32 block sums
+// are exact and each term ((float)isum*dw)*dx is rounded exactly as the
+// reference rounds it.  The terms go to term buffers in shared memory, where
+// dedicated merge warps -- one thread per (token, row) -- add them to the
+// running sums in block order, each buffer handed over on its own pair of
+// mbarriers, so loads, terms and adds of neighbouring chunks overlap.  The
+// result is bit-identical to the reference's serial loop.
+//
+// For small token counts this kernel is HBM-bound: at one token the 72B down
+// projection (136 MB of weights) streams at about 90 % of the measured copy
+// bandwidth.
 //
 // SwiGLU mode streams the gate rows and then the up rows of the same slice
 // through the ring, then forms act = silu(g) * u and quantises it to Q8_0

@@ -89,37 +89,4 @@ __device__ __forceinline__ int8_t q8_lane(float x, uint16_t &d16) {
 __device__ __forceinline__ int lo_nib_s8x16(uint32_t w) { return (int)((w << 4) & 0xF0F0F0F0u); }
 __device__ __forceinline__ int hi_nib_s8x16(uint32_t w) { return (int)(w & 0xF0F0F0F0u); }
 
-// 16 bytes of one Q4_0 block (elements j | j+16 per byte) against 32 int8
-// activations: returns the exact int32 block sum of qwen_one_layer.c:137-144.
-__device__ __forceinline__ int block_isum(const uint4 w, const int4 a0, const int4 a1) {
-  int acc = 0;
-  acc = __dp4a(lo_nib_s8x16(w.x), a0.x, acc);
-  acc = __dp4a(lo_nib_s8x16(w.y), a0.y, acc);
-  acc = __dp4a(lo_nib_s8x16(w.z), a0.z, acc);
-  acc = __dp4a(lo_nib_s8x16(w.w), a0.w, acc);
-  acc = __dp4a(hi_nib_s8x16(w.x), a1.x, acc);
-  acc = __dp4a(hi_nib_s8x16(w.y), a1.y, acc);
-  acc = __dp4a(hi_nib_s8x16(w.z), a1.z, acc);
-  acc = __dp4a(hi_nib_s8x16(w.w), a1.w, acc);
-  return acc >> 4;
-}
-
-// The same sum with the nibbles unpacked once (lo[i] = lo_nib_s8x16(w_i),
-// hi[i] = hi_nib_s8x16(w_i)), for reuse across tokens.
-// Four independent partial sums (integer addition is exact in any order), so
-// the eight dp4a form two-deep chains instead of one eight-deep chain.
-__device__ __forceinline__ int block_isum_unpacked(const int (&lo)[4], const int (&hi)[4],
-                                                   const int4 a0, const int4 a1) {
-  const int s0 = __dp4a(hi[0], a1.x, __dp4a(lo[0], a0.x, 0));
-  const int s1 = __dp4a(hi[1], a1.y, __dp4a(lo[1], a0.y, 0));
-  const int s2 = __dp4a(hi[2], a1.z, __dp4a(lo[2], a0.z, 0));
-  const int s3 = __dp4a(hi[3], a1.w, __dp4a(lo[3], a0.w, 0));
-  return ((s0 + s1) + (s2 + s3)) >> 4;
-}
-
-// ((float)isum * dw) * dx with the reference's two roundings (qwen_one_layer.c:158).
-__device__ __forceinline__ float block_term(int isum, float dw, float dx) {
-  return __fmul_rn(__fmul_rn((float)isum, dw), dx);
-}
-
 }  // namespace si
