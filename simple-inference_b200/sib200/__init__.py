@@ -261,6 +261,13 @@ class Context:
               "si_layer_upload")
         return Layer(self, h, dims)
 
+    def layer_gguf(self, path: str, layer: int, mlp: bool = True) -> "Layer":
+        """Decoder layer `layer` of a Qwen2 GGUF file (Q4_0 matrices, F32/F16
+        vectors), dimensions from the file's metadata; see sib200.gguf."""
+        from . import gguf
+        dims, host = gguf.layer_host(path, layer, mlp=mlp)
+        return self.layer(dims, host)
+
     def layer_synth(self, dims: dict, seed: int) -> "Layer":
         dm = Dims.of(dims)
         h = C.c_void_p()
