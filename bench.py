@@ -220,6 +220,46 @@ DIMS_7B = dict(hidden=3584, n_q_heads=28, n_kv_heads=4, head_dim=128, intermedia
                rope_theta=1e6, rms_eps=1e-6)
 
 
+def decode_gemv_roofline(ctx, torch, stream, max_over_ranks):
+    """Kernel-level decode roofline where the GEMV is HBM-bound.  The config-1
+    matrices (1.3-15.5 MB) are too small for that -- launch and first-byte
+    latency dominate them -- so this times the 72B down projection (8192 x
+    29568, 136 MB of Q4_0 weights) at 1 token (dp4a form) and at 8 tokens
+    (tensor-core form, config 4's decode batch), and the 7B down projection
+    (3584 x 18944, config 2) at 1 token.  Weight copies rotate (272-305 MB,
+    more than twice L2) so every launch streams from HBM; launches are CUDA
+    graph replays timed with CUDA events on the library's stream."""
+    pk = peaks()
+    out = {}
+    for label, N, K, M, ncopy in (("72B down, 1 token", 8192, 29568, 1, 2),
+                                  ("72B down, 8 tokens", 8192, 29568, 8, 2),
+                                  ("7B down, 1 token", 3584, 18944, 1, 8)):
+        mats = [ctx.matrix_synth(N, K, seed=90 + i) for i in range(ncopy)]
+        x = torch.randn(M, K, device="cuda")
+        qs = torch.empty(M * K, dtype=torch.int8, device="cuda")
+        d = torch.empty(M * K // 32, dtype=torch.int16, device="cuda")
+        y = torch.empty(M * N, device="cuda")
+        torch.cuda.synchronize()
+        ctx.q8_quantize(x, M, K, qs, d)
+        ctx.sync()
+        g = ctx.capture(lambda: [ctx.matmul(m, qs, d, M, None, y) for m in mats])
+        for _ in range(3):
+            g.launch()
+        reps = 20
+        t = max_over_ranks(time_region(torch, stream, lambda i: g.launch(), reps)) / (reps * ncopy)
+        wb = N * K * 18 // 32
+        out[label] = {"kernel": "k_gemv (dp4a form)" if M <= 2 else "k_gemv_mma (tensor-core form)",
+                      "shape": f"{N}x{K}", "tokens": M, "us": round(t * 1e6, 2),
+                      "weight_bytes": wb, "achieved_gbs": round(wb / t / 1e9, 1),
+                      "peak_gbs": pk["hbm_gbs"], "peak_src": pk["src"],
+                      "frac": round(wb / t / 1e9 / pk["hbm_gbs"], 4)}
+        g.free()
+        for m in mats:
+            m.free()
+        del x, qs, d, y
+    return out
+
+
 def run_layers_7b(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
     """BASELINE configs 2 and 3 on each rank (replicas): one Qwen2.5-7B layer.
     Config 2: a 2048-token prefill (fp16 KV), then 128 sequential decode steps
@@ -566,6 +606,12 @@ def run_ours(args, rank, world, local_rank):
     log("configs 2 and 3")
     result.update(run_layers_7b(args, rank, world, ctx, torch, barrier_sync, max_over_ranks))
     log(f"configs 2/3 {result['config2']} {result['config3']}")
+    try:
+        result["decode_gemv_roofline"] = decode_gemv_roofline(ctx, torch, stream, max_over_ranks)
+        log(f"decode GEMV roofline {result['decode_gemv_roofline']}")
+    except Exception as exc:  # a failed extra measurement must not lose the bench line
+        result["decode_gemv_roofline"] = {"error": str(exc)[:200]}
+        log(f"decode GEMV roofline failed: {exc}")
     if not args.no_tp:
         log("tp config 4")
         result["tp_config4"] = run_tp_config4(args, rank, world, ctx, torch, barrier_sync,
