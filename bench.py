@@ -260,6 +260,97 @@ def decode_gemv_roofline(ctx, torch, stream, max_over_ranks):
     return out
 
 
+def reference_layer_decode(ctx, torch, stream, n_tokens=32, context0=512):
+    """The reference's own workload, apples to apples: its attention layer
+    (RMSNorm, QKV + bias, RoPE, fp16 KV append, flash attention, o-projection;
+    qwen_one_layer.c:237-281) at its compiled 1.5B dims, decoding n_tokens
+    after a context0-position fp16 history.  Timed three ways: the reference's
+    run_layer on one host core; this library's drop-in run_layer (host
+    buffers, si_ref_run_layer: the call a reference caller makes); and the
+    device-resident decode step (si_decode_step_dev, CUDA events).  Reports
+    the largest output difference against the reference, over the outputs'
+    largest magnitude."""
+    import ctypes as C
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import sib200
+    from sib200 import synth
+    dims = dict(hidden=1536, n_q_heads=12, n_kv_heads=2, head_dim=128, intermediate=0,
+                rope_theta=1e6, rms_eps=1e-6)
+    H, KVD, L = 1536, 256, context0 + n_tokens
+    rng = np.random.default_rng(5)
+    layer = synth.random_layer(dims, 5, mlp=False)
+    kc0 = (rng.standard_normal(L * KVD) * 0.5).astype(np.float16).view(np.uint16)
+    vc0 = (rng.standard_normal(L * KVD) * 0.5).astype(np.float16).view(np.uint16)
+    xs = rng.standard_normal((n_tokens, H)).astype(np.float32)
+    ctxs = [context0 + i + 1 for i in range(n_tokens)]
+    res = {"workload": f"reference attention layer (1536 hidden, 12 Q / 2 KV heads, fp16 KV), "
+                       f"{n_tokens} decode steps after {context0} positions",
+           "tokens": n_tokens}
+
+    # The reference on the host (single-threaded, as it is written).
+    ys_ref = None
+    if os.path.exists(oracle.LIB_REF):
+        ref = oracle.Reference()
+        kr, vr = kc0.copy(), vc0.copy()
+        ys_ref = np.zeros((n_tokens, H), np.float32)
+        t0 = time.perf_counter()
+        for i in range(n_tokens):
+            ys_ref[i] = ref.run_layer(layer, xs[i], kr, vr, ctxs[i])[0]
+        res["reference_host_us_per_token"] = round((time.perf_counter() - t0) / n_tokens * 1e6, 1)
+        res["reference_cores"] = 1
+
+    # This library's drop-in run_layer: host weights (cached on the device by
+    # address), host KV, host x and y per call.
+    class LayerT(C.Structure):
+        _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "norm", "bq", "bk", "bv")]
+
+    class PhaseT(C.Structure):
+        _fields_ = [(n, C.c_float) for n in ("rms", "q8_input", "q_proj", "k_proj", "v_proj",
+                                             "rope_cache", "attention", "q8_output", "out_proj")]
+    Lb = ctx.L
+    Lb.si_ref_run_layer.restype = PhaseT
+    Lb.si_ref_run_layer.argtypes = ([C.c_void_p] * 4 + [C.c_int, C.c_void_p, C.c_int] +
+                                    [C.c_void_p] * 3 + [C.c_int] * 4 + [C.c_float] * 2)
+    lt = LayerT(*[layer[k].ctypes.data for k in ("wq", "wk", "wv", "wo", "norm", "bq", "bk", "bv")])
+    kd, vd = kc0.copy(), vc0.copy()
+    y = np.zeros(H, np.float32)
+    ys_drop = np.zeros((n_tokens, H), np.float32)
+    call = lambda i: Lb.si_ref_run_layer(C.addressof(lt), xs[i].ctypes.data, kd.ctypes.data,
+                                         vd.ctypes.data, ctxs[i], y.ctypes.data, 1, None, None,
+                                         None, H, 12, 2, 128, 1e6, 1e-6)
+    call(0)  # uploads and caches the weights
+    kd[:], vd[:] = kc0, vc0
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        call(i)
+        ys_drop[i] = y
+    res["dropin_run_layer_us_per_token"] = round((time.perf_counter() - t0) / n_tokens * 1e6, 1)
+    for k in ("wq", "wk", "wv", "wo"):
+        Lb.si_forget_host_weights(layer[k].ctypes.data)
+
+    # Device-resident decode of the same layer.
+    gl = ctx.layer(dims, layer)
+    kv = ctx.kv(dims, 1, L, False)
+    kv.write(0, 0, kc0[: context0 * KVD].reshape(context0, KVD),
+             vc0[: context0 * KVD].reshape(context0, KVD))
+    xd = torch.from_numpy(xs).cuda()
+    yd = torch.zeros_like(xd)
+    torch.cuda.synchronize()
+    t = time_region(torch, stream, lambda i: gl.decode_dev(kv, xd[i], [ctxs[i]], yd[i],
+                                                           sib200.SI_LAYER_ATTN), n_tokens)
+    res["device_us_per_token"] = round(t / n_tokens * 1e6, 2)
+    ys_dev = yd.cpu().numpy()
+    if ys_ref is not None:
+        scale = float(np.abs(ys_ref).max())
+        res["max_err_vs_reference"] = {
+            "dropin": float(np.abs(ys_drop - ys_ref).max() / scale),
+            "device": float(np.abs(ys_dev - ys_ref).max() / scale)}
+    kv.free()
+    gl.free()
+    return res
+
+
 def run_layers_7b(args, rank, world, ctx, torch, barrier_sync, max_over_ranks):
     """BASELINE configs 2 and 3 on each rank (replicas): one Qwen2.5-7B layer.
     Config 2: a 2048-token prefill (fp16 KV), then 128 sequential decode steps
@@ -612,6 +703,13 @@ def run_ours(args, rank, world, local_rank):
     except Exception as exc:  # a failed extra measurement must not lose the bench line
         result["decode_gemv_roofline"] = {"error": str(exc)[:200]}
         log(f"decode GEMV roofline failed: {exc}")
+    if rank == 0:
+        try:
+            result["reference_layer"] = reference_layer_decode(ctx, torch, stream)
+            log(f"reference layer {result['reference_layer']}")
+        except Exception as exc:  # a failed extra measurement must not lose the bench line
+            result["reference_layer"] = {"error": str(exc)[:200]}
+            log(f"reference layer failed: {exc}")
     if not args.no_tp:
         log("tp config 4")
         result["tp_config4"] = run_tp_config4(args, rank, world, ctx, torch, barrier_sync,
