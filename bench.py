@@ -15,7 +15,13 @@ of the whole set over M tokens of synthetic activations.
 * decode = the same set at M = 1 (microseconds per token) in `decode`;
 * roofline: the dominant kernel's algorithmic throughput against MEASURED_PEAKS.json;
 * cpu_baseline: the reference's own matvec_q4q8/quantize_q8 (oracle/_ref when built
-  here, else the oracle restatement) on the host cores, on a bounded token sample.
+  here, else the oracle restatement) on the host cores, on a bounded token sample;
+* config2 / config3 / tp_config4: the other BASELINE configurations' layer steps;
+* decode_gemv_roofline: the decode GEMV at shapes where it is HBM-bound (72B and
+  7B down projections, 1 and 8 tokens) against the measured HBM bandwidth;
+* reference_layer: the reference's own attention layer (1.5B dims, fp16 KV)
+  timed as its run_layer on one host core, this library's drop-in run_layer
+  and the device decode step, with the error against the reference.
 
 Weights are seeded synthetic Q4_0 (N(0, 0.02)); ten weight copies (263 MB, over
 twice the 126 MB L2) are rotated across steps so every step streams from HBM.
