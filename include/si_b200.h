@@ -180,6 +180,10 @@ SI_API si_status si_ctx_synchronize(si_ctx *ctx);
 /* Synchronises, then returns and clears the device error word. */
 SI_API si_status si_ctx_status(si_ctx *ctx);
 SI_API void *si_ctx_stream(si_ctx *ctx); /* the cudaStream_t all work is queued on */
+/* Bytes of device memory the context currently holds in its on-demand
+ * buffers (step arena, index arrays, GEMM activation-scale scratch); they grow
+ * when a call needs more and are freed by si_ctx_destroy. */
+SI_API size_t si_ctx_scratch_bytes(const si_ctx *ctx);
 SI_API const char *si_last_error(void);  /* message of the last failing call on this thread */
 
 /* Weight matrices.  Upload GGUF Q4_0 rows and repack on the device into the

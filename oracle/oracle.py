@@ -29,6 +29,14 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
 
 
+def reference_dir():
+    """The reference checkout: $SI_REFERENCE_DIR, else a checkout named
+    `reference` beside this repository; None when neither exists."""
+    cand = os.environ.get("SI_REFERENCE_DIR") or os.path.join(HERE, "..", "..", "reference")
+    cand = os.path.abspath(cand)
+    return cand if os.path.exists(os.path.join(cand, "qwen_one_layer.c")) else None
+
+
 def build(quiet: bool = True) -> None:
     """Compile oracle/liboracle.so (and oracle/_ref when the reference exists)."""
     out = subprocess.run(["make", "-C", HERE, "all"], capture_output=True, text=True)

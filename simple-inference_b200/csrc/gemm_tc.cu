@@ -665,9 +665,11 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
     tmS2 = tmS;
   }
 
-  static int sms = 0;
-  if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess)
-    sms = 148;
+  // SM count of the device this launch targets (the caller made it current).
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return cudaErrorInvalidDevice;
   Params p{};
   p.N = a.N; p.K = a.K; p.M = a.M;
   p.scl = a.scl; p.scl2 = a.scl2; p.bias = a.bias; p.resid = a.resid;

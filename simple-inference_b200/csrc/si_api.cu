@@ -309,6 +309,9 @@ extern "C" SI_API si_status si_ctx_status(si_ctx *ctx) {
 }
 
 extern "C" SI_API void *si_ctx_stream(si_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+extern "C" SI_API size_t si_ctx_scratch_bytes(const si_ctx *ctx) {
+  return ctx ? ctx->work.bytes + ctx->idx.bytes + ctx->gemm.bytes : 0;
+}
 
 // ----------------------------------------------------------------------------
 // CUDA graphs
@@ -1366,7 +1369,8 @@ extern "C" SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, cons
   SI_CHECK(kv && q && out && ctx_lens && batch > 0 && batch <= kv->batch, "bad arguments");
   int max_len = 0;
   for (int i = 0; i < batch; ++i) {
-    SI_CHECK(ctx_lens[i] >= 0 && ctx_lens[i] <= kv->max_ctx, "context out of range");
+    SI_CHECK(ctx_lens[i] >= 1 && ctx_lens[i] <= kv->max_ctx, "context length %d out of range [1, %d]",
+             ctx_lens[i], kv->max_ctx);
     max_len = ctx_lens[i] > max_len ? ctx_lens[i] : max_len;
   }
   const int nsplit = si::attn_pick_splits(batch, true, max_len);

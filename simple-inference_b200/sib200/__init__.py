@@ -79,6 +79,7 @@ def lib() -> C.CDLL:
         "si_ctx_synchronize": (i32, [vp]),
         "si_ctx_status": (i32, [vp]),
         "si_ctx_stream": (vp, [vp]),
+        "si_ctx_scratch_bytes": (C.c_size_t, [vp]),
         "si_matrix_upload": (i32, [vp, vp, i32, i32, pp]),
         "si_matrix_upload_dev": (i32, [vp, vp, i32, i32, pp]),
         "si_matrix_synth": (i32, [vp, i32, i32, u64, f32, pp]),
@@ -188,6 +189,10 @@ class Context:
 
     def sync(self):
         check(self.L.si_ctx_synchronize(self.h), "si_ctx_synchronize")
+
+    def scratch_bytes(self) -> int:
+        """Device bytes held by the context's on-demand buffers."""
+        return int(self.L.si_ctx_scratch_bytes(self.h))
 
     def status(self):
         check(self.L.si_ctx_status(self.h), "si_ctx_status")

@@ -29,6 +29,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 import common  # noqa: E402,F401  (import paths)
 from gguf_writer import make_qwen2_gguf  # noqa: E402
+from oracle import reference_dir  # noqa: E402
 
 OUT = os.path.join(HERE, "gguf_extract_golden.json")
 DIMS = dict(hidden=1536, n_q_heads=12, n_kv_heads=2, head_dim=128, intermediate=256,
@@ -44,8 +45,12 @@ def sha(path: str) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-dir", default=os.environ.get("SI_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--ref-dir", default=reference_dir(),
+                    help="the reference checkout (default: $SI_REFERENCE_DIR, else a "
+                         "checkout named reference beside this repository)")
     args = ap.parse_args()
+    if not args.ref_dir:
+        sys.exit("no reference checkout: pass --ref-dir or set SI_REFERENCE_DIR")
     script = os.path.join(args.ref_dir, "extract_weights.py")
     with tempfile.TemporaryDirectory() as tmp:
         gguf = os.path.join(tmp, "synthetic.gguf")

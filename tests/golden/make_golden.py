@@ -25,6 +25,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 from common import (DIMS_15B, Oracle, Reference, stream, xs_kv_history, xs_layer)  # noqa: E402
+from oracle import reference_dir  # noqa: E402
 
 OUT = os.path.join(HERE, "reference_golden.npz")
 LAYER_SEED = 0x1234
@@ -77,8 +78,12 @@ def run_repack(ref_dir: str, layer: dict) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-dir", default="/root/reference")
+    ap.add_argument("--ref-dir", default=reference_dir(),
+                    help="the reference checkout (default: $SI_REFERENCE_DIR, else a "
+                         "checkout named reference beside this repository)")
     args = ap.parse_args()
+    if not args.ref_dir:
+        sys.exit("no reference checkout: pass --ref-dir or set SI_REFERENCE_DIR")
     ref, oc = Reference(), Oracle()
     g: dict[str, np.ndarray] = {}
 

@@ -235,6 +235,21 @@ def test_attention_batched_vs_oracle(si_ctx, oc, dims, ctxs, kv_f32):
         assert_close(want, got[b], ATT_ATOL, ATT_RTOL, f"attention b={b} ctx={ctxs[b]}")
 
 
+def test_attention_decode_rejects_empty_context(si_ctx):
+    """A context length of 0 has no key to attend to: the entry point returns
+    SI_ERR_INVALID instead of launching (the decode step requires >= 1 too)."""
+    import sib200
+    dims = dict(hidden=896, n_q_heads=14, n_kv_heads=2, head_dim=64)
+    kv = si_ctx.kv(dims, 2, 16, True)
+    q = empty(2 * 14 * 64, torch.float32)
+    out = empty(2 * 14 * 64, torch.float32)
+    with pytest.raises(sib200.SiError) as e:
+        si_ctx.attention_decode(kv, dims, q, 2, [3, 0], out)
+    assert e.value.status == sib200.SI_ERR_INVALID
+    si_ctx.status()
+    kv.free()
+
+
 @pytest.mark.parametrize("case", range(len(RUN_CASES)))
 def test_run_layer_golden(si_ctx, golden, oc, case):
     """run_layer with the reference's signature against the reference's own outputs."""

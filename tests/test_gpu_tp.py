@@ -1,7 +1,10 @@
-"""Tensor parallelism on two (and, where the host has them, four) GPUs: the
-sharded layer (one process per GPU)
-against the same layer on one GPU, for decode steps (GEMV path) and a
-40-token prefill (tcgen05 GEMM path).  Decode runs both ways the group can
+"""Tensor parallelism on two, four and eight GPUs (where the host has them):
+the sharded layer (one process per GPU) against the same layer on one GPU, for
+decode steps (GEMV path) and a prefill (40 tokens at two and four ranks: the
+GEMV, then an NCCL all-reduce; 300 tokens at eight ranks: the GEMM, then NCCL).
+At eight ranks the layer has the Qwen2.5-72B dimensions, so the MLP splits
+unevenly (231 units of 128 intermediate rows: 29 on seven ranks, 28 on the
+last) exactly as in the 72B tensor-parallel stack.  Decode runs both ways the group can
 add the row-parallel partial sums: fused into the projection (peer stores over
 NVLink plus a flag-gated combine kernel) and through NCCL's all-reduce.
 Five consecutive decode steps exercise both receive-slot parities and the
@@ -20,11 +23,15 @@ pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
 FULLS = {2: dict(hidden=1024, n_q_heads=8, n_kv_heads=2, head_dim=128, intermediate=2816,
                  rope_theta=1e6, rms_eps=1e-6),
          4: dict(hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, intermediate=2816,
+                 rope_theta=1e6, rms_eps=1e-6),
+         8: dict(hidden=8192, n_q_heads=64, n_kv_heads=8, head_dim=128, intermediate=29568,
                  rope_theta=1e6, rms_eps=1e-6)}
-SEED, CTX, PREFIX, NTOK, L, STEPS, BATCH = 5, 37, 11, 40, 64, 5, 3
+SEED, CTX, PREFIX, STEPS, BATCH = 5, 37, 11, 5, 3
+NTOKS = {2: 40, 4: 40, 8: 300}   # prefill tokens per world size
+L = 320                          # cache positions: PREFIX + the longest prefill fits
 
 
-def _inputs(FULL):
+def _inputs(FULL, NTOK):
     rng = np.random.default_rng(17)
     kvd = FULL["n_kv_heads"] * FULL["head_dim"]
     k = (rng.standard_normal((L, kvd)) * 0.5).astype(np.float32)
@@ -67,10 +74,10 @@ def _prefill(ctx, step, dims, k, v, X):
 
 def _rank(rank, world, uid, path):
     import sib200
-    FULL = FULLS[world]
+    FULL, NTOK = FULLS[world], NTOKS[world]
     torch.cuda.set_device(rank)
     ctx = sib200.Context(rank, 4096, 1e6, 128)
-    k, v, x, X = _inputs(FULL)
+    k, v, x, X = _inputs(FULL, NTOK)
     d, _ = sib200.tp_local_dims(FULL, rank, world)
     kvd = d["n_kv_heads"] * d["head_dim"]
     sl = slice(rank * kvd, (rank + 1) * kvd)
@@ -100,7 +107,7 @@ def _rank(rank, world, uid, path):
     ctx.close()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_layer_matches_one_gpu(tmp_path, world):
     import sib200
     import torch.multiprocessing as mp
@@ -118,7 +125,7 @@ def test_tp_layer_matches_one_gpu(tmp_path, world):
     for rk in range(1, world):
         np.testing.assert_array_equal(np.load(path + ".rank0.npy"),
                                       np.load(path + f".rank{rk}.npy"))
-    for t in range(NTOK):
+    for t in range(NTOKS[world]):
         assert_layer_close(r["one_pre"][t], r["pre"][t], 1e-3, f"TP={world} prefill token {t}")
 
 

@@ -46,6 +46,50 @@ def run_case(ctx, N, K, M, seed):
     w.free()
 
 
+def test_static_scratch_gemm_allocates_nothing():
+    """On a fresh context the static entry point runs before anything has sized
+    the context's GEMM scratch, and it must leave the context's on-demand
+    buffers empty; a second call at a larger size must not change the device's
+    free memory either.  Only then is its output compared with the allocating
+    tcgen05 entry point's."""
+    ctx = sib200.Context(0, max_positions=256, rope_theta=1e6, head_dim=128)
+    try:
+        N, K = 256, 1536
+        w = ctx.matrix_synth(N, K, seed=21)
+        g = torch.Generator(device="cuda").manual_seed(21)
+        M1, M2 = 64, 1024
+        x = torch.randn(M2, K, device="cuda", generator=g)
+        qs = torch.zeros(M2 * K, dtype=torch.int8, device="cuda")
+        d = torch.zeros(M2 * K // 32, dtype=torch.int16, device="cuda")
+        got1 = torch.full((M1 * N,), float("nan"), device="cuda")
+        got2 = torch.full((M2 * N,), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        ctx.q8_quantize(x, M2, K, qs, d)
+        ctx.sync()
+        held = ctx.scratch_bytes()
+        # First call on this device resolves the array's address (set-up).
+        sib200.check(ctx.L.si_matmul_tc_static_dev(ctx.h, w.h, _p(qs), _p(d), M1, None,
+                                                   _p(got1)), "si_matmul_tc_static_dev")
+        ctx.sync()
+        assert ctx.scratch_bytes() == held, "the static entry point grew the context's buffers"
+        free0 = torch.cuda.mem_get_info()[0]
+        sib200.check(ctx.L.si_matmul_tc_static_dev(ctx.h, w.h, _p(qs), _p(d), M2, None,
+                                                   _p(got2)), "si_matmul_tc_static_dev")
+        ctx.sync()
+        assert torch.cuda.mem_get_info()[0] == free0, "device memory was allocated"
+        assert ctx.scratch_bytes() == held
+        ctx.status()
+        for M, got in ((M1, got1), (M2, got2)):
+            want = torch.zeros(M * N, device="cuda")
+            torch.cuda.synchronize()
+            ctx.matmul(w, qs, d, M, None, want, kernel=1)
+            ctx.sync()
+            assert torch.equal(got, want), f"M={M}"
+        w.free()
+    finally:
+        ctx.close()
+
+
 def test_static_scratch_gemm_matches_tcgen05_entry_point(si_ctx):
     assert scratch_bytes(8960, 3744) <= LIMIT
     # Large scratch use first, then smaller shapes over its leftovers, then the
