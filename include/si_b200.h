@@ -184,6 +184,9 @@ SI_API void *si_ctx_stream(si_ctx *ctx); /* the cudaStream_t all work is queued 
  * buffers (step arena, index arrays, GEMM activation-scale scratch); they grow
  * when a call needs more and are freed by si_ctx_destroy. */
 SI_API size_t si_ctx_scratch_bytes(const si_ctx *ctx);
+/* Kernels this library has queued so far, process-wide (all devices and
+ * contexts); the difference across a region counts its kernel launches. */
+SI_API unsigned long long si_kernel_launches(void);
 SI_API const char *si_last_error(void);  /* message of the last failing call on this thread */
 
 /* Weight matrices.  Upload GGUF Q4_0 rows and repack on the device into the
@@ -245,6 +248,13 @@ SI_API si_status si_matmul_tc_static_dev(si_ctx *ctx, const si_matrix *w, const 
                                          const uint16_t *d_dev, int M, const float *bias_dev,
                                          float *out_dev);
 /* Per-(row, block) int32 partial sums [M][rows][cols/32] (parity checks). */
+/* Int8 tensor-core throughput probe (no reference counterpart: it measures
+ * the prefill GEMM's roofline denominator).  Queues one launch on the
+ * context's stream: one CTA per SM, each issuing iters x 4 tcgen05 kind::i8
+ * MMAs of 128 x n x 32 (n = 128 or 256) from operands resident in shared
+ * memory; *ops_per_launch receives the int8 operations the launch performs.
+ * Time it with events on si_ctx_stream(). */
+SI_API si_status si_tc_i8_peak_dev(si_ctx *ctx, int n, int iters, double *ops_per_launch);
 SI_API si_status si_block_isums_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                     int M, int32_t *isum_dev);
 /* SwiGLU pair: act = silu(gate@x) * (up@x), quantised to Q8 in the epilogue. */

@@ -85,6 +85,8 @@ class Oracle:
         L.oc_rope_table.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, _f32p]
         for fn in (L.oc_attention_flash,):
             fn.argtypes = [C.POINTER(Dims), _f32p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, _f32p]
+        L.oc_attention_flash_heads.argtypes = [C.POINTER(Dims), _f32p, C.c_void_p, C.c_void_p,
+                                               C.c_int, C.c_int, _f32p, C.c_int, C.c_int]
         L.oc_attention_standard.argtypes = [C.POINTER(Dims), _f32p, C.c_void_p, C.c_void_p,
                                             C.c_int, C.c_int, _f32p, _f32p]
         L.oc_run_layer.argtypes = [C.POINTER(Dims), C.POINTER(LayerPtrs), _f32p, C.c_void_p,

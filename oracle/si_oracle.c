@@ -166,12 +166,13 @@ static inline float oc_kv(const void *base, size_t idx, int kv_f32) {
 }
 
 /* attention_kernels.h:80-164: one exp per token, branch on a new maximum. */
-void oc_attention_flash(const oc_dims *dm, const float *q, const void *kc, const void *vc,
-                        int kv_f32, int context, float *out) {
+void oc_attention_flash_heads(const oc_dims *dm, const float *q, const void *kc,
+                              const void *vc, int kv_f32, int context, float *out, int h0,
+                              int h1) {
     const int D = dm->head_dim, Hq = dm->n_q_heads, Hkv = dm->n_kv_heads;
     const float scale = 1.0f / sqrtf((float)D);
     const size_t stride = (size_t)Hkv * D;
-    for (int h = 0; h < Hq; ++h) {
+    for (int h = h0; h < h1 && h < Hq; ++h) {
         const int group = h / (Hq / Hkv);
         const float *qh = q + (size_t)h * D;
         float *oh = out + (size_t)h * D;
@@ -201,6 +202,13 @@ void oc_attention_flash(const oc_dims *dm, const float *q, const void *kc, const
         const float inv = 1.0f / norm;
         for (int d = 0; d < D; ++d) oh[d] *= inv;
     }
+}
+
+/* The whole layer's heads; heads are independent, so the host baseline may
+ * also call oc_attention_flash_heads on disjoint head ranges in parallel. */
+void oc_attention_flash(const oc_dims *dm, const float *q, const void *kc, const void *vc,
+                        int kv_f32, int context, float *out) {
+    oc_attention_flash_heads(dm, q, kc, vc, kv_f32, context, out, 0, dm->n_q_heads);
 }
 
 /* attention_kernels.h:33-78: materialised scores, softmax, then P*V. */

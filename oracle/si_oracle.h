@@ -86,6 +86,9 @@ void oc_rope_table(int pos0, int npos, int head_dim, float theta, float *cos_out
  * attention_kernels.h:33-78 (standard; scores is Hq*context floats). */
 void oc_attention_flash(const oc_dims *d, const float *q, const void *kc, const void *vc,
                         int kv_f32, int context, float *out);
+void oc_attention_flash_heads(const oc_dims *dm, const float *q, const void *kc,
+                              const void *vc, int kv_f32, int context, float *out, int h0,
+                              int h1);
 void oc_attention_standard(const oc_dims *d, const float *q, const void *kc, const void *vc,
                            int kv_f32, int context, float *out, float *scores);
 

@@ -141,18 +141,21 @@ static inline unsigned nblk(size_t n, int t) { return (unsigned)((n + t - 1) / t
 cudaError_t launch_repack_gguf(const uint8_t *gguf, int rows, int KB, uint8_t *nib,
                                uint16_t *scl, cudaStream_t s) {
   size_t n = (size_t)rows * KB;
+  count_launch();
   k_repack_gguf<<<nblk(n, 256), 256, 0, s>>>(gguf, rows, KB, nib, scl);
   return cudaGetLastError();
 }
 cudaError_t launch_unpack_to_gguf(const uint8_t *nib, const uint16_t *scl, int rows, int KB,
                                   uint8_t *gguf, cudaStream_t s) {
   size_t n = (size_t)rows * KB;
+  count_launch();
   k_unpack_to_gguf<<<nblk(n, 256), 256, 0, s>>>(nib, scl, rows, KB, gguf);
   return cudaGetLastError();
 }
 cudaError_t launch_synth_q4(int rows, int KB, uint64_t seed, float stdv, uint8_t *nib,
                             uint16_t *scl, cudaStream_t s, int row0, int cb0, int full_KB) {
   size_t n = (size_t)rows * KB;
+  count_launch();
   k_synth_q4<<<nblk(n, 128), 128, 0, s>>>(rows, KB, seed, stdv, nib, scl, row0, cb0,
                                           full_KB > 0 ? full_KB : KB);
   return cudaGetLastError();
@@ -160,12 +163,14 @@ cudaError_t launch_synth_q4(int rows, int KB, uint64_t seed, float stdv, uint8_t
 cudaError_t launch_synth_f32(float *dst, size_t n, uint64_t seed, float mean, float stdv,
                              cudaStream_t s, size_t i0) {
   if (n == 0) return cudaSuccess;
+  count_launch();
   k_synth_f32<<<nblk(n, 256), 256, 0, s>>>(dst, n, seed, mean, stdv, i0);
   return cudaGetLastError();
 }
 cudaError_t launch_synth_kv(void *dst, size_t n, int f32, uint64_t seed, float stdv,
                             cudaStream_t s) {
   if (n == 0) return cudaSuccess;
+  count_launch();
   k_synth_kv<<<nblk(n, 256), 256, 0, s>>>(dst, n, f32, seed, stdv);
   return cudaGetLastError();
 }
@@ -173,6 +178,7 @@ cudaError_t launch_q8_to_blocks(const int8_t *qs, const uint16_t *d, int M, int 
                                 uint8_t *blocks, cudaStream_t s) {
   size_t n = (size_t)M * (K / 32);
   if (n == 0) return cudaSuccess;
+  count_launch();
   k_q8_to_blocks<<<nblk(n, 128), 128, 0, s>>>(qs, d, n, blocks);
   return cudaGetLastError();
 }
@@ -180,6 +186,7 @@ cudaError_t launch_q8_from_blocks(const uint8_t *blocks, int M, int K, int8_t *q
                                   cudaStream_t s) {
   size_t n = (size_t)M * (K / 32);
   if (n == 0) return cudaSuccess;
+  count_launch();
   k_q8_from_blocks<<<nblk(n, 128), 128, 0, s>>>(blocks, n, qs, d);
   return cudaGetLastError();
 }
@@ -268,6 +275,7 @@ cudaError_t launch_colsoa_to_rt(const uint8_t *tiles, int kind, int nrows, int r
                                 uint16_t *scl, cudaStream_t s) {
   size_t n = (size_t)nrows * KB;
   if (n == 0) return cudaSuccess;
+  count_launch();
   k_colsoa_to_rt<<<nblk(n, 256), 256, 0, s>>>(tiles, kind, nrows, row0, KB, hidden, tile_bytes,
                                              kv_rows, nib, scl);
   return cudaGetLastError();
@@ -276,6 +284,7 @@ cudaError_t launch_colsoa_to_rt(const uint8_t *tiles, int kind, int nrows, int r
 cudaError_t launch_colsoa_matvec(const uint8_t *tile, const uint8_t *x_blocks, int nblocks,
                                  const float *bias_lo, const float *bias_hi, float *out, int add,
                                  cudaStream_t s) {
+  count_launch();
   k_colsoa_matvec<<<1, 256, 0, s>>>(tile, x_blocks, nblocks, bias_lo, bias_hi, out, add);
   return cudaGetLastError();
 }

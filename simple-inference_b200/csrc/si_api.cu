@@ -107,6 +107,7 @@ struct si_ctx {
   DevBuf work;                  // layer-schedule arena
   DevBuf idx;                   // per-token index arrays
   DevBuf gemm;                  // tcgen05 GEMM scratch (transposed activation scales)
+  DevBuf hx, hy;                // device staging of the host-pointer step forms
   int *pinned_idx = nullptr;    // host staging for idx: kIdxSlots slots of pinned_idx_n ints
   size_t pinned_idx_n = 0;
   cudaEvent_t idx_ev[4] = {};   // per slot: its host->device copy has run
@@ -284,6 +285,8 @@ extern "C" SI_API void si_ctx_destroy(si_ctx *c) {
   c->work.release();
   c->idx.release();
   c->gemm.release();
+  c->hx.release();
+  c->hy.release();
   if (c->pinned_idx) cudaFreeHost(c->pinned_idx);
   for (cudaEvent_t e : c->idx_ev)
     if (e) cudaEventDestroy(e);
@@ -309,8 +312,16 @@ extern "C" SI_API si_status si_ctx_status(si_ctx *ctx) {
 }
 
 extern "C" SI_API void *si_ctx_stream(si_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+namespace si {
+unsigned long long g_kernel_launches = 0;
+}
+extern "C" SI_API unsigned long long si_kernel_launches(void) {
+  return __atomic_load_n(&si::g_kernel_launches, __ATOMIC_RELAXED);
+}
+
 extern "C" SI_API size_t si_ctx_scratch_bytes(const si_ctx *ctx) {
-  return ctx ? ctx->work.bytes + ctx->idx.bytes + ctx->gemm.bytes : 0;
+  return ctx ? ctx->work.bytes + ctx->idx.bytes + ctx->gemm.bytes + ctx->hx.bytes + ctx->hy.bytes
+             : 0;
 }
 
 // ----------------------------------------------------------------------------
@@ -624,6 +635,18 @@ extern "C" SI_API si_status si_matmul_tc_static_dev(si_ctx *ctx, const si_matrix
   a.out = out;
   a.scratch = scratch;
   SI_CUDA(si::launch_gemm_tc(a, false, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_tc_i8_peak_dev(si_ctx *ctx, int n, int iters,
+                                              double *ops_per_launch) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(ops_per_launch && (n == 128 || n == 256) && iters >= 1 && iters <= (1 << 22),
+           "bad probe arguments (n must be 128 or 256, 1 <= iters <= 4194304)");
+  SI_TRY(ctx->idx.reserve(1024 * sizeof(int)));
+  int ctas = 0;
+  SI_CUDA(si::launch_tc_i8_peak(n, iters, ctx->err, static_cast<int *>(ctx->idx.p), &ctas,
+                                ops_per_launch, ctx->stream));
   return SI_OK;
 }
 
@@ -1298,12 +1321,16 @@ extern "C" SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, 
   return run_step(ctx, l, kv, x, ntok, nullptr, nullptr, seq, prefix, y, mode, nullptr, false);
 }
 
-// Host-pointer forms: stage x/y through a device buffer.
+// Host-pointer forms: x and y are staged through two context-owned device
+// buffers that grow to the largest step seen (no allocation per call).
 struct HostStage {
   float *x = nullptr, *y = nullptr;
-  ~HostStage() {
-    cudaFree(x);
-    cudaFree(y);
+  si_status reserve(si_ctx *ctx, size_t n) {
+    SI_TRY(ctx->hx.reserve(n * 4));
+    SI_TRY(ctx->hy.reserve(n * 4));
+    x = static_cast<float *>(ctx->hx.p);
+    y = static_cast<float *>(ctx->hy.p);
+    return SI_OK;
   }
 };
 
@@ -1316,8 +1343,7 @@ extern "C" SI_API si_status si_decode_step(si_ctx *ctx, si_layer *l, si_kv *kv,
   const int KVD = l->d.n_kv_heads * l->d.head_dim;
   HostStage hs;
   size_t n = (size_t)batch * H;
-  SI_CUDA(cudaMalloc(&hs.x, n * 4));
-  SI_CUDA(cudaMalloc(&hs.y, n * 4));
+  SI_TRY(hs.reserve(ctx, n));
   si_captures dcap{};
   std::vector<void *> owned;
   if (cap_host) {
@@ -1352,8 +1378,7 @@ extern "C" SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int 
   SI_CHECK(l && x_host && y_host && ntok > 0, "null argument");
   HostStage hs;
   size_t n = (size_t)ntok * l->d.hidden;
-  SI_CUDA(cudaMalloc(&hs.x, n * 4));
-  SI_CUDA(cudaMalloc(&hs.y, n * 4));
+  SI_TRY(hs.reserve(ctx, n));
   SI_CUDA(cudaMemcpyAsync(hs.x, x_host, n * 4, cudaMemcpyHostToDevice, ctx->stream));
   SI_TRY(si_prefill_dev(ctx, l, kv, seq, hs.x, ntok, prefix, hs.y, mode));
   SI_CUDA(cudaMemcpyAsync(y_host, hs.y, n * 4, cudaMemcpyDeviceToHost, ctx->stream));

@@ -34,6 +34,11 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // launched without the attribute.
 constexpr unsigned kPdlMaxCtas = 4096;
 
+// Process-wide count of kernels this library has queued (all devices and
+// contexts), read through si_kernel_launches(); every launch site bumps it.
+extern unsigned long long g_kernel_launches;
+inline void count_launch() { __atomic_fetch_add(&g_kernel_launches, 1ull, __ATOMIC_RELAXED); }
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                        cudaStream_t s, Args &&...args) {
@@ -47,6 +52,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (unsigned long long)grid.x * grid.y * grid.z <= kPdlMaxCtas ? 1 : 0;
+  count_launch();
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 

@@ -114,6 +114,13 @@ bool gemm_mma_supported(int N, int K, int M, bool swiglu);
 // Scratch the GEMM needs for its transposed fp32 activation scales.
 size_t gemm_tc_scratch_bytes(int K, int M);
 
+// ---- tc_peak.cu (int8 tensor-core throughput probe) ---------------------------
+// One CTA per SM, `iters` x 4 tcgen05 kind::i8 MMAs of 128 x n x 32 each (n =
+// 128 or 256); *ops = int8 operations per launch, *ctas = CTAs launched;
+// sink needs one int per SM.
+cudaError_t launch_tc_i8_peak(int n, int iters, int *err, int *sink, int *ctas, double *ops,
+                              cudaStream_t s);
+
 // ---- rope_kv.cu -------------------------------------------------------------
 struct RopeKvArgs {
   const float *qkv;      // [T][QD + 2*KVD] projections (bias included)

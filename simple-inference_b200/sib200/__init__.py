@@ -30,6 +30,11 @@ class SiError(RuntimeError):
         self.status = status
 
 
+def kernel_launches() -> int:
+    """Kernels libsi_b200 has queued so far in this process."""
+    return int(lib().si_kernel_launches())
+
+
 def build(jobs: int = 8) -> str:
     """Compile libsi_b200.so (sm_100a) in-tree with nvcc."""
     out = subprocess.run(["make", "-C", PKG_DIR, f"-j{jobs}"], capture_output=True, text=True)
@@ -80,6 +85,8 @@ def lib() -> C.CDLL:
         "si_ctx_status": (i32, [vp]),
         "si_ctx_stream": (vp, [vp]),
         "si_ctx_scratch_bytes": (C.c_size_t, [vp]),
+        "si_kernel_launches": (C.c_ulonglong, []),
+        "si_tc_i8_peak_dev": (i32, [vp, i32, i32, C.POINTER(C.c_double)]),
         "si_matrix_upload": (i32, [vp, vp, i32, i32, pp]),
         "si_matrix_upload_dev": (i32, [vp, vp, i32, i32, pp]),
         "si_matrix_synth": (i32, [vp, i32, i32, u64, f32, pp]),
@@ -189,6 +196,12 @@ class Context:
 
     def sync(self):
         check(self.L.si_ctx_synchronize(self.h), "si_ctx_synchronize")
+
+    def tc_i8_peak(self, n: int, iters: int) -> float:
+        """Queue the int8 tensor-core probe; returns its int8 ops per launch."""
+        ops = C.c_double()
+        check(self.L.si_tc_i8_peak_dev(self.h, n, iters, C.byref(ops)), "si_tc_i8_peak_dev")
+        return ops.value
 
     def scratch_bytes(self) -> int:
         """Device bytes held by the context's on-demand buffers."""

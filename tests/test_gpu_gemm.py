@@ -109,3 +109,28 @@ def test_gemm_swiglu_epilogue(si_ctx, oc, M, kernel):
         want = (gate / (np.float32(1) + np.exp(-gate))).astype(np.float32) * up
         assert_close(want, act[t], 1e-7, 1e-6, f"silu(gate)*up token {t}")
         np.testing.assert_array_equal(blk[t], oc.quantize_q8(act[t]))
+
+
+@pytest.mark.parametrize("n", [128, 256])
+def test_int8_tensor_core_probe(si_ctx, n):
+    """The int8 throughput probe that supplies the prefill roofline's
+    denominator: it completes (its bounded wait does not expire), reports the
+    operation count it performs, and its measured rate is a plausible B200
+    dense int8 rate (between 1 and 6 POPS; the data sheet gives 4.5)."""
+    stream = torch.cuda.ExternalStream(si_ctx.stream)
+    iters = 8192
+    ops = si_ctx.tc_i8_peak(n, iters)
+    si_ctx.sync()
+    si_ctx.status()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert ops == sms * iters * 4 * 2 * 128 * n * 32
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record()
+        for _ in range(3):
+            si_ctx.tc_i8_peak(n, iters)
+        end.record()
+    end.synchronize()
+    si_ctx.status()
+    tops = 3 * ops / (start.elapsed_time(end) / 1e3) / 1e12
+    assert 1000 < tops < 6000, tops
