@@ -226,7 +226,11 @@ SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs
                                float *out_dev);
 /* Force a kernel: 0 = GEMV (its form picked by M), 1 = tcgen05 GEMM,
  * 2 = GEMV in its tensor-core (mma.sync s8) form, 3 = GEMV in its dp4a form,
- * 4 = mma.sync GEMM (rows % 128, cols % 32).  Every kernel returns the same bits. */
+ * 4 = mma.sync GEMM (rows % 128, cols % 32).  Kernels 0-4 return the same bits
+ * (the reference's).  5 = tcgen05 GEMM in its fused-rescale mode: each block's
+ * term is added with one FMA, acc = fma(round(isum*dw), dx, acc), one rounding
+ * fewer than the reference's ((float)isum*dw)*dx then +=, so outputs differ
+ * from the reference's by far less than the 1e-5 relative projection bar. */
 SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                       const uint16_t *d_dev, int M, const float *bias_dev,
                                       float *out_dev, int kernel);

@@ -7,33 +7,47 @@
 //
 // Tile: 128 weight rows (TMEM lanes) x 128 tokens (TMEM columns).  Per K block
 // one tcgen05.mma.kind::i8 (K = 32 = one Q4_0/Q8_0 block) writes the exact int32
-// block sums of the whole tile into a fresh TMEM accumulator; the epilogue
-// warps rescale it in fp32 and add it to register accumulators in block order,
+// block sums of the whole tile into a TMEM accumulator; the epilogue warps
+// rescale them in fp32 and add them to register accumulators in block order,
 // so results are bit-identical to the reference's serial loop.  Four TMEM
 // accumulators (512 columns) let the MMA run up to four blocks ahead of the
-// rescale.  The accumulators are pre-set to the integer 0x4B400000 and the MMA
-// accumulates onto it, so each read-back is already the float C + 16*isum; one
-// exact FMA per element folds that into round(isum*dw), then a
-// round-to-nearest multiply by dx (packed in pairs) and a scalar add keep the
-// reference's rounding.
+// rescale.
+//
+// Exact int -> float without a conversion instruction: after reading an
+// accumulator each epilogue warp re-arms its part of it with tcgen05.st of the
+// integer 0x4B400000 (the bits of C = 1.5 * 2^23), and the next MMA into it
+// accumulates onto that, so every read-back is the float C + 16*isum (exact:
+// |16*isum| < 2^22).  (Re-arming from shared memory with tcgen05.cp instead
+// reads 64 KB of shared memory per block and measured 1.7x slower.)  The epilogue then needs three FP32 operations per (row, token,
+// block) -- the floor for the reference's three roundings:
+//   p   = (C + 16*isum) * dw/16 - C*dw/16   one packed FMA: round(isum*dw)
+//   q   = p * dx                            one packed multiply, round-to-nearest
+//   acc = acc + q                           one scalar add (a packed add after the
+//                                           packed multiply is contracted by ptxas)
+// A tolerance mode (`fused_rescale`) replaces the last two by one FMA, acc =
+// fma(p, dx, acc): one rounding fewer per term (differences of order 2^-24 of a
+// term, far inside the 1e-5 projection bar) for two FP32 operations per element.
 //
 // The kernel is persistent (one CTA per SM, tiles visited token-tile fastest)
 // so the TMA / unpack / MMA / epilogue pipeline never drains between tiles.
 //
-// Warp roles (640 threads):
+// Warp roles (384 threads):
 //   warp 0      TMA producer: packed Q4 nibbles and their fp16 scales, int8
 //               activations (128-byte swizzle) and the stage's fp32
 //               activation scales
-//   warp 1      TMEM allocation; lane 0 issues the MMAs, one commit per stage
+//   warp 1      TMEM allocation; lane 0 issues the MMAs, two accumulator
+//               commits and one stage commit per stage
 //   warps 2-3   nibble unpack: Q4 -> signed int8 in the 128B-swizzled K-major
 //               layout the MMA reads (byte = 16*(q-8), so sums are 16*isum)
-//   warps 4-19  epilogue (4 per TMEM lane quarter, 32 columns each, read in
-//               double-buffered 8-column chunks): TMEM -> registers, rescale,
-//               accumulate, re-arm, store
-// Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  The
-// epilogue hands each accumulator back to the MMA issuer on an mbarrier.  Every wait is
-// bounded (about 2 s); on expiry the kernel records SI_ERR_TIMEOUT in the
-// context's error word, stops all roles, frees its TMEM and returns.
+//   warps 4-11  epilogue: warp w reads TMEM lane quarter w % 4 (32 rows) and
+//               one half of the tile's tokens (64 columns, two 32-column
+//               loads per block), re-arms it, rescales and accumulates in
+//               registers, hands the accumulator back on an mbarrier, stores
+//               per tile
+// Stages hold 4 blocks (K = 128 bytes, one swizzle row) and are 4 deep.  Every
+// wait is bounded (about 2 s); on expiry the kernel records SI_ERR_TIMEOUT in
+// the context's error word, stops all roles, waits (bounded) for its own TMA
+// loads and MMAs in flight, frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -51,8 +65,9 @@ constexpr int KBS = 4;                    // blocks per stage
 constexpr int STAGES = 4;
 constexpr int NACC = 4;                   // TMEM accumulators (= blocks per stage)
 constexpr uint32_t TMEM_COLS = NACC * BN; // 512
-constexpr int EPI_WARP0 = 4, EPI_WARPS = 16;
+constexpr int EPI_WARP0 = 4, EPI_WARPS = 8;
 constexpr int THREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+constexpr int NC = BN * 4 / EPI_WARPS;    // 64 token columns per epilogue warp
 constexpr uint32_t kMagic = 0x4B400000u;  // bits of 12582912.0f = 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
@@ -61,20 +76,23 @@ constexpr int B_BYTES = BN * 128;            // 16 KB, SW128 K-major (TMA swizzl
 constexpr int A_PACK_BYTES = BM * KBS * 16;  // 8 KB
 constexpr int DX_BYTES = KBS * BN * 4;       // 2 KB
 constexpr int SW_BYTES = BM * KBS * 2;       // 1 KB: weight scales [4 row tiles][4 blocks][32]
+constexpr int XCHG_BYTES = 64 * BN * 4;      // SwiGLU up-row hand-off, 32 KB
 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_INT8_BYTES;
 constexpr int OFF_PACK = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_DX = OFF_PACK + STAGES * A_PACK_BYTES;
-constexpr int XCHG_BYTES = 64 * BN * 4;      // SwiGLU up-row hand-off, 32 KB
 constexpr int OFF_SW = OFF_DX + STAGES * DX_BYTES;
 constexpr int OFF_XCHG = OFF_SW + STAGES * SW_BYTES;
 constexpr int OFF_BAR = OFF_XCHG + XCHG_BYTES;
-constexpr int NBAR = 4 * STAGES + 2 * NACC + NACC;
+constexpr int NBAR = 4 * STAGES + 2 * NACC + 1;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
 
 static_assert(KBS == NACC, "one accumulator per block of a stage");
+static_assert(NC == 64, "two 32-column TMEM loads per block and warp");
+static_assert(OFF_B % 1024 == 0 && OFF_A % 1024 == 0, "alignment");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 struct Params {
   int N, K, M;              // rows (or gate rows for SwiGLU), inputs, tokens
@@ -87,41 +105,70 @@ struct Params {
   int *err;
 };
 
-// ---------------------------------------------------------------------------
-// the kernel
-// ---------------------------------------------------------------------------
-// Columns per epilogue warp: the 4 TMEM lane quarters x (EPI_WARPS / 4) slices.
-constexpr int NC = BN * 4 / EPI_WARPS;
-constexpr int CW = 8;         // columns per TMEM load chunk
-constexpr int NCH = NC / CW;  // chunks per block
-static_assert(NCH >= 2 && NCH % 2 == 0, "chunk double-buffering needs an even chunk count");
+// 32 columns of this warp's 32 lanes set to v (tmem_fill32: four 8-column
+// stores, so the value occupies 8 registers rather than 32).
+__device__ __forceinline__ void tmem_fill32x(uint32_t taddr, uint32_t v) { tmem_fill32(taddr, v); }
+// Bounded wait that ignores the abort flag: used on the way out of an aborted
+// kernel for the CTA's own asynchronous copies and MMAs.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_sleep(bar, parity))
+    if (globaltimer() - t0 > 2000000000ull) return false;
+  return true;
+}
 
-// One CW-column chunk h of the rescale: acc[h*CW + c] += ((C+D)*dw16 - C*dw16) * dx.
-// The fold is a packed FMA (exact, see above) and the product a packed
-// multiply; the sum stays scalar so product and sum keep the reference's
-// separate roundings.
-__device__ __forceinline__ void rescale(float (&acc)[NC], int h, const uint32_t (&d)[CW],
-                                        const float4 *dx4, float2 dw2, float2 nc2) {
+__device__ __forceinline__ void tmem_ld16r(uint32_t taddr, uint32_t (&r)[16]) { tmem_ld16(taddr, r); }
+
+// One 16-column chunk K of a block's rescale for this warp (columns 16K..16K+15
+// of its 64).
+template <bool FUSED, int K>
+__device__ __forceinline__ void rescale16(float (&acc)[NC], const uint32_t (&v)[16],
+                                          const float4 *dx4, float2 dw2, float2 nc2) {
 #pragma unroll
-  for (int c4 = 0; c4 < CW / 4; ++c4) {
-    const float4 x = dx4[h * (CW / 4) + c4];
-    const float2 f0 = make_float2(__uint_as_float(d[4 * c4]), __uint_as_float(d[4 * c4 + 1]));
-    const float2 f1 = make_float2(__uint_as_float(d[4 * c4 + 2]), __uint_as_float(d[4 * c4 + 3]));
+  for (int c4 = 0; c4 < 4; ++c4) {
+    const float4 x = dx4[K * 4 + c4];
+    const float2 f0 = make_float2(__uint_as_float(v[4 * c4]), __uint_as_float(v[4 * c4 + 1]));
+    const float2 f1 = make_float2(__uint_as_float(v[4 * c4 + 2]), __uint_as_float(v[4 * c4 + 3]));
     const float2 p0 = fma2_rn(f0, dw2, nc2), p1 = fma2_rn(f1, dw2, nc2);
-    const int a = h * CW + 4 * c4;
-    // Packed product, scalar sum: with both packed, ptxas fuses them into one
-    // packed FMA (a single rounding) despite the explicit .rn -- measured here;
-    // either one packed alone keeps both roundings.
-    const float2 q0 = mul2_rn(p0, make_float2(x.x, x.y)), q1 = mul2_rn(p1, make_float2(x.z, x.w));
-    acc[a] = __fadd_rn(acc[a], q0.x);
-    acc[a + 1] = __fadd_rn(acc[a + 1], q0.y);
-    acc[a + 2] = __fadd_rn(acc[a + 2], q1.x);
-    acc[a + 3] = __fadd_rn(acc[a + 3], q1.y);
+    const int a = K * 16 + 4 * c4;
+    if constexpr (FUSED) {
+      const float2 s0 = fma2_rn(p0, make_float2(x.x, x.y), make_float2(acc[a], acc[a + 1]));
+      const float2 s1 = fma2_rn(p1, make_float2(x.z, x.w), make_float2(acc[a + 2], acc[a + 3]));
+      acc[a] = s0.x; acc[a + 1] = s0.y; acc[a + 2] = s1.x; acc[a + 3] = s1.y;
+    } else {
+      const float2 q0 = mul2_rn(p0, make_float2(x.x, x.y));
+      const float2 q1 = mul2_rn(p1, make_float2(x.z, x.w));
+      acc[a] = __fadd_rn(acc[a], q0.x);
+      acc[a + 1] = __fadd_rn(acc[a + 1], q0.y);
+      acc[a + 2] = __fadd_rn(acc[a + 2], q1.x);
+      acc[a + 3] = __fadd_rn(acc[a + 3], q1.y);
+    }
   }
 }
 
-template <bool SWIGLU>
-__global__ void __launch_bounds__(THREADS, 1)
+// Bounded wait for the roles off the critical path (producer, unpack): between
+// polls the warp sleeps, so it leaves the issue slots of its SM sub-partition
+// to the epilogue warps that share it.
+__device__ __forceinline__ bool mbar_wait_lazy_warp(uint32_t bar, uint32_t parity,
+                                                    volatile int *abort) {
+  bool ok = true;
+  if (!mbar_try(bar, parity)) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try(bar, parity)) {
+      __nanosleep(200);
+      if (*abort || globaltimer() - t0 > 2000000000ull) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// (__launch_bounds__ without a minimum-blocks hint: with the hint ptxas
+// schedules for 168 registers and spills; without it it needs 138.)
+template <bool SWIGLU, bool FUSED>
+__global__ void __launch_bounds__(THREADS)
     k_gemm_q4q8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                 const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
                 const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
@@ -134,15 +181,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  // tma_full: packed A + B + activation scales landed; a_ready: A unpacked;
-  // stage_empty: the MMAs of the stage finished; dx_empty: the epilogue used
-  // the stage's scales; acc_full[h]: accumulators 2h and 2h+1 of a stage
-  // written (two commits per stage, so the epilogue starting a stage never
-  // waits on the MMA that the release of its last accumulator unblocks);
-  // acc_empty[j]: every epilogue warp re-armed accumulator j (the MMA thread
-  // sleeps in try_wait rather than polling, so no issue slots go to waiting).
+  // tma_full[s]: packed A, B and the scales of stage s landed; a_ready[s]: A
+  // unpacked; stage_empty[s]: the stage's MMAs finished; dx_empty[s]: every
+  // epilogue warp is done with the stage's scales; acc_full[h]: accumulators
+  // 2h and 2h+1 hold blocks 2h and 2h+1 of a stage (two commits per stage: an
+  // mbarrier wait costs a few hundred cycles even when already complete, and
+  // the epilogue starting block 2 never waits on the MMA that its release of
+  // accumulator 3 a stage earlier unblocked); acc_empty[j]: every epilogue
+  // warp has read accumulator j; final: the MMA thread's last tcgen05
+  // operations completed.
   const int B_TMA = 0, B_AREADY = STAGES, B_SEMPTY = 2 * STAGES, B_DXEMPTY = 3 * STAGES,
-            B_ACCFULL = 4 * STAGES, B_ACCEMPTY = 4 * STAGES + 2 * NACC;
+            B_ACCFULL = 4 * STAGES, B_ACCEMPTY = 4 * STAGES + NACC,
+            B_FINAL = 4 * STAGES + 2 * NACC;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC + 16);
 
@@ -153,9 +203,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar(B_SEMPTY + s), 1);
       mbar_init(bar(B_DXEMPTY + s), EPI_WARPS);
     }
-    mbar_init(bar(B_ACCFULL), 1);
-    mbar_init(bar(B_ACCFULL + 1), 1);
-    for (int j = 0; j < NACC; ++j) mbar_init(bar(B_ACCEMPTY + j), EPI_WARPS);
+    for (int j = 0; j < NACC; ++j) {
+      mbar_init(bar(B_ACCFULL + j), 1);  // only the first two are used
+      mbar_init(bar(B_ACCEMPTY + j), EPI_WARPS);
+    }
+    mbar_init(bar(B_FINAL), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -184,10 +236,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
       const int nt = tile / p.mtiles, t0 = (tile % p.mtiles) * BN;
-      for (int g = 0; g < G; ++g, ++it) {
+      for (int g = 0; g < G; ++g) {
         const int s = it % STAGES;
         const uint32_t ph = ((it / STAGES) & 1) ^ 1;
-        if (!mbar_wait2_warp(bar(B_SEMPTY + s), ph, bar(B_DXEMPTY + s), ph, abort_flag)) {
+        if (!mbar_wait_lazy_warp(bar(B_SEMPTY + s), ph, abort_flag) ||
+            !mbar_wait_lazy_warp(bar(B_DXEMPTY + s), ph, abort_flag)) {
           if (lane == 0) fail();
           ok = false;
           break;
@@ -204,8 +257,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_2d(sw, &tmS, g * 128, nt * tiles_per_row, full);
           if (SWIGLU) tma_load_2d(sw + SW_BYTES / 2, &tmS2, g * 128, nt * 2, full);
         }
+        ++it;
         __syncwarp();
       }
+    }
+    if (!ok && lane == 0) {
+      // Let the loads this warp issued land before the CTA can exit.
+      for (int k = it > STAGES ? it - STAGES : 0; k < it; ++k)
+        mbar_drain(bar(B_TMA + k % STAGES), (k / STAGES) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -223,16 +282,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + OFF_A + s * A_INT8_BYTES);
           const uint32_t b0 = smem_u32(smem + OFF_B + s * B_BYTES);
-          for (int j = 0; j < KBS && ok; ++j) {
-            // Use number `it` of accumulator j needs the epilogue to have
-            // (re)armed it with the magic constant it+1 times (each of its warps).
+          for (int j = 0; j < KBS; ++j) {
+            // Use number `it` of accumulator j needs every epilogue warp to
+            // have read and re-armed its previous block (it + 1 completions,
+            // counting the initial one).
             if (!mbar_wait(bar(B_ACCEMPTY + j), it & 1, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
             mma_i8(tmem_base + j * BN, smem_desc(a0 + 32 * j), smem_desc(b0 + 32 * j), idesc, 1);
-            // Phase `it` of acc_full[h]: block sums 2h and 2h+1 of the stage are in TMEM.
             if (j % 2 == 1) mma_commit(bar(B_ACCFULL + j / 2));
           }
           if (!ok) break;
@@ -240,7 +299,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) fail();
+      // Every tcgen05 operation this thread issued has completed before TMEM
+      // can be freed.
+      mma_commit(bar(B_FINAL));
+      mbar_drain(bar(B_FINAL), 0);
     }
+    __syncwarp();
   } else if (warp < EPI_WARP0) {
     // ---------------- nibble unpack ----------------
     const int u = threadIdx.x - 64;  // 0..63
@@ -249,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
       for (int g = 0; g < G; ++g, ++it) {
         const int s = it % STAGES;
-        if (!mbar_wait_warp(bar(B_TMA + s), (it / STAGES) & 1, abort_flag)) {
+        if (!mbar_wait_lazy_warp(bar(B_TMA + s), (it / STAGES) & 1, abort_flag)) {
           if (lane == 0) fail();
           ok = false;
           break;
@@ -276,27 +340,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------- epilogue ----------------
-    // Warp e: lane quarter q = warp % 4, column slice hc = e / 4 (NC columns).
-    // Each warp walks its columns of every block in CW-column chunks,
-    // software-pipelined: the TMEM load of chunk k+1 is in flight while chunk k
-    // is rescaled, and the accumulator's re-arm store overlaps the last chunk.
     const int e = warp - EPI_WARP0;
     const int q = warp & 3;       // TMEM lane quarter this warp may access
-    const int hc = e >> 2;        // column slice of the tile
+    const int hc = e >> 2;        // token half of the tile
     const int r = q * 32 + lane;  // tile row
     const uint32_t tcol = tmem_base + ((uint32_t)(q * 32) << 16) + hc * NC;
-    // Accumulators hold C + 16*isum as float bits: the MMA accumulates onto the
-    // integer 0x4B400000 (C = 1.5*2^23 as a float), so C + D is an exactly
-    // representable float in [2^23, 2^24) and no int->float conversion is needed.
-    for (int j = 0; j < NACC; ++j)
-      for (int f = 0; f < NC / 32; ++f) tmem_fill32(tcol + j * BN + 32 * f, kMagic);
+    // Every accumulator starts armed and free.
+    for (int j = 0; j < NACC; ++j) {
+      tmem_fill32x(tcol + j * BN, kMagic);
+      tmem_fill32x(tcol + j * BN + 32, kMagic);
+    }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
       for (int j = 0; j < NACC; ++j) mbar_arrive(bar(B_ACCEMPTY + j));
-    float *xchg = reinterpret_cast<float *>(smem + OFF_XCHG);  // [64 rows][BN]
-    int pending = -1;  // accumulator re-armed but not yet handed back to the MMA
+    // SwiGLU hand-off, [token column][row]: consecutive lanes, consecutive
+    // words.  Gate warp (q, hc) and up warp (q + 2, hc) hold the same 32
+    // intermediate rows and 64 tokens; each hands the other one half of its
+    // columns, so both share the activation and Q8 work.
+    float *xchg = reinterpret_cast<float *>(smem + OFF_XCHG);
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
@@ -306,86 +369,71 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float init = (!SWIGLU && p.bias) ? p.bias[n] : 0.0f;
 #pragma unroll
       for (int c = 0; c < NC; ++c) acc[c] = init;
-      const int it0 = it;  // stage counter at the tile's first block
-      uint32_t dbuf[2][CW];
-      // Prime: block 0 of the tile, chunk 0.
-      if (!mbar_wait2_warp(bar(B_TMA + it0 % STAGES), (it0 / STAGES) & 1, bar(B_ACCFULL),
-                           it0 & 1, abort_flag))
+      // Software pipeline over the tile's blocks in 16-column chunks: the
+      // TMEM load of the next chunk is always in flight while the current one
+      // is rescaled (va / vb alternate).  The four blocks of a stage are
+      // unrolled, so every TMEM, scale and dx offset is a constant.
+      uint32_t va[16], vb[16];
+      if (!mbar_wait2_warp(bar(B_TMA + it % STAGES), (it / STAGES) & 1, bar(B_ACCFULL), it & 1,
+                           abort_flag))
         ok = false;
       if (ok) {
         tc_fence_after();
-        tmem_ld<CW>(tcol, dbuf[0]);
-        tmem_wait_ld();
+        tmem_ld16r(tcol, va);
       }
-      for (int b = 0; ok && b < KB; ++b) {
-        const int j = b % KBS, itb = it0 + b / KBS, s = itb % STAGES;
-        // This row's scale of block b, staged by TMA with the stage's tiles
-        // ([row tile][block][32 rows] fp16; SwiGLU: gate tiles 0-1, up tiles 2-3).
-        const uint16_t dw_cur = reinterpret_cast<const uint16_t *>(
-            smem + OFF_SW + s * SW_BYTES)[((r >> 5) * KBS + j) * 32 + lane];
-        // (C + D) * dw/16 - C * dw/16 = isum * dw in one rounding: C*dw/16 is exact
-        // (dw has 11 significant bits, C/16 = 3*2^18), so this equals the
-        // reference's (float)isum * dw.
-        const float dw16 = __fmul_rn(f16_to_f32(dw_cur), 0.0625f);
-        const float ncdw = -__fmul_rn(kMagicF, dw16);
-        const float2 dw2 = make_float2(dw16, dw16), nc2 = make_float2(ncdw, ncdw);
-        const float4 *dx4 = reinterpret_cast<const float4 *>(smem + OFF_DX + s * DX_BYTES) +
-                            (j * BN + hc * NC) / 4;
-        const uint32_t ta = tcol + j * BN;
-        bool more = b + 1 < KB;
+#pragma unroll 1
+      for (int g = 0; ok && g < G; ++g) {
+        const int itg = it + g, s = itg % STAGES;
+        const uint16_t *swp = reinterpret_cast<const uint16_t *>(smem + OFF_SW + s * SW_BYTES) +
+                              (r >> 5) * KBS * 32 + lane;
+        const float4 *dxs = reinterpret_cast<const float4 *>(smem + OFF_DX + s * DX_BYTES) +
+                            hc * NC / 4;
 #pragma unroll
-        for (int h = 0; h < NCH; ++h) {  // dbuf[h & 1] holds chunk h on entry
-          if (h + 1 < NCH) {
-            tmem_ld<CW>(ta + (h + 1) * CW, dbuf[(h + 1) & 1]);
-          } else {
-            // Every chunk of block b is in registers.  Hand back the accumulator
-            // re-armed one block ago (its store has long completed, so this wait
-            // is short), then re-arm this one and start block b+1 (next
-            // accumulator, maybe next stage) into dbuf[0].
-            if (pending >= 0) {
-              tmem_wait_st();
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(bar(B_ACCEMPTY + pending));
-            }
-#pragma unroll
-            for (int f = 0; f < NC / 32; ++f) tmem_fill32(ta + 32 * f, kMagic);
-            pending = j;
-            // Blocks 2-3 of a stage are committed together; the MMAs behind that
-            // commit needed only releases made before this point.
-            if (more && j == KBS / 2 - 1 &&
-                !mbar_wait_warp(bar(B_ACCFULL + 1), itb & 1, abort_flag)) {
-              ok = false;
-              more = false;
-            }
-            if (more && j != KBS - 1) {
-              tc_fence_after();
-              tmem_ld<CW>(tcol + (j + 1) * BN, dbuf[0]);
-            }
+        for (int j = 0; j < KBS; ++j) {
+          // (C + D) * dw/16 - C * dw/16 = isum * dw in one rounding: C*dw/16
+          // is exact (dw has 11 significant bits, C/16 = 3*2^18).
+          const float dw16 = __fmul_rn(f16_to_f32(swp[j * 32]), 0.0625f);
+          const float ncdw = -__fmul_rn(kMagicF, dw16);
+          const float2 dw2 = make_float2(dw16, dw16), nc2 = make_float2(ncdw, ncdw);
+          const float4 *dx4 = dxs + j * BN / 4;
+          const uint32_t ta = tcol + j * BN;
+          tmem_wait_ld();               // va: chunk 0
+          tmem_ld16r(ta + 16, vb);
+          rescale16<FUSED, 0>(acc, va, dx4, dw2, nc2);
+          tmem_wait_ld();               // vb: chunk 1
+          tmem_ld16r(ta + 32, va);
+          rescale16<FUSED, 1>(acc, vb, dx4, dw2, nc2);
+          tmem_wait_ld();               // va: chunk 2
+          tmem_ld16r(ta + 48, vb);
+          rescale16<FUSED, 2>(acc, va, dx4, dw2, nc2);
+          tmem_wait_ld();               // vb: chunk 3 -- the whole block is read
+          // Re-arm this warp's part of the accumulator, then start the next
+          // block's first chunk.
+          tmem_fill32x(ta, kMagic);
+          tmem_fill32x(ta + 32, kMagic);
+          bool next = j + 1 < KBS || g + 1 < G;
+          if (j == 1) {
+            if (!mbar_wait_warp(bar(B_ACCFULL + 1), itg & 1, abort_flag)) ok = next = false;
+          } else if (j == KBS - 1 && next) {  // a new stage: its scales and first two blocks
+            const int itn = itg + 1;
+            if (!mbar_wait2_warp(bar(B_TMA + itn % STAGES), (itn / STAGES) & 1, bar(B_ACCFULL),
+                                 itn & 1, abort_flag))
+              ok = next = false;
           }
-          rescale(acc, h, dbuf[h & 1], dx4, dw2, nc2);
-          if (h + 1 < NCH) tmem_wait_ld();
-        }
-        if (j == KBS - 1) {
+          if (next) {
+            tc_fence_after();
+            tmem_ld16r(tcol + ((j + 1) % KBS) * BN, va);
+          }
+          rescale16<FUSED, 3>(acc, vb, dx4, dw2, nc2);
+          tmem_wait_st();
+          tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(B_DXEMPTY + s));
-          if (more) {
-            // A new stage: its scales and its first two block sums (their
-            // accumulators were released during blocks 1 and 2 of this stage).
-            const int it1 = itb + 1;
-            if (!mbar_wait2_warp(bar(B_TMA + it1 % STAGES), (it1 / STAGES) & 1, bar(B_ACCFULL),
-                                 it1 & 1, abort_flag)) {
-              ok = false;
-              more = false;
-            } else {
-              tc_fence_after();
-              tmem_ld<CW>(tcol, dbuf[0]);
-            }
-          }
+          if (lane == 0) mbar_arrive(bar(B_ACCEMPTY + j));
         }
-        if (more) tmem_wait_ld();
+        if (lane == 0) mbar_arrive(bar(B_DXEMPTY + s));
       }
-      it = it0 + G;
+      tmem_wait_ld();  // nothing may be left in flight (an aborted prefetch)
+      it += G;
       if (!ok && lane == 0) fail();
       if (!SWIGLU) {
         if (!ok) break;
@@ -398,19 +446,30 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       } else {
-        // Up rows (lanes 64..127) hand their sums to the gate rows.  Every
-        // epilogue warp reaches both named barriers, aborted or not.
-        if (ok && q >= 2) {
+        // Gate warps (q < 2) pass columns 32..63 of their gate sums, up warps
+        // columns 0..31 of their up sums; every epilogue warp reaches both
+        // named barriers, aborted or not.
+        const bool gate = q < 2;
+        float *xg = xchg + hc * (2 * 32 * 64);  // [gate sums 32 cols][up sums 32 cols] x 64 rows
+        const int rr = r & 63;
+        if (ok) {
 #pragma unroll
-          for (int c = 0; c < NC; ++c) xchg[(size_t)(r - 64) * BN + hc * NC + c] = acc[c];
+          for (int c = 0; c < 32; ++c) {
+            if (gate) xg[c * 64 + rr] = acc[32 + c];
+            else xg[(32 + c) * 64 + rr] = acc[c];
+          }
         }
         asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32));
-        if (ok && !*abort_flag && q < 2) {
+        if (ok && !*abort_flag) {
           const int I = p.N;
 #pragma unroll
-          for (int c = 0; c < NC; ++c) {
-            const int t = t0 + hc * NC + c;
-            const float act = silu_mul(acc[c], xchg[(size_t)r * BN + hc * NC + c]);
+          for (int c = 0; c < 32; ++c) {
+            // gate warps: columns 0..31 (own gate, partner's up);
+            // up warps: columns 32..63 (partner's gate, own up).
+            const float gv = gate ? acc[c] : xg[c * 64 + rr];
+            const float uv = gate ? xg[(32 + c) * 64 + rr] : acc[32 + c];
+            const int t = t0 + hc * NC + (gate ? c : 32 + c);
+            const float act = silu_mul(gv, uv);
             uint16_t d16;
             const int8_t qv = q8_lane(act, d16);
             if (t < p.M) {
@@ -425,7 +484,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok || *abort_flag) break;
       }
     }
-    tmem_wait_st();  // the last re-arm completes before TMEM is freed
   }
 
   tc_fence_before();
@@ -538,7 +596,8 @@ cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s) {
   p.mtiles = (a.M + BN - 1) / BN;
   p.ntiles = (swiglu ? a.N / 64 : a.N / BM) * p.mtiles;
   const int grid = p.ntiles < sms ? p.ntiles : sms;
-  auto kern = swiglu ? k_gemm_q4q8<true> : k_gemm_q4q8<false>;
+  auto kern = swiglu ? (a.fused_rescale ? k_gemm_q4q8<true, true> : k_gemm_q4q8<true, false>)
+                     : (a.fused_rescale ? k_gemm_q4q8<false, true> : k_gemm_q4q8<false, false>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
   count_launch();

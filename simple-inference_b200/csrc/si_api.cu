@@ -546,10 +546,11 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
     SI_CUDA(si::launch_gemm_mma(a, false, ctx->stream));
     return SI_OK;
   }
-  if (kernel == 1) {
+  if (kernel == 1 || kernel == 5) {
     if (!si::gemm_tc_supported(w->rows, w->cols, M))
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support %dx%d at M=%d", w->rows,
                   w->cols, M);
+    a.fused_rescale = kernel == 5;
     SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(w->cols, M)));
     a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, false, ctx->stream));
@@ -570,9 +571,9 @@ extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w
                                                  const int8_t *qs, const uint16_t *d, int M,
                                                  const float *bias, float *out, int kernel) {
   SI_TRY(set_device(ctx));
-  SI_CHECK(kernel >= 0 && kernel <= 4,
-           "kernel must be 0 (GEMV), 1 (tcgen05 GEMM), 2 (GEMV, mma form), 3 (GEMV, dp4a form) "
-           "or 4 (mma GEMM)");
+  SI_CHECK(kernel >= 0 && kernel <= 5,
+           "kernel must be 0 (GEMV), 1 (tcgen05 GEMM), 2 (GEMV, mma form), 3 (GEMV, dp4a form), "
+           "4 (mma GEMM) or 5 (tcgen05 GEMM, fused rescale)");
   return matmul(ctx, w, qs, d, M, bias, nullptr, out, kernel);
 }
 
@@ -685,7 +686,7 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
                                                     const uint16_t *d, int M, int8_t *act_qs,
                                                     uint16_t *act_d, float *act_f32, int kernel) {
   SI_TRY(set_device(ctx));
-  SI_CHECK(kernel >= -1 && kernel <= 4, "bad kernel selector %d", kernel);
+  SI_CHECK(kernel >= -1 && kernel <= 5, "bad kernel selector %d", kernel);
   SI_CHECK(gate && up && qs && d && act_qs && act_d, "null pointer");
   SI_CHECK(gate->rows == up->rows && gate->cols == up->cols, "gate/up shape mismatch");
   si::GemvArgs a = gemv_args(gate, qs, d, M);
@@ -710,10 +711,11 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
     SI_CUDA(si::launch_gemm_mma(a, true, ctx->stream));
     return SI_OK;
   }
-  if (kernel == 1) {
+  if (kernel == 1 || kernel == 5) {
     if (!gemm_ok)
       return fail(SI_ERR_UNSUPPORTED, "tcgen05 GEMM does not support gate/up %dx%d at M=%d",
                   gate->rows, gate->cols, M);
+    a.fused_rescale = kernel == 5;
     SI_TRY(ctx->gemm.reserve(si::gemm_tc_scratch_bytes(gate->cols, M)));
     a.scratch = static_cast<float *>(ctx->gemm.p);
     SI_CUDA(si::launch_gemm_tc(a, true, ctx->stream));

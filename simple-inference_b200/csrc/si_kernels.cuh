@@ -96,6 +96,8 @@ struct GemvArgs {
   int *err;                // context device error word (bounded waits), or null
   float *scratch;          // tcgen05 GEMM: gemm_tc_scratch_bytes() of device memory
   int variant;             // GEMV form: kGemvAuto, kGemvDp4a or kGemvMma
+  int fused_rescale;       // tcgen05 GEMM: acc = fma(round(isum*dw), dx, acc) (one rounding
+                           // fewer per block; within 1e-5) instead of the exact two roundings
   PeerOut peer;            // tensor-core form only: partial sums to every rank's slot
 };
 enum { kGemvAuto = 0, kGemvDp4a = 1, kGemvMma = 2 };

@@ -134,3 +134,55 @@ def test_int8_tensor_core_probe(si_ctx, n):
     si_ctx.status()
     tops = 3 * ops / (start.elapsed_time(end) / 1e3) / 1e12
     assert 1000 < tops < 6000, tops
+
+
+# The fused-rescale mode (kernel 5) drops one rounding per block term, so it is
+# held to the projection bar of the north star, 1e-5 relative: every output
+# within 1e-5 of the row's largest magnitude and the whole matrix within 1e-6
+# relative L2 of the exact kernel's bits (which the tests above pin to the
+# reference).
+FUSED_MAX_REL, FUSED_L2_REL = 1e-5, 1e-6
+
+
+@pytest.mark.parametrize("N,K,M", [(256, 1536, 16), (2048, 1536, 130), (1536, 8960, 257),
+                                   (8192, 29568, 64)])
+def test_gemm_fused_rescale_within_projection_bar(si_ctx, oc, N, K, M):
+    m = si_ctx.matrix_synth(N, K, seed=N + K + M)
+    x = torch.randn(M, K, device="cuda")
+    bias = torch.randn(N, device="cuda") * 0.02
+    torch.cuda.synchronize()
+    qs, d = z(M * K, torch.int8), z(M * K // 32, torch.int16)
+    si_ctx.q8_quantize(x, M, K, qs, d)
+    exact, fused = z(M * N, torch.float32), z(M * N, torch.float32)
+    si_ctx.matmul(m, qs, d, M, bias, exact, kernel=1)
+    si_ctx.matmul(m, qs, d, M, bias, fused, kernel=5)
+    si_ctx.status()
+    e = exact.double().reshape(M, N)
+    f = fused.double().reshape(M, N)
+    assert torch.isfinite(f).all()
+    scale = e.abs().amax(dim=1, keepdim=True)
+    assert float(((f - e).abs() / scale).max()) <= FUSED_MAX_REL
+    assert float((f - e).norm() / e.norm()) <= FUSED_L2_REL
+
+
+@pytest.mark.parametrize("M", [64, 300])
+def test_gemm_swiglu_fused_rescale_within_projection_bar(si_ctx, M):
+    H, I = 1536, 8960
+    mg, mu = si_ctx.matrix_synth(I, H, seed=31), si_ctx.matrix_synth(I, H, seed=32)
+    x = torch.randn(M, H, device="cuda")
+    torch.cuda.synchronize()
+    qs, d = z(M * H, torch.int8), z(M * H // 32, torch.int16)
+    si_ctx.q8_quantize(x, M, H, qs, d)
+    outs = {}
+    for k in (1, 5):
+        aq, ad, af = z(M * I, torch.int8), z(M * I // 32, torch.int16), z(M * I, torch.float32)
+        si_ctx.gateup_q8(mg, mu, qs, d, M, aq, ad, af, kernel=k)
+        si_ctx.status()
+        outs[k] = (aq, ad, af)
+    e, f = outs[1][2].double().reshape(M, I), outs[5][2].double().reshape(M, I)
+    scale = e.abs().amax(dim=1, keepdim=True)
+    # silu(g)*u amplifies the gate and up terms' relative differences at most 2x
+    assert float(((f - e).abs() / scale).max()) <= 2 * FUSED_MAX_REL
+    # Q8 of the activation: codes move by at most one step, and rarely
+    dq = (outs[5][0].int() - outs[1][0].int()).abs()
+    assert int(dq.max()) <= 1 and float((dq > 0).float().mean()) < 1e-3
