@@ -515,13 +515,15 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
 }
 
 // Kernel choice for M tokens (measured on B200 at the 1.5B/7B/72B shapes):
-// the GEMV streams the weights once per 16 tokens, the GEMM keeps every
-// output's block-ordered sum in one warp and tiles 128 rows x 64 tokens.
-// The SwiGLU pair (two matrices, the Q8 epilogue) favours the GEMM from 64
-// tokens on, single matrices from 256.  The mma.sync GEMM outruns the tcgen05
-// one at every measured shape (its rescale runs straight from registers), so
-// it is the default where its shape rules allow.
+// the GEMV streams the weights once per 16 tokens, the GEMMs tile 128 rows x
+// 64 (mma.sync) or 128 (tcgen05) tokens.  The SwiGLU pair (two matrices, the
+// Q8 epilogue) favours a GEMM from 64 tokens on, single matrices from 256.
+// Between the GEMMs: the tcgen05 kernel is ahead from K = 2048 on (72B gate/up
+// at 4096 tokens 371 against 352 TOP/s, down 384 against 373; 7B gate/up 337
+// against 331); at K = 1536 (the 1.5B shapes) the mma.sync kernel's shorter
+// tile start-up wins (gate/up 279 against 262 TOP/s).
 static bool prefer_gemm(bool swiglu, int M) { return M >= (swiglu ? 64 : 256); }
+static bool prefer_tc(int K) { return K >= 2048; }
 
 static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
                         int M, const float *bias, const float *resid, float *out, int kernel) {
@@ -531,10 +533,13 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
   a.bias = bias;
   a.resid = resid;
   a.out = out;
-  if (kernel < 0)
+  if (kernel < 0) {
+    const bool tc = si::gemm_tc_supported(w->rows, w->cols, M);
+    const bool mma = si::gemm_mma_supported(w->rows, w->cols, M, false);
     kernel = !prefer_gemm(false, M) ? 0
-             : si::gemm_mma_supported(w->rows, w->cols, M, false) ? 4
-             : si::gemm_tc_supported(w->rows, w->cols, M) ? 1 : 0;
+             : tc && (prefer_tc(w->cols) || !mma) ? 1
+             : mma ? 4 : 0;
+  }
   if (kernel == 2) a.variant = si::kGemvMma;
   if (kernel == 3) a.variant = si::kGemvDp4a;
   if (kernel == 4) {
@@ -696,10 +701,12 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
   a.act_qs = act_qs;
   a.act_d = act_d;
   const bool gemm_ok = si::gemm_tc_supported(2 * gate->rows, gate->cols, M) && gate->rows % 64 == 0;
-  if (kernel < 0)
+  if (kernel < 0) {
+    const bool mma = si::gemm_mma_supported(gate->rows, gate->cols, M, true);
     kernel = !prefer_gemm(true, M) ? 0
-             : si::gemm_mma_supported(gate->rows, gate->cols, M, true) ? 4
-             : gemm_ok ? 1 : 0;
+             : gemm_ok && (prefer_tc(gate->cols) || !mma) ? 1
+             : mma ? 4 : 0;
+  }
   if (kernel == 2) a.variant = si::kGemvMma;
   if (kernel == 3) a.variant = si::kGemvDp4a;
   if (kernel == 4) {
