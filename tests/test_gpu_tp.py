@@ -8,8 +8,18 @@ last) exactly as in the 72B tensor-parallel stack.  Decode runs both ways the gr
 add the row-parallel partial sums: fused into the projection (peer stores over
 NVLink plus a flag-gated combine kernel) and through NCCL's all-reduce.
 Five consecutive decode steps exercise both receive-slot parities and the
-flag epochs.  Cross-rank summation reorders the fp32 sums, so the bar is the
-layer bar, 1e-3; every rank must hold identical outputs.  Skipped on hosts
+flag epochs.  Cross-rank summation reorders the fp32 sums, so at two and four
+ranks the bar is the layer bar, 1e-3; every rank must hold identical outputs.
+
+At eight ranks and 72B dimensions a reordered sum cannot be held to 1e-3
+against the one-GPU layer: when a last-bit difference flips one Q8 rounding of
+the MLP input, the 72B layer output moves by about 2e-3 (some 350 of the
+activation's Q8 codes follow it; measured with the oracle), in the reference's
+arithmetic as much as here, and a reordered sum causes such a flip for some
+tokens.  So at eight ranks: the attention sublayer alone (no Q8 after the
+row-parallel sum) must match one GPU within 1e-5, decode through NCCL and
+prefill; and the full layer must stay within the bound of a few such flips,
+5e-3, with most tokens (where nothing flipped) inside 1e-3.  Skipped on hosts
 with fewer GPUs than ranks.
 """
 import numpy as np
@@ -92,6 +102,14 @@ def _rank(rank, world, uid, path):
     pre = _prefill(ctx, lambda kv, xin, y: tp.prefill_dev(layer, kv, 0, xin, NTOK, PREFIX, y), d,
                    ks, vs, X)
     np.save(f"{path}.rank{rank}.npy", fused)
+    attn = {}
+    if world == 8:  # NCCL on the attention sublayer alone (see the module docstring)
+        tp.set_options(fused=False)
+        attn["nccl_dec"] = _decode(ctx, lambda kv, xin, lens, y: tp.decode_dev(
+            layer, kv, xin, lens, y, sib200.SI_LAYER_ATTN), d, ks, vs, x)
+        tp.set_options(fused=True)
+        attn["pre"] = _prefill(ctx, lambda kv, xin, y: tp.prefill_dev(
+            layer, kv, 0, xin, NTOK, PREFIX, y, sib200.SI_LAYER_ATTN), d, ks, vs, X)
     if rank == 0:
         full = ctx.layer_synth(FULL, SEED)
         one_dec = _decode(ctx, lambda kv, xin, lens, y: full.decode_dev(kv, xin, lens, y,
@@ -100,7 +118,14 @@ def _rank(rank, world, uid, path):
         one_pre = _prefill(ctx, lambda kv, xin, y: full.prefill_dev(kv, 0, xin, NTOK, PREFIX, y,
                                                                     sib200.SI_LAYER_FULL),
                            FULL, k, v, X)
-        np.savez(path, one_dec=one_dec, fused=fused, nccl=nccl, one_pre=one_pre, pre=pre)
+        extra = {}
+        if world == 8:
+            extra["one_attn_dec"] = _decode(ctx, lambda kv, xin, lens, y: full.decode_dev(
+                kv, xin, lens, y, sib200.SI_LAYER_ATTN), FULL, k, v, x)
+            extra["one_attn_pre"] = _prefill(ctx, lambda kv, xin, y: full.prefill_dev(
+                kv, 0, xin, NTOK, PREFIX, y, sib200.SI_LAYER_ATTN), FULL, k, v, X)
+            extra.update({f"attn_{k_}": v_ for k_, v_ in attn.items()})
+        np.savez(path, one_dec=one_dec, fused=fused, nccl=nccl, one_pre=one_pre, pre=pre, **extra)
         full.free()
     layer.free()
     tp.free()
@@ -117,16 +142,40 @@ def test_tp_layer_matches_one_gpu(tmp_path, world):
     path = str(tmp_path / "tp")
     mp.spawn(_rank, args=(world, uid, path), nprocs=world, join=True)
     r = np.load(path + ".npz")
-    for s in range(STEPS):
-        for b in range(BATCH):
-            assert_layer_close(r["one_dec"][s, b], r["fused"][s, b], 1e-3, f"fused step {s} seq {b}")
-            assert_layer_close(r["one_dec"][s, b], r["nccl"][s, b], 1e-3, f"NCCL step {s} seq {b}")
     # every rank sums the slots in the same order: identical hidden states
     for rk in range(1, world):
         np.testing.assert_array_equal(np.load(path + ".rank0.npy"),
                                       np.load(path + f".rank{rk}.npy"))
+    if world == 8:
+        _check_world8(r, path)
+        return
+    for s in range(STEPS):
+        for b in range(BATCH):
+            assert_layer_close(r["one_dec"][s, b], r["fused"][s, b], 1e-3, f"fused step {s} seq {b}")
+            assert_layer_close(r["one_dec"][s, b], r["nccl"][s, b], 1e-3, f"NCCL step {s} seq {b}")
     for t in range(NTOKS[world]):
         assert_layer_close(r["one_pre"][t], r["pre"][t], 1e-3, f"TP={world} prefill token {t}")
+
+
+def _check_world8(r, path):
+    """Eight ranks, 72B dimensions (see the module docstring for the bars)."""
+    errs = []
+    for s in range(STEPS):
+        for b in range(BATCH):
+            assert_layer_close(r["one_attn_dec"][s, b], r["attn_nccl_dec"][s, b], 1e-5,
+                               f"NCCL attention sublayer step {s} seq {b}")
+            for mode in ("fused", "nccl"):
+                assert_layer_close(r["one_dec"][s, b], r[mode][s, b], 5e-3, f"{mode} step {s} seq {b}")
+                d = r[mode][s, b].astype(np.float64) - r["one_dec"][s, b]
+                errs.append(np.linalg.norm(d) / np.linalg.norm(r["one_dec"][s, b]))
+    for t in range(NTOKS[8]):
+        assert_layer_close(r["one_attn_pre"][t], r["attn_pre"][t], 1e-5,
+                           f"NCCL attention sublayer prefill token {t}")
+        assert_layer_close(r["one_pre"][t], r["pre"][t], 5e-3, f"TP=8 prefill token {t}")
+        d = r["pre"][t].astype(np.float64) - r["one_pre"][t]
+        errs.append(np.linalg.norm(d) / np.linalg.norm(r["one_pre"][t]))
+    errs = np.array(errs)
+    assert np.mean(errs <= 1e-3) >= 0.5, f"most tokens should see no Q8 flip: {np.sort(errs)[-10:]}"
 
 
 def test_fused_reduction_wait_times_out(si_ctx):
