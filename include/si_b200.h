@@ -180,6 +180,13 @@ SI_API si_status si_ctx_synchronize(si_ctx *ctx);
 /* Synchronises, then returns and clears the device error word. */
 SI_API si_status si_ctx_status(si_ctx *ctx);
 SI_API void *si_ctx_stream(si_ctx *ctx); /* the cudaStream_t all work is queued on */
+/* Prefill attention kernel of this context (no reference counterpart: the
+ * reference has one CPU loop).  0 (default): tcgen05 tensor cores on split
+ * fp16 operands, within about 1e-6 relative of the fp32 kernel, for head_dim
+ * 128; 1: the fp32 kernel, whose prefill tokens are bit-identical to the
+ * same tokens' decode steps.  The reference-shaped pf_run_batch always uses
+ * the fp32 kernel. */
+SI_API si_status si_ctx_set_exact_attention(si_ctx *ctx, int exact);
 /* Bytes of device memory the context currently holds in its on-demand
  * buffers (step arena, index arrays, GEMM activation-scale scratch); they grow
  * when a call needs more and are freed by si_ctx_destroy. */
@@ -388,6 +395,15 @@ SI_API int si_graph_kernel_nodes(const si_graph *g);
 SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *dims,
                                          const float *q_dev, int batch, const int *ctx_lens,
                                          float *out_dev);
+/* Causal attention of a prefill on its own (no reference counterpart as an
+ * entry point: the prefill attention inside pf_run_batch,
+ * prefill_weight_stationary.h:245-287): q [ntok][Hq][D] (RoPE applied) of
+ * tokens at positions prefix .. prefix+ntok-1 of sequence seq, attending the
+ * cache's keys 0 .. position; out [ntok][Hq][D].  The kernel follows the
+ * context's si_ctx_set_exact_attention setting. */
+SI_API si_status si_attention_prefill_dev(si_ctx *ctx, si_kv *kv, const si_dims *d,
+                                          const float *q_dev, int ntok, int seq, int prefix,
+                                          float *out_dev);
 
 /* ------------------------------------------------------------------------ */
 /* Reference-shaped entry points (host pointers, implicit context).          */

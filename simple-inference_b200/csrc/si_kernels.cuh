@@ -150,12 +150,21 @@ struct AttnArgs {
   float *out;            // [T][Hq][D]
   float *part;           // split-K scratch, >= attn_part_floats() floats
   int nsplit;
+  int *err;              // context device error word (bounded waits), or null
 };
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
 // Splits the launch needs: 1 when the prefill kernel runs (contiguous tokens
 // of one sequence, T >= 16), else ceil(max_len / 128).
 int attn_pick_splits(int T, bool decode_form, int max_len);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
+
+// ---- attention_tc.cu (tcgen05 causal prefill, split fp16 operands) ------------
+// The prefill form (no per-token arrays) at head_dim 128 and groups <= 8.
+bool attn_tc_supported(const AttnArgs &a);
+// Scratch for the operand splits (Q, K and V^T as fp16 hi / lo halves).
+size_t attn_tc_scratch_bytes(const AttnArgs &a);
+cudaError_t launch_attention_tc(const AttnArgs &a, void *scratch, size_t scratch_bytes,
+                                cudaStream_t s);
 
 // ---- tp_peer.cu --------------------------------------------------------------
 // y[i] = resid[i] + sum over ranks (in rank order) of the receive slots of

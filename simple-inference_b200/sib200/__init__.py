@@ -133,6 +133,8 @@ def lib() -> C.CDLL:
         "si_decode_step_tp_dev": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
         "si_prefill_tp_dev": (i32, [vp, vp, vp, vp, i32, vp, i32, i32, vp, i32]),
         "si_attention_decode_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, vp, vp]),
+        "si_attention_prefill_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, i32, i32, vp]),
+        "si_ctx_set_exact_attention": (i32, [vp, i32]),
         "si_graph_begin": (i32, [vp]),
         "si_graph_end": (i32, [vp, pp]),
         "si_graph_launch": (i32, [vp, vp]),
@@ -316,6 +318,16 @@ class Context:
         check(self.L.si_kv_create(self.h, C.byref(dm), batch, max_ctx, int(kv_f32), C.byref(h)),
               "si_kv_create")
         return KV(self, h, dims, batch, max_ctx, kv_f32)
+
+    def attention_prefill(self, kv: "KV", dims: dict, q, ntok, seq, prefix, out):
+        dm = Dims.of(dims)
+        check(self.L.si_attention_prefill_dev(self.h, kv.h, C.byref(dm), _p(q), ntok, seq, prefix,
+                                              _p(out)), "si_attention_prefill_dev")
+
+    def set_exact_attention(self, exact: bool):
+        """True: prefill attention by the fp32 kernel (bit-identical to decode
+        steps); False (default): the tcgen05 tensor-core kernel."""
+        check(self.L.si_ctx_set_exact_attention(self.h, int(exact)), "si_ctx_set_exact_attention")
 
     def attention_decode(self, kv: "KV", dims: dict, q, batch, ctx_lens, out):
         dm = Dims.of(dims)

@@ -1,0 +1,105 @@
+"""GPU parity of the tcgen05 prefill attention (the default prefill kernel at
+head_dim 128): split fp16 operands (hi + lo) with fp32 accumulation on the
+tensor cores, against the oracle's attention_flash (attention_kernels.h:80-164)
+per token at context prefix + t + 1, to the reference's own attention bar
+(1e-5 + 1e-4 |x|, audit_fusion_timing.c:108), for fp32 and fp16 caches, group
+sizes 6, 7 and 8, token counts that leave a ragged last tile and prefixes that
+start mid-tile; and a 7B layer's prefill through it against the exact fp32
+kernel's.
+
+At the layer level a ~1e-6 difference in the attention can flip one Q8
+rounding of the attention output or of the MLP input, and one flipped MLP
+input code moves a 7B or 72B layer's output by ~1e-3 (Q8 codes of the SwiGLU
+activation follow it); so the layer comparison takes the bound of a few such
+flips, 1e-2 per token, with most tokens within 1e-3 (measured on B200: 74% of
+the tokens bit-identical, 90th percentile 4.3e-3, largest 6.6e-3).
+"""
+import numpy as np
+import pytest
+
+from common import assert_close, assert_layer_close
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ATT_ATOL, ATT_RTOL = 1e-5, 1e-4
+FLIP_BOUND = 1e-2  # a handful of flipped Q8 codes at 7B dimensions
+
+
+@pytest.mark.parametrize("kv_f32", [True, False])
+@pytest.mark.parametrize("hq,hkv,prefix,ntok", [(28, 4, 0, 200), (64, 8, 100, 150),
+                                                (12, 2, 37, 131)])
+def test_tc_prefill_attention_vs_oracle(si_ctx, oc, hq, hkv, prefix, ntok, kv_f32):
+    D = 128
+    dims = dict(hidden=hq * D, n_q_heads=hq, n_kv_heads=hkv, head_dim=D, intermediate=0,
+                rope_theta=1e6, rms_eps=1e-6)
+    L = prefix + ntok
+    rng = np.random.default_rng(hq * 7 + prefix + int(kv_f32))
+    k = rng.standard_normal((L, hkv * D)).astype(np.float32)
+    v = rng.standard_normal((L, hkv * D)).astype(np.float32)
+    if not kv_f32:
+        k, v = k.astype(np.float16).view(np.uint16), v.astype(np.float16).view(np.uint16)
+    q = (rng.standard_normal((ntok, hq * D)) * 2).astype(np.float32)
+    kv = si_ctx.kv(dims, 1, L, kv_f32)
+    kv.write(0, 0, k, v)
+    qd = torch.from_numpy(q).cuda()
+    out_tc = torch.zeros(ntok * hq * D, device="cuda")
+    out_ex = torch.zeros_like(out_tc)
+    torch.cuda.synchronize()
+    si_ctx.attention_prefill(kv, dims, qd, ntok, 0, prefix, out_tc)
+    si_ctx.set_exact_attention(True)
+    try:
+        si_ctx.attention_prefill(kv, dims, qd, ntok, 0, prefix, out_ex)
+    finally:
+        si_ctx.set_exact_attention(False)
+    si_ctx.status()
+    got = out_tc.cpu().numpy().reshape(ntok, -1)
+    ex = out_ex.cpu().numpy().reshape(ntok, -1)
+    assert np.all(np.isfinite(got))
+    for t in sorted({0, 1, ntok // 3, ntok // 2, ntok - 2, ntok - 1}):
+        ctx_len = prefix + t + 1
+        want = oc.attention(dims, q[t], k[:ctx_len].reshape(-1), v[:ctx_len].reshape(-1),
+                            ctx_len, 1)
+        assert_close(want, got[t], ATT_ATOL, ATT_RTOL, f"tensor-core token {t} ctx {ctx_len}")
+    # every token against the exact kernel (itself pinned to the oracle)
+    assert_close(ex, got, ATT_ATOL, ATT_RTOL, "tensor-core vs exact kernel")
+    kv.free()
+
+
+def test_tc_prefill_layer_vs_exact(si_ctx):
+    import sib200
+    dims = dict(hidden=3584, n_q_heads=28, n_kv_heads=4, head_dim=128, intermediate=18944,
+                rope_theta=1e6, rms_eps=1e-6)
+    ntok = 512
+    layer = si_ctx.layer_synth(dims, 2)
+    X = torch.randn(ntok, dims["hidden"], device="cuda",
+                    generator=torch.Generator("cuda").manual_seed(5))
+    ya, yb = torch.zeros_like(X), torch.zeros_like(X)
+    kva, kvb = si_ctx.kv(dims, 1, ntok, False), si_ctx.kv(dims, 1, ntok, False)
+    torch.cuda.synchronize()
+    layer.prefill_dev(kva, 0, X, ntok, 0, ya, sib200.SI_LAYER_FULL)
+    si_ctx.set_exact_attention(True)
+    try:
+        layer.prefill_dev(kvb, 0, X, ntok, 0, yb, sib200.SI_LAYER_FULL)
+    finally:
+        si_ctx.set_exact_attention(False)
+    si_ctx.status()
+    a, b = ya.cpu().numpy(), yb.cpu().numpy()
+    errs = np.array([np.linalg.norm(a[t].astype(np.float64) - b[t]) / np.linalg.norm(b[t])
+                     for t in range(ntok)])
+    print(f"\nTC vs exact prefill, 7B layer, {ntok} tokens: per-token rel-L2 "
+          f"quantiles 50/90/99/max = {np.quantile(errs, 0.5):.3g} {np.quantile(errs, 0.9):.3g} "
+          f"{np.quantile(errs, 0.99):.3g} {errs.max():.3g}; exact matches {np.mean(errs == 0):.2f}")
+    for t in range(ntok):
+        assert_layer_close(b[t], a[t], FLIP_BOUND, f"token {t}")
+    assert np.mean(errs <= 1e-3) >= 0.6, np.sort(errs)[-10:]
+    # the KV cache does not depend on the attention kernel
+    kvd = dims["n_kv_heads"] * dims["head_dim"]
+    ka, va_ = np.zeros((ntok, kvd), np.uint16), np.zeros((ntok, kvd), np.uint16)
+    kb, vb = np.zeros_like(ka), np.zeros_like(va_)
+    kva.read(0, 0, ntok, ka, va_)
+    kvb.read(0, 0, ntok, kb, vb)
+    np.testing.assert_array_equal(ka, kb)
+    np.testing.assert_array_equal(va_, vb)
+    for o in (kva, kvb, layer):
+        o.free()

@@ -4,12 +4,14 @@ that do not depend on size plus oracle checks on sampled tokens.
 * config 1 (1.5B projection sweep, M in {1, 16, 128, 512, 2048}): both GEMMs
   (tcgen05, mma.sync) equal the in-order GEMV element for element at M = 16, 128, 512
   (M = 2048 is in test_gpu_gemm.py, M = 1 is the GEMV itself).
-* config 2 (7B layer, 2048-token prefill, then decode): the prefill equals 2048
-  sequential decode steps (the reference's prefill oracle,
-  bench_ai_dma_prefill.c:104-108) bit for bit -- outputs and KV cache: the
-  projections keep the reference's block order in both kernels and a token's
-  attention splits depend only on its own context length; the decode steps
-  after it match the oracle's decoder layer.
+* config 2 (7B layer, 2048-token prefill, then decode): with the exact
+  attention kernel the prefill equals 2048 sequential decode steps (the
+  reference's prefill oracle, bench_ai_dma_prefill.c:104-108) bit for bit --
+  outputs and KV cache: the projections keep the reference's block order in
+  both kernels and a token's attention splits depend only on its own context
+  length; the decode steps after it match the oracle's decoder layer.  The
+  tensor-core prefill attention (the default) is checked in
+  test_gpu_attention_tc.py.
 * config 3 (7B, batch 64, fp32 KV of 4096 positions): the batched decode step
   (GEMM gate/up projection) equals single-sequence decode steps (GEMV) bit
   for bit, and matches the oracle's decoder layer on sampled sequences.
@@ -52,6 +54,14 @@ def test_config1_sweep_gemm_equals_gemv(si_ctx, name, N, K, M, kernel):
 
 
 def test_config2_prefill_then_decode(si_ctx, oc):
+    si_ctx.set_exact_attention(True)
+    try:
+        _config2_prefill_then_decode(si_ctx, oc)
+    finally:
+        si_ctx.set_exact_attention(False)
+
+
+def _config2_prefill_then_decode(si_ctx, oc):
     import sib200
     ntok, ndec = 2048, 4
     L = ntok + ndec
@@ -145,6 +155,7 @@ def test_prefill_kernel_equals_decode_kernel(hq, hkv, hd, kv_f32):
     prefix, ntok = 130, 150
     L = prefix + ntok
     ctx = sib200.Context(0, 4096, 1e6, hd)
+    ctx.set_exact_attention(True)
     try:
         layer = ctx.layer_synth(dims, 11 + hq)
         g = torch.Generator("cuda").manual_seed(hq + hkv)

@@ -332,10 +332,12 @@ def test_decode_batched_vs_oracle(si_ctx, oc, mode):
         ctx64.close()
 
 
+@pytest.mark.parametrize("exact", [True, False], ids=["exact-attention", "tcgen05-attention"])
 @pytest.mark.parametrize("kv_f32", [False, True])
-def test_prefill_vs_sequential_decode(si_ctx, oc, kv_f32):
+def test_prefill_vs_sequential_decode(si_ctx, oc, kv_f32, exact):
     """Causal prefill equals the reference's prefill oracle: decode token by token
-    with context prefix+t+1 (bench_ai_dma_prefill.c:104-108)."""
+    with context prefix+t+1 (bench_ai_dma_prefill.c:104-108), with either
+    prefill attention kernel, to the layer bar."""
     dims, layer = _layer_case(oc, DIMS_15B, 55, mlp=False)
     prefix, ntok, L = 7, 24, 64
     k, v = xs_kv_history(oc, 56, prefix + 1, 256, f32=kv_f32, total=L)
@@ -344,7 +346,11 @@ def test_prefill_vs_sequential_decode(si_ctx, oc, kv_f32):
     kv.write(0, 0, k.reshape(L, 256), v.reshape(L, 256))
     gl = si_ctx.layer(dims, layer)
     y = np.zeros_like(x)
-    gl.prefill(kv, 0, x, ntok, prefix, y, 0)
+    si_ctx.set_exact_attention(exact)
+    try:
+        gl.prefill(kv, 0, x, ntok, prefix, y, 0)
+    finally:
+        si_ctx.set_exact_attention(False)
     k2, v2 = k.copy(), v.copy()
     want = oc.prefill_sequential(dims, layer, x, prefix, k2, v2)
     assert_layer_close(want, y, LAYER_RTOL, "prefill output")
