@@ -58,7 +58,9 @@ INT8_SPEC_TOPS = 4500.0  # B200 dense int8 data-sheet figure, shown beside the m
 CONFIG4 = dict(hidden=8192, n_q_heads=64, n_kv_heads=8, head_dim=128, intermediate=29568,
                rope_theta=1e6, rms_eps=1e-6)
 TP_LAYERS, TP_PREFILL, TP_BATCH, TP_DECODE = 8, 4096, 8, 256
-TP_MAX_CTX = TP_PREFILL + TP_DECODE
+# Cache capacity: the prefill and 256 decode positions, plus the slot a
+# device-side length reaches after the last step's advance.
+TP_MAX_CTX = TP_PREFILL + TP_DECODE + 1
 DIMS_7B = dict(hidden=3584, n_q_heads=28, n_kv_heads=4, head_dim=128, intermediate=18944,
                rope_theta=1e6, rms_eps=1e-6)
 C2_PREFILL, C2_DECODE = 2048, 128
@@ -439,6 +441,10 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
     log(f"config4 e2e {te / args.steps * 1e3:.2f} ms/step")
 
     # ---- decode: 256 steps of a batch of 8 -----------------------------------
+    # The 8-layer step is captured once as a CUDA graph with the context
+    # lengths on the device (si_decode_state) and replayed step after step; on
+    # several ranks the fused exchanges' epochs come from a device counter the
+    # step's advance moves on.  The NCCL variant runs eagerly.
     def decode(s):
         lens = [TP_PREFILL + s + 1] * TP_BATCH
         for j, (layer, kv) in enumerate(zip(layers, kvs)):
@@ -452,7 +458,34 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
         barrier_sync()
         return max_over_ranks(time_region(torch, stream, decode, TP_DECODE)) / TP_DECODE
 
-    tdec = time_decode()
+    def time_decode_graph():
+        lens0 = [TP_PREFILL + 1] * TP_BATCH
+        st = ctx.decode_state(lens0, TP_MAX_CTX)
+
+        def step():
+            for j, (layer, kv) in enumerate(zip(layers, kvs)):
+                if world > 1:
+                    tp.decode_state_dev(layer, kv, xd[j % 2], st, xd[(j + 1) % 2])
+                else:
+                    layer.decode_state_dev(kv, xd[j % 2], st, xd[(j + 1) % 2],
+                                           sib200.SI_LAYER_FULL)
+            st.advance()
+        step()  # sizes the context's buffers before the capture
+        ctx.sync()
+        gph = ctx.capture(step)
+        for _ in range(3):
+            gph.launch()
+        st.set(lens0)
+        with torch.cuda.stream(stream):
+            xd[0].copy_(x0)
+        barrier_sync()
+        t_ = time_region(torch, stream, lambda i: gph.launch(), TP_DECODE) / TP_DECODE
+        ctx.status()
+        gph.free()
+        st.free()
+        return t_
+
+    tdec = time_decode_graph()
     tdec_nccl = None
     if world > 1:
         tp.set_options(fused=False)
@@ -500,13 +533,15 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
                        "pinned host memory; copies of neighbouring steps overlap on two copy "
                        "streams"},
         "decode": {"batch": TP_BATCH, "steps": TP_DECODE,
-                   "context": f"{TP_PREFILL + 1}..{TP_MAX_CTX}",
+                   "context": f"{TP_PREFILL + 1}..{TP_PREFILL + TP_DECODE}",
+                   "launch": "one 8-layer step captured as a CUDA graph (device-resident "
+                             "context lengths and exchange epochs), replayed per step",
                    "us_per_step": round(tdec * 1e6, 2),
                    "us_per_token": round(tdec * 1e6 / TP_BATCH, 3),
                    "tok_s": round(TP_BATCH / tdec, 1),
                    "reduction": ("fused into the projection (epoch-tagged NVLink peer stores)"
                                  if world > 1 else "none (one rank)"),
-                   "us_per_step_nccl_allreduce": round(tdec_nccl * 1e6, 2) if tdec_nccl else None},
+                   "us_per_step_nccl_allreduce_eager": round(tdec_nccl * 1e6, 2) if tdec_nccl else None},
         "roofline": {"bound": "tensor", "kernel": "gate/up GEMM + SiLU*mul + Q8 (4096 tokens, "
                                                   f"2x{Il}x{Hd} per rank)",
                      "achieved": round(gu_ops / tg / 1e12, 2),
@@ -542,7 +577,7 @@ def run_config2(ctx, torch, stream, args, peak):
     layer = ctx.layer_synth(DIMS_7B, 2)
     H = DIMS_7B["hidden"]
     g = torch.Generator(device="cuda").manual_seed(2)
-    kv = ctx.kv(DIMS_7B, 1, C2_PREFILL + C2_DECODE, False)
+    kv = ctx.kv(DIMS_7B, 1, C2_PREFILL + C2_DECODE + 1, False)
     X = torch.randn(C2_PREFILL, H, device="cuda", generator=g)
     Y = torch.empty_like(X)
     xd = torch.randn(C2_DECODE, H, device="cuda", generator=g)
@@ -552,10 +587,29 @@ def run_config2(ctx, torch, stream, args, peak):
     for _ in range(3):
         pf()
     tpf = time_region(torch, stream, pf, 5) / 5
+    # Decode: two steps (x -> y -> x) captured with device context lengths and
+    # replayed, 128 steps in all.
+    st = ctx.decode_state([C2_PREFILL + 1], C2_PREFILL + C2_DECODE + 1)
+    xa, ya = xd[0:1].clone(), torch.empty_like(xd[0:1])
+
+    def two_steps():
+        layer.decode_state_dev(kv, xa, st, ya, sib200.SI_LAYER_FULL)
+        st.advance()
+        layer.decode_state_dev(kv, ya, st, xa, sib200.SI_LAYER_FULL)
+        st.advance()
+    two_steps()
+    ctx.sync()
+    gph = ctx.capture(two_steps)
+    gph.launch()
+    st.set([C2_PREFILL + 1])
+    tdec = time_region(torch, stream, lambda i: gph.launch(), C2_DECODE // 2) / C2_DECODE
+    ctx.status()
+    gph.free()
+    st.free()
     dec = lambda i: layer.decode_dev(kv, xd[i], [C2_PREFILL + i + 1], yd[i], sib200.SI_LAYER_FULL)
     for i in range(3):
         dec(i)
-    tdec = time_region(torch, stream, dec, C2_DECODE) / C2_DECODE
+    tdec_eager = time_region(torch, stream, dec, C2_DECODE) / C2_DECODE
     # e2e: the host-pointer C ABI (si_prefill / si_decode_step), pinned numpy buffers
     hx = torch.randn(C2_PREFILL, H).pin_memory().numpy()
     hy = torch.empty(C2_PREFILL, H).pin_memory().numpy()
@@ -594,6 +648,8 @@ def run_config2(ctx, torch, stream, args, peak):
                         "decode steps at batch 1",
             "prefill_ms": round(tpf * 1e3, 3), "prefill_tok_s": round(C2_PREFILL / tpf, 1),
             "decode_us_per_token": round(tdec * 1e6, 2),
+            "decode_launch": "CUDA graph of two steps with device-resident context lengths",
+            "decode_us_per_token_eager": round(tdec_eager * 1e6, 2),
             "e2e": {"prefill_tok_s": round(C2_PREFILL / te, 1),
                     "decode_us_per_token": round(ted * 1e6, 2),
                     "h2d_bytes_per_step": C2_PREFILL * H * 4, "d2h_bytes_per_step": C2_PREFILL * H * 4,

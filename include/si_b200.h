@@ -324,6 +324,29 @@ SI_API si_status si_decode_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float
 SI_API si_status si_decode_step_dev(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x_dev,
                                     int batch, const int *ctx_lens, float *y_dev, int mode,
                                     const si_captures *cap_dev);
+/* Decode positions kept on the device (no reference counterpart: the
+ * reference passes `context` per call, qwen_one_layer.c:237).  A decode step
+ * given a state reads sequence b's context length from device memory instead
+ * of a host array, so a whole multi-layer step -- the layers' calls and then
+ * si_decode_state_advance -- can be captured once (si_graph_begin/end) and
+ * replayed for step after step with no host work per step.  Sequence b is
+ * batch entry b; 1 <= batch <= 256; lengths stay within [1, max_ctx] (the
+ * advance that would pass max_ctx leaves the lengths and records
+ * SI_ERR_INVALID in the context's error word). */
+typedef struct si_decode_state si_decode_state;
+SI_API si_status si_decode_state_create(si_ctx *ctx, int batch, const int *ctx_lens_host,
+                                        int max_ctx, si_decode_state **out);
+SI_API void si_decode_state_free(si_decode_state *st);
+/* Queues "set the lengths to ctx_lens_host" (their values are taken now). */
+SI_API si_status si_decode_state_set(si_ctx *ctx, si_decode_state *st, const int *ctx_lens_host);
+/* Queues "every length + 1" on the context's stream. */
+SI_API si_status si_decode_state_advance(si_ctx *ctx, si_decode_state *st);
+/* Synchronises and copies the current lengths to the host. */
+SI_API si_status si_decode_state_read(si_ctx *ctx, si_decode_state *st, int *ctx_lens_host);
+/* si_decode_step_dev with the lengths of st (batch = st's batch; the KV cache's
+ * max_ctx must equal st's). */
+SI_API si_status si_decode_step_state_dev(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x_dev,
+                                          si_decode_state *st, float *y_dev, int mode);
 /* Causal prefill of ntok tokens of sequence seq at positions [prefix,
  * prefix+ntok): token t attends over [0, prefix+t+1) (prefill_weight_stationary.h:173-186). */
 SI_API si_status si_prefill(si_ctx *ctx, si_layer *l, si_kv *kv, int seq, const float *x_host,
@@ -376,6 +399,13 @@ SI_API si_status si_layer_tp_synth(si_ctx *ctx, const si_dims *full, uint64_t se
 SI_API si_status si_decode_step_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,
                                        const float *x_dev, int batch, const int *ctx_lens,
                                        float *y_dev, int mode);
+/* si_decode_step_tp_dev with the lengths of a decode state.  The fused
+ * exchanges' epochs are then counted from a device counter that
+ * si_decode_state_advance moves on, so the whole multi-layer step (every
+ * layer's call, then the advance) can be captured once and replayed. */
+SI_API si_status si_decode_step_state_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,
+                                             const float *x_dev, si_decode_state *st,
+                                             float *y_dev, int mode);
 SI_API si_status si_prefill_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv, int seq,
                                    const float *x_dev, int ntok, int prefix, float *y_dev,
                                    int mode);

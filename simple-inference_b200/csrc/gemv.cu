@@ -665,8 +665,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
     // area, free once both warps have read their sums), so each token's 32
     // rows cross NVLink as 256 contiguous bytes.
     const PeerOut &pr = a.peer;
-    const size_t slot0 = ((size_t)(pr.epoch & 1) * pr.world + pr.rank) * pr.slot;
-    const unsigned long long tag = (unsigned long long)(unsigned)pr.epoch << 32;
+    const unsigned long long ep = peer_epoch(pr);
+    const size_t slot0 = ((size_t)(ep & 1) * pr.world + pr.rank) * pr.slot;
+    const unsigned long long tag = (unsigned long long)(unsigned)ep << 32;
     named_sync(kBarEpi, kMmaGroups * 32);
     float *tile_s = acc_s;  // MT * 32 floats == S::ACCS
 #pragma unroll

@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
     // h = x + the ranks' partial sums, added in rank order (tp_peer.cu's order),
     // each word waited for until it carries this call's epoch.
     const unsigned long long deadline = globaltimer() + rp.timeout_ns;
-    const unsigned ep = (unsigned)rp.p.epoch;
+    const unsigned long long ep64 = peer_epoch(rp.p);
+    const unsigned ep = (unsigned)ep64;
     bool bad = false;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
@@ -79,11 +80,11 @@ __global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
         const size_t e0 = (size_t)row * n + 4 * i;
         float sum[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sum[c] = peer_word(peer_slot(rp.p, 0) + e0 + c, ep, deadline, rp.err, bad);
+        for (int c = 0; c < 4; ++c) sum[c] = peer_word(peer_slot(rp.p, ep64, 0) + e0 + c, ep, deadline, rp.err, bad);
         for (int src = 1; src < rp.p.world; ++src)
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            sum[c] = __fadd_rn(sum[c], peer_word(peer_slot(rp.p, src) + e0 + c, ep, deadline, rp.err, bad));
+            sum[c] = __fadd_rn(sum[c], peer_word(peer_slot(rp.p, ep64, src) + e0 + c, ep, deadline, rp.err, bad));
         v[j] = make_float4(__fadd_rn(v[j].x, sum[0]), __fadd_rn(v[j].y, sum[1]),
                            __fadd_rn(v[j].z, sum[2]), __fadd_rn(v[j].w, sum[3]));
         if (!bad) reinterpret_cast<float4 *>(rp.h_out + (size_t)row * n)[i] = v[j];

@@ -58,6 +58,43 @@ __global__ void __launch_bounds__(256) k_rope_kv(const RopeKvArgs a) {
   }
 }
 
+// Per-token index arrays of a decode step, [seq T][pos T][ctx T], written from
+// kernel parameters (no host staging buffer, no host synchronisation).
+__global__ void k_set_idx(const IdxParams p, int *__restrict__ idx) {
+  pdl_trigger();
+  pdl_wait();
+  for (int t = threadIdx.x; t < p.T; t += blockDim.x) {
+    idx[t] = p.seq[t];
+    idx[p.T + t] = p.ctx[t] - 1;
+    idx[2 * p.T + t] = p.ctx[t];
+  }
+}
+
+// One decode step later: every position and context length + 1.  A length that
+// would pass max_ctx stays where it is and records SI_ERR_INVALID (1).
+__global__ void k_advance_idx(int *__restrict__ idx, int T, int max_ctx, int *err) {
+  pdl_trigger();
+  pdl_wait();
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int c = idx[2 * T + t];
+    if (c + 1 > max_ctx) {
+      raise_error(err, 1);
+      continue;
+    }
+    idx[T + t] = c;
+    idx[2 * T + t] = c + 1;
+  }
+}
+
+cudaError_t launch_set_idx(const IdxParams &p, int *idx, cudaStream_t s) {
+  if (p.T <= 0 || p.T > kIdxMaxByValue) return cudaErrorInvalidValue;
+  return launch_pdl(k_set_idx, dim3(1), dim3(256), 0, s, p, idx);
+}
+
+cudaError_t launch_advance_idx(int *idx, int T, int max_ctx, int *err, cudaStream_t s) {
+  return launch_pdl(k_advance_idx, dim3(1), dim3(256), 0, s, idx, T, max_ctx, err);
+}
+
 cudaError_t launch_rope_kv(const RopeKvArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
   const int pairs = (a.n_q_heads + a.n_kv_heads) * (a.head_dim / 2);

@@ -189,7 +189,12 @@ struct si_tp {
   char *sym = nullptr;                 // own symmetric buffer
   char *peer[si::kPeerMaxWorld] = {};  // every rank's buffer as mapped here
   int slot = 0;                        // floats per receive slot
-  unsigned long long epoch = 0;        // fused calls so far
+  // Epochs of the fused exchanges: call k of a step (k = 1, 2, ...) uses
+  // *epoch_dev + k; when the step ends a kernel adds the step's count to the
+  // device counter.  The base lives on the device so that a captured step
+  // replays with new epochs every time.
+  unsigned long long *epoch_dev = nullptr;
+  unsigned pending = 0;                // exchanges since the counter last moved
 };
 
 struct si_kv {
@@ -532,9 +537,11 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
 // Between the GEMMs: the tcgen05 kernel is ahead from K = 2048 on (72B gate/up
 // at 4096 tokens 371 against 352 TOP/s, down 384 against 373; 7B gate/up 337
 // against 331); at K = 1536 (the 1.5B shapes) the mma.sync kernel's shorter
-// tile start-up wins (gate/up 279 against 262 TOP/s).
+// tile start-up wins (gate/up 279 against 262 TOP/s).  Below 512 tokens the
+// tcgen05 kernel's 128-token tiles waste too much of a tile (a batch-64 7B
+// decode step: 627 against 568 us), so it needs M >= 512 as well.
 static bool prefer_gemm(bool swiglu, int M) { return M >= (swiglu ? 64 : 256); }
-static bool prefer_tc(int K) { return K >= 2048; }
+static bool prefer_tc(int K, int M) { return K >= 2048 && M >= 512; }
 
 static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
                         int M, const float *bias, const float *resid, float *out, int kernel) {
@@ -548,7 +555,7 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
     const bool tc = si::gemm_tc_supported(w->rows, w->cols, M);
     const bool mma = si::gemm_mma_supported(w->rows, w->cols, M, false);
     kernel = !prefer_gemm(false, M) ? 0
-             : tc && (prefer_tc(w->cols) || !mma) ? 1
+             : tc && (prefer_tc(w->cols, M) || !mma) ? 1
              : mma ? 4 : 0;
   }
   if (kernel == 2) a.variant = si::kGemvMma;
@@ -715,7 +722,7 @@ extern "C" SI_API si_status si_gateup_q8_dev_kernel(si_ctx *ctx, const si_matrix
   if (kernel < 0) {
     const bool mma = si::gemm_mma_supported(gate->rows, gate->cols, M, true);
     kernel = !prefer_gemm(true, M) ? 0
-             : gemm_ok && (prefer_tc(gate->cols) || !mma) ? 1
+             : gemm_ok && (prefer_tc(gate->cols, M) || !mma) ? 1
              : mma ? 4 : 0;
   }
   if (kernel == 2) a.variant = si::kGemvMma;
@@ -1104,7 +1111,9 @@ static si_status tp_sym_reserve(si_ctx *ctx, si_tp *tp, int slot) {
   SI_CUDA(cudaMalloc(&tp->sym, bytes));
   SI_CUDA(cudaMemset(tp->sym, 0, bytes));
   tp->slot = slot;
-  tp->epoch = 0;
+  // Every word starts at epoch 0, which no call uses.
+  SI_CUDA(cudaMemset(tp->epoch_dev, 0, sizeof(unsigned long long)));
+  tp->pending = 0;
   cudaIpcMemHandle_t h;
   SI_CUDA(cudaIpcGetMemHandle(&h, tp->sym));
   static_assert(sizeof(cudaIpcMemHandle_t) <= 64, "IPC handle size");
@@ -1156,7 +1165,8 @@ static si_status tp_gemv_peer(si_ctx *ctx, si_tp *tp, const si_matrix *w, const 
   a.peer.world = tp->world;
   a.peer.rank = tp->rank;
   a.peer.slot = tp->slot;
-  a.peer.epoch = ++tp->epoch;
+  a.peer.epoch = ++tp->pending;
+  a.peer.epoch_base = tp->epoch_dev;
   for (int r = 0; r < tp->world; ++r) a.peer.base[r] = tp->peer[r];
   SI_CUDA(si::launch_gemv(a, false, ctx->stream));
   *po = a.peer;
@@ -1181,10 +1191,19 @@ static si_status tp_rowparallel(si_ctx *ctx, si_tp *tp, const si_matrix *w, cons
 // One layer step.  With tp, the layer holds this rank's shard (its Q/KV heads
 // and its slice of the MLP); the O and down projections then produce partial
 // sums, which are all-reduced before the residual adds.
+// A decode step whose context lengths live on the device (si_decode_state):
+// the step reads them from there, so it can be captured once and replayed.
+struct si_decode_state {
+  si_ctx *ctx = nullptr;
+  int batch = 0, max_ctx = 0;
+  int *idx = nullptr;  // [seq batch][pos batch][ctx batch]
+  si_tp *tp = nullptr; // the group whose exchange epochs the advance also moves on
+};
+
 static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, int T,
                           const int *seq_host, const int *ctx_host, int seq0, int prefix,
                           float *y, int mode, const si_captures *cap, bool timing,
-                          si_tp *tp = nullptr) {
+                          si_tp *tp = nullptr, const si_decode_state *st = nullptr) {
   const si_dims &d = l->d;
   const int H = d.hidden, QD = d.n_q_heads * d.head_dim, KVD = d.n_kv_heads * d.head_dim;
   SI_CHECK(mode == SI_LAYER_ATTN || mode == SI_LAYER_FULL, "bad layer mode");
@@ -1196,7 +1215,15 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
            ctx->head_dim);
   SI_CHECK(T > 0 && x && y, "bad step arguments");
   int max_len = 0;
-  if (ctx_host) {
+  if (st) {
+    // Lengths are on the device: the kernels bound every position by the
+    // cache (rope_kv appends nothing past it, attention clamps), and the
+    // split count covers the whole cache.
+    SI_CHECK(st->ctx == ctx && T == st->batch && st->max_ctx == kv->max_ctx &&
+                 kv->max_ctx <= ctx->max_positions,
+             "decode state does not match this context, batch or cache");
+    max_len = kv->max_ctx;
+  } else if (ctx_host) {
     for (int t = 0; t < T; ++t) {
       SI_CHECK(ctx_host[t] >= 1 && ctx_host[t] <= kv->max_ctx && ctx_host[t] <= ctx->max_positions,
                "context length %d out of range [1, %d]", ctx_host[t], kv->max_ctx);
@@ -1209,16 +1236,33 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
              "prefill range [%d, %d) exceeds the cache", prefix, prefix + T);
     max_len = prefix + T;
   }
-  const int nsplit = si::attn_pick_splits(T, ctx_host != nullptr, max_len);
+  const bool decode_form = ctx_host != nullptr || st != nullptr;
+  const int nsplit = si::attn_pick_splits(T, decode_form, max_len);
   SI_TRY(ctx->work.reserve(step_bytes(d, T, nsplit, true)));
   StepBuffers b = carve(ctx->work.p, d, T, nsplit);
   cudaStream_t s = ctx->stream;
 
-  // Per-token sequence / position / context arrays for the decode form, staged
-  // through a ring of pinned slots: a slot is rewritten only after its previous
-  // copy has run, so the host can queue several steps ahead without draining
-  // the stream.
-  if (ctx_host) {
+  // Per-token sequence / position / context arrays for the decode form: from
+  // the device state, as kernel parameters (up to kIdxMaxByValue tokens: no
+  // staging buffer and no host synchronisation), or staged through a ring of
+  // pinned slots, a slot rewritten only after its previous copy has run.
+  if (st) {
+    b.tok_seq = st->idx;
+    b.tok_pos = st->idx + T;
+    b.tok_ctx = st->idx + 2 * T;
+  } else if (ctx_host && T <= si::kIdxMaxByValue) {
+    si::IdxParams ip;
+    ip.T = T;
+    for (int t = 0; t < T; ++t) {
+      ip.seq[t] = seq_host[t];
+      ip.ctx[t] = ctx_host[t];
+    }
+    SI_TRY(ctx->idx.reserve((size_t)3 * T * sizeof(int)));
+    SI_CUDA(si::launch_set_idx(ip, static_cast<int *>(ctx->idx.p), s));
+    b.tok_seq = static_cast<int *>(ctx->idx.p);
+    b.tok_pos = b.tok_seq + T;
+    b.tok_ctx = b.tok_seq + 2 * T;
+  } else if (ctx_host) {
     constexpr int kIdxSlots = 4;
     size_t n = (size_t)3 * T;
     if (ctx->pinned_idx_n < n) {
@@ -1326,6 +1370,12 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
     }
     if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_MLP], s));
   }
+  // A step on its own (not part of a device-state step) moves the group's
+  // epoch counter past its exchanges at once.
+  if (tp && !st && tp->pending) {
+    SI_CUDA(si::launch_epoch_advance(tp->epoch_dev, tp->pending, s));
+    tp->pending = 0;
+  }
   return SI_OK;
 }
 
@@ -1338,6 +1388,95 @@ extern "C" SI_API si_status si_decode_step_dev(si_ctx *ctx, si_layer *l, si_kv *
   std::vector<int> seqs(batch);
   for (int i = 0; i < batch; ++i) seqs[i] = i;
   return run_step(ctx, l, kv, x, batch, seqs.data(), ctx_lens, 0, 0, y, mode, cap, false);
+}
+
+extern "C" SI_API si_status si_decode_state_create(si_ctx *ctx, int batch, const int *ctx_lens,
+                                                   int max_ctx, si_decode_state **out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(out && ctx_lens && batch > 0 && batch <= si::kIdxMaxByValue && max_ctx > 0,
+           "bad decode state arguments (1 <= batch <= %d)", si::kIdxMaxByValue);
+  for (int i = 0; i < batch; ++i)
+    SI_CHECK(ctx_lens[i] >= 1 && ctx_lens[i] <= max_ctx, "context length %d out of range [1, %d]",
+             ctx_lens[i], max_ctx);
+  si_decode_state *st = new si_decode_state();
+  st->ctx = ctx;
+  st->batch = batch;
+  st->max_ctx = max_ctx;
+  if (cudaMalloc(&st->idx, (size_t)3 * batch * sizeof(int)) != cudaSuccess) {
+    delete st;
+    return fail(SI_ERR_OOM, "decode state");
+  }
+  si::IdxParams ip;
+  ip.T = batch;
+  for (int i = 0; i < batch; ++i) {
+    ip.seq[i] = i;
+    ip.ctx[i] = ctx_lens[i];
+  }
+  cudaError_t e = si::launch_set_idx(ip, st->idx, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    cudaFree(st->idx);
+    delete st;
+    return fail(SI_ERR_CUDA, "decode state: %s", cudaGetErrorString(e));
+  }
+  *out = st;
+  return SI_OK;
+}
+
+extern "C" SI_API void si_decode_state_free(si_decode_state *st) {
+  if (!st) return;
+  if (st->ctx && set_device(st->ctx) == SI_OK) {
+    cudaStreamSynchronize(st->ctx->stream);
+    cudaFree(st->idx);
+  }
+  delete st;
+}
+
+extern "C" SI_API si_status si_decode_state_set(si_ctx *ctx, si_decode_state *st,
+                                                const int *ctx_lens) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(st && st->ctx == ctx && ctx_lens, "bad arguments");
+  si::IdxParams ip;
+  ip.T = st->batch;
+  for (int i = 0; i < st->batch; ++i) {
+    SI_CHECK(ctx_lens[i] >= 1 && ctx_lens[i] <= st->max_ctx,
+             "context length %d out of range [1, %d]", ctx_lens[i], st->max_ctx);
+    ip.seq[i] = i;
+    ip.ctx[i] = ctx_lens[i];
+  }
+  SI_CUDA(si::launch_set_idx(ip, st->idx, ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_decode_state_advance(si_ctx *ctx, si_decode_state *st) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(st && st->ctx == ctx, "decode state of another context");
+  SI_CUDA(si::launch_advance_idx(st->idx, st->batch, st->max_ctx, ctx->err, ctx->stream));
+  if (st->tp && st->tp->pending) {
+    SI_CUDA(si::launch_epoch_advance(st->tp->epoch_dev, st->tp->pending, ctx->stream));
+    st->tp->pending = 0;
+  }
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_decode_state_read(si_ctx *ctx, si_decode_state *st,
+                                                 int *ctx_lens) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(st && st->ctx == ctx && ctx_lens, "bad arguments");
+  SI_CUDA(cudaMemcpyAsync(ctx_lens, st->idx + 2 * st->batch, st->batch * sizeof(int),
+                          cudaMemcpyDeviceToHost, ctx->stream));
+  SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  return SI_OK;
+}
+
+extern "C" SI_API si_status si_decode_step_state_dev(si_ctx *ctx, si_layer *l, si_kv *kv,
+                                                     const float *x, si_decode_state *st,
+                                                     float *y, int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(l && kv && st, "null argument");
+  SI_CHECK(st->batch <= kv->batch, "batch %d exceeds the KV cache's %d", st->batch, kv->batch);
+  return run_step(ctx, l, kv, x, st->batch, nullptr, nullptr, 0, 0, y, mode, nullptr, false,
+                  nullptr, st);
 }
 
 extern "C" SI_API si_status si_prefill_dev(si_ctx *ctx, si_layer *l, si_kv *kv, int seq,
@@ -2143,8 +2282,15 @@ extern "C" SI_API si_status si_tp_create(si_ctx *ctx, const void *id, int rank, 
   tp->rank = rank;
   tp->world = world;
   tp->ctx = ctx;
+  if (cudaMalloc(&tp->epoch_dev, sizeof(unsigned long long)) != cudaSuccess ||
+      cudaMemset(tp->epoch_dev, 0, sizeof(unsigned long long)) != cudaSuccess) {
+    cudaFree(tp->epoch_dev);
+    delete tp;
+    return fail(SI_ERR_OOM, "TP epoch counter");
+  }
   ncclResult_t r = api->comm_init_rank(&tp->comm, world, uid, rank);
   if (r != ncclSuccess) {
+    cudaFree(tp->epoch_dev);
     delete tp;
     return fail(SI_ERR_CUDA, "ncclCommInitRank: %s", api->error_string(r));
   }
@@ -2156,6 +2302,7 @@ extern "C" SI_API void si_tp_free(si_tp *tp) {
   if (!tp) return;
   if (tp->sym && tp->ctx && set_device(tp->ctx) == SI_OK) tp_sym_release(tp->ctx, tp);
   if (tp->comm && nccl_api()) nccl_api()->comm_destroy(tp->comm);
+  if (tp->epoch_dev && tp->ctx && set_device(tp->ctx) == SI_OK) cudaFree(tp->epoch_dev);
   delete tp;
 }
 
@@ -2296,6 +2443,19 @@ extern "C" SI_API si_status si_decode_step_tp_dev(si_ctx *ctx, si_tp *tp, si_lay
   std::vector<int> seqs(batch);
   for (int i = 0; i < batch; ++i) seqs[i] = i;
   return run_step(ctx, l, kv, x, batch, seqs.data(), ctx_lens, 0, 0, y, mode, nullptr, false, tp);
+}
+
+extern "C" SI_API si_status si_decode_step_state_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l,
+                                                        si_kv *kv, const float *x,
+                                                        si_decode_state *st, float *y,
+                                                        int mode) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(tp && l && kv && st, "null argument");
+  SI_CHECK(st->batch <= kv->batch, "batch %d exceeds the KV cache's %d", st->batch, kv->batch);
+  SI_CHECK(!st->tp || st->tp == tp, "decode state used with another TP group");
+  st->tp = tp;
+  return run_step(ctx, l, kv, x, st->batch, nullptr, nullptr, 0, 0, y, mode, nullptr, false, tp,
+                  st);
 }
 
 extern "C" SI_API si_status si_prefill_tp_dev(si_ctx *ctx, si_tp *tp, si_layer *l, si_kv *kv,

@@ -19,8 +19,16 @@ struct PeerOut {
   int world;                  // 0: no peer output
   int rank;
   int slot;                   // words per receive slot (>= M * N)
-  unsigned long long epoch;   // this call's number, 1, 2, ...; parity picks the slot set
+  unsigned long long epoch;   // this call's number (1, 2, ...), or its offset from
+                              // *epoch_base; the parity picks the slot set
+  const unsigned long long *epoch_base;  // device counter added to epoch, or null
 };
+
+// The call's effective epoch, read after griddepcontrol.wait (the counter is
+// advanced by an earlier kernel of the stream).
+__device__ __forceinline__ unsigned long long peer_epoch(const PeerOut &p) {
+  return p.epoch + (p.epoch_base ? *p.epoch_base : 0ull);
+}
 
 
 // ---- layout.cu -------------------------------------------------------------
@@ -137,6 +145,16 @@ struct RopeKvArgs {
   int max_positions;
 };
 cudaError_t launch_rope_kv(const RopeKvArgs &a, cudaStream_t s);
+// Decode-step index arrays [seq T][pos T][ctx T] (pos = ctx - 1).
+constexpr int kIdxMaxByValue = 256;
+struct IdxParams {
+  int T;
+  int seq[kIdxMaxByValue];
+  int ctx[kIdxMaxByValue];
+};
+cudaError_t launch_set_idx(const IdxParams &p, int *idx, cudaStream_t s);
+// All positions / lengths + 1, bounded by max_ctx (SI_ERR_INVALID past it).
+cudaError_t launch_advance_idx(int *idx, int T, int max_ctx, int *err, cudaStream_t s);
 
 // ---- attention.cu -----------------------------------------------------------
 struct AttnArgs {
@@ -172,5 +190,7 @@ cudaError_t launch_attention_tc(const AttnArgs &a, void *scratch, size_t scratch
 // carries the epoch.
 cudaError_t launch_tp_combine(const PeerOut &p, const float *resid, float *y, size_t n,
                               unsigned long long timeout_ns, int *err, cudaStream_t s);
+// *counter += n: the exchanges of a finished step move the epoch base on.
+cudaError_t launch_epoch_advance(unsigned long long *counter, unsigned n, cudaStream_t s);
 
 }  // namespace si

@@ -28,10 +28,11 @@ __device__ __forceinline__ float peer_word(const unsigned long long *p, unsigned
   return __uint_as_float((unsigned)w);
 }
 
-// Word i of source rank src of this call's slot set, on this rank.
-__device__ __forceinline__ const unsigned long long *peer_slot(const PeerOut &p, int src) {
+// Word 0 of source rank src's slot for the call of effective epoch ep, on this rank.
+__device__ __forceinline__ const unsigned long long *peer_slot(const PeerOut &p,
+                                                               unsigned long long ep, int src) {
   return reinterpret_cast<const unsigned long long *>(p.base[p.rank] + kPeerData) +
-         ((size_t)(p.epoch & 1) * p.world + src) * p.slot;
+         ((size_t)(ep & 1) * p.world + src) * p.slot;
 }
 
 }  // namespace si

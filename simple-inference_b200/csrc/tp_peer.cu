@@ -29,18 +29,28 @@ __global__ void __launch_bounds__(256) k_tp_combine(const PeerOut p, const float
   pdl_trigger();
   pdl_wait();
   const unsigned long long deadline = globaltimer() + timeout_ns;
-  const unsigned ep = (unsigned)p.epoch;
+  const unsigned long long ep64 = peer_epoch(p);
+  const unsigned ep = (unsigned)ep64;
   bool bad = false;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    float s = peer_word(peer_slot(p, 0) + i, ep, deadline, err, bad);
+    float s = peer_word(peer_slot(p, ep64, 0) + i, ep, deadline, err, bad);
     for (int src = 1; src < p.world; ++src)
-      s = __fadd_rn(s, peer_word(peer_slot(p, src) + i, ep, deadline, err, bad));
+      s = __fadd_rn(s, peer_word(peer_slot(p, ep64, src) + i, ep, deadline, err, bad));
     if (bad) return;
     y[i] = resid ? __fadd_rn(resid[i], s) : s;
   }
 }
+__global__ void k_epoch_advance(unsigned long long *counter, unsigned n) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) *counter += n;
+}
 }  // namespace
+
+cudaError_t launch_epoch_advance(unsigned long long *counter, unsigned n, cudaStream_t s) {
+  return launch_pdl(k_epoch_advance, dim3(1), dim3(32), 0, s, counter, n);
+}
 
 cudaError_t launch_tp_combine(const PeerOut &p, const float *resid, float *y, size_t n,
                               unsigned long long timeout_ns, int *err, cudaStream_t s) {

@@ -135,6 +135,13 @@ def lib() -> C.CDLL:
         "si_attention_decode_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, vp, vp]),
         "si_attention_prefill_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, i32, i32, vp]),
         "si_ctx_set_exact_attention": (i32, [vp, i32]),
+        "si_decode_state_create": (i32, [vp, i32, vp, i32, pp]),
+        "si_decode_state_free": (None, [vp]),
+        "si_decode_state_advance": (i32, [vp, vp]),
+        "si_decode_state_set": (i32, [vp, vp, vp]),
+        "si_decode_state_read": (i32, [vp, vp, vp]),
+        "si_decode_step_state_dev": (i32, [vp, vp, vp, vp, vp, vp, i32]),
+        "si_decode_step_state_tp_dev": (i32, [vp, vp, vp, vp, vp, vp, vp, i32]),
         "si_graph_begin": (i32, [vp]),
         "si_graph_end": (i32, [vp, pp]),
         "si_graph_launch": (i32, [vp, vp]),
@@ -324,6 +331,14 @@ class Context:
         check(self.L.si_attention_prefill_dev(self.h, kv.h, C.byref(dm), _p(q), ntok, seq, prefix,
                                               _p(out)), "si_attention_prefill_dev")
 
+    def decode_state(self, ctx_lens, max_ctx: int) -> "DecodeState":
+        """Device-resident decode positions for a batch (see si_decode_state_create)."""
+        lens = (C.c_int * len(ctx_lens))(*ctx_lens)
+        h = C.c_void_p()
+        check(self.L.si_decode_state_create(self.h, len(ctx_lens), lens, max_ctx, C.byref(h)),
+              "si_decode_state_create")
+        return DecodeState(self, h, len(ctx_lens))
+
     def set_exact_attention(self, exact: bool):
         """True: prefill attention by the fp32 kernel (bit-identical to decode
         steps); False (default): the tcgen05 tensor-core kernel."""
@@ -334,6 +349,34 @@ class Context:
         lens = (C.c_int * batch)(*ctx_lens)
         check(self.L.si_attention_decode_dev(self.h, kv.h, C.byref(dm), _p(q), batch, lens,
                                              _p(out)), "si_attention_decode_dev")
+
+
+class DecodeState:
+    def __init__(self, ctx: "Context", h, batch: int):
+        self.ctx, self.h, self.batch = ctx, h, batch
+
+    def advance(self):
+        check(self.ctx.L.si_decode_state_advance(self.ctx.h, self.h), "si_decode_state_advance")
+
+    def set(self, ctx_lens):
+        lens = (C.c_int * len(ctx_lens))(*ctx_lens)
+        check(self.ctx.L.si_decode_state_set(self.ctx.h, self.h, lens), "si_decode_state_set")
+
+    def lens(self) -> list:
+        out = (C.c_int * self.batch)()
+        check(self.ctx.L.si_decode_state_read(self.ctx.h, self.h, out), "si_decode_state_read")
+        return list(out)
+
+    def free(self):
+        if self.h:
+            self.ctx.L.si_decode_state_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 class Graph:
@@ -448,6 +491,10 @@ class Layer:
         check(self.ctx.L.si_decode_step_dev(self.ctx.h, self.h, kv.h, _p(x), len(ctx_lens),
                                             lens, _p(y), mode, None), "si_decode_step_dev")
 
+    def decode_state_dev(self, kv: "KV", x, state: "DecodeState", y, mode=SI_LAYER_ATTN):
+        check(self.ctx.L.si_decode_step_state_dev(self.ctx.h, self.h, kv.h, _p(x), state.h,
+                                                  _p(y), mode), "si_decode_step_state_dev")
+
     def prefill(self, kv: "KV", seq, x_host, ntok, prefix, y_host, mode=SI_LAYER_ATTN):
         check(self.ctx.L.si_prefill(self.ctx.h, self.h, kv.h, seq, _p(x_host), ntok, prefix,
                                     _p(y_host), mode), "si_prefill")
@@ -489,6 +536,11 @@ class TP:
         check(self.ctx.L.si_decode_step_tp_dev(self.ctx.h, self.h, layer.h, kv.h, _p(x),
                                                len(ctx_lens), lens, _p(y), mode),
               "si_decode_step_tp_dev")
+
+    def decode_state_dev(self, layer: "Layer", kv: "KV", x, state, y, mode=SI_LAYER_FULL):
+        check(self.ctx.L.si_decode_step_state_tp_dev(self.ctx.h, self.h, layer.h, kv.h, _p(x),
+                                                     state.h, _p(y), mode),
+              "si_decode_step_state_tp_dev")
 
     def prefill_dev(self, layer: "Layer", kv: "KV", seq, x, ntok, prefix, y, mode=SI_LAYER_FULL):
         check(self.ctx.L.si_prefill_tp_dev(self.ctx.h, self.h, layer.h, kv.h, seq, _p(x), ntok,

@@ -8,7 +8,8 @@ last) exactly as in the 72B tensor-parallel stack.  Decode runs both ways the gr
 add the row-parallel partial sums: fused into the projection (peer stores over
 NVLink plus a flag-gated combine kernel) and through NCCL's all-reduce.
 Five consecutive decode steps exercise both receive-slot parities and the
-flag epochs.  Cross-rank summation reorders the fp32 sums, so at two and four
+flag epochs, eagerly and as replays of one captured step whose exchange epochs
+come from a device counter (same bits required).  Cross-rank summation reorders the fp32 sums, so at two and four
 ranks the bar is the layer bar, 1e-3; every rank must hold identical outputs.
 
 At eight ranks and 72B dimensions a reordered sum cannot be held to 1e-3
@@ -69,6 +70,43 @@ def _decode(ctx, step, dims, k, v, x):
     return np.stack(out)
 
 
+def _decode_graph(ctx, tp, layer, dims, k, v, x):
+    """The fused decode steps again, with device-resident lengths: the first
+    step eager, the rest replays of one captured step (input copied into the
+    captured input buffer before each replay)."""
+    import sib200
+    kvd = dims["n_kv_heads"] * dims["head_dim"]
+    kv = ctx.kv(dims, BATCH, L, True)
+    for b in range(BATCH):
+        kv.write(b, 0, np.ascontiguousarray(k[:CTX - 1, :kvd]), np.ascontiguousarray(v[:CTX - 1, :kvd]))
+    st = ctx.decode_state([CTX] * BATCH, L)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    xin = torch.from_numpy(x[0]).cuda()
+    y = torch.zeros_like(xin)
+    xs = [torch.from_numpy(x[s]).cuda() for s in range(STEPS)]
+    torch.cuda.synchronize()
+
+    def step():
+        tp.decode_state_dev(layer, kv, xin, st, y, sib200.SI_LAYER_FULL)
+        st.advance()
+    out = []
+    step()
+    ctx.sync()
+    out.append(y.cpu().numpy())
+    graph = ctx.capture(step)
+    for s in range(1, STEPS):
+        with torch.cuda.stream(stream):
+            xin.copy_(xs[s])
+        graph.launch()
+        ctx.sync()
+        out.append(y.cpu().numpy())
+    ctx.status()
+    graph.free()
+    st.free()
+    kv.free()
+    return np.stack(out)
+
+
 def _prefill(ctx, step, dims, k, v, X):
     kvd = dims["n_kv_heads"] * dims["head_dim"]
     kv = ctx.kv(dims, 1, L, True)
@@ -96,6 +134,9 @@ def _rank(rank, world, uid, path):
     layer = ctx.layer_tp_synth(FULL, SEED, rank, world)
     dec = lambda kv, xin, lens, y: tp.decode_dev(layer, kv, xin, lens, y)
     fused = _decode(ctx, dec, d, ks, vs, x)
+    graphed = _decode_graph(ctx, tp, layer, d, ks, vs, x)
+    # device-counted epochs and graph replays: the same bits as the eager steps
+    np.testing.assert_array_equal(graphed, fused)
     tp.set_options(fused=False)
     nccl = _decode(ctx, dec, d, ks, vs, x)
     tp.set_options(fused=True)
