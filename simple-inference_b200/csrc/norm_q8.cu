@@ -73,18 +73,17 @@ __global__ void __launch_bounds__(512) k_rmsnorm_q8(const float *__restrict__ x,
     const unsigned long long ep64 = peer_epoch(rp.p);
     const unsigned ep = (unsigned)ep64;
     bool bad = false;
+    const unsigned long long *slot[kPeerMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kPeerMaxWorld; ++r)
+      slot[r] = peer_slot(rp.p, ep64, r < rp.p.world ? r : 0);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int i = threadIdx.x + j * blockDim.x;
       if (i < n4) {
         const size_t e0 = (size_t)row * n + 4 * i;
         float sum[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sum[c] = peer_word(peer_slot(rp.p, ep64, 0) + e0 + c, ep, deadline, rp.err, bad);
-        for (int src = 1; src < rp.p.world; ++src)
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            sum[c] = __fadd_rn(sum[c], peer_word(peer_slot(rp.p, ep64, src) + e0 + c, ep, deadline, rp.err, bad));
+        peer_sum4(slot, rp.p.world, e0, ep, deadline, rp.err, bad, sum);
         v[j] = make_float4(__fadd_rn(v[j].x, sum[0]), __fadd_rn(v[j].y, sum[1]),
                            __fadd_rn(v[j].z, sum[2]), __fadd_rn(v[j].w, sum[3]));
         if (!bad) reinterpret_cast<float4 *>(rp.h_out + (size_t)row * n)[i] = v[j];

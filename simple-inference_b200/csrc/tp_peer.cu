@@ -32,11 +32,12 @@ __global__ void __launch_bounds__(256) k_tp_combine(const PeerOut p, const float
   const unsigned long long ep64 = peer_epoch(p);
   const unsigned ep = (unsigned)ep64;
   bool bad = false;
+  const unsigned long long *slot[kPeerMaxWorld];
+#pragma unroll
+  for (int r = 0; r < kPeerMaxWorld; ++r) slot[r] = peer_slot(p, ep64, r < p.world ? r : 0);
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
-    float s = peer_word(peer_slot(p, ep64, 0) + i, ep, deadline, err, bad);
-    for (int src = 1; src < p.world; ++src)
-      s = __fadd_rn(s, peer_word(peer_slot(p, ep64, src) + i, ep, deadline, err, bad));
+    const float s = peer_sum(slot, p.world, i, ep, deadline, err, bad);
     if (bad) return;
     y[i] = resid ? __fadd_rn(resid[i], s) : s;
   }
