@@ -760,8 +760,9 @@ def decode_gemv_roofline(ctx, torch, stream):
     """Kernel-level decode roofline where the GEMV is HBM-bound: the 72B down
     projection (8192 x 29568, 136 MB of Q4_0) at 1 token (dp4a form) and at 8
     tokens (tensor-core form, config 4's batch), and the 7B down projection at
-    1 token; weight copies (272-305 MB) rotate so every launch streams from
-    HBM; CUDA graph replays timed with CUDA events."""
+    1 token, each also from row-major GGUF blocks without the repack; weight
+    copies (272-305 MB) rotate so every launch streams from HBM; CUDA graph
+    replays timed with CUDA events."""
     pk = peaks()
     out = {}
     for label, N, K, M, ncopy in (("72B down, 1 token", 8192, 29568, 1, 2),
@@ -787,6 +788,21 @@ def decode_gemv_roofline(ctx, torch, stream):
                       "peak_gbs": pk["hbm_gbs"], "peak_src": pk["src"],
                       "frac": round(wb / t / 1e9 / pk["hbm_gbs"], 4)}
         gph.free()
+        if M <= 8:
+            # The same projection from row-major GGUF blocks (no repack).
+            gg = [torch.from_numpy(m.download_gguf()).cuda() for m in mats]
+            torch.cuda.synchronize()
+            gph = ctx.capture(lambda: [ctx.matvec_gguf(w_, N, K, qs, d, M, None, y) for w_ in gg])
+            for _ in range(3):
+                gph.launch()
+            t = time_region(torch, stream, lambda i: gph.launch(), reps) / (reps * ncopy)
+            out[label + ", row-major GGUF (no repack)"] = {
+                "kernel": "k_gemv_gguf", "shape": f"{N}x{K}", "tokens": M,
+                "us": round(t * 1e6, 2), "weight_bytes": wb,
+                "achieved_gbs": round(wb / t / 1e9, 1), "peak_gbs": pk["hbm_gbs"],
+                "frac": round(wb / t / 1e9 / pk["hbm_gbs"], 4)}
+            gph.free()
+            del gg
         for m in mats:
             m.free()
     return out

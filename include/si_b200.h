@@ -241,6 +241,13 @@ SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const int8_t *qs
 SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w, const int8_t *qs_dev,
                                       const uint16_t *d_dev, int M, const float *bias_dev,
                                       float *out_dev, int kernel);
+/* matvec_q4q8 (qwen_one_layer.c:148-162) for M <= 8 tokens straight from
+ * row-major GGUF Q4_0 blocks in device memory (rows x cols/32 blocks of 18
+ * bytes, the reference's own layout), no repack: the same bits as the
+ * repacked GEMV.  cols % 128 == 0; weights and qs 16-byte aligned. */
+SI_API si_status si_matvec_gguf_dev(si_ctx *ctx, const uint8_t *w_gguf_dev, int rows, int cols,
+                                    const int8_t *qs_dev, const uint16_t *d_dev, int M,
+                                    const float *bias_dev, float *out_dev);
 /* The tcgen05 GEMM of si_matmul_dev_kernel(..., 1) with the same results, but
  * allocating nothing: its scratch (the transposed fp32 activation scales,
  * (cols/32) * round_up(M, 4) * 4 bytes) is a fixed array of

@@ -590,6 +590,21 @@ extern "C" SI_API si_status si_matmul_dev(si_ctx *ctx, const si_matrix *w, const
   return matmul(ctx, w, qs, d, M, bias, nullptr, out, -1);
 }
 
+extern "C" SI_API si_status si_matvec_gguf_dev(si_ctx *ctx, const uint8_t *w_gguf, int rows,
+                                               int cols, const int8_t *qs, const uint16_t *d,
+                                               int M, const float *bias, float *out) {
+  SI_TRY(set_device(ctx));
+  SI_CHECK(w_gguf && qs && d && out, "null pointer");
+  if (!si::gemv_gguf_supported(rows, cols, M))
+    return fail(SI_ERR_UNSUPPORTED,
+                "row-major GGUF GEMV needs cols %% 128 == 0 and 1 <= M <= 8 (got %dx%d, M=%d)",
+                rows, cols, M);
+  SI_CHECK(((reinterpret_cast<uintptr_t>(w_gguf) | reinterpret_cast<uintptr_t>(qs)) & 15) == 0,
+           "weights and activations must be 16-byte aligned");
+  SI_CUDA(si::launch_gemv_gguf(w_gguf, rows, cols, qs, d, M, bias, out, ctx->stream));
+  return SI_OK;
+}
+
 extern "C" SI_API si_status si_matmul_dev_kernel(si_ctx *ctx, const si_matrix *w,
                                                  const int8_t *qs, const uint16_t *d, int M,
                                                  const float *bias, float *out, int kernel) {

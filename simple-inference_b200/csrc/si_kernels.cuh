@@ -111,6 +111,13 @@ struct GemvArgs {
 enum { kGemvAuto = 0, kGemvDp4a = 1, kGemvMma = 2 };
 cudaError_t launch_gemv(const GemvArgs &a, bool swiglu, cudaStream_t s);
 
+// ---- gemv_gguf.cu (row-major GGUF Q4_0, no repack) ------------------------------
+// out[M][N] = bias + blocks in order, from GGUF rows [N][K/32] x 18 B; K % 128,
+// 1 <= M <= 8; w and xq 16-byte aligned.
+bool gemv_gguf_supported(int N, int K, int M);
+cudaError_t launch_gemv_gguf(const uint8_t *w, int N, int K, const int8_t *xq, const uint16_t *xd,
+                             int M, const float *bias, float *out, cudaStream_t s);
+
 // ---- gemm_tc.cu (tcgen05) ------------------------------------------------------
 cudaError_t launch_gemm_tc(const GemvArgs &a, bool swiglu, cudaStream_t s);
 bool gemm_tc_supported(int N, int K, int M);

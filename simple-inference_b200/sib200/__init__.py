@@ -135,6 +135,7 @@ def lib() -> C.CDLL:
         "si_attention_decode_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, vp, vp]),
         "si_attention_prefill_dev": (i32, [vp, vp, C.POINTER(Dims), vp, i32, i32, i32, vp]),
         "si_ctx_set_exact_attention": (i32, [vp, i32]),
+        "si_matvec_gguf_dev": (i32, [vp, vp, i32, i32, vp, vp, i32, vp, vp]),
         "si_decode_state_create": (i32, [vp, i32, vp, i32, pp]),
         "si_decode_state_free": (None, [vp]),
         "si_decode_state_advance": (i32, [vp, vp]),
@@ -261,6 +262,11 @@ class Context:
         else:
             check(self.L.si_matmul_dev_kernel(self.h, w.h, _p(qs), _p(d), M, _p(bias), _p(out),
                                               kernel), "si_matmul_dev_kernel")
+
+    def matvec_gguf(self, w_gguf, rows, cols, qs, d, M, bias, out):
+        """GEMV straight from row-major GGUF Q4_0 bytes on the device (no repack)."""
+        check(self.L.si_matvec_gguf_dev(self.h, _p(w_gguf), rows, cols, _p(qs), _p(d), M,
+                                        _p(bias), _p(out)), "si_matvec_gguf_dev")
 
     def block_isums(self, w: "Matrix", qs, M, out):
         check(self.L.si_block_isums_dev(self.h, w.h, _p(qs), M, _p(out)), "si_block_isums_dev")
