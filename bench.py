@@ -69,10 +69,10 @@ H1, I1, QKV1 = 1536, 8960, 2048          # config 1: the 1.5B projection set
 C1_COPIES, C1_M = 10, 2048
 SWEEP_M = (1, 16, 128, 512, 2048)
 # DRAM bytes (read + write) of one launch of the headline's dominant kernel,
-# from an `ncu --set full -k regex:k_gemm -c 1` capture of
+# from an `ncu --set full -k regex:k_gemm_q4q8 -s 1 -c 1` capture of
 # `bench.py --probe gateup-72b` (its gate/up GEMM at 4096 tokens on one 72B
-# layer); None until captured for the current kernel.
-NCU_TRAFFIC_GATEUP_72B = None
+# layer): 324.2 MB read + 126.3 MB written.  Re-measure when the kernel changes.
+NCU_TRAFFIC_GATEUP_72B = 450505728
 
 
 def peaks():
@@ -1108,8 +1108,29 @@ def probe_config2_decode():
     print("ok")
 
 
+def probe_attn_prefill_72b():
+    """The prefill attention of one 72B layer (4096 causal tokens, 64 Q / 8 KV
+    heads, fp32 KV) through the default (tcgen05) kernel, three launches, no
+    timing."""
+    import torch
+    import sib200
+    torch.cuda.set_device(0)
+    ctx = sib200.Context(0, max_positions=TP_PREFILL, rope_theta=1e6, head_dim=128)
+    dims = dict(CONFIG4, intermediate=0)
+    kv = ctx.kv(dims, 1, TP_PREFILL, True)
+    kv.fill_synth(4, 1.0, TP_PREFILL)
+    q = torch.randn(TP_PREFILL * CONFIG4["n_q_heads"] * 128, device="cuda")
+    out = torch.empty_like(q)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        ctx.attention_prefill(kv, dims, q, TP_PREFILL, 0, 0, out)
+    ctx.sync()
+    ctx.status()
+    print("ok")
+
+
 PROBES = {"config4-layer": probe_config4_layer, "config2-decode": probe_config2_decode,
-          "gateup-72b": probe_gateup_72b}
+          "gateup-72b": probe_gateup_72b, "attn-prefill-72b": probe_attn_prefill_72b}
 
 
 def main():

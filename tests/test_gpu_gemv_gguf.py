@@ -27,7 +27,8 @@ def test_gguf_gemv_bit_exact(si_ctx, oc, N, K, M):
         w = m.download_gguf()
     else:
         w = synth.random_q4(rng, N, K)
-        m = si_ctx.matrix(w, N, K)
+        # the repacked layout needs whole 32-row tiles; the GGUF GEMV does not
+        m = si_ctx.matrix(w, N, K) if N % 32 == 0 else None
     x = rng.standard_normal((M, K)).astype(np.float32)
     bias = rng.normal(0, 0.02, N).astype(np.float32)
     xd = dev(x)
@@ -41,9 +42,11 @@ def test_gguf_gemv_bit_exact(si_ctx, oc, N, K, M):
     b = dev(bias)
     torch.cuda.synchronize()
     si_ctx.matvec_gguf(wg, N, K, qs, d, M, b, got)
-    si_ctx.matmul(m, qs, d, M, b, want, kernel=0)
+    if m is not None:
+        si_ctx.matmul(m, qs, d, M, b, want, kernel=0)
     si_ctx.status()
-    assert torch.equal(got, want)
+    if m is not None:
+        assert torch.equal(got, want)
     blk = torch.zeros(M * K // 32 * 34, dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
     si_ctx.q8_to_blocks(qs, d, M, K, blk)
@@ -55,7 +58,8 @@ def test_gguf_gemv_bit_exact(si_ctx, oc, N, K, M):
         np.testing.assert_array_equal(
             g[t, rows], oc.matvec(w.reshape(N, -1)[rows], blk[t], K, rows.stop, bias[rows]),
             f"token {t}")
-    m.free()
+    if m is not None:
+        m.free()
 
 
 def test_gguf_gemv_rejects_unsupported(si_ctx):
