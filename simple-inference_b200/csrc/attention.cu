@@ -33,6 +33,8 @@
 // of 128 keys in shared memory, S = Q.K^T and P.V as register-tiled fp32 FMA
 // chains (two chains per packed f32x2 FMA), and the same merges, so it needs
 // no split scratch.
+#include <type_traits>
+
 #include "si_common.cuh"
 #include "si_kernels.cuh"
 #include "si_tma.cuh"
@@ -121,25 +123,57 @@ struct DecShape {
   static constexpr int ES = F32 ? 4 : 2;
   static constexpr int RB = D * ES;     // bytes per K row
   static constexpr int CPR = RB / 16;   // 16-byte chunks per row (8..32)
+  static constexpr int RPI = 32 / CPR;  // rows one warp-wide cp.async covers
+  static constexpr int NV = D / 32;     // dims per lane in P.V
   static constexpr int Q = kMaxGroup * D * 4;
-  static constexpr int KW = kSub * RB;  // one warp's K rows (>= its G x D merge floats)
-  static constexpr int P = kSub * kMaxGroup * 4;
-  static constexpr int bytes() { return Q + kSubPerSplit * (KW + P) + kSubPerSplit * kMaxGroup * 8; }
-  static_assert(CPR >= 8, "the row swizzle needs at least 8 chunks per row");
-  static_assert(KW >= kMaxGroup * D * 4, "the merge floats must fit over the K rows");
+  static constexpr int KW = kSub * RB;  // one warp's K rows; later its P, then its O
+  static constexpr int PB = kSub * kMaxGroup * 8;  // P as (p, p) pairs per key and head
+  static constexpr int bytes() { return Q + kSubPerSplit * KW + kSubPerSplit * kMaxGroup * 8; }
+  static_assert(CPR >= 8 && CPR <= 32, "the row swizzle needs 8..32 chunks per row");
+  static_assert(KW >= PB && KW >= kMaxGroup * D * 4, "P and O must fit over the K rows");
 };
 
-template <int D, bool F32>
+// V row chunk of one lane (NV dims) as floats.
+template <int NV, bool F32>
+struct VRow {
+  using T = typename std::conditional<F32, typename std::conditional<NV == 4, float4, float2>::type,
+                                      typename std::conditional<NV == 4, uint2, uint32_t>::type>::type;
+  static __device__ __forceinline__ T load(const uint8_t *p) {
+    return __ldg(reinterpret_cast<const T *>(p));
+  }
+  static __device__ __forceinline__ T zero() { return T{}; }
+  static __device__ __forceinline__ void to_f32(const T &x, float (&v)[NV]) {
+    if constexpr (F32 && NV == 4) {
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else if constexpr (F32) {
+      v[0] = x.x; v[1] = x.y;
+    } else if constexpr (NV == 4) {
+      v[0] = f16_to_f32((uint16_t)x.x); v[1] = f16_to_f32((uint16_t)(x.x >> 16));
+      v[2] = f16_to_f32((uint16_t)x.y); v[3] = f16_to_f32((uint16_t)(x.y >> 16));
+    } else {
+      v[0] = f16_to_f32((uint16_t)x); v[1] = f16_to_f32((uint16_t)(x >> 16));
+    }
+  }
+};
+
+// One CTA per (split, KV head, token), one warp per 32-key sub-tile, NP pairs
+// of query heads (G <= 2 NP; a head past G computes on zero queries and is
+// never written).  Every per-key and per-dim loop is unrolled against
+// compile-time offsets from a few per-lane bases, and a full sub-tile (the
+// common case) runs without per-key predicates; a partial one zero-fills the
+// K rows past the context (their scores are masked to -inf, so p = 0) and
+// loads no V row there -- fmaf(0, 0, o) == o, so the results equal those of
+// skipping the keys.
+template <int D, bool F32, int NP>
 __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a) {
   using S = DecShape<D, F32>;
-  constexpr int NV = D / 32;  // dims per lane in P.V
+  using VR = VRow<S::NV, F32>;
+  constexpr int NV = S::NV, NH = 2 * NP;
   extern __shared__ __align__(16) uint8_t smem[];
-  float *q_s = reinterpret_cast<float *>(smem);                       // [G][D]
+  float *q_s = reinterpret_cast<float *>(smem);                       // [D][8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t *k_w = smem + S::Q + warp * S::KW;                           // [32][RB] swizzled
-  float *p_w = reinterpret_cast<float *>(smem + S::Q + kSubPerSplit * S::KW) +
-               warp * kSub * kMaxGroup;                                // [32][8]
-  float2 *ml_s = reinterpret_cast<float2 *>(smem + S::Q + kSubPerSplit * (S::KW + S::P));
+  float2 *ml_s = reinterpret_cast<float2 *>(smem + S::Q + kSubPerSplit * S::KW);  // [4][8]
 
   pdl_trigger();
   pdl_wait();
@@ -151,137 +185,162 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   if (split >= ns) return;  // this token needs fewer splits than the grid has
   const int key0 = (split * kSubPerSplit + warp) * kSub;
   const int nvalid = L - key0 < 0 ? 0 : (L - key0 > kSub ? kSub : L - key0);
-  const size_t rowstride = (size_t)Hkv * D;
-  const size_t base = (size_t)seq * a.max_ctx * rowstride + (size_t)kvh * D;
-  const uint8_t *kg = static_cast<const uint8_t *>(a.kc) + base * S::ES;
-  const uint8_t *vg = static_cast<const uint8_t *>(a.vc) + base * S::ES;
+  const uint32_t rsb = (uint32_t)Hkv * D * S::ES;  // bytes between positions
+  const size_t base = ((size_t)seq * a.max_ctx * Hkv + kvh) * D * S::ES;
+  const uint8_t *kg = static_cast<const uint8_t *>(a.kc) + base + (size_t)key0 * rsb;
+  const uint8_t *vg = static_cast<const uint8_t *>(a.vc) + base + (size_t)key0 * rsb +
+                      lane * NV * S::ES;
 
-  // This warp's K rows into shared memory; the group's queries.
-  for (int i = lane; i < nvalid * S::CPR; i += 32) {
-    const int r = i / S::CPR, c = i % S::CPR;
-    cp_async16(smem_u32(k_w + r * S::RB + ((c ^ (r & 7)) << 4)),
-               kg + ((size_t)(key0 + r) * rowstride) * S::ES + c * 16, 16);
+  // K rows into shared memory: lane = chunk (lane % CPR) of rows lane / CPR + RPI i,
+  // chunks XOR-swizzled by row so that lane = key reads are conflict-free.
+  constexpr int NI = kSub / S::RPI;
+  typename VR::T vb[16];  // V rows 0..15 of the sub-tile, in flight during the scores
+  if (nvalid > 0) {
+    const int c = lane % S::CPR, ro = lane / S::CPR;
+    const uint8_t *src = kg + (size_t)ro * rsb + c * 16;
+    const uint32_t dst = smem_u32(k_w) + ro * S::RB;
+    const uint32_t cr = (uint32_t)(c ^ ro) << 4;
+    if (nvalid == kSub) {
+#pragma unroll
+      for (int i = 0; i < NI; ++i)
+        cp_async16(dst + i * S::RPI * S::RB + (cr ^ (((S::RPI * i) & 7) << 4)),
+                   src + (size_t)(i * S::RPI) * rsb, 16);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)k * rsb);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const bool ok = ro + i * S::RPI < nvalid;
+        cp_async16(dst + i * S::RPI * S::RB + (cr ^ (((S::RPI * i) & 7) << 4)),
+                   ok ? src + (size_t)(i * S::RPI) * rsb : kg, ok ? 16 : 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) vb[k] = k < nvalid ? VR::load(vg + (size_t)k * rsb) : VR::zero();
+    }
+    // V rows 16..31 into L2 while the scores are computed.
+    constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
+    constexpr int RPP = 32 / LPR;             // rows per warp-wide prefetch
+    const uint8_t *vrow = static_cast<const uint8_t *>(a.vc) + base +
+                          (size_t)(key0 + 16 + lane / LPR) * rsb + (lane % LPR) * 128;
+#pragma unroll
+    for (int i = 0; i < (16 + RPP - 1) / RPP; ++i)
+      if (16 + lane / LPR + i * RPP < nvalid)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + (size_t)(i * RPP) * rsb));
   }
-  // This warp's V rows into L2 while the scores are computed (P.V then reads
-  // them straight from global memory, lane = dims).
-  constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
-  for (int i = lane; i < nvalid * LPR; i += 32) {
-    const uint8_t *p = vg + ((size_t)(key0 + i / LPR) * rowstride) * S::ES + (i % LPR) * 128;
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-  }
-  // Queries as [D][8 heads] (heads of one dim adjacent, for packed FMAs).
-  for (int i = threadIdx.x; i < kMaxGroup * D; i += blockDim.x) {
-    const int h = i / D, d = i % D;
-    q_s[d * kMaxGroup + h] = h < G ? a.q[((size_t)t * Hq + kvh * G + h) * D + d] : 0.0f;
+  // The group's queries as [D][8 heads] (heads of one dim adjacent).
+  if (threadIdx.x < D) {
+    const int d = threadIdx.x;
+    const float *qg = a.q + ((size_t)t * Hq + (size_t)kvh * G) * D + d;
+    float qv[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) qv[h] = h < G ? qg[(size_t)h * D] : 0.0f;
+    *reinterpret_cast<float4 *>(q_s + d * kMaxGroup) = make_float4(qv[0], qv[1], qv[2], qv[3]);
+    *reinterpret_cast<float4 *>(q_s + d * kMaxGroup + 4) = make_float4(qv[4], qv[5], qv[6], qv[7]);
   }
   cp_async_wait_all();
   __syncthreads();
 
-  // Heads in pairs (2q, 2q+1): two independent chains per packed FMA; each
-  // chain keeps the order of the procedure above.
-  constexpr int NP = kMaxGroup / 2;
-  float m[kMaxGroup], l[kMaxGroup];
-  float2 o2[NP][NV];
+  float m[NH], l[NH];
+  float2 o2[NH][NV / 2];  // head h, dims (2j, 2j+1) of this lane's NV
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
+  for (int h = 0; h < NH; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV / 2; ++j) o2[h][j] = make_float2(0.0f, 0.0f);
   }
-#pragma unroll
-  for (int q = 0; q < NP; ++q)
-#pragma unroll
-    for (int j = 0; j < NV; ++j) o2[q][j] = make_float2(0.0f, 0.0f);
   if (nvalid > 0) {
-    // Scores, lane = key.
+    // Scores, lane = key: heads in pairs (2q, 2q+1), two chains per packed FMA,
+    // each in the order d = 0..D-1.
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
     float2 s2[NP];
 #pragma unroll
     for (int q = 0; q < NP; ++q) s2[q] = make_float2(0.0f, 0.0f);
+    // Row `lane`, chunk c sits at byte ((c ^ (lane & 7)) << 4): one base per
+    // value of c & 7, the rest compile-time offsets.
     const uint8_t *kr = k_w + lane * S::RB;
-#pragma unroll 2
+    const uint8_t *kb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) kb[j] = kr + ((j ^ (lane & 7)) << 4);
+#pragma unroll
     for (int c4 = 0; c4 < D / 4; ++c4) {
-      // dims 4*c4 .. 4*c4+3 live in chunk (4*c4*ES)/16 at byte (4*c4*ES)%16
-      const int byte = c4 * 4 * S::ES;
-      const int c = byte >> 4;
-      const float4 k = load4<F32>(kr + (((c ^ (lane & 7)) << 4) | (byte & 15)));
+      const int byte = c4 * 4 * S::ES, c = byte >> 4;
+      const float4 k = load4<F32>(kb[c & 7] + (c & ~7) * 16 + (byte & 15));
       const float kd[4] = {k.x, k.y, k.z, k.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 kk = make_float2(kd[e], kd[e]);
-        const float4 qa = *reinterpret_cast<const float4 *>(q_s + (c4 * 4 + e) * kMaxGroup);
-        const float4 qb = *reinterpret_cast<const float4 *>(q_s + (c4 * 4 + e) * kMaxGroup + 4);
+        const float *qd = q_s + (c4 * 4 + e) * kMaxGroup;
+        const float4 qa = *reinterpret_cast<const float4 *>(qd);
         s2[0] = fma2(make_float2(qa.x, qa.y), kk, s2[0]);
-        if (G > 2) s2[1] = fma2(make_float2(qa.z, qa.w), kk, s2[1]);
-        if (G > 4) s2[2] = fma2(make_float2(qb.x, qb.y), kk, s2[2]);
-        if (G > 6) s2[3] = fma2(make_float2(qb.z, qb.w), kk, s2[3]);
+        if constexpr (NP > 1) s2[1] = fma2(make_float2(qa.z, qa.w), kk, s2[1]);
+        if constexpr (NP > 2) {
+          const float4 qb = *reinterpret_cast<const float4 *>(qd + 4);
+          s2[2] = fma2(make_float2(qb.x, qb.y), kk, s2[2]);
+          if constexpr (NP > 3) s2[3] = fma2(make_float2(qb.z, qb.w), kk, s2[3]);
+        }
       }
     }
+    __syncwarp();  // every lane is done with the K rows: P goes over them
+    float2 *p_w = reinterpret_cast<float2 *>(k_w);  // [32 keys][8 heads] as (p, p)
     const bool valid = lane < nvalid;
+    float pv[NH];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g < G) {
-        const float sg = (g & 1) ? s2[g >> 1].y : s2[g >> 1].x;
-        const float sc = valid ? __fmul_rn(sg, scale) : -INFINITY;
-        m[g] = warp_max(sc);
-        const float p = expf(__fsub_rn(sc, m[g]));
-        l[g] = warp_sum(p);
-        p_w[lane * kMaxGroup + g] = p;
-      } else {
-        p_w[lane * kMaxGroup + g] = 0.0f;
-      }
+    for (int h = 0; h < NH; ++h) {
+      const float sg = (h & 1) ? s2[h >> 1].y : s2[h >> 1].x;
+      const float sc = valid ? __fmul_rn(sg, scale) : -INFINITY;
+      m[h] = warp_max(sc);
+      pv[h] = expf(__fsub_rn(sc, m[h]));
+      l[h] = warp_sum(pv[h]);
     }
+#pragma unroll
+    for (int h = 0; h < NH; h += 2)
+      *reinterpret_cast<float4 *>(p_w + lane * kMaxGroup + h) =
+          make_float4(pv[h], pv[h], pv[h + 1], pv[h + 1]);
     __syncwarp();
-    // P.V, lane = dims NV*lane .. NV*lane+NV-1, keys in order.
-    const uint8_t *vr = vg + (size_t)key0 * rowstride * S::ES + lane * NV * S::ES;
-    for (int k0 = 0; k0 < nvalid; k0 += 8) {
-      float v[8][NV];
+    // P.V, lane = dims NV*lane .. NV*lane+NV-1, keys in order: o[h][d] =
+    // fmaf(p[key][h], v[key][d], o[h][d]), dims in packed pairs.
+    auto pv_key = [&](int k, const typename VR::T &vx) {
+      float v[NV];
+      VR::to_f32(vx, v);
+      const float4 *pk = reinterpret_cast<const float4 *>(p_w + k * kMaxGroup);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (k0 + k < nvalid) {
-          const uint8_t *p = vr + (size_t)(k0 + k) * rowstride * S::ES;
-          if constexpr (NV == 4) {
-            const float4 x = load4<F32>(p);
-            v[k][0] = x.x; v[k][1] = x.y; v[k][2] = x.z; v[k][3] = x.w;
-          } else if constexpr (F32) {
-            const float2 x = *reinterpret_cast<const float2 *>(p);
-            v[k][0] = x.x; v[k][1] = x.y;
-          } else {
-            const uint32_t x = *reinterpret_cast<const uint32_t *>(p);
-            v[k][0] = f16_to_f32((uint16_t)x); v[k][1] = f16_to_f32((uint16_t)(x >> 16));
-          }
+      for (int q = 0; q < NP; ++q) {
+        const float4 pp = pk[q];  // (p_2q, p_2q, p_2q+1, p_2q+1)
+#pragma unroll
+        for (int j = 0; j < NV / 2; ++j) {
+          const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
+          o2[2 * q][j] = fma2(make_float2(pp.x, pp.y), vv, o2[2 * q][j]);
+          o2[2 * q + 1][j] = fma2(make_float2(pp.z, pp.w), vv, o2[2 * q + 1][j]);
         }
       }
+    };
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (k0 + k < nvalid) {
-          const float4 pa = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup);
-          const float4 pb = *reinterpret_cast<const float4 *>(p_w + (k0 + k) * kMaxGroup + 4);
-          const float2 pp[NP] = {make_float2(pa.x, pa.y), make_float2(pa.z, pa.w),
-                                 make_float2(pb.x, pb.y), make_float2(pb.z, pb.w)};
+    for (int k = 0; k < 16; ++k) pv_key(k, vb[k]);
+    if (nvalid > 16) {
+      if (nvalid == kSub) {
 #pragma unroll
-          for (int j = 0; j < NV; ++j) {
-            const float2 vv = make_float2(v[k][j], v[k][j]);
+        for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)(16 + k) * rsb);
+      } else {
 #pragma unroll
-            for (int q = 0; q < NP; ++q)
-              if (2 * q < G) o2[q][j] = fma2(pp[q], vv, o2[q][j]);
-          }
-        }
+        for (int k = 0; k < 16; ++k)
+          vb[k] = 16 + k < nvalid ? VR::load(vg + (size_t)(16 + k) * rsb) : VR::zero();
       }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) pv_key(16 + k, vb[k]);
     }
   }
   // Merge the sub-tiles of this split in order (warp 0 first).
   __syncwarp();
-  float *o_w = reinterpret_cast<float *>(k_w);  // [G][D], over this warp's K rows
+  float *o_w = reinterpret_cast<float *>(k_w);  // [8][D], over this warp's P
 #pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g)
-    if (g < G)
+  for (int h = 0; h < NH; ++h)
 #pragma unroll
-      for (int j = 0; j < NV; ++j)
-        o_w[g * D + lane * NV + j] = (g & 1) ? o2[g >> 1][j].y : o2[g >> 1][j].x;
+    for (int j = 0; j < NV / 2; ++j)
+      *reinterpret_cast<float2 *>(o_w + h * D + lane * NV + 2 * j) = o2[h][j];
   if (lane == 0)
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g)
-      if (g < G) ml_s[warp * kMaxGroup + g] = make_float2(m[g], l[g]);
+    for (int h = 0; h < NH; ++h) ml_s[warp * kMaxGroup + h] = make_float2(m[h], l[h]);
   __syncthreads();
   const int nsub = (L - split * kSplitKeys + kSub - 1) / kSub;  // valid sub-tiles, >= 1
   // The merge factors depend on the head only: one thread per head runs the
@@ -299,21 +358,27 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
     mls[g] = make_float2(M, Ls);
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+  constexpr int PER = kMaxGroup * D / (kSubPerSplit * 32);  // outputs per thread (8 or 4 x 2)
+  const float *ob = reinterpret_cast<const float *>(smem + S::Q);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int idx = threadIdx.x + i * kSubPerSplit * 32;
     const int g = idx / D, d = idx % D;
-    const float M = mls[g].x, Ls = mls[g].y;
-    float O = reinterpret_cast<const float *>(smem + S::Q)[g * D + d];
-    for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
-      const float2 f = fab[g * kSubPerSplit + w];
-      O = merge_o(O, f.x, reinterpret_cast<const float *>(smem + S::Q + w * S::KW)[g * D + d], f.y);
-    }
-    const int h = kvh * G + g;
-    if (a.nsplit == 1) {  // no combine pass follows
-      a.out[((size_t)t * Hq + h) * D + d] = __fdiv_rn(O, Ls);
-    } else {
-      float *p = a.part + (((size_t)t * Hq + h) * a.nsplit + split) * (D + 2);
-      if (d == 0) { p[0] = M; p[1] = Ls; }
-      p[2 + d] = O;
+    if (g < G) {
+      const float M = mls[g].x, Ls = mls[g].y;
+      float O = ob[g * D + d];
+      for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
+        const float2 f = fab[g * kSubPerSplit + w];
+        O = merge_o(O, f.x, ob[w * (S::KW / 4) + g * D + d], f.y);
+      }
+      const int h = kvh * G + g;
+      if (a.nsplit == 1) {  // no combine pass follows
+        a.out[((size_t)t * Hq + h) * D + d] = __fdiv_rn(O, Ls);
+      } else {
+        float *p = a.part + (((size_t)t * Hq + h) * a.nsplit + split) * (D + 2);
+        if (d == 0) { p[0] = M; p[1] = Ls; }
+        p[2 + d] = O;
+      }
     }
   }
 }
@@ -644,10 +709,14 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
                       dim3(kPrefillThreads), P::bytes(), s, a);
   }
   using Sd = DecShape<D, F32>;
-  cudaError_t e = with_smem(k_attn_dec<D, F32>, Sd::bytes());
+  const int G = a.n_q_heads / a.n_kv_heads;
+  auto kern = G <= 2 ? k_attn_dec<D, F32, 1>
+              : G <= 4 ? k_attn_dec<D, F32, 2>
+              : G <= 6 ? k_attn_dec<D, F32, 3> : k_attn_dec<D, F32, 4>;
+  cudaError_t e = with_smem(kern, Sd::bytes());
   if (e != cudaSuccess) return e;
-  e = launch_pdl(k_attn_dec<D, F32>, dim3(a.nsplit, a.n_kv_heads, a.T),
-                 dim3(kSubPerSplit * 32), Sd::bytes(), s, a);
+  e = launch_pdl(kern, dim3(a.nsplit, a.n_kv_heads, a.T), dim3(kSubPerSplit * 32), Sd::bytes(),
+                 s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
   return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D),
                     (size_t)(a.nsplit + 1) * sizeof(float2), s, a);

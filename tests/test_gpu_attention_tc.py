@@ -28,7 +28,8 @@ FLIP_BOUND = 1e-2  # a handful of flipped Q8 codes at 7B dimensions
 
 @pytest.mark.parametrize("kv_f32", [True, False])
 @pytest.mark.parametrize("hq,hkv,prefix,ntok", [(28, 4, 0, 200), (64, 8, 100, 150),
-                                                (12, 2, 37, 131)])
+                                                (12, 2, 37, 131), (28, 4, 1000, 200),
+                                                (8, 1, 1500, 70)])
 def test_tc_prefill_attention_vs_oracle(si_ctx, oc, hq, hkv, prefix, ntok, kv_f32):
     D = 128
     dims = dict(hidden=hq * D, n_q_heads=hq, n_kv_heads=hkv, head_dim=D, intermediate=0,
