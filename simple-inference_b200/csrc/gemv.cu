@@ -402,7 +402,7 @@ __device__ __forceinline__ void named_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int MT, bool SWIGLU>
+template <int MT, bool SWIGLU, bool ISUM>
 __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
     k_gemv_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
@@ -557,28 +557,29 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       for (int j = 0; j < NB; ++j) {
 #pragma unroll
         for (int wi = 0; wi < W; ++wi) {
-          // Rows (g, g+8) of one token per packed operation: the mma result
-          // 0x4B400000 + d (d = 16*isum) is the float 1.5*2^23 + d (|d| <
-          // 2^22), and fma(f, dw, -1.5*2^23*dw) = round(d * dw) with one
-          // rounding -- the product (float)d * dw without an int-to-float
-          // conversion, which runs on a narrow pipe.  -1.5*2^23*dw is exact
-          // (fp16 dw).
-          const float2 dw = make_float2(f16_to_f32((uint16_t)dwp[j][wi][0]),
-                                        f16_to_f32((uint16_t)dwp[j][wi][1]));
-          const float2 nk = mul2_rn(dw, make_float2(-12582912.0f, -12582912.0f));
+          // One row, the lane's two tokens (2c, 2c+1) per packed operation --
+          // the mma's adjacent result registers and the adjacent dx/16 pair:
+          // the mma result 0x4B400000 + d (d = 16*isum) is the float
+          // 1.5*2^23 + d (|d| < 2^22), and fma(f, dw, -1.5*2^23*dw) =
+          // round(d * dw) with one rounding -- the product (float)d * dw
+          // without an int-to-float conversion, which runs on a narrow pipe.
+          // -1.5*2^23*dw is exact (fp16 dw).
 #pragma unroll
-          for (int q = 0; q < NT; ++q)
+          for (int h = 0; h < 2; ++h) {
+            const float x = f16_to_f32((uint16_t)dwp[j][wi][h]);
+            const float2 dw = make_float2(x, x);
+            const float2 nk = mul2_rn(dw, make_float2(-12582912.0f, -12582912.0f));
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float dxe = e ? dx[j][q].y : dx[j][q].x;
-              float2 f = make_float2(__int_as_float(d[j][wi][q][e]),
-                                     __int_as_float(d[j][wi][q][2 + e]));
-              f = mul2_rn(fma2_rn(f, dw, nk), make_float2(dxe, dxe));
-              t[bl0 + j][wi][q][0][e] = f.x;
-              t[bl0 + j][wi][q][1][e] = f.y;
+            for (int q = 0; q < NT; ++q) {
+              float2 f = make_float2(__int_as_float(d[j][wi][q][2 * h]),
+                                     __int_as_float(d[j][wi][q][2 * h + 1]));
+              f = mul2_rn(fma2_rn(f, dw, nk), dx[j][q]);
+              t[bl0 + j][wi][q][h][0] = f.x;
+              t[bl0 + j][wi][q][h][1] = f.y;
             }
+          }
         }
-        if (!SWIGLU && a.isum_out) {
+        if constexpr (ISUM) {
           const int bx = ci * CB + bl0 + j;
 #pragma unroll
           for (int q = 0; q < NT; ++q)
@@ -628,13 +629,22 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
       for (int i = 0; i < NV; ++i) ac[i] = src[i];
     }
     if (got) {
+      if (nb == CB) {
 #pragma unroll
-      for (int bl = 0; bl < CB; ++bl)
-        if (bl < nb) {
+        for (int bl = 0; bl < CB; ++bl) {
           const float *tb = &t[bl][0][0][0][0];
 #pragma unroll
           for (int i = 0; i < NV; ++i) ac[i] = __fadd_rn(ac[i], tb[i]);
         }
+      } else {
+#pragma unroll
+        for (int bl = 0; bl < CB; ++bl)
+          if (bl < nb) {
+            const float *tb = &t[bl][0][0][0][0];
+#pragma unroll
+            for (int i = 0; i < NV; ++i) ac[i] = __fadd_rn(ac[i], tb[i]);
+          }
+      }
     }
     if (ci + 1 < nchunks) {
       float *dst = acc_s + (rg * 32 + lane) * NV;
@@ -783,7 +793,8 @@ cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
     tmN2 = tmN;
     tmS2 = tmS;
   }
-  auto kern = k_gemv_mma<MT, SWIGLU>;
+  auto kern = (!SWIGLU && a.isum_out) ? k_gemv_mma<MT, SWIGLU, !SWIGLU>
+                                      : k_gemv_mma<MT, SWIGLU, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
