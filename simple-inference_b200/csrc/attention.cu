@@ -373,7 +373,14 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
       }
       const int h = kvh * G + g;
       if (a.nsplit == 1) {  // no combine pass follows
-        a.out[((size_t)t * Hq + h) * D + d] = __fdiv_rn(O, Ls);
+        const size_t o = ((size_t)t * Hq + h) * D + d;
+        const float y = __fdiv_rn(O, Ls);
+        a.out[o] = y;
+        if (a.q8_qs) {  // a warp holds 32 consecutive dims of one head: one Q8 block
+          uint16_t d16;
+          a.q8_qs[o] = q8_lane(y, d16);
+          if ((d & 31) == 0) a.q8_d[o / 32] = d16;
+        }
       } else {
         float *p = a.part + (((size_t)t * Hq + h) * a.nsplit + split) * (D + 2);
         if (d == 0) { p[0] = M; p[1] = Ls; }
@@ -416,7 +423,14 @@ __global__ void k_attn_combine(const AttnArgs a) {
     for (int j = 0; j < 8; ++j) O = merge_o(O, fs[s + j].x, oo[j], fs[s + j].y);
   }
   for (; s < S; ++s) O = merge_o(O, fs[s].x, p[(size_t)s * (D + 2) + 2 + d], fs[s].y);
-  a.out[((size_t)t * a.n_q_heads + h) * D + d] = __fdiv_rn(O, fs[S].y);
+  const size_t o = ((size_t)t * a.n_q_heads + h) * D + d;
+  const float y = __fdiv_rn(O, fs[S].y);
+  a.out[o] = y;
+  if (a.q8_qs) {  // warp w holds dims 32w .. 32w+31 of the head: one Q8 block
+    uint16_t d16;
+    a.q8_qs[o] = q8_lane(y, d16);
+    if ((d & 31) == 0) a.q8_d[o / 32] = d16;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -722,6 +736,8 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
                     (size_t)(a.nsplit + 1) * sizeof(float2), s, a);
 }
 }  // namespace
+
+bool attn_decode_form(const AttnArgs &a) { return !use_prefill(a); }
 
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit) {
   return nsplit > 1 ? (size_t)T * n_q_heads * nsplit * (head_dim + 2) : 0;

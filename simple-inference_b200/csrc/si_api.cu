@@ -1331,16 +1331,23 @@ static si_status run_step(si_ctx *ctx, si_layer *l, si_kv *kv, const float *x, i
   aa.max_ctx = kv->max_ctx; aa.tok_seq = b.tok_seq; aa.tok_ctx = b.tok_ctx; aa.seq0 = seq0;
   aa.ctx0 = prefix + 1; aa.out = b.attn; aa.part = b.part; aa.nsplit = nsplit;
   aa.err = ctx->err;
+  // 5. Q8 of the attention output (qwen_one_layer.c:272): in the decode form
+  // the attention kernel that writes each output row quantises it too.
+  bool q8_done = false;
   if (!ctx->exact_attention && si::attn_tc_supported(aa)) {
     const size_t need = si::attn_tc_scratch_bytes(aa);
     SI_TRY(ctx->attn.reserve(need));
     SI_CUDA(si::launch_attention_tc(aa, ctx->attn.p, ctx->attn.bytes, s));
   } else {
+    if (si::attn_decode_form(aa)) {
+      aa.q8_qs = b.aq;
+      aa.q8_d = b.ad;
+      q8_done = true;
+    }
     SI_CUDA(si::launch_attention(aa, s));
   }
   if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_ATTN], s));
-  // 5. Q8 of the attention output (qwen_one_layer.c:272).
-  SI_CUDA(si::launch_q8_quantize(b.attn, T, QD, b.aq, b.ad, s));
+  if (!q8_done) SI_CUDA(si::launch_q8_quantize(b.attn, T, QD, b.aq, b.ad, s));
   if (timing) SI_CUDA(cudaEventRecord(ctx->ev[EV_Q8O], s));
   if (cap && cap->attn)
     SI_CUDA(cudaMemcpyAsync(cap->attn, b.attn, (size_t)T * QD * 4, cudaMemcpyDeviceToDevice, s));

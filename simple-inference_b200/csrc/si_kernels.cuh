@@ -176,12 +176,19 @@ struct AttnArgs {
   float *part;           // split-K scratch, >= attn_part_floats() floats
   int nsplit;
   int *err;              // context device error word (bounded waits), or null
+  // Decode form only: also the Q8_0 pair of out ([T][Hq*D] int8 and one fp16
+  // scale per 32), written by the kernel that writes out; null: out only.
+  int8_t *q8_qs;
+  uint16_t *q8_d;
 };
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
 // Splits the launch needs: 1 when the prefill kernel runs (contiguous tokens
 // of one sequence, T >= 16), else ceil(max_len / 128).
 int attn_pick_splits(int T, bool decode_form, int max_len);
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
+// True when launch_attention runs the decode form (per-token arrays, or
+// fewer than 16 tokens): the only form that honours q8_qs / q8_d.
+bool attn_decode_form(const AttnArgs &a);
 
 // ---- attention_tc.cu (tcgen05 causal prefill, split fp16 operands) ------------
 // The prefill form (no per-token arrays) at head_dim 128 and groups <= 8.
