@@ -540,8 +540,25 @@ static si::GemvArgs gemv_args(const si_matrix *w, const int8_t *qs, const uint16
 // tile start-up wins (gate/up 279 against 262 TOP/s).  Below 512 tokens the
 // tcgen05 kernel's 128-token tiles waste too much of a tile (a batch-64 7B
 // decode step: 627 against 568 us), so it needs M >= 512 as well.
+// Single matrices, measured at 4096 tokens on the 72B tensor-parallel shard
+// shapes: the mma.sync kernel is ahead up to K = 3712 (o at K = 2048: 348
+// against 322 TOP/s; down at K = 3712: 359 against 350), level at K = 7424
+// and behind from K = 14848 (378 against 370); and with few 128 x 128 tiles
+// the tcgen05 kernel's last wave runs part-empty (the QKV shard at TP = 8,
+// 1280 rows: 320 tiles over 148 SMs, 252 against 302 TOP/s), so it also needs
+// its tiles to fill at least 85 % of the waves they take.
 static bool prefer_gemm(bool swiglu, int M) { return M >= (swiglu ? 64 : 256); }
 static bool prefer_tc(int K, int M) { return K >= 2048 && M >= 512; }
+static bool prefer_tc_single(const si_ctx *ctx, int N, int K, int M) {
+  if (K < 4096 || M < 512) return false;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device) != cudaSuccess ||
+      sms <= 0)
+    return true;
+  const long tiles = (long)((N + 127) / 128) * ((M + 127) / 128);
+  const long waves = (tiles + sms - 1) / sms;
+  return tiles * 100 >= 85 * waves * sms;
+}
 
 static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const uint16_t *d,
                         int M, const float *bias, const float *resid, float *out, int kernel) {
@@ -555,7 +572,7 @@ static si_status matmul(si_ctx *ctx, const si_matrix *w, const int8_t *qs, const
     const bool tc = si::gemm_tc_supported(w->rows, w->cols, M);
     const bool mma = si::gemm_mma_supported(w->rows, w->cols, M, false);
     kernel = !prefer_gemm(false, M) ? 0
-             : tc && (prefer_tc(w->cols, M) || !mma) ? 1
+             : tc && (prefer_tc_single(ctx, w->rows, w->cols, M) || !mma) ? 1
              : mma ? 4 : 0;
   }
   if (kernel == 2) a.variant = si::kGemvMma;
