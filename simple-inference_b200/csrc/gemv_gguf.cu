@@ -6,123 +6,211 @@
 // (low nibble of byte j = element j, high = element j + 16).  No repack: this
 // kernel measures what skipping the device SoA layout costs.
 //
-// One warp per row.  The row streams in chunks of 32 blocks (576 bytes: 36
-// aligned 16-byte loads shared by the lanes, or 72 8-byte loads where rows are
-// only 8-byte aligned; the next chunk's loads in flight while this one is
-// used) through shared memory, where lane i finds block i
-// at byte 18i -- 2-byte aligned, so its nibble words are funnel-shifted out of
-// aligned 32-bit words.  Lane i forms block i's term per token exactly as the
-// reference: isum from dp4a over the nibbles XORed with 0x88 and moved to the
-// high half of each byte (16*(q-8), so the sum is 16*isum), then
-// ((float)isum * dw) * dx, each product rounded.  The terms of a chunk are then
-// added to the running sum in block order by the lane that owns the token
-// (lane t for token t), from the bias on: the reference's serial chain, so the
-// output is bit-identical to matvec_q4q8.
+// A CTA owns RPC rows (16 or 32) and walks K in chunks of 32 blocks through
+// a 4-stage shared-memory ring filled with cp.async three chunks ahead: per
+// stage the RPC rows' bytes (576 per row: 16-byte pieces, or 8-byte pieces
+// where rows are only 8-byte aligned -- the 72B down projection's 924 blocks
+// per row) and the chunk's activations (int8 blocks and fp16 scales), which
+// the rows share.  Eight warps compute the terms, each for RPC/8 rows in turn
+// with lane i on block i: in the staged row block i sits at byte 18i --
+// 2-byte aligned, so its nibble words are funnel-shifted out of aligned
+// 32-bit words -- and its term per token is formed exactly as the reference
+// does: isum from dp4a over the nibbles XORed with 0x88 and moved to the high
+// half of each byte (16*(q-8), so the sum is 16*isum), then ((float)isum *
+// dw) * dx, each product rounded.  Then warp t adds token t's terms, one lane
+// per row, to the running sums in block order, from the bias on: the
+// reference's serial chain for every row at once, so the output is
+// bit-identical to matvec_q4q8.
 #include <type_traits>
 
 #include "si_common.cuh"
 #include "si_kernels.cuh"
+#include "si_tma.cuh"
 
 namespace si {
 namespace {
 
-constexpr int kRowsPerCta = 8;
 constexpr int kChunk = 32;                 // blocks per chunk
 constexpr int kChunkBytes = kChunk * 18;   // 576 = 36 x 16
+constexpr int kStages = 4;                 // ring stages (chunks in flight: kStages - 1)
 
-// Piece: the load width (16 bytes when rows start 16-byte aligned, KB % 8 == 0;
-// else 8 bytes, KB % 4 == 0 -- the 72B down projection's 924 blocks per row).
 template <int PIECE>
-struct ChunkPieces {
-  using T = typename std::conditional<PIECE == 16, uint4, uint2>::type;
-  static constexpr int PER_LANE = (kChunkBytes / PIECE + 31) / 32;
+__device__ __forceinline__ void cp_async_piece(uint32_t dst, const void *src) {
+  if constexpr (PIECE == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+
+constexpr int kWarps = 8;
+constexpr int kRowBytes = kChunkBytes + 16;  // staged row, padded
+
+// Shared memory of one CTA: the ring's rows [stage][RPC][592], the
+// activations [stage][token][32 blocks x 32], their scales [stage][token][32]
+// and two buffers of terms [buffer][token][RPC][33].
+template <int MT, int RPC>
+struct GgufSmem {
+  static constexpr int W = 0;
+  static constexpr int ACT = W + kStages * RPC * kRowBytes;
+  static constexpr int XD = ACT + kStages * MT * kChunk * 32;
+  static constexpr int TERM = XD + kStages * MT * kChunk * 2;
+  static constexpr int TERMS = MT * RPC * (kChunk + 1);  // floats per term buffer
+  static constexpr int BYTES = TERM + 2 * TERMS * 4;
+  static_assert(ACT % 16 == 0 && XD % 16 == 0 && TERM % 16 == 0, "alignment");
 };
 
-template <int MT, int PIECE>
-__global__ void __launch_bounds__(kRowsPerCta * 32)
+// Piece: the load width (16 bytes when rows start 16-byte aligned, KB % 8 == 0;
+// else 8 bytes, KB % 4 == 0).
+template <int MT, int PIECE, int RPC>
+__global__ void __launch_bounds__(kWarps * 32)
     k_gemv_gguf(const uint8_t *__restrict__ w, int N, int KB, const int8_t *__restrict__ xq,
                 const uint16_t *__restrict__ xd, int M, const float *__restrict__ bias,
                 float *__restrict__ out) {
-  using CP = ChunkPieces<PIECE>;
-  using P = typename CP::T;
-  __shared__ __align__(16) uint8_t chunk_s[kRowsPerCta][kChunkBytes + 16];
-  __shared__ float term_s[kRowsPerCta][MT][kChunk + 1];
+  static_assert(MT <= kWarps && RPC % kWarps == 0 && RPC <= 32, "shape");
+  using S = GgufSmem<MT, RPC>;
+  constexpr int NT = kWarps * 32, RPW = RPC / kWarps;
+  extern __shared__ __align__(16) uint8_t smem_g[];
+  uint8_t *w_s = smem_g + S::W;                                   // [stage][RPC][kRowBytes]
+  int8_t *act_s = reinterpret_cast<int8_t *>(smem_g + S::ACT);   // [stage][MT][1024]
+  uint16_t *xd_s = reinterpret_cast<uint16_t *>(smem_g + S::XD); // [stage][MT][32]
+  float *term_s = reinterpret_cast<float *>(smem_g + S::TERM);   // [2][MT][RPC][33]
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRowsPerCta + warp;
-  if (row >= N) return;  // warp-level work only: no block barrier below
-  const P *wr = reinterpret_cast<const P *>(w + (size_t)row * KB * 18);
+  const int row0 = blockIdx.x * RPC;
   const int K = KB * 32;
-  // Weights are never written by an earlier kernel: the first chunk's loads
-  // go out before the wait for the previous kernel.
-  P cur[CP::PER_LANE];
-  auto load = [&](int g, P (&r)[CP::PER_LANE]) {
-    const int pieces = min(kChunk, KB - g) * 18 / PIECE;
-    const P *src = wr + (size_t)g * 18 / PIECE;
-#pragma unroll
-    for (int k = 0; k < CP::PER_LANE; ++k)
-      if (lane + 32 * k < pieces) r[k] = __ldg(src + lane + 32 * k);
-  };
-  load(0, cur);
-  pdl_wait();
-  float s = (lane < M && bias) ? bias[row] : 0.0f;  // lane t: token t's running sum
-  for (int g = 0; g < KB; g += kChunk) {
-    const int nb = min(kChunk, KB - g);
-    // Stage this chunk; start the next one's loads.
-    P *dst = reinterpret_cast<P *>(chunk_s[warp]);
+  const int nchunks = (KB + kChunk - 1) / kChunk;
+  // Chunk c into stage c % kStages: warp w's rows, then the CTA's share of the
+  // activations and their scales; one commit group per chunk and thread.
+  auto issue_weights = [&](int c) {
+    const int b0 = c * kChunk, nb = min(kChunk, KB - b0);
     const int pieces = nb * 18 / PIECE;
 #pragma unroll
-    for (int k = 0; k < CP::PER_LANE; ++k)
-      if (lane + 32 * k < pieces) dst[lane + 32 * k] = cur[k];
-    if (g + kChunk < KB) load(g + kChunk, cur);
-    __syncwarp();
-    float t[MT];
+    for (int j = 0; j < RPW; ++j) {
+      const int r = warp * RPW + j;
+      if (row0 + r < N) {
+        const uint8_t *src = w + (size_t)(row0 + r) * KB * 18 + (size_t)b0 * 18;
+        const uint32_t dst = smem_u32(w_s + ((c % kStages) * RPC + r) * kRowBytes);
+        for (int k = lane; k < pieces; k += 32) cp_async_piece<PIECE>(dst + k * PIECE, src + k * PIECE);
+      }
+    }
+  };
+  auto issue_acts = [&](int c) {
+    const int b0 = c * kChunk, nb = min(kChunk, KB - b0);
+    const int st = c % kStages;
+    for (int p = threadIdx.x; p < MT * kChunk * 2; p += NT) {
+      const int tk = p / (kChunk * 2), q = p % (kChunk * 2);
+      if (tk < M && q / 2 < nb)
+        cp_async_piece<16>(smem_u32(act_s + (st * MT + tk) * kChunk * 32 + q * 16),
+                           xq + (size_t)tk * K + (size_t)b0 * 32 + q * 16);
+    }
+    // Scales: 4-byte pieces of two (K % 128 == 0, so KB and nb are even and
+    // every piece is 4-byte aligned).
+    for (int p = threadIdx.x; p < MT * kChunk / 2; p += NT) {
+      const int tk = p / (kChunk / 2), bl = 2 * (p % (kChunk / 2));
+      if (tk < M && bl < nb)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                         smem_u32(xd_s + (st * MT + tk) * kChunk + bl)),
+                     "l"(xd + (size_t)tk * KB + b0 + bl)
+                     : "memory");
+    }
+  };
+  auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+  // Weights are never written by an earlier kernel: their first chunks go out
+  // before the wait for the previous kernel.
+  for (int c = 0; c < kStages - 1; ++c)
+    if (c < nchunks) issue_weights(c);
+  pdl_wait();
+  for (int c = 0; c < kStages - 1; ++c) {
+    if (c < nchunks) issue_acts(c);
+    commit();
+  }
+  // Warp t (t < M) keeps token t's running sums, lane r for row row0 + r.
+  const int mrow = row0 + lane;
+  const bool merger = warp < M && lane < RPC && mrow < N;
+  float s = (merger && bias) ? bias[mrow] : 0.0f;
+  // Chunk c's terms go to buffer c & 1 and are added while chunk c + 1 is
+  // computed (by the merging warps first), so one barrier per chunk orders
+  // both: a buffer is rewritten two chunks later, after the next barrier.
+  auto merge = [&](int c) {
+    if (!merger) return;
+    const int nb = min(kChunk, KB - c * kChunk);
+    const float *tr = term_s + (c & 1) * S::TERMS + (warp * RPC + lane) * (kChunk + 1);
+    if (nb == kChunk) {  // all 32 terms loaded first, then the chain of adds
+      float v[kChunk];
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k) v[k] = tr[k];
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k) s = __fadd_rn(s, v[k]);
+    } else {
+      for (int k = 0; k < nb; ++k) s = __fadd_rn(s, tr[k]);
+    }
+  };
+  for (int c = 0; c < nchunks; ++c) {
+    const int nb = min(kChunk, KB - c * kChunk);
+    const int st = c % kStages;
+    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2) : "memory");
+    __syncthreads();  // chunk c visible, chunk c - 1's terms in; stage (c - 1) % kStages free
+    if (c + kStages - 1 < nchunks) {
+      issue_weights(c + kStages - 1);
+      issue_acts(c + kStages - 1);
+    }
+    commit();
+    if (c > 0) merge(c - 1);
+    float *tb = term_s + (c & 1) * S::TERMS;
     if (lane < nb) {
-      const uint8_t *blk = chunk_s[warp] + lane * 18;
-      const float dw = f16_to_f32(*reinterpret_cast<const uint16_t *>(blk));
-      // The 16 nibble bytes start at byte 18*lane + 2: funnel them out of the
-      // five aligned words that cover them.
-      const int off = lane * 18 + 2, a0 = off & ~3, sh = (off & 3) * 8;
-      const uint32_t *wa = reinterpret_cast<const uint32_t *>(chunk_s[warp] + a0);
-      uint32_t u[5];
-#pragma unroll
-      for (int k = 0; k < 5; ++k) u[k] = wa[k];
-      int lo[4], hi[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t x = __funnelshift_r(u[k], u[k + 1], sh) ^ 0x88888888u;
-        lo[k] = (int)((x << 4) & 0xF0F0F0F0u);
-        hi[k] = (int)(x & 0xF0F0F0F0u);
-      }
-      const int b = g + lane;
-#pragma unroll
-      for (int tk = 0; tk < MT; ++tk) {
-        if (tk < M) {
-          const int4 *xa = reinterpret_cast<const int4 *>(xq + (size_t)tk * K + (size_t)b * 32);
-          const int4 a0v = xa[0], a1v = xa[1];
-          int acc = 0;
-          acc = __dp4a(lo[0], a0v.x, acc);
-          acc = __dp4a(lo[1], a0v.y, acc);
-          acc = __dp4a(lo[2], a0v.z, acc);
-          acc = __dp4a(lo[3], a0v.w, acc);
-          acc = __dp4a(hi[0], a1v.x, acc);
-          acc = __dp4a(hi[1], a1v.y, acc);
-          acc = __dp4a(hi[2], a1v.z, acc);
-          acc = __dp4a(hi[3], a1v.w, acc);
-          const float dx = f16_to_f32(xd[(size_t)tk * KB + b]);
-          t[tk] = __fmul_rn(__fmul_rn((float)(acc >> 4), dw), dx);
-        }
-      }
+      // This lane's block of the chunk: activations and scales per token.
+      int4 av[MT][2];
+      float dx[MT];
 #pragma unroll
       for (int tk = 0; tk < MT; ++tk)
-        if (tk < M) term_s[warp][tk][lane] = t[tk];
+        if (tk < M) {
+          const int4 *xa = reinterpret_cast<const int4 *>(act_s + (st * MT + tk) * kChunk * 32 + lane * 32);
+          av[tk][0] = xa[0];
+          av[tk][1] = xa[1];
+          dx[tk] = f16_to_f32(xd_s[(st * MT + tk) * kChunk + lane]);
+        }
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) {
+        const int r = warp * RPW + j;
+        const uint8_t *wrow = w_s + (st * RPC + r) * kRowBytes;
+        const float dw = f16_to_f32(*reinterpret_cast<const uint16_t *>(wrow + lane * 18));
+        // The 16 nibble bytes start at byte 18*lane + 2: funnel them out of
+        // the five aligned words that cover them.
+        const int off = lane * 18 + 2, a0 = off & ~3, sh = (off & 3) * 8;
+        const uint32_t *wa = reinterpret_cast<const uint32_t *>(wrow + a0);
+        uint32_t u[5];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) u[k] = wa[k];
+        int lo[4], hi[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t x = __funnelshift_r(u[k], u[k + 1], sh) ^ 0x88888888u;
+          lo[k] = (int)((x << 4) & 0xF0F0F0F0u);
+          hi[k] = (int)(x & 0xF0F0F0F0u);
+        }
+#pragma unroll
+        for (int tk = 0; tk < MT; ++tk) {
+          if (tk < M) {
+            int acc = 0;
+            acc = __dp4a(lo[0], av[tk][0].x, acc);
+            acc = __dp4a(lo[1], av[tk][0].y, acc);
+            acc = __dp4a(lo[2], av[tk][0].z, acc);
+            acc = __dp4a(lo[3], av[tk][0].w, acc);
+            acc = __dp4a(hi[0], av[tk][1].x, acc);
+            acc = __dp4a(hi[1], av[tk][1].y, acc);
+            acc = __dp4a(hi[2], av[tk][1].z, acc);
+            acc = __dp4a(hi[3], av[tk][1].w, acc);
+            tb[(tk * RPC + r) * (kChunk + 1) + lane] =
+                __fmul_rn(__fmul_rn((float)(acc >> 4), dw), dx[tk]);
+          }
+        }
+      }
     }
-    __syncwarp();
-    if (lane < M)
-      for (int k = 0; k < nb; ++k) s = __fadd_rn(s, term_s[warp][lane][k]);
-    __syncwarp();
   }
-  if (lane < M) out[(size_t)lane * N + row] = s;
+  __syncthreads();
+  merge(nchunks - 1);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (merger) out[(size_t)warp * N + mrow] = s;
 }
 
 }  // namespace
@@ -134,12 +222,32 @@ bool gemv_gguf_supported(int N, int K, int M) {
 template <int PIECE>
 cudaError_t launch_pieces(const uint8_t *w, int N, int KB, const int8_t *xq, const uint16_t *xd,
                           int M, const float *bias, float *out, cudaStream_t s) {
-  const dim3 grid((N + kRowsPerCta - 1) / kRowsPerCta), block(kRowsPerCta * 32);
-  if (M == 1)
-    return launch_pdl(k_gemv_gguf<1, PIECE>, grid, block, 0, s, w, N, KB, xq, xd, M, bias, out);
-  if (M <= 4)
-    return launch_pdl(k_gemv_gguf<4, PIECE>, grid, block, 0, s, w, N, KB, xq, xd, M, bias, out);
-  return launch_pdl(k_gemv_gguf<8, PIECE>, grid, block, 0, s, w, N, KB, xq, xd, M, bias, out);
+  // 32 rows per CTA when that still gives every SM two CTAs, else 16 (more
+  // CTAs, each with a shorter chunk step); eight tokens always take 16.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  auto go = [&](auto mt, auto rpc) -> cudaError_t {
+    constexpr int MT = decltype(mt)::value, RPC = decltype(rpc)::value;
+    auto kern = k_gemv_gguf<MT, PIECE, RPC>;
+    const int bytes = GgufSmem<MT, RPC>::BYTES;
+    if (bytes > 48 * 1024) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+      if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(kern, dim3((N + RPC - 1) / RPC), dim3(kWarps * 32), bytes, s, w, N, KB, xq,
+                      xd, M, bias, out);
+  };
+  using I1 = std::integral_constant<int, 1>;
+  using I4 = std::integral_constant<int, 4>;
+  using I8 = std::integral_constant<int, 8>;
+  using R16 = std::integral_constant<int, 16>;
+  using R32 = std::integral_constant<int, 32>;
+  const bool wide = (N + 31) / 32 >= 2 * sms;
+  if (M == 1) return wide ? go(I1{}, R32{}) : go(I1{}, R16{});
+  if (M <= 4) return wide ? go(I4{}, R32{}) : go(I4{}, R16{});
+  return go(I8{}, R16{});
 }
 
 cudaError_t launch_gemv_gguf(const uint8_t *w, int N, int K, const int8_t *xq, const uint16_t *xd,
