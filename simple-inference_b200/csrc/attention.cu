@@ -142,6 +142,21 @@ struct VRow {
     return __ldg(reinterpret_cast<const T *>(p));
   }
   static __device__ __forceinline__ T zero() { return T{}; }
+  // NV raw fp32 values in the cache's format (fp16: round to nearest even).
+  static __device__ __forceinline__ T from_raw(const float *p) {
+    T x;
+    if constexpr (F32 && NV == 4) {
+      x = make_float4(p[0], p[1], p[2], p[3]);
+    } else if constexpr (F32) {
+      x = make_float2(p[0], p[1]);
+    } else if constexpr (NV == 4) {
+      x = make_uint2((uint32_t)f32_to_f16(p[0]) | ((uint32_t)f32_to_f16(p[1]) << 16),
+                     (uint32_t)f32_to_f16(p[2]) | ((uint32_t)f32_to_f16(p[3]) << 16));
+    } else {
+      x = (uint32_t)f32_to_f16(p[0]) | ((uint32_t)f32_to_f16(p[1]) << 16);
+    }
+    return x;
+  }
   static __device__ __forceinline__ void to_f32(const T &x, float (&v)[NV]) {
     if constexpr (F32 && NV == 4) {
       v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
@@ -185,6 +200,12 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   if (split >= ns) return;  // this token needs fewer splits than the grid has
   const int key0 = (split * kSubPerSplit + warp) * kSub;
   const int nvalid = L - key0 < 0 ? 0 : (L - key0 > kSub ? kSub : L - key0);
+  // With raw projections, this warp's last valid key is the token's own new
+  // key when the sub-tile holds position L - 1: its row comes from the
+  // projections, not from the cache.
+  const bool fused = a.qkv != nullptr;
+  const bool has_new = fused && L - key0 >= 1 && L - key0 <= kSub;
+  const int ncache = nvalid - (has_new ? 1 : 0);  // rows read from the cache
   const uint32_t rsb = (uint32_t)Hkv * D * S::ES;  // bytes between positions
   const size_t base = ((size_t)seq * a.max_ctx * Hkv + kvh) * D * S::ES;
   const uint8_t *kg = static_cast<const uint8_t *>(a.kc) + base + (size_t)key0 * rsb;
@@ -200,7 +221,7 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
     const uint8_t *src = kg + (size_t)ro * rsb + c * 16;
     const uint32_t dst = smem_u32(k_w) + ro * S::RB;
     const uint32_t cr = (uint32_t)(c ^ ro) << 4;
-    if (nvalid == kSub) {
+    if (ncache == kSub) {
 #pragma unroll
       for (int i = 0; i < NI; ++i)
         cp_async16(dst + i * S::RPI * S::RB + (cr ^ (((S::RPI * i) & 7) << 4)),
@@ -208,14 +229,15 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
 #pragma unroll
       for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)k * rsb);
     } else {
+      // Rows past the cached ones are not copied (their scores are masked, or
+      // the new key's row is written below).
 #pragma unroll
-      for (int i = 0; i < NI; ++i) {
-        const bool ok = ro + i * S::RPI < nvalid;
-        cp_async16(dst + i * S::RPI * S::RB + (cr ^ (((S::RPI * i) & 7) << 4)),
-                   ok ? src + (size_t)(i * S::RPI) * rsb : kg, ok ? 16 : 0);
-      }
+      for (int i = 0; i < NI; ++i)
+        if (ro + i * S::RPI < ncache)
+          cp_async16(dst + i * S::RPI * S::RB + (cr ^ (((S::RPI * i) & 7) << 4)),
+                     src + (size_t)(i * S::RPI) * rsb, 16);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) vb[k] = k < nvalid ? VR::load(vg + (size_t)k * rsb) : VR::zero();
+      for (int k = 0; k < 16; ++k) vb[k] = k < ncache ? VR::load(vg + (size_t)k * rsb) : VR::zero();
     }
     // V rows 16..31 into L2 while the scores are computed.
     constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
@@ -224,21 +246,96 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
                           (size_t)(key0 + 16 + lane / LPR) * rsb + (lane % LPR) * 128;
 #pragma unroll
     for (int i = 0; i < (16 + RPP - 1) / RPP; ++i)
-      if (16 + lane / LPR + i * RPP < nvalid)
+      if (16 + lane / LPR + i * RPP < ncache)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + (size_t)(i * RPP) * rsb));
   }
   // The group's queries as [D][8 heads] (heads of one dim adjacent).
+  constexpr int HALF = D / 2;
+  const size_t qkv_row = (size_t)(Hq + 2 * Hkv) * D;
   if (threadIdx.x < D) {
     const int d = threadIdx.x;
-    const float *qg = a.q + ((size_t)t * Hq + (size_t)kvh * G) * D + d;
     float qv[kMaxGroup];
+    if (fused) {
+      // rope (qwen_one_layer.c:171-183) at position L - 1, as rope_kv.cu.
+      const int i = d < HALF ? d : d - HALF;
+      const size_t ti = (size_t)(L - 1) * HALF + i;
+      const float c = a.cos_tab[ti], sn = a.sin_tab[ti];
+      const float *qg = a.qkv + (size_t)t * qkv_row + (size_t)kvh * G * D + i;
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) qv[h] = h < G ? qg[(size_t)h * D] : 0.0f;
+      for (int h = 0; h < kMaxGroup; ++h) {
+        if (h < G) {
+          const float x0 = qg[(size_t)h * D], x1 = qg[(size_t)h * D + HALF];
+          qv[h] = d < HALF ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn))
+                           : __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
+        } else {
+          qv[h] = 0.0f;
+        }
+      }
+    } else {
+      const float *qg = a.q + ((size_t)t * Hq + (size_t)kvh * G) * D + d;
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) qv[h] = h < G ? qg[(size_t)h * D] : 0.0f;
+    }
     *reinterpret_cast<float4 *>(q_s + d * kMaxGroup) = make_float4(qv[0], qv[1], qv[2], qv[3]);
     *reinterpret_cast<float4 *>(q_s + d * kMaxGroup + 4) = make_float4(qv[4], qv[5], qv[6], qv[7]);
   }
   cp_async_wait_all();
   __syncthreads();
+  // The new key: rotated K and raw V appended to the cache at position L - 1
+  // (rope_kv.cu's arithmetic and rounding), the K row also into this warp's
+  // staged rows in the cache's format, the lane's V dims kept for P.V.  Only
+  // this warp reads its staged rows, so the other warps do not wait for it.
+  typename VR::T vnew = VR::zero();
+  if (has_new) {
+    const int pos = L - 1, r = nvalid - 1;
+    const float *__restrict__ kraw = a.qkv + (size_t)t * qkv_row + (size_t)Hq * D + (size_t)kvh * D;
+    const float *__restrict__ vraw = kraw + (size_t)Hkv * D;
+    constexpr int KP = HALF / 32;  // rotated pairs per lane
+    float c[KP], sn[KP], x0[KP], x1[KP], vv[D / 32];
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const int i = lane + 32 * j;
+      c[j] = a.cos_tab[(size_t)pos * HALF + i];
+      sn[j] = a.sin_tab[(size_t)pos * HALF + i];
+      x0[j] = kraw[i];
+      x1[j] = kraw[i + HALF];
+    }
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) vv[j] = vraw[lane + 32 * j];
+    vnew = VR::from_raw(vraw + lane * NV);
+    const size_t o = (((size_t)seq * a.max_ctx + pos) * Hkv + kvh) * D;
+    uint8_t *krow = k_w + r * S::RB;
+    // (the fused form appends: the cache pointers are written here)
+    auto put = [&](int dd, float kval) {  // dim dd: staged row (swizzled) and cache
+      const int byte = dd * S::ES;
+      uint8_t *p = krow + ((((byte >> 4) ^ (r & 7)) << 4) | (byte & 15));
+      if constexpr (F32) {
+        *reinterpret_cast<float *>(p) = kval;
+        static_cast<float *>(const_cast<void *>(a.kc))[o + dd] = kval;
+      } else {
+        const uint16_t hb = f32_to_f16(kval);
+        *reinterpret_cast<uint16_t *>(p) = hb;
+        static_cast<uint16_t *>(const_cast<void *>(a.kc))[o + dd] = hb;
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const int i = lane + 32 * j;
+      put(i, __fsub_rn(__fmul_rn(x0[j], c[j]), __fmul_rn(x1[j], sn[j])));
+      put(i + HALF, __fadd_rn(__fmul_rn(x1[j], c[j]), __fmul_rn(x0[j], sn[j])));
+    }
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      if constexpr (F32) static_cast<float *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = vv[j];
+      else static_cast<uint16_t *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = f32_to_f16(vv[j]);
+    }
+    if (r < 16) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k == r) vb[k] = vnew;
+    }
+    __syncwarp();
+  }
 
   float m[NH], l[NH];
   float2 o2[NH][NV / 2];  // head h, dims (2j, 2j+1) of this lane's NV
@@ -318,13 +415,15 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
 #pragma unroll
     for (int k = 0; k < 16; ++k) pv_key(k, vb[k]);
     if (nvalid > 16) {
-      if (nvalid == kSub) {
+      if (ncache == kSub) {
 #pragma unroll
         for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)(16 + k) * rsb);
       } else {
+        const int rn = has_new ? nvalid - 1 - 16 : -1;  // the new key's row in this half
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          vb[k] = 16 + k < nvalid ? VR::load(vg + (size_t)(16 + k) * rsb) : VR::zero();
+          vb[k] = 16 + k < ncache ? VR::load(vg + (size_t)(16 + k) * rsb)
+                                  : (k == rn ? vnew : VR::zero());
       }
 #pragma unroll
       for (int k = 0; k < 16; ++k) pv_key(16 + k, vb[k]);
@@ -738,6 +837,7 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
 }  // namespace
 
 bool attn_decode_form(const AttnArgs &a) { return !use_prefill(a); }
+long attn_decode_ctas(const AttnArgs &a) { return (long)a.nsplit * a.n_kv_heads * a.T; }
 
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit) {
   return nsplit > 1 ? (size_t)T * n_q_heads * nsplit * (head_dim + 2) : 0;
@@ -757,6 +857,7 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   if (!use_prefill(a) && a.nsplit < splits_for(a.tok_ctx ? 1 : min(a.ctx0 + a.T - 1, a.max_ctx)))
     return cudaErrorInvalidValue;
+  if (a.qkv ? (use_prefill(a) || !a.cos_tab || !a.sin_tab) : !a.q) return cudaErrorInvalidValue;
   if (a.head_dim == 128) return a.kv_f32 ? run<128, true>(a, s) : run<128, false>(a, s);
   if (a.head_dim == 64) return a.kv_f32 ? run<64, true>(a, s) : run<64, false>(a, s);
   return cudaErrorInvalidValue;

@@ -180,6 +180,12 @@ struct AttnArgs {
   // scale per 32), written by the kernel that writes out; null: out only.
   int8_t *q8_qs;
   uint16_t *q8_d;
+  // Decode form only, with distinct sequences per token: the raw projections
+  // [T][QD + 2*KVD] instead of q.  The kernel then rotates the queries itself
+  // and appends each token's rotated K and raw V at position ctx - 1 (the
+  // RoPE of rope_kv.cu, the same tables), so no separate RoPE kernel runs.
+  const float *qkv;
+  const float *cos_tab, *sin_tab;  // [positions][D/2]
 };
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit);
 // Splits the launch needs: 1 when the prefill kernel runs (contiguous tokens
@@ -189,6 +195,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
 // True when launch_attention runs the decode form (per-token arrays, or
 // fewer than 16 tokens): the only form that honours q8_qs / q8_d.
 bool attn_decode_form(const AttnArgs &a);
+// CTAs the decode form launches (splits x KV heads x tokens).
+long attn_decode_ctas(const AttnArgs &a);
 
 // ---- attention_tc.cu (tcgen05 causal prefill, split fp16 operands) ------------
 // The prefill form (no per-token arrays) at head_dim 128 and groups <= 8.
