@@ -808,6 +808,75 @@ def decode_gemv_roofline(ctx, torch, stream):
     return out
 
 
+def gemm_schemes(ctx, torch, stream, int8_peak_tops):
+    """The prefill projection's schemes side by side on the 72B o shape (8192 x
+    8192 Q4_0, 4096 tokens): this library's exact tcgen05 kind::i8 GEMM (the
+    dispatched prefill path from K = 4096), its fused-rescale form (one FMA per
+    block, within 1e-6), the mma.sync GEMM, and the bf16 / fp16-dequant
+    alternative -- weights dequantised once to bf16 / fp16 ((q - 8) * dw,
+    stored as such), activations (qx * dx) likewise, a cuBLAS GEMM with fp32
+    accumulation through torch.matmul.  Per scheme: time, int8-equivalent
+    TOP/s (2*M*N*K), that against its own measured peak (the int8 tcgen05
+    probe; MEASURED_PEAKS' bf16 figure for cuBLAS), and the largest difference
+    from the exact scheme relative to the output's largest element."""
+    import numpy as np
+    N = K = 8192
+    M = 4096
+    m = ctx.matrix_synth(N, K, seed=21)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    qs = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    d = torch.empty(M * K // 32, dtype=torch.int16, device="cuda")
+    torch.cuda.synchronize()
+    ctx.q8_quantize(x, M, K, qs, d)
+    ctx.sync()
+    ops = 2.0 * M * N * K
+    out, ys = {}, {}
+    for name, kern in (("tcgen05 i8, exact", 1), ("tcgen05 i8, fused rescale", 5),
+                       ("mma.sync i8, exact", 4)):
+        y = torch.empty(M * N, device="cuda")
+        ctx.matmul(m, qs, d, M, None, y, kernel=kern)
+        ctx.sync()
+        reps = 5
+        t = time_region(torch, stream, lambda i: ctx.matmul(m, qs, d, M, None, y, kernel=kern),
+                        reps) / reps
+        ctx.status()
+        ys[name] = y.view(M, N)
+        out[name] = {"us": round(t * 1e6, 1), "tops": round(ops / t / 1e12, 1),
+                     "frac_of_peak": round(ops / t / 1e12 / int8_peak_tops, 4) if int8_peak_tops else None,
+                     "peak": "int8 tcgen05 probe"}
+    ref = ys["tcgen05 i8, exact"].double()
+    scale = float(ref.abs().max())
+    # Dequantised operands: W[n][k] = (q - 8) * dw from the GGUF rows.
+    raw = m.download_gguf().reshape(N, K // 32, 18)
+    dw = raw[:, :, :2].copy().view(np.float16).astype(np.float32)          # [N][KB][1]
+    nib = raw[:, :, 2:]
+    q = np.concatenate([nib & 15, nib >> 4], axis=2).astype(np.float32) - 8.0
+    w32 = torch.from_numpy((q * dw).reshape(N, K)).cuda()
+    xq = qs.view(M, K // 32, 32).float() * d.view(M, K // 32, 1).view(torch.float16).float()
+    xq = xq.view(M, K)
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    for name, dt in (("bf16-dequant, cuBLAS", torch.bfloat16), ("fp16-dequant, cuBLAS", torch.float16)):
+        wd, xd = w32.to(dt), xq.to(dt)
+        torch.cuda.synchronize()
+        yd = torch.matmul(xd, wd.t())
+        torch.cuda.synchronize()
+        reps = 5
+        t = time_region(torch, stream, lambda i: torch.matmul(xd, wd.t()), reps) / reps
+        err = float((yd.double() - ref).abs().max()) / scale
+        out[name] = {"us": round(t * 1e6, 1), "tops": round(ops / t / 1e12, 1),
+                     "frac_of_peak": round(ops / t / 1e12 / pk["bf16_tflops"], 4) if pk.get("bf16_tflops") else None,
+                     "peak": "MEASURED_PEAKS bf16 (cuBLAS)", "max_err_vs_exact": err}
+        del wd, xd, yd
+    for name in ("tcgen05 i8, fused rescale", "mma.sync i8, exact"):
+        out[name]["max_err_vs_exact"] = float((ys[name].double() - ref).abs().max()) / scale
+    out["shape"] = f"{N}x{K} Q4_0, {M} tokens"
+    out["bar"] = "projection outputs within 1e-5 relative of the reference (bit-exact for the exact schemes)"
+    m.free()
+    return out
+
+
 def reference_layer_decode(ctx, torch, stream, n_tokens=32, context0=512):
     """The reference's own workload, apples to apples: its attention layer
     (RMSNorm, QKV + bias, RoPE, fp16 KV append, flash attention, o-projection;
@@ -962,6 +1031,8 @@ def run_ours(args, rank, world, local_rank):
         extra(result, "config2", cfg23)
         extra(result, "config1", lambda: run_config1(ctx, torch, stream))
         extra(result, "decode_gemv_roofline", lambda: decode_gemv_roofline(ctx, torch, stream))
+        extra(result, "gemm_schemes", lambda: gemm_schemes(
+            ctx, torch, stream, (result.get("int8_peak") or {}).get("tops")))
         extra(result, "reference_layer", lambda: reference_layer_decode(ctx, torch, stream))
         if not args.no_cpu_baseline:
             log("cpu baselines")
