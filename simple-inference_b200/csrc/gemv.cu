@@ -339,6 +339,7 @@ constexpr int kMmaGroups = 2;                                  // 16-row groups 
 constexpr int kMmaWarps = kMmaPhases * kMmaGroups + 1;         // + producer
 constexpr int kMmaMaxRing = 12;                                 // stages, at most
 constexpr size_t kMmaCtaBudget = 113 * 1024;  // shared memory that keeps two CTAs per SM
+constexpr size_t kMmaCtaBudget3 = 74 * 1024;  // ... and three
 
 template <int MT, bool SWIGLU>
 struct MmaShape {
@@ -402,8 +403,11 @@ __device__ __forceinline__ void named_arrive(int id, int threads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int MT, bool SWIGLU, bool ISUM>
-__global__ void __launch_bounds__(kMmaWarps * 32, MmaShape<MT, SWIGLU>::MINB)
+// MB: CTAs per SM the launch is built for (registers; the ring is sized to
+// match): MmaShape::MINB, or 3 for one-token-octet shapes whose tiles need
+// between two and three per SM to fit in one wave.
+template <int MT, bool SWIGLU, bool ISUM, int MB>
+__global__ void __launch_bounds__(kMmaWarps * 32, MB)
     k_gemv_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
                const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
@@ -764,9 +768,19 @@ template <int MT, bool SWIGLU>
 cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
   using S = MmaShape<MT, SWIGLU>;
   const int KB = a.K / 32, tiles = a.N / SI_RT;
-  // The deepest ring (5..12 stages) that keeps two CTAs per SM.
+  // One wave: with more tiles than two CTAs per SM hold but no more than three
+  // do (the 72B QKV projection's 320 tiles), three per SM -- 72 registers and
+  // a shallower ring -- instead of a second, nearly empty wave.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid_y = (a.M + MT - 1) / MT;
+  const bool three = S::MINB == 2 && (long)tiles * grid_y > 2L * sms &&
+                     (long)tiles * grid_y <= 3L * sms && S::smem(5, KB) <= kMmaCtaBudget3;
+  // The deepest ring (5..12 stages) that keeps that many CTAs per SM.
   int ns = kMmaMaxRing;
-  while (ns > 5 && S::smem(ns, KB) > kMmaCtaBudget) --ns;
+  const size_t budget = three ? kMmaCtaBudget3 : kMmaCtaBudget;
+  while (ns > 5 && S::smem(ns, KB) > budget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
@@ -793,14 +807,17 @@ cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
     tmN2 = tmN;
     tmS2 = tmS;
   }
-  auto kern = (!SWIGLU && a.isum_out) ? k_gemv_mma<MT, SWIGLU, !SWIGLU>
-                                      : k_gemv_mma<MT, SWIGLU, false>;
+  constexpr int MB = S::MINB;
+  constexpr int MB3 = S::MINB == 2 ? 3 : S::MINB;
+  auto kern = (!SWIGLU && a.isum_out) ? k_gemv_mma<MT, SWIGLU, !SWIGLU, MB>
+              : three                 ? k_gemv_mma<MT, SWIGLU, false, MB3>
+                                      : k_gemv_mma<MT, SWIGLU, false, MB>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid(tiles, (a.M + MT - 1) / MT);
+  dim3 grid(tiles, grid_y);
   return launch_pdl(kern, grid, dim3(kMmaWarps * 32), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
 }
 
