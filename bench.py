@@ -401,6 +401,13 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
     log(f"config4 prefill {t / args.steps * 1e3:.2f} ms/step")
 
     # ---- e2e: pinned host input in, prefill, pinned host output out --------
+    # One process serves the request: rank 0 copies the input in from its
+    # pinned host buffer and the output (identical on every rank after the
+    # last all-reduce) back out; with several ranks the input reaches the
+    # others by an NCCL broadcast over NVLink inside the timed step.
+    host_io = rank == 0
+    if world > 1:
+        import torch.distributed as tdist
     hx = torch.randn(TP_PREFILL, Hd, generator=torch.Generator().manual_seed(4)).pin_memory()
     hy = [torch.empty(TP_PREFILL, Hd).pin_memory() for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
@@ -413,28 +420,33 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
     def e2e_step(i):
         k = i % 2
         a, b = sets[k]
-        s_in.wait_event(ev_comp[k])           # step i-2 has finished with this set
-        with torch.cuda.stream(s_in):
-            a.copy_(hx, non_blocking=True)
-            ev_in[k].record(s_in)
-        stream.wait_event(ev_in[k])
-        stream.wait_event(ev_out[k])          # step i-2's output has left this set
+        if host_io:
+            s_in.wait_event(ev_comp[k])       # step i-2 has finished with this set
+            with torch.cuda.stream(s_in):
+                a.copy_(hx, non_blocking=True)
+                ev_in[k].record(s_in)
+            stream.wait_event(ev_in[k])
+            stream.wait_event(ev_out[k])      # step i-2's output has left this set
+        if world > 1:
+            with torch.cuda.stream(stream):
+                tdist.broadcast(a, src=0)
         prefill_on(a, b)
         ev_comp[k].record(stream)
-        s_out.wait_event(ev_comp[k])
-        with torch.cuda.stream(s_out):
-            hy[k].copy_(a, non_blocking=True)
-            ev_out[k].record(s_out)
+        if host_io:
+            s_out.wait_event(ev_comp[k])
+            with torch.cuda.stream(s_out):
+                hy[k].copy_(a, non_blocking=True)
+                ev_out[k].record(s_out)
 
     for i in range(2):
         e2e_step(i)
     torch.cuda.synchronize()
     barrier_sync()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s_in)
+    e0.record(s_in if host_io else stream)
     for i in range(args.steps):
         e2e_step(i)
-    e1.record(s_out)
+    e1.record(s_out if host_io else stream)
     e1.synchronize()
     te = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     barrier_sync()
@@ -528,10 +540,11 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
         "clocks": clk.summary(),
         "e2e": {"value": round(TP_PREFILL * args.steps / te, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": TP_PREFILL * Hd * 4, "d2h_bytes_per_step": TP_PREFILL * Hd * 4,
-                "how": "per rank and step: the 4096 x 8192 fp32 input from pinned host memory, "
-                       "the 8-layer prefill through si_prefill_tp_dev, the output back to "
-                       "pinned host memory; copies of neighbouring steps overlap on two copy "
-                       "streams"},
+                "how": "per step: the 4096 x 8192 fp32 input from rank 0's pinned host memory "
+                       "(with several ranks, broadcast from rank 0 over NVLink by NCCL inside "
+                       "the step), the 8-layer prefill through si_prefill_tp_dev, the output "
+                       "(identical on every rank) back to rank 0's pinned host memory; copies of "
+                       "neighbouring steps overlap on two copy streams; time = max over ranks"},
         "decode": {"batch": TP_BATCH, "steps": TP_DECODE,
                    "context": f"{TP_PREFILL + 1}..{TP_PREFILL + TP_DECODE}",
                    "launch": "one 8-layer step captured as a CUDA graph (device-resident "
