@@ -437,7 +437,8 @@ SI_API si_status si_attention_decode_dev(si_ctx *ctx, si_kv *kv, const si_dims *
  * prefill_weight_stationary.h:245-287): q [ntok][Hq][D] (RoPE applied) of
  * tokens at positions prefix .. prefix+ntok-1 of sequence seq, attending the
  * cache's keys 0 .. position; out [ntok][Hq][D].  The kernel follows the
- * context's si_ctx_set_exact_attention setting. */
+ * context's si_ctx_set_exact_attention setting; the tensor-core kernel needs
+ * q 16-byte aligned. */
 SI_API si_status si_attention_prefill_dev(si_ctx *ctx, si_kv *kv, const si_dims *d,
                                           const float *q_dev, int ntok, int seq, int prefix,
                                           float *out_dev);

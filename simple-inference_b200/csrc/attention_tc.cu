@@ -320,9 +320,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const float p0 = valid ? exp2f(sv[j] - m) : 0.0f;
         const float p1 = valid ? exp2f(sv[j + 1] - m) : 0.0f;
         sum += p0 + p1;
-        const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-        hw[j / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        lw[j / 2] = pack_half2(p0 - __half2float(h0), p1 - __half2float(h1));
+        // hi = fp16(p), lo = fp16(p - hi), two values per packed conversion.
+        const __half2 h = __floats2half2_rn(p0, p1);
+        const float2 hf = __half22float2(h);
+        const __half2 lo = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+        hw[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        lw[j / 2] = *reinterpret_cast<const uint32_t *>(&lo);
       }
       l = fmaf(l, alpha, sum);
       // P and O belong to the previous tile's P.V until it has completed.
@@ -416,17 +419,26 @@ __global__ void __launch_bounds__(THREADS, 1)
                  "r"(TMEM_COLS));
 }
 
-// q (fp32, [T][Hq][D]) * scale -> hi / lo halves.
+// q (fp32, [T][Hq][D]) * scale -> hi / lo halves, four elements per step (n is
+// a multiple of 4: D is 128), two per packed conversion.
 __global__ void k_split_q(const float *__restrict__ q, size_t n, float scale,
                           __half *__restrict__ qh, __half *__restrict__ ql) {
   pdl_trigger();
   pdl_wait();
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+  const float4 *q4 = reinterpret_cast<const float4 *>(q);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4;
        i += (size_t)gridDim.x * blockDim.x) {
-    const float x = __fmul_rn(q[i], scale);
-    const __half h = __float2half_rn(x);
-    qh[i] = h;
-    ql[i] = __float2half_rn(x - __half2float(h));
+    const float4 v = q4[i];
+    const float x0 = __fmul_rn(v.x, scale), x1 = __fmul_rn(v.y, scale);
+    const float x2 = __fmul_rn(v.z, scale), x3 = __fmul_rn(v.w, scale);
+    const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(x0 - f01.x, x1 - f01.y);
+    const __half2 l23 = __floats2half2_rn(x2 - f23.x, x3 - f23.y);
+    reinterpret_cast<__half2 *>(qh)[2 * i] = h01;
+    reinterpret_cast<__half2 *>(qh)[2 * i + 1] = h23;
+    reinterpret_cast<__half2 *>(ql)[2 * i] = l01;
+    reinterpret_cast<__half2 *>(ql)[2 * i + 1] = l23;
   }
 }
 
@@ -508,6 +520,7 @@ cudaError_t launch_attention_tc(const AttnArgs &a, void *scratch, size_t scratch
   __half *vl = reinterpret_cast<__half *>(cur);
 
   const float scale = 1.4426950408889634f / sqrtf((float)D);
+  if (reinterpret_cast<uintptr_t>(a.q) & 15) return cudaErrorMisalignedAddress;  // float4 reads
   cudaError_t e = launch_pdl(k_split_q, dim3((unsigned)((q + 255) / 256 < 4096 ? (q + 255) / 256 : 4096)),
                              dim3(256), 0, s, a.q, q, scale, qh, ql);
   if (e != cudaSuccess) return e;
