@@ -108,9 +108,12 @@ __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
     if (globaltimer() - t0 > 2000000000ull) return false;
   return true;
 }
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-  return (uint32_t)__half_as_ushort(__float2half_rn(a)) |
-         ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+// 2^x by the hardware's approximate exponential (relative error a few units
+// of 2^-23, far inside the attention bar; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -317,8 +320,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t hw[32], lw[32];
 #pragma unroll
       for (int j = 0; j < BK; j += 2) {
-        const float p0 = valid ? exp2f(sv[j] - m) : 0.0f;
-        const float p1 = valid ? exp2f(sv[j + 1] - m) : 0.0f;
+        const float p0 = valid ? ex2_approx(sv[j] - m) : 0.0f;
+        const float p1 = valid ? ex2_approx(sv[j + 1] - m) : 0.0f;
         sum += p0 + p1;
         // hi = fp16(p), lo = fp16(p - hi), two values per packed conversion.
         const __half2 h = __floats2half2_rn(p0, p1);
