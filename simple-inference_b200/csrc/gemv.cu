@@ -335,14 +335,16 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
 // block's integer sums, which mma.sync returns in registers; a tcgen05 MMA
 // would put each block's sums in tensor memory and need a round trip per block.
 constexpr int kMmaPhases = 4;
-constexpr int kMmaGroups = 2;                                  // 16-row groups per tile
-constexpr int kMmaWarps = kMmaPhases * kMmaGroups + 1;         // + producer
+// G: 16-row groups per CTA -- 2 (a whole 32-row tile), or 1 (half a tile, for
+// matrices with fewer tiles than SMs: twice the CTAs).
+__host__ __device__ constexpr int mma_warps(int G) { return kMmaPhases * G + 1; }  // + producer
 constexpr int kMmaMaxRing = 12;                                 // stages, at most
 constexpr size_t kMmaCtaBudget = 113 * 1024;  // shared memory that keeps two CTAs per SM
 constexpr size_t kMmaCtaBudget3 = 74 * 1024;  // ... and three
 
-template <int MT, bool SWIGLU>
+template <int MT, bool SWIGLU, int G = 2>
 struct MmaShape {
+  static constexpr int RWS = 16 * G;                  // rows per CTA
   static constexpr int W = SWIGLU ? 2 : 1;            // weight streams
   static constexpr int NT = MT / 8;                   // token octets
   // A chunk's terms stay in registers until the hand-off (36-80 per lane);
@@ -350,18 +352,18 @@ struct MmaShape {
   static constexpr int CB = W * NT == 1 ? 9 : 5;      // blocks per chunk
   static constexpr int GB = W * NT == 1 ? 3 : 1;
   static constexpr int MINB = NT == 2 ? 1 : 2;        // CTAs per SM the registers allow
-  static constexpr int NIB = CB * SI_RT * 16;         // [CB][32 rows][16 B]
-  static constexpr int SCL = (CB * SI_RT * 2 + 127) / 128 * 128;  // [CB][32] fp16, padded
+  static constexpr int NIB = CB * RWS * 16;           // [CB][RWS rows][16 B]
+  static constexpr int SCL = (CB * RWS * 2 + 127) / 128 * 128;    // [CB][RWS] fp16, padded
   static constexpr int ACT = MT * CB * 32;            // [MT][CB][32 B]
   static constexpr int WS = (NIB + SCL + 127) / 128 * 128;        // one weight stream
   static constexpr int STAGE = W * WS + (ACT + 127) / 128 * 128;
-  static constexpr int TX = W * (NIB + CB * SI_RT * 2) + ACT;  // bytes the TMA boxes deliver
+  static constexpr int TX = W * (NIB + CB * RWS * 2) + ACT;  // bytes the TMA boxes deliver
   static constexpr int NV = W * NT * 4;               // sums per lane
-  static constexpr int ACCS = kMmaGroups * 32 * NV;   // hand-off floats
+  static constexpr int ACCS = G * 32 * NV;            // hand-off floats
   // ring, 256 B of barriers and flags, hand-off sums, the per-warp amax of
   // the Q8 epilogue, dx/16 per (block, token) as fp32, slack
   static size_t smem(int ns, int KB) {
-    return (size_t)ns * STAGE + 256 + ACCS * 4 + kMmaGroups * MT * 4 + (size_t)KB * MT * 4 + 128;
+    return (size_t)ns * STAGE + 256 + ACCS * 4 + G * MT * 4 + (size_t)KB * MT * 4 + 128;
   }
   static_assert(NIB % 128 == 0 && WS % 128 == 0 && STAGE % 128 == 0, "TMA destinations");
 };
@@ -406,14 +408,16 @@ __device__ __forceinline__ void named_arrive(int id, int threads) {
 // MB: CTAs per SM the launch is built for (registers; the ring is sized to
 // match): MmaShape::MINB, or 3 for one-token-octet shapes whose tiles need
 // between two and three per SM to fit in one wave.
-template <int MT, bool SWIGLU, bool ISUM, int MB>
-__global__ void __launch_bounds__(kMmaWarps * 32, MB)
+template <int MT, bool SWIGLU, bool ISUM, int MB, int G>
+__global__ void __launch_bounds__(mma_warps(G) * 32, MB)
     k_gemv_mma(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
                const __grid_constant__ CUtensorMap tmX, const GemvArgs a, int ns) {
-  using S = MmaShape<MT, SWIGLU>;
-  constexpr int CB = S::CB, NT = S::NT, W = S::W, NV = S::NV, P = kMmaPhases;
-  constexpr int HAND = 2 * kMmaGroups * 32;  // threads in one hand-off
+  static_assert(G == 2 || !SWIGLU, "the SwiGLU Q8 epilogue needs whole 32-row tiles");
+  using S = MmaShape<MT, SWIGLU, G>;
+  constexpr int CB = S::CB, NT = S::NT, W = S::W, NV = S::NV, P = kMmaPhases, RWS = S::RWS;
+  constexpr int WARPS = mma_warps(G);
+  constexpr int HAND = 2 * G * 32;  // threads in one hand-off
   // Named barriers: 1..P hand-offs (id 1+k: into phase k), P+1 the compute
   // warps' start, P+2 the Q8 epilogue's warps.
   constexpr int kBarStart = P + 1, kBarEpi = P + 2;
@@ -424,10 +428,13 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kMmaMaxRing);
   float *acc_s = reinterpret_cast<float *>(smem + ns * S::STAGE + 256);  // [group][lane][NV]
   unsigned *red = reinterpret_cast<unsigned *>(acc_s + S::ACCS);         // [group][MT]
-  float *dxs = reinterpret_cast<float *>(red + kMmaGroups * MT);         // [KB][MT], dx/16
+  float *dxs = reinterpret_cast<float *>(red + G * MT);                  // [KB][MT], dx/16
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int tile = blockIdx.x, m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
+  // CTA x: 32-row tile x / (2 / G), its RWS-row slice x % (2 / G).
+  const int tile = blockIdx.x / (2 / G), slice = blockIdx.x % (2 / G);
+  const int rbase = tile * SI_RT + slice * RWS;  // the CTA's first row
+  const int m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
   const int KB = a.K / 32, nchunks = (KB + CB - 1) / CB;
   auto fb = [&](int i) { return smem_u32(full + i); };
   auto eb = [&](int i) { return smem_u32(empty + i); };
@@ -436,14 +443,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
   if (threadIdx.x == 0) {
     for (int i = 0; i < ns; ++i) {
       mbar_init(fb(i), 1);
-      mbar_init(eb(i), kMmaGroups);
+      mbar_init(eb(i), G);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  if (warp == kMmaWarps - 1) {
+  if (warp == WARPS - 1) {
     // ---- producer ----------------------------------------------------------
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
@@ -454,8 +461,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
         uint8_t *st = smem + slot * S::STAGE;
         const int y = tile * KB + ci * CB;
         mbar_expect_tx(fb(slot), S::TX);
-        tma_load_2d(smem_u32(st), &tmN, 0, y, fb(slot));
-        tma_load_2d(smem_u32(st + S::NIB), &tmS, 0, y, fb(slot));
+        tma_load_2d(smem_u32(st), &tmN, slice * RWS * 2, y, fb(slot));
+        tma_load_2d(smem_u32(st + S::NIB), &tmS, slice * RWS, y, fb(slot));
         if (SWIGLU) {
           tma_load_2d(smem_u32(st + S::WS), &tmN2, 0, y, fb(slot));
           tma_load_2d(smem_u32(st + S::WS + S::NIB), &tmS2, 0, y, fb(slot));
@@ -488,12 +495,12 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
   }
 
   // ---- compute warps: phase k, 16-row group rg ---------------------------
-  const int k = warp / kMmaGroups, rg = warp % kMmaGroups;
+  const int k = warp / G, rg = warp % G;
   pdl_wait();
   {
     // Eight independent loads in flight per thread (a K of 29568 has 7392
     // scales per 8 tokens).
-    constexpr int NTH = (kMmaWarps - 1) * 32;
+    constexpr int NTH = (WARPS - 1) * 32;
     for (int i0 = threadIdx.x; i0 < MT * KB; i0 += 8 * NTH) {
       uint16_t v[8];
 #pragma unroll
@@ -508,9 +515,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
       }
     }
   }
-  named_sync(kBarStart, (kMmaWarps - 1) * 32);  // dxs visible
+  named_sync(kBarStart, (WARPS - 1) * 32);  // dxs visible
 
-  const int r0 = tile * SI_RT + 16 * rg + g;  // this lane's rows r0 and r0 + 8
+  const int r0 = rbase + 16 * rg + g;  // this lane's rows r0 and r0 + 8
   // sums [stream][octet][row half][token of the pair]
   float acc[W][NT][2][2];
   bool ok = true;
@@ -545,14 +552,14 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
 #pragma unroll
         for (int wi = 0; wi < W; ++wi) {
           const uint8_t *ws = st + wi * S::WS;
-          const uint8_t *wr = ws + bl * 512 + (16 * rg + g) * 16 + 4 * c;
+          const uint8_t *wr = ws + bl * (RWS * 16) + (16 * rg + g) * 16 + 4 * c;
           const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wr);
           const uint32_t w8 = *reinterpret_cast<const uint32_t *>(wr + 8 * 16);
           const uint32_t a0 = (uint32_t)lo_nib_s8x16(w0), a2 = (uint32_t)hi_nib_s8x16(w0);
           const uint32_t a1 = (uint32_t)lo_nib_s8x16(w8), a3 = (uint32_t)hi_nib_s8x16(w8);
 #pragma unroll
           for (int q = 0; q < NT; ++q) mma_s8_16832(d[j][wi][q], a0, a1, a2, a3, b[q][0], b[q][1]);
-          const uint16_t *sr = reinterpret_cast<const uint16_t *>(ws + S::NIB) + bl * 32 + 16 * rg + g;
+          const uint16_t *sr = reinterpret_cast<const uint16_t *>(ws + S::NIB) + bl * RWS + 16 * rg + g;
           dwp[j][wi][0] = sr[0];
           dwp[j][wi][1] = sr[8];
         }
@@ -682,23 +689,24 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
     const unsigned long long ep = peer_epoch(pr);
     const size_t slot0 = ((size_t)(ep & 1) * pr.world + pr.rank) * pr.slot;
     const unsigned long long tag = (unsigned long long)(unsigned)ep << 32;
-    named_sync(kBarEpi, kMmaGroups * 32);
-    float *tile_s = acc_s;  // MT * 32 floats == S::ACCS
+    named_sync(kBarEpi, G * 32);
+    float *tile_s = acc_s;  // MT * RWS floats == S::ACCS
 #pragma unroll
     for (int q = 0; q < NT; ++q)
 #pragma unroll
       for (int e = 0; e < 2; ++e)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          tile_s[(8 * q + 2 * c + e) * 32 + 16 * rg + g + 8 * h] = acc[0][q][h][e];
-    named_sync(kBarEpi, kMmaGroups * 32);
-    const int et = rg * 32 + lane;  // 0..63: token et / 8, rows 4 * (et % 8) ..
-    for (int i = et; i < mcount * 8; i += kMmaGroups * 32) {
-      const int tok = i / 8, r4 = (i % 8) * 4;
-      const float4 v = *reinterpret_cast<const float4 *>(tile_s + tok * 32 + r4);
+          tile_s[(8 * q + 2 * c + e) * RWS + 16 * rg + g + 8 * h] = acc[0][q][h][e];
+    named_sync(kBarEpi, G * 32);
+    constexpr int R4 = RWS / 4;      // four-row pieces per token
+    const int et = rg * 32 + lane;   // token et / R4, rows 4 * (et % R4) ..
+    for (int i = et; i < mcount * R4; i += G * 32) {
+      const int tok = i / R4, r4 = (i % R4) * 4;
+      const float4 v = *reinterpret_cast<const float4 *>(tile_s + tok * RWS + r4);
       const unsigned long long w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
       const unsigned long long w2 = tag | __float_as_uint(v.z), w3 = tag | __float_as_uint(v.w);
-      const size_t o = slot0 + (size_t)(m0 + tok) * a.N + (size_t)tile * SI_RT + r4;
+      const size_t o = slot0 + (size_t)(m0 + tok) * a.N + (size_t)rbase + r4;
       for (int dst = 0; dst < pr.world; ++dst) {
         unsigned long long *wp = reinterpret_cast<unsigned long long *>(pr.base[dst] + kPeerData) + o;
         asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(wp), "l"(w0), "l"(w1)
@@ -741,7 +749,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));
         if (g == 0) red[rg * MT + 8 * q + 2 * c + e] = m;
       }
-    named_sync(kBarEpi, kMmaGroups * 32);
+    named_sync(kBarEpi, G * 32);
 #pragma unroll
     for (int q = 0; q < NT; ++q)
 #pragma unroll
@@ -764,18 +772,15 @@ __global__ void __launch_bounds__(kMmaWarps * 32, MB)
   }
 }
 
-template <int MT, bool SWIGLU>
-cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
-  using S = MmaShape<MT, SWIGLU>;
+template <int MT, bool SWIGLU, int G>
+cudaError_t run_mma_g(const GemvArgs &a, int sms, cudaStream_t s) {
+  using S = MmaShape<MT, SWIGLU, G>;
   const int KB = a.K / 32, tiles = a.N / SI_RT;
+  const int grid_y = (a.M + MT - 1) / MT;
   // One wave: with more tiles than two CTAs per SM hold but no more than three
   // do (the 72B QKV projection's 320 tiles), three per SM -- 72 registers and
   // a shallower ring -- instead of a second, nearly empty wave.
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid_y = (a.M + MT - 1) / MT;
-  const bool three = S::MINB == 2 && (long)tiles * grid_y > 2L * sms &&
+  const bool three = G == 2 && S::MINB == 2 && (long)tiles * grid_y > 2L * sms &&
                      (long)tiles * grid_y <= 3L * sms && S::smem(5, KB) <= kMmaCtaBudget3;
   // The deepest ring (5..12 stages) that keeps that many CTAs per SM.
   int ns = kMmaMaxRing;
@@ -783,11 +788,14 @@ cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
   while (ns > 5 && S::smem(ns, KB) > budget) --ns;
   const size_t smem = S::smem(ns, KB);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  // Nibbles [tiles*KB blocks][32 rows x 16 B] as (64 x u64, tiles*KB), a box
+  // of one CTA's RWS rows; scales [tiles*KB][32] fp16 likewise; activations
+  // [M][K] int8 as (K/8 x u64, M).
   CUtensorMap tmN, tmN2, tmS, tmS2, tmX;
   const cuuint64_t dN[2] = {64, (cuuint64_t)tiles * KB}, sN[1] = {512};
-  const cuuint32_t bN[2] = {64, (cuuint32_t)S::CB};
+  const cuuint32_t bN[2] = {(cuuint32_t)S::RWS * 2, (cuuint32_t)S::CB};
   const cuuint64_t dS[2] = {32, (cuuint64_t)tiles * KB}, sS[1] = {64};
-  const cuuint32_t bS[2] = {32, (cuuint32_t)S::CB};
+  const cuuint32_t bS[2] = {(cuuint32_t)S::RWS, (cuuint32_t)S::CB};
   const cuuint64_t dX[2] = {(cuuint64_t)a.K / 8, (cuuint64_t)a.M}, sX[1] = {(cuuint64_t)a.K};
   const cuuint32_t bX[2] = {(cuuint32_t)S::CB * 4, (cuuint32_t)MT};
   if (!tma_encode(&tmN, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, a.nib, dN, sN, bN,
@@ -808,17 +816,35 @@ cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
     tmS2 = tmS;
   }
   constexpr int MB = S::MINB;
-  constexpr int MB3 = S::MINB == 2 ? 3 : S::MINB;
-  auto kern = (!SWIGLU && a.isum_out) ? k_gemv_mma<MT, SWIGLU, !SWIGLU, MB>
-              : three                 ? k_gemv_mma<MT, SWIGLU, false, MB3>
-                                      : k_gemv_mma<MT, SWIGLU, false, MB>;
+  constexpr int MB3 = G == 2 && S::MINB == 2 ? 3 : S::MINB;
+  auto kern = (!SWIGLU && a.isum_out) ? k_gemv_mma<MT, SWIGLU, !SWIGLU, MB, G>
+              : three                 ? k_gemv_mma<MT, SWIGLU, false, MB3, G>
+                                      : k_gemv_mma<MT, SWIGLU, false, MB, G>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid(tiles, grid_y);
-  return launch_pdl(kern, grid, dim3(kMmaWarps * 32), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
+  dim3 grid(tiles * (2 / G), grid_y);
+  return launch_pdl(kern, grid, dim3(mma_warps(G) * 32), smem, s, tmN, tmN2, tmS, tmS2, tmX, a,
+                    ns);
+}
+
+// Half-tile CTAs (16 rows) for plain projections with fewer tiles than SMs --
+// the tensor-parallel QKV shards (1280 rows at TP = 8: 40 tiles) -- so twice
+// the CTAs stream the weights; whole tiles otherwise, and always for SwiGLU
+// (its Q8 block is a tile's 32 rows), the peer-store mode and the block-sum
+// instantiation.
+template <int MT, bool SWIGLU>
+cudaError_t run_mma(const GemvArgs &a, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long ctas = (long)(a.N / SI_RT) * ((a.M + MT - 1) / MT);
+  if constexpr (!SWIGLU) {
+    if (a.peer.world == 0 && !a.isum_out && ctas < sms) return run_mma_g<MT, false, 1>(a, sms, s);
+  }
+  return run_mma_g<MT, SWIGLU, 2>(a, sms, s);
 }
 
 template <int MT, int RW, bool SWIGLU>
