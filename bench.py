@@ -15,9 +15,10 @@ QKV/gate/up, row-sharded o/down; one rank per GPU).
 * decode = 256 decode steps of a batch of 8 (contexts 4097..4352), us per step
            and per token, beside the headline;
 * e2e    = the headline through the C ABI with host buffers: every step copies
-           its 128 MiB fp32 input in from pinned host memory and its 128 MiB
-           output back (two buffer sets, so the copies of neighbouring steps
-           overlap the compute on their own streams);
+           its 128 MiB fp32 input in from rank 0's pinned host memory (with
+           several ranks, broadcast from rank 0 over NVLink inside the step) and
+           its 128 MiB output back to rank 0 (two buffer sets, so the copies of
+           neighbouring steps overlap the compute on their own streams);
 * roofline: the prefill's dominant kernel (the gate/up GEMM at 4096 tokens)
            against the int8 tensor-core rate measured here by a tcgen05
            kind::i8 probe; `layer_roofline` adds the whole prefill (int8 ops)
@@ -32,8 +33,10 @@ At N = 1 the line also carries the other BASELINE configurations, each with its
 own measurement: config2 (one 7B layer: 2048-token prefill, 128 decode steps;
 e2e through the host-pointer C ABI; CPU baseline on the same dims), config3
 (batch-64 7B decode over 4096-position fp32 caches), config1 (the 1.5B
-projection set and its token sweep), decode_gemv_roofline and reference_layer
-(the reference's own attention layer timed on the host against this library).
+projection set and its token sweep), decode_gemv_roofline, gemm_schemes (the
+prefill GEMM's exact int8 kernels beside bf16/fp16-dequant cuBLAS GEMMs, with
+their errors) and reference_layer (the reference's own attention layer timed
+on the host against this library).
 `--impl reference` times the reference's CPU path on the headline workload.
 """
 from __future__ import annotations
