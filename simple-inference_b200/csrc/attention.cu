@@ -837,7 +837,6 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
 }  // namespace
 
 bool attn_decode_form(const AttnArgs &a) { return !use_prefill(a); }
-long attn_decode_ctas(const AttnArgs &a) { return (long)a.nsplit * a.n_kv_heads * a.T; }
 
 size_t attn_part_floats(int T, int n_q_heads, int head_dim, int nsplit) {
   return nsplit > 1 ? (size_t)T * n_q_heads * nsplit * (head_dim + 2) : 0;

@@ -195,8 +195,6 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t s);
 // True when launch_attention runs the decode form (per-token arrays, or
 // fewer than 16 tokens): the only form that honours q8_qs / q8_d.
 bool attn_decode_form(const AttnArgs &a);
-// CTAs the decode form launches (splits x KV heads x tokens).
-long attn_decode_ctas(const AttnArgs &a);
 
 // ---- attention_tc.cu (tcgen05 causal prefill, split fp16 operands) ------------
 // The prefill form (no per-token arrays) at head_dim 128 and groups <= 8.
