@@ -67,6 +67,9 @@ TP_MAX_CTX = TP_PREFILL + TP_DECODE + 1
 DIMS_7B = dict(hidden=3584, n_q_heads=28, n_kv_heads=4, head_dim=128, intermediate=18944,
                rope_theta=1e6, rms_eps=1e-6)
 C2_PREFILL, C2_DECODE = 2048, 128
+DIMS_05B = dict(hidden=896, n_q_heads=14, n_kv_heads=2, head_dim=64, intermediate=4864,
+                rope_theta=1e6, rms_eps=1e-6)
+C0_PREFILL = 64
 C3_BATCH, C3_CTX = 64, 4096
 H1, I1, QKV1 = 1536, 8960, 2048          # config 1: the 1.5B projection set
 C1_COPIES, C1_M = 10, 2048
@@ -585,6 +588,47 @@ def run_config4(args, rank, world, local_rank, ctx, torch, barrier_sync, max_ove
     return res
 
 
+def run_config0(torch):
+    """BASELINE config 0 (the reference's own CPU-runnable scale): one
+    Qwen2.5-0.5B layer (hidden 896, 14 Q / 2 KV heads, head_dim 64,
+    intermediate 4864), a 64-token prefill then one decode step at context 65,
+    fp32 KV.  Device time of each with CUDA events (the prefill re-run over the
+    same positions), on its own context (RoPE tables for head_dim 64)."""
+    import sib200
+    c0 = sib200.Context(0, max_positions=256, rope_theta=1e6, head_dim=64)
+    stream = torch.cuda.ExternalStream(c0.stream)
+    try:
+        layer = c0.layer_synth(DIMS_05B, 0)
+        kv = c0.kv(DIMS_05B, 1, C0_PREFILL + 2, True)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        X = torch.randn(C0_PREFILL, DIMS_05B["hidden"], device="cuda", generator=g)
+        Y = torch.empty_like(X)
+        xd = torch.randn(1, DIMS_05B["hidden"], device="cuda", generator=g)
+        yd = torch.empty_like(xd)
+        torch.cuda.synchronize()
+        pf = lambda _=0: layer.prefill_dev(kv, 0, X, C0_PREFILL, 0, Y, sib200.SI_LAYER_FULL)
+        dec = lambda _=0: layer.decode_dev(kv, xd, [C0_PREFILL + 1], yd, sib200.SI_LAYER_FULL)
+        for _ in range(3):
+            pf()
+            dec()
+        reps = 50
+        tpf = time_region(torch, stream, pf, reps) / reps
+        tdec = time_region(torch, stream, dec, reps) / reps
+        c0.status()
+        out = {"workload": "BASELINE config 0: one Qwen2.5-0.5B layer (hidden 896, 14 Q / 2 KV "
+                           "heads, head_dim 64, intermediate 4864), 64-token prefill then one "
+                           "decode step (context 65), fp32 KV",
+               "prefill_us": round(tpf * 1e6, 1), "prefill_tok_s": round(C0_PREFILL / tpf, 1),
+               "decode_us_per_token": round(tdec * 1e6, 2),
+               "timing": "CUDA events, eager launches, 50 repetitions"}
+        kv.free()
+        layer.free()
+        return out
+    finally:
+        c0.sync()
+        c0.close()
+
+
 def run_config2(ctx, torch, stream, args, peak):
     """one Qwen2.5-7B layer, a 2048-token prefill (fp16 KV)
     then 128 decode steps at batch 1; and config 3: one decode step of 64
@@ -1046,6 +1090,7 @@ def run_ours(args, rank, world, local_rank):
             return c2
         extra(result, "config2", cfg23)
         extra(result, "config1", lambda: run_config1(ctx, torch, stream))
+        extra(result, "config0", lambda: run_config0(torch))
         extra(result, "decode_gemv_roofline", lambda: decode_gemv_roofline(ctx, torch, stream))
         extra(result, "gemm_schemes", lambda: gemm_schemes(
             ctx, torch, stream, (result.get("int8_peak") or {}).get("tops")))
@@ -1061,6 +1106,10 @@ def run_ours(args, rank, world, local_rank):
                     args.cpu_seconds / 2, 2, "config 2 (7B dims, fp16 KV)"))
             if isinstance(result.get("config3"), dict):
                 extra(result["config3"], "cpu_baseline", lambda: cpu_config3(args.cpu_seconds / 3))
+            if isinstance(result.get("config0"), dict) and "error" not in result["config0"]:
+                extra(result["config0"], "cpu_baseline", lambda: cpu_layer_baseline(
+                    DIMS_05B, 1, C0_PREFILL, C0_PREFILL + 1, True, min(3.0, args.cpu_seconds),
+                    0, "config 0 (0.5B dims, fp32 KV)"))
     torch.cuda.synchronize()
     ctx.sync()
     gc.collect()
