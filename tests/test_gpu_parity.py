@@ -110,10 +110,13 @@ def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M, kernel):
         np.testing.assert_array_equal(got[t], oc.matvec(w, blocks[t], K, N, bias))
 
 
-@pytest.mark.parametrize("N,K", [(8192, 8192), (10240, 8192), (8192, 29568), (4608, 3584)])
+@pytest.mark.parametrize("N,K", [(8192, 8192), (10240, 8192), (8192, 29568), (4608, 3584),
+                                 (1280, 8192), (2560, 8192)])
 @pytest.mark.parametrize("M", [3, 8, 16])
 def test_gemv_mma_equals_dp4a_large(si_ctx, N, K, M):
-    """At the 7B/72B decode shapes the two GEMV forms return the same bits."""
+    """At the 7B/72B decode shapes -- whole-tile CTAs at two or three per SM
+    (10240 rows: 320 tiles) and half-tile CTAs for the tensor-parallel QKV
+    shards (1280, 2560 rows) -- the two GEMV forms return the same bits."""
     m = si_ctx.matrix_synth(N, K, seed=N + K + M)
     x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
     torch.cuda.synchronize()
