@@ -496,32 +496,52 @@ __global__ void k_attn_combine(const AttnArgs a) {
   const int D = a.head_dim;
   const int S = splits_for(ctx_of(a, t));
   const float *p = a.part + ((size_t)t * a.n_q_heads + h) * a.nsplit * (D + 2);
-  // Merge factors per split: one (max, sum) chain, run by thread 0 with the
-  // splits' pairs loaded into shared memory first; every d then applies them.
-  extern __shared__ float2 fs[];  // [S]: (m, l), then (a, b); [S] = final (M, L)
+  // Merge factors per split, the values of the sequential chain M' = max(M, m),
+  // a = expf(M - M'), b = expf(m - M'), L = fmaf(L, a, l*b) (merge_ml): the
+  // running maxima are a prefix max, so warp 0 computes every split's M, a and
+  // b in parallel (a scan over 32 splits at a time); only the L chain stays
+  // serial (thread 0).  Every d then applies (a, b) to its O chain in order.
+  extern __shared__ float2 fs[];  // [S] (m, l); [S] = final (M, L); then [S] (a, b)
+  float2 *fab = fs + S + 1;
   for (int s = d; s < S; s += blockDim.x)
     fs[s] = make_float2(p[(size_t)s * (D + 2)], p[(size_t)s * (D + 2) + 1]);
   __syncthreads();
-  if (d == 0) {
-    float M = fs[0].x, Ls = fs[0].y;
-    for (int s = 1; s < S; ++s) {
-      float fa, fb;
-      merge_ml(M, Ls, fs[s].x, fs[s].y, fa, fb);
-      fs[s] = make_float2(fa, fb);
+  if (d < 32) {
+    float run = -INFINITY;  // M after the splits before this batch of 32
+    for (int base = 0; base < S; base += 32) {
+      const int s = base + d;
+      const float m = s < S ? fs[s].x : -INFINITY;
+      float x = m;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (d >= o) x = fmaxf(x, y);
+      }
+      const float Ms = fmaxf(run, x);  // M after split s
+      float Mp = __shfl_up_sync(0xffffffffu, Ms, 1);
+      if (d == 0) Mp = run;            // M before split s
+      if (s < S && s > 0) fab[s] = make_float2(expf(__fsub_rn(Mp, Ms)), expf(__fsub_rn(m, Ms)));
+      run = __shfl_sync(0xffffffffu, Ms, 31);
     }
-    fs[S] = make_float2(M, Ls);
+    if (d == 0) fs[S].x = run;
+  }
+  __syncthreads();
+  if (d == 0) {
+    float Ls = fs[0].y;
+    for (int s = 1; s < S; ++s) Ls = fmaf(Ls, fab[s].x, __fmul_rn(fs[s].y, fab[s].y));
+    fs[S].y = Ls;
   }
   __syncthreads();
   float O = p[2 + d];
   int s = 1;
-  for (; s + 8 <= S; s += 8) {  // eight splits' loads in flight, merged in order
-    float oo[8];
+  for (; s + 16 <= S; s += 16) {  // sixteen splits' loads in flight, merged in order
+    float oo[16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) oo[j] = p[(size_t)(s + j) * (D + 2) + 2 + d];
+    for (int j = 0; j < 16; ++j) oo[j] = p[(size_t)(s + j) * (D + 2) + 2 + d];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) O = merge_o(O, fs[s + j].x, oo[j], fs[s + j].y);
+    for (int j = 0; j < 16; ++j) O = merge_o(O, fab[s + j].x, oo[j], fab[s + j].y);
   }
-  for (; s < S; ++s) O = merge_o(O, fs[s].x, p[(size_t)s * (D + 2) + 2 + d], fs[s].y);
+  for (; s < S; ++s) O = merge_o(O, fab[s].x, p[(size_t)s * (D + 2) + 2 + d], fab[s].y);
   const size_t o = ((size_t)t * a.n_q_heads + h) * D + d;
   const float y = __fdiv_rn(O, fs[S].y);
   a.out[o] = y;
@@ -832,7 +852,7 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
                  s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
   return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D),
-                    (size_t)(a.nsplit + 1) * sizeof(float2), s, a);
+                    (size_t)(2 * a.nsplit + 1) * sizeof(float2), s, a);
 }
 }  // namespace
 
