@@ -171,9 +171,13 @@ struct VRow {
   }
 };
 
-// One CTA per (split, KV head, token), one warp per 32-key sub-tile, NP pairs
-// of query heads (G <= 2 NP; a head past G computes on zero queries and is
-// never written).  Every per-key and per-dim loop is unrolled against
+// One CTA per (split, KV head, head chunk, token), one warp per 32-key
+// sub-tile, NP pairs of query heads: the CTA takes heads h0 .. h0 + 2 NP - 1 of
+// the KV head's group of G (a head past G computes on zero queries and is
+// never written).  Small grids (batch 1-2) split the group into chunks so that
+// more CTAs, each with a shorter per-warp chain, share the work; each chunk's
+// CTA reads the same K/V rows (the second read hits the L2), and only chunk
+// 0 appends the new key.  Every per-key and per-dim loop is unrolled against
 // compile-time offsets from a few per-lane bases, and a full sub-tile (the
 // common case) runs without per-key predicates; a partial one zero-fills the
 // K rows past the context (their scores are masked to -inf, so p = 0) and
@@ -192,8 +196,11 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
 
   pdl_trigger();
   pdl_wait();
-  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
   const int Hq = a.n_q_heads, Hkv = a.n_kv_heads, G = Hq / Hkv;
+  const int HS = gridDim.y / Hkv;  // head chunks per group
+  const int split = blockIdx.x, kvh = blockIdx.y / HS, t = blockIdx.z;
+  const int h0 = (blockIdx.y % HS) * NH;  // this CTA's first head in the group
+  const int Gc = min(NH, G - h0);         // its heads
   const int seq = a.tok_seq ? a.tok_seq[t] : a.seq0;
   const int L = ctx_of(a, t);
   const int ns = splits_for(L);
@@ -260,10 +267,10 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
       const int i = d < HALF ? d : d - HALF;
       const size_t ti = (size_t)(L - 1) * HALF + i;
       const float c = a.cos_tab[ti], sn = a.sin_tab[ti];
-      const float *qg = a.qkv + (size_t)t * qkv_row + (size_t)kvh * G * D + i;
+      const float *qg = a.qkv + (size_t)t * qkv_row + (size_t)(kvh * G + h0) * D + i;
 #pragma unroll
       for (int h = 0; h < kMaxGroup; ++h) {
-        if (h < G) {
+        if (h < Gc) {
           const float x0 = qg[(size_t)h * D], x1 = qg[(size_t)h * D + HALF];
           qv[h] = d < HALF ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn))
                            : __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
@@ -272,9 +279,9 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
         }
       }
     } else {
-      const float *qg = a.q + ((size_t)t * Hq + (size_t)kvh * G) * D + d;
+      const float *qg = a.q + ((size_t)t * Hq + (size_t)(kvh * G + h0)) * D + d;
 #pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) qv[h] = h < G ? qg[(size_t)h * D] : 0.0f;
+      for (int h = 0; h < kMaxGroup; ++h) qv[h] = h < Gc ? qg[(size_t)h * D] : 0.0f;
     }
     *reinterpret_cast<float4 *>(q_s + d * kMaxGroup) = make_float4(qv[0], qv[1], qv[2], qv[3]);
     *reinterpret_cast<float4 *>(q_s + d * kMaxGroup + 4) = make_float4(qv[4], qv[5], qv[6], qv[7]);
@@ -311,11 +318,11 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
       uint8_t *p = krow + ((((byte >> 4) ^ (r & 7)) << 4) | (byte & 15));
       if constexpr (F32) {
         *reinterpret_cast<float *>(p) = kval;
-        static_cast<float *>(const_cast<void *>(a.kc))[o + dd] = kval;
+        if (h0 == 0) static_cast<float *>(const_cast<void *>(a.kc))[o + dd] = kval;
       } else {
         const uint16_t hb = f32_to_f16(kval);
         *reinterpret_cast<uint16_t *>(p) = hb;
-        static_cast<uint16_t *>(const_cast<void *>(a.kc))[o + dd] = hb;
+        if (h0 == 0) static_cast<uint16_t *>(const_cast<void *>(a.kc))[o + dd] = hb;
       }
     };
 #pragma unroll
@@ -324,10 +331,12 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
       put(i, __fsub_rn(__fmul_rn(x0[j], c[j]), __fmul_rn(x1[j], sn[j])));
       put(i + HALF, __fadd_rn(__fmul_rn(x1[j], c[j]), __fmul_rn(x0[j], sn[j])));
     }
+    if (h0 == 0) {  // one head chunk appends the new key to the cache
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) {
-      if constexpr (F32) static_cast<float *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = vv[j];
-      else static_cast<uint16_t *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = f32_to_f16(vv[j]);
+      for (int j = 0; j < D / 32; ++j) {
+        if constexpr (F32) static_cast<float *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = vv[j];
+        else static_cast<uint16_t *>(const_cast<void *>(a.vc))[o + lane + 32 * j] = f32_to_f16(vv[j]);
+      }
     }
     if (r < 16) {
 #pragma unroll
@@ -446,7 +455,7 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   // (max, sum) chain once; every output element then applies them.
   float2 *fab = reinterpret_cast<float2 *>(q_s);  // [G][4] (the queries are no longer read)
   __shared__ float2 mls[kMaxGroup];
-  if (threadIdx.x < G) {
+  if (threadIdx.x < Gc) {
     const int g = threadIdx.x;
     float M = ml_s[g].x, Ls = ml_s[g].y;
     for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
@@ -463,14 +472,14 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   for (int i = 0; i < PER; ++i) {
     const int idx = threadIdx.x + i * kSubPerSplit * 32;
     const int g = idx / D, d = idx % D;
-    if (g < G) {
+    if (g < Gc) {
       const float M = mls[g].x, Ls = mls[g].y;
       float O = ob[g * D + d];
       for (int w = 1; w < kSubPerSplit && w < nsub; ++w) {
         const float2 f = fab[g * kSubPerSplit + w];
         O = merge_o(O, f.x, ob[w * (S::KW / 4) + g * D + d], f.y);
       }
-      const int h = kvh * G + g;
+      const int h = kvh * G + h0 + g;
       if (a.nsplit == 1) {  // no combine pass follows
         const size_t o = ((size_t)t * Hq + h) * D + d;
         const float y = __fdiv_rn(O, Ls);
@@ -503,6 +512,12 @@ __global__ void k_attn_combine(const AttnArgs a) {
   // serial (thread 0).  Every d then applies (a, b) to its O chain in order.
   extern __shared__ float2 fs[];  // [S] (m, l); [S] = final (M, L); then [S] (a, b)
   float2 *fab = fs + S + 1;
+  // The first 17 splits' outputs of this d, in flight while the factors are formed.
+  const float *po = p + 2 + d;
+  float O = po[0];
+  float o1[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o1[j] = 1 + j < S ? po[(size_t)(1 + j) * (D + 2)] : 0.0f;
   for (int s = d; s < S; s += blockDim.x)
     fs[s] = make_float2(p[(size_t)s * (D + 2)], p[(size_t)s * (D + 2) + 1]);
   __syncthreads();
@@ -526,14 +541,15 @@ __global__ void k_attn_combine(const AttnArgs a) {
     if (d == 0) fs[S].x = run;
   }
   __syncthreads();
-  if (d == 0) {
+  if (d == 0) {  // the normaliser chain, while the other warps merge their O chains
     float Ls = fs[0].y;
     for (int s = 1; s < S; ++s) Ls = fmaf(Ls, fab[s].x, __fmul_rn(fs[s].y, fab[s].y));
     fs[S].y = Ls;
   }
-  __syncthreads();
-  float O = p[2 + d];
-  int s = 1;
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    if (1 + j < S) O = merge_o(O, fab[1 + j].x, o1[j], fab[1 + j].y);
+  int s = 17;
   for (; s + 16 <= S; s += 16) {  // sixteen splits' loads in flight, merged in order
     float oo[16];
 #pragma unroll
@@ -542,6 +558,7 @@ __global__ void k_attn_combine(const AttnArgs a) {
     for (int j = 0; j < 16; ++j) O = merge_o(O, fab[s + j].x, oo[j], fab[s + j].y);
   }
   for (; s < S; ++s) O = merge_o(O, fab[s].x, p[(size_t)s * (D + 2) + 2 + d], fab[s].y);
+  __syncthreads();  // the normaliser
   const size_t o = ((size_t)t * a.n_q_heads + h) * D + d;
   const float y = __fdiv_rn(O, fs[S].y);
   a.out[o] = y;
@@ -843,13 +860,29 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
   }
   using Sd = DecShape<D, F32>;
   const int G = a.n_q_heads / a.n_kv_heads;
-  auto kern = G <= 2 ? k_attn_dec<D, F32, 1>
-              : G <= 4 ? k_attn_dec<D, F32, 2>
-              : G <= 6 ? k_attn_dec<D, F32, 3> : k_attn_dec<D, F32, 4>;
+  // Heads per CTA: the whole group, or -- while the grid stays within two
+  // CTAs per SM -- chunks of 4 or 2 heads (the per-warp score and P.V chains
+  // shrink with the chunk; small decode batches leave most SMs idle otherwise).
+  int np = (G + 1) / 2;
+  {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long base = (long)a.nsplit * a.n_kv_heads * a.T;
+    for (int c : {1, 2})
+      if (c < np && base * ((G + 2 * c - 1) / (2 * c)) <= 2L * sms) {
+        np = c;
+        break;
+      }
+  }
+  const int hs = (G + 2 * np - 1) / (2 * np);  // head chunks per group
+  auto kern = np == 1 ? k_attn_dec<D, F32, 1>
+              : np == 2 ? k_attn_dec<D, F32, 2>
+              : np == 3 ? k_attn_dec<D, F32, 3> : k_attn_dec<D, F32, 4>;
   cudaError_t e = with_smem(kern, Sd::bytes());
   if (e != cudaSuccess) return e;
-  e = launch_pdl(kern, dim3(a.nsplit, a.n_kv_heads, a.T), dim3(kSubPerSplit * 32), Sd::bytes(),
-                 s, a);
+  e = launch_pdl(kern, dim3(a.nsplit, a.n_kv_heads * hs, a.T), dim3(kSubPerSplit * 32),
+                 Sd::bytes(), s, a);
   if (e != cudaSuccess || a.nsplit == 1) return e;
   return launch_pdl(k_attn_combine, dim3(a.n_q_heads, a.T), dim3(D),
                     (size_t)(2 * a.nsplit + 1) * sizeof(float2), s, a);
