@@ -860,17 +860,22 @@ cudaError_t run(const AttnArgs &a, cudaStream_t s) {
   }
   using Sd = DecShape<D, F32>;
   const int G = a.n_q_heads / a.n_kv_heads;
-  // Heads per CTA: the whole group, or -- while the grid stays within two
-  // CTAs per SM -- chunks of 4 or 2 heads (the per-warp score and P.V chains
-  // shrink with the chunk; small decode batches leave most SMs idle otherwise).
+  // Heads per CTA: the whole group, or chunks of 2 or 4 heads when the launch
+  // is latency-bound -- at most 16 MB of K/V (each chunk's CTA reads the rows
+  // again) and at most eight CTAs per SM.  Measured on B200 (graph replays):
+  // 7B step at batch 1 61.4 -> 57.2 us, at batch 2 72.5 -> 67.8 us; the
+  // TP = 8 shard at batch 8 (35 MB of fp32 K/V) 560 -> 576 us when chunked,
+  // so it is not.
   int np = (G + 1) / 2;
-  {
+  const double kv_bytes =
+      (double)a.nsplit * kSplitKeys * a.n_kv_heads * a.T * Sd::RB * 2.0;
+  if (kv_bytes <= 16e6) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long base = (long)a.nsplit * a.n_kv_heads * a.T;
     for (int c : {1, 2})
-      if (c < np && base * ((G + 2 * c - 1) / (2 * c)) <= 2L * sms) {
+      if (c < np && base * ((G + 2 * c - 1) / (2 * c)) <= 8L * sms) {
         np = c;
         break;
       }
