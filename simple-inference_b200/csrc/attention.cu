@@ -259,6 +259,27 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   // The group's queries as [D][8 heads] (heads of one dim adjacent).
   constexpr int HALF = D / 2;
   const size_t qkv_row = (size_t)(Hq + 2 * Hkv) * D;
+  // The new key's raw K/V and RoPE factors (used after the staging barrier),
+  // requested now so that they arrive with the staged rows.
+  constexpr int KP = HALF / 32;  // rotated pairs per lane
+  float nc[KP], nsn[KP], nx0[KP], nx1[KP], nvv[D / 32], nvr[NV];
+  if (has_new) {
+    const int pos = L - 1;
+    const float *__restrict__ kraw = a.qkv + (size_t)t * qkv_row + (size_t)Hq * D + (size_t)kvh * D;
+    const float *__restrict__ vraw = kraw + (size_t)Hkv * D;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const int i = lane + 32 * j;
+      nc[j] = a.cos_tab[(size_t)pos * HALF + i];
+      nsn[j] = a.sin_tab[(size_t)pos * HALF + i];
+      nx0[j] = kraw[i];
+      nx1[j] = kraw[i + HALF];
+    }
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) nvv[j] = vraw[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) nvr[j] = vraw[lane * NV + j];
+  }
   if (threadIdx.x < D) {
     const int d = threadIdx.x;
     float qv[kMaxGroup];
@@ -295,21 +316,8 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   typename VR::T vnew = VR::zero();
   if (has_new) {
     const int pos = L - 1, r = nvalid - 1;
-    const float *__restrict__ kraw = a.qkv + (size_t)t * qkv_row + (size_t)Hq * D + (size_t)kvh * D;
-    const float *__restrict__ vraw = kraw + (size_t)Hkv * D;
-    constexpr int KP = HALF / 32;  // rotated pairs per lane
-    float c[KP], sn[KP], x0[KP], x1[KP], vv[D / 32];
-#pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      const int i = lane + 32 * j;
-      c[j] = a.cos_tab[(size_t)pos * HALF + i];
-      sn[j] = a.sin_tab[(size_t)pos * HALF + i];
-      x0[j] = kraw[i];
-      x1[j] = kraw[i + HALF];
-    }
-#pragma unroll
-    for (int j = 0; j < D / 32; ++j) vv[j] = vraw[lane + 32 * j];
-    vnew = VR::from_raw(vraw + lane * NV);
+    const float *c = nc, *sn = nsn, *x0 = nx0, *x1 = nx1, *vv = nvv;
+    vnew = VR::from_raw(nvr);
     const size_t o = (((size_t)seq * a.max_ctx + pos) * Hkv + kvh) * D;
     uint8_t *krow = k_w + r * S::RB;
     // (the fused form appends: the cache pointers are written here)
