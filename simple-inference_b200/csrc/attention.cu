@@ -222,7 +222,12 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
   // K rows into shared memory: lane = chunk (lane % CPR) of rows lane / CPR + RPI i,
   // chunks XOR-swizzled by row so that lane = key reads are conflict-free.
   constexpr int NI = kSub / S::RPI;
-  typename VR::T vb[16];  // V rows 0..15 of the sub-tile, in flight during the scores
+  // V rows 0..15 of the sub-tile, in flight during the scores, and with an
+  // fp16 cache rows 16..31 too (7B step at batch 1 55.5 -> 54.3 us); fp32
+  // caches prefetch rows 16..31 to the L2 and load them after the first half
+  // (the extra registers cost more there: 0.5B step 25.6 -> 26.0 us).
+  constexpr bool kEarlyV = !F32;
+  typename VR::T vb[kEarlyV ? 32 : 16];
   if (nvalid > 0) {
     const int c = lane % S::CPR, ro = lane / S::CPR;
     const uint8_t *src = kg + (size_t)ro * rsb + c * 16;
@@ -235,6 +240,10 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
                    src + (size_t)(i * S::RPI) * rsb, 16);
 #pragma unroll
       for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)k * rsb);
+      if constexpr (kEarlyV) {
+#pragma unroll
+        for (int k = 16; k < 32; ++k) vb[k] = VR::load(vg + (size_t)k * rsb);
+      }
     } else {
       // Rows past the cached ones are not copied (their scores are masked, or
       // the new key's row is written below).
@@ -245,16 +254,22 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
                      src + (size_t)(i * S::RPI) * rsb, 16);
 #pragma unroll
       for (int k = 0; k < 16; ++k) vb[k] = k < ncache ? VR::load(vg + (size_t)k * rsb) : VR::zero();
-    }
-    // V rows 16..31 into L2 while the scores are computed.
-    constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
-    constexpr int RPP = 32 / LPR;             // rows per warp-wide prefetch
-    const uint8_t *vrow = static_cast<const uint8_t *>(a.vc) + base +
-                          (size_t)(key0 + 16 + lane / LPR) * rsb + (lane % LPR) * 128;
+      if constexpr (kEarlyV) {
 #pragma unroll
-    for (int i = 0; i < (16 + RPP - 1) / RPP; ++i)
-      if (16 + lane / LPR + i * RPP < ncache)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + (size_t)(i * RPP) * rsb));
+        for (int k = 16; k < 32; ++k) vb[k] = k < ncache ? VR::load(vg + (size_t)k * rsb) : VR::zero();
+      }
+    }
+    if constexpr (!kEarlyV) {
+      // V rows 16..31 into L2 while the scores are computed.
+      constexpr int LPR = (S::RB + 127) / 128;  // 128-byte lines per row
+      constexpr int RPP = 32 / LPR;             // rows per warp-wide prefetch
+      const uint8_t *vrow = static_cast<const uint8_t *>(a.vc) + base +
+                            (size_t)(key0 + 16 + lane / LPR) * rsb + (lane % LPR) * 128;
+#pragma unroll
+      for (int i = 0; i < (16 + RPP - 1) / RPP; ++i)
+        if (16 + lane / LPR + i * RPP < ncache)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(vrow + (size_t)(i * RPP) * rsb));
+    }
   }
   // The group's queries as [D][8 heads] (heads of one dim adjacent).
   constexpr int HALF = D / 2;
@@ -350,6 +365,10 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
 #pragma unroll
       for (int k = 0; k < 16; ++k)
         if (k == r) vb[k] = vnew;
+    } else if constexpr (kEarlyV) {
+#pragma unroll
+      for (int k = 16; k < 32; ++k)
+        if (k == r) vb[k] = vnew;
     }
     __syncwarp();
   }
@@ -431,7 +450,12 @@ __global__ void __launch_bounds__(kSubPerSplit * 32) k_attn_dec(const AttnArgs a
     };
 #pragma unroll
     for (int k = 0; k < 16; ++k) pv_key(k, vb[k]);
-    if (nvalid > 16) {
+    if constexpr (kEarlyV) {
+      if (nvalid > 16) {
+#pragma unroll
+        for (int k = 16; k < 32; ++k) pv_key(k, vb[k]);
+      }
+    } else if (nvalid > 16) {
       if (ncache == kSub) {
 #pragma unroll
         for (int k = 0; k < 16; ++k) vb[k] = VR::load(vg + (size_t)(16 + k) * rsb);
