@@ -92,7 +92,7 @@ struct Shape {
 // and scaling by a power of two commutes with both roundings (the products
 // stay far inside the normal range), so the term is bit-identical to the
 // reference's.
-template <int MT, int RW, bool SWIGLU>
+template <int MT, int RW, bool SWIGLU, bool MULTI>
 __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
     k_gemv(const __grid_constant__ CUtensorMap tmN, const __grid_constant__ CUtensorMap tmN2,
            const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmS2,
@@ -109,20 +109,29 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
   float *dxs = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256);  // [KB][MT]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x / SLICES, r0 = (blockIdx.x % SLICES) * RW;
+  // Units (an RW-row slice of a tile) of this CTA: blockIdx.x + i * gridDim.x.
+  // One, or (MULTI) where the units fill between one and two CTA slots per
+  // SM, up to two streamed back to back through the same ring (the second
+  // unit's loads overlap the first one's tail instead of a second wave's
+  // start-up).
+  const int units = (a.N / SI_RT) * SLICES;
+  const int nu = MULTI ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 1;
+  auto unit_tile = [&](int i) { return ((int)blockIdx.x + i * (int)gridDim.x) / SLICES; };
+  auto unit_r0 = [&](int i) { return ((int)blockIdx.x + i * (int)gridDim.x) % SLICES * RW; };
   const int m0 = blockIdx.y * MT, mcount = min(MT, a.M - m0);
   const int KB = a.K / 32;
   const int npass = (KB + CB - 1) / CB;                 // chunks per matrix
-  const int nchunks = SWIGLU ? 2 * npass : npass;
+  const int nchunks = SWIGLU ? 2 * npass : npass;       // chunks per unit
+  const int ntot = nu * nchunks;
   auto bar = [&](uint64_t *b, int i) { return smem_u32(b + i); };
 
   pdl_trigger();
 
-  // Chunk c: pass c / npass (gate, then up), blocks [cc*CB, cc*CB + CB).
-  auto load_weights = [&](int c, int slot) {
+  // Chunk c of unit i: pass c / npass (gate, then up), blocks [cc*CB, cc*CB + CB).
+  auto load_weights = [&](int i, int c, int slot) {
     const int pass = c >= npass, cc = pass ? c - npass : c;
     uint8_t *st = smem + slot * S::STAGE;
-    const int y = tile * KB + cc * CB;
+    const int y = unit_tile(i) * KB + cc * CB, r0 = unit_r0(i);
     mbar_expect_tx(bar(full, slot), S::STAGE);
     tma_load_2d(smem_u32(st), pass ? &tmN2 : &tmN, r0 * 2, y, bar(full, slot));
     tma_load_2d(smem_u32(st + S::NIB), pass ? &tmS2 : &tmS, r0, y, bar(full, slot));
@@ -135,7 +144,7 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
   // Thread 0 sets the barriers up and requests the weights of the first
   // chunks right away -- before the previous kernel (which may still be
   // running) has produced the activations.
-  const int pre = nchunks < ns ? nchunks : ns;
+  const int pre = ntot < ns ? ntot : ns;
   if (threadIdx.x == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmN)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmS)) : "memory");
@@ -150,11 +159,11 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int c = 0; c < pre; ++c) load_weights(c, c);
+    for (int g = 0; g < pre; ++g) load_weights(g / nchunks, g % nchunks, g);
   }
   pdl_wait();
   if (threadIdx.x == 0)
-    for (int c = 0; c < pre; ++c) load_acts(c, c);
+    for (int g = 0; g < pre; ++g) load_acts(g % nchunks, g);
   for (int i = threadIdx.x; i < mcount * KB; i += blockDim.x) {
     const int m = i / KB, b = i - m * KB;
     dxs[b * MT + m] = __fmul_rn(f16_to_f32(a.xd[(size_t)(m0 + m) * KB + b]), 0.0625f);
@@ -166,16 +175,18 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
     if (lane != 0) return;
     int slot = pre == ns ? 0 : pre, phase = 0;
     int issued = pre;
-    for (int c = pre; c < nchunks; ++c) {
+    int ui = pre / nchunks, uc = pre - ui * nchunks;  // unit and chunk of the next load
+    for (int g = pre; g < ntot; ++g) {
       if (!mbar_wait(bar(empty, slot), phase, abort_flag)) {
         *abort_flag = 1;
         raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
         break;
       }
-      load_weights(c, slot);
-      load_acts(c, slot);
+      load_weights(ui, uc, slot);
+      load_acts(uc, slot);
       ++issued;
       if (++slot == ns) { slot = 0; phase ^= 1; }
+      if (++uc == nchunks) { uc = 0; ++ui; }
     }
     if (*abort_flag) {
       // Let the copies still in flight land before the CTA's shared memory
@@ -193,10 +204,19 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
     const int bo = lane / RW, rl = lane % RW;
     const bool want_isum = !SWIGLU && a.isum_out != nullptr;
     int slot = 0, sp = 0, tb = 0, tp = 0;
-    for (int c = 0; c < nchunks; ++c) {
+    int ui = 0, c = 0, tile = unit_tile(0), r0 = unit_r0(0);  // the chunk's unit
+    for (int g = 0; g < ntot; ++g) {
+      if constexpr (MULTI) {
+        if (c == nchunks) {
+          c = 0;
+          ++ui;
+          tile = unit_tile(ui);
+          r0 = unit_r0(ui);
+        }
+      }
       const int cc = c >= npass ? c - npass : c;
       bool ok = mbar_wait(bar(full, slot), sp, abort_flag);
-      if (ok && c >= NTB) ok = mbar_wait(bar(tempty, tb), tp ^ 1, abort_flag);
+      if (ok && g >= NTB) ok = mbar_wait(bar(tempty, tb), tp ^ 1, abort_flag);
       if (!ok) {
         *abort_flag = 1;
         raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
@@ -247,6 +267,7 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
       mbar_arrive(bar(tfull, tb));    // and its terms are written
       if (++slot == ns) { slot = 0; sp ^= 1; }
       if (++tb == NTB) { tb = 0; tp ^= 1; }
+      ++c;
     }
     return;
   }
@@ -255,50 +276,53 @@ __global__ void __launch_bounds__(Shape<MT, RW>::THREADS, 2)
   const int mt = threadIdx.x - (1 + kComputeWarps) * 32;
   const int tm = mt / RW, tr = mt % RW;
   const bool merging = tm < mcount;
-  float acc = 0.0f, first = 0.0f;
-  if (!SWIGLU && merging && a.bias) acc = a.bias[tile * SI_RT + r0 + tr];
   int tb = 0, tp = 0;
-  for (int c = 0; c < nchunks; ++c) {
-    const int cc = c >= npass ? c - npass : c;
-    if (!mbar_wait(bar(tfull, tb), tp, abort_flag)) {
-      *abort_flag = 1;
-      raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
-      return;
-    }
-    if (merging) {
-      // The adds are a serial chain; load the terms 16 at a time ahead of it.
-      const int nvalid = min(CB, KB - cc * CB);
-      const float *Tm = T + tb * S::TERMS + tm * CB * RW + tr;
-      if (SWIGLU && c == npass) {  // the up rows begin
-        first = acc;
-        acc = 0.0f;
+  for (int i = 0; i < nu; ++i) {
+    const int tile = unit_tile(i), r0 = unit_r0(i);
+    float acc = 0.0f, first = 0.0f;
+    if (!SWIGLU && merging && a.bias) acc = a.bias[tile * SI_RT + r0 + tr];
+    for (int c = 0; c < nchunks; ++c) {
+      const int cc = c >= npass ? c - npass : c;
+      if (!mbar_wait(bar(tfull, tb), tp, abort_flag)) {
+        *abort_flag = 1;
+        raise_error(a.err, 6 /* SI_ERR_TIMEOUT */);
+        return;
       }
-      int j = 0;
-      for (; j + 16 <= nvalid; j += 16) {
-        float v[16];
+      if (merging) {
+        // The adds are a serial chain; load the terms 16 at a time ahead of it.
+        const int nvalid = min(CB, KB - cc * CB);
+        const float *Tm = T + tb * S::TERMS + tm * CB * RW + tr;
+        if (SWIGLU && c == npass) {  // the up rows begin
+          first = acc;
+          acc = 0.0f;
+        }
+        int j = 0;
+        for (; j + 16 <= nvalid; j += 16) {
+          float v[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = Tm[(j + q) * RW];
+          for (int q = 0; q < 16; ++q) v[q] = Tm[(j + q) * RW];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) acc = __fadd_rn(acc, v[q]);
+          for (int q = 0; q < 16; ++q) acc = __fadd_rn(acc, v[q]);
+        }
+        for (; j < nvalid; ++j) acc = __fadd_rn(acc, Tm[j * RW]);
       }
-      for (; j < nvalid; ++j) acc = __fadd_rn(acc, Tm[j * RW]);
+      mbar_arrive(bar(tempty, tb));
+      if (++tb == NTB) { tb = 0; tp ^= 1; }
     }
-    mbar_arrive(bar(tempty, tb));
-    if (++tb == NTB) { tb = 0; tp ^= 1; }
-  }
-  if (!merging) return;
-  const int row = tile * SI_RT + r0 + tr;
-  const size_t o = (size_t)(m0 + tm) * a.N + row;
-  if (!SWIGLU) {
-    a.out[o] = a.resid ? __fadd_rn(a.resid[o], acc) : acc;
-  } else {
-    // RW == 32: merge warp m holds token m's 32 outputs of the tile, one Q8 block.
-    const float act = silu_mul(first, acc);
-    if (a.out) a.out[o] = act;
-    uint16_t d16;
-    const int8_t q = q8_lane(act, d16);
-    a.act_qs[o] = q;
-    if (tr == 0) a.act_d[(size_t)(m0 + tm) * (a.N / 32) + tile] = d16;
+    if (!merging) continue;
+    const int row = tile * SI_RT + r0 + tr;
+    const size_t o = (size_t)(m0 + tm) * a.N + row;
+    if (!SWIGLU) {
+      a.out[o] = a.resid ? __fadd_rn(a.resid[o], acc) : acc;
+    } else {
+      // RW == 32: merge warp m holds token m's 32 outputs of the tile, one Q8 block.
+      const float act = silu_mul(first, acc);
+      if (a.out) a.out[o] = act;
+      uint16_t d16;
+      const int8_t q = q8_lane(act, d16);
+      a.act_qs[o] = q;
+      if (tr == 0) a.act_d[(size_t)(m0 + tm) * (a.N / 32) + tile] = d16;
+    }
   }
 }
 
@@ -887,13 +911,25 @@ cudaError_t run(const GemvArgs &a, cudaStream_t s) {
     tmN2 = tmN;
     tmS2 = tmS;
   }
-  auto kern = k_gemv<MT, RW, SWIGLU>;
+  // One CTA per unit, or -- when the units (row slices) number between one
+  // and two CTA slots per SM (two CTAs per SM fit the shared-memory budget) --
+  // one CTA per slot, each streaming its units back to back.
+  const int units = tiles * (SI_RT / RW);
+  int gx = units;
+  {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int slots = 2 * sms;
+    if (units > slots && units <= 2 * slots) gx = slots;
+  }
+  auto kern = gx < units ? k_gemv<MT, RW, SWIGLU, true> : k_gemv<MT, RW, SWIGLU, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid(tiles * (SI_RT / RW), (a.M + MT - 1) / MT);
+  dim3 grid(gx, (a.M + MT - 1) / MT);
   return launch_pdl(kern, grid, dim3(S::THREADS), smem, s, tmN, tmN2, tmS, tmS2, tmX, a, ns);
 }
 

@@ -112,11 +112,12 @@ def test_gemv_bit_exact_vs_oracle(si_ctx, oc, N, K, M, kernel):
 
 @pytest.mark.parametrize("N,K", [(8192, 8192), (10240, 8192), (8192, 29568), (4608, 3584),
                                  (1280, 8192), (2560, 8192)])
-@pytest.mark.parametrize("M", [3, 8, 16])
+@pytest.mark.parametrize("M", [1, 2, 3, 8, 16])
 def test_gemv_mma_equals_dp4a_large(si_ctx, N, K, M):
     """At the 7B/72B decode shapes -- whole-tile CTAs at two or three per SM
-    (10240 rows: 320 tiles) and half-tile CTAs for the tensor-parallel QKV
-    shards (1280, 2560 rows) -- the two GEMV forms return the same bits."""
+    (10240 rows: 320 tiles; the dp4a form then streams two tiles in some
+    CTAs) and half-tile CTAs for the tensor-parallel QKV shards (1280, 2560
+    rows) -- the two GEMV forms return the same bits."""
     m = si_ctx.matrix_synth(N, K, seed=N + K + M)
     x = torch.randn(M, K, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
     torch.cuda.synchronize()
@@ -381,10 +382,12 @@ def test_bad_context_is_rejected_cleanly(si_ctx, oc):
     assert np.all(np.isfinite(y))
 
 
-@pytest.mark.parametrize("I,H", [(18944, 3584), (3712, 8192)])
-@pytest.mark.parametrize("M", [3, 8, 16])
+@pytest.mark.parametrize("I,H", [(18944, 3584), (3712, 8192), (14784, 8192)])
+@pytest.mark.parametrize("M", [1, 2, 3, 8, 16])
 def test_gateup_mma_equals_dp4a(si_ctx, I, H, M):
-    """SwiGLU + Q8 epilogue: both GEMV forms return the same activation bits."""
+    """SwiGLU + Q8 epilogue: both GEMV forms return the same activation bits
+    (the 7B pair's 592 tiles and the TP = 2 shard's 462: the dp4a form streams
+    two tiles per CTA)."""
     mg, mu = si_ctx.matrix_synth(I, H, seed=I + M), si_ctx.matrix_synth(I, H, seed=H + M)
     x = torch.randn(M, H, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
     torch.cuda.synchronize()
