@@ -6,7 +6,9 @@
 //
 // Mapping.  One CTA owns an RW-row slice (32, 16 or 8 rows) of one 32-row
 // tile of the SoA layout and the whole K range, for up to MT tokens; narrow
-// slices give matrices with few tiles enough CTAs to fill the GPU.  The slice
+// slices give matrices with few tiles enough CTAs to fill the GPU, and where
+// the slices number between one and two CTA slots per SM a CTA streams two
+// slices back to back instead of a second wave starting.  The slice
 // streams through a shared-memory ring of up to 8 chunks of CB blocks: a
 // producer thread issues three 2-D TMA loads per chunk (nibbles RW*16 B x CB,
 // their fp16 scales, the int8 activations of the chunk's blocks) on the
